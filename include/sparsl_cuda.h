@@ -1,0 +1,240 @@
+/*
+ * sparsl_cuda.h -- C ABI of the B200 (sm_100a) substrate for sparsl.
+ *
+ * This is the library `src/backend/cuda.rs` of bharathvbcr/sparsl declares
+ * but never provides (cuda.rs:23-44 lists the landing steps).  A Rust host
+ * binds these symbols from `CudaDevice` / `CudaSparse` and adds one
+ * `DeviceInner::Cuda` / `OpResident::Cuda` arm per dispatch site in
+ * src/backend/mod.rs; the shapes arrive already validated, exactly as the
+ * Metal substrate receives them (metal.rs:1048-1057).
+ *
+ * Conventions
+ *  - Every entry point returns a status: SPARSL_OK, or an error whose static
+ *    reason is available from sparsl_last_reason() and whose detail (copy it
+ *    immediately; thread-local) from sparsl_last_error().  The statuses map
+ *    one-to-one onto the reference's error enums:
+ *      SPARSL_ERR_BACKEND     -> OpError::Backend / SparsePlanError::Backend
+ *      SPARSL_ERR_EXECUTION   -> OpError::Execution { operation, detail }
+ *      SPARSL_ERR_ALLOCATION  -> SparsePlanError::Allocation { what }
+ *      SPARSL_ERR_INVALID     -> SparsePlanError::{EmptyRowPtr .. WeightsLen}
+ *                                (detail code in sparsl_plan_error)
+ *      SPARSL_ERR_LENGTH      -> OpError::{Length, TooShort, SizeOverflow}
+ *      SPARSL_ERR_NO_TRANSPOSE-> OpError::TransposeNotPrepared
+ *  - Host pointers are borrowed for the duration of the call only.  Calls
+ *    with host buffers block until the device finished (bounded wait, see
+ *    sparsl_set_timeout_ms) and check the canary tails of the buffers the
+ *    device wrote.  There is no CPU fallback anywhere: with no usable GPU,
+ *    sparsl_device_open fails.
+ *  - bool arrays are uint8_t 0/1 (Rust bool), State arrays are float pairs
+ *    [a0, b0, a1, b1, ...] (src/scan.rs:78-96, repr(C)).
+ *  - Precision: 0 = f32, 1 = binary16, 2 = bfloat16 (WeightPrecision,
+ *    src/backend/mod.rs:588-652).  The library quantises exactly as
+ *    WeightPrecision::quantise (mod.rs:624-641) with the half.rs encoders.
+ *  - Every floating-point result is bit-identical to the reference's
+ *    CpuSequential arm on the same inputs (NaN payloads excepted; NaN class is
+ *    preserved), because every output is one strict left fold with separate
+ *    round-to-nearest multiply and add, as in mod.rs:2259-2267.
+ */
+#ifndef SPARSL_CUDA_H
+#define SPARSL_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  SPARSL_OK = 0,
+  SPARSL_ERR_BACKEND = 1,
+  SPARSL_ERR_EXECUTION = 2,
+  SPARSL_ERR_ALLOCATION = 3,
+  SPARSL_ERR_INVALID = 4,
+  SPARSL_ERR_LENGTH = 5,
+  SPARSL_ERR_NO_TRANSPOSE = 6
+};
+
+/* SparsePlanError variants (src/backend/mod.rs:277-305), in validate_csr's
+ * check order (mod.rs:2116-2182). */
+enum {
+  SPARSL_PLAN_OK = 0,
+  SPARSL_PLAN_EMPTY_ROW_PTR = 1,
+  SPARSL_PLAN_NONZERO_START = 2,
+  SPARSL_PLAN_NOT_MONOTONIC = 3,
+  SPARSL_PLAN_NNZ_MISMATCH = 4,
+  SPARSL_PLAN_NCOLS_MISMATCH = 5,
+  SPARSL_PLAN_COLUMN_OUT_OF_RANGE = 6,
+  SPARSL_PLAN_ROW_UNSORTED = 7,
+  SPARSL_PLAN_TOO_LARGE = 8,
+  SPARSL_PLAN_WEIGHTS_LEN = 9
+};
+
+typedef struct sparsl_dev sparsl_dev;
+typedef struct sparsl_op sparsl_op;
+typedef struct sparsl_net sparsl_net;
+
+/* Validated dimensions (SparseShape, mod.rs:457-503) or the first failure. */
+typedef struct {
+  int32_t code;          /* SPARSL_PLAN_* */
+  uint64_t a, b, c;      /* error payload: index/edge/row, col/end, ncols */
+  uint64_t nrows, ncols, nnz, max_row_nnz;
+} sparsl_shape;
+
+/* ---- diagnostics ------------------------------------------------------- */
+const char *sparsl_last_error(void);   /* thread-local detail of the last failure */
+const char *sparsl_last_reason(void);  /* static reason (&'static str) of the last failure */
+const char *sparsl_version(void);
+/* Completion deadline for host-facing calls (metal.rs:346-355 uses 60 s). */
+void sparsl_set_timeout_ms(uint64_t ms);
+
+/* ---- availability gate: Backend::unavailable_reason (mod.rs:106-112) ---- */
+/* 0 when a usable sm_100 device exists, else SPARSL_ERR_BACKEND with a static
+ * reason.  Replaces cuda::UNAVAILABLE_REASON (cuda.rs:47-48). */
+int sparsl_cuda_probe(const char **reason);
+int sparsl_device_count(void);
+
+/* ---- Device (mod.rs:805-1230) ------------------------------------------ */
+/* Device::try_new(Backend::Cuda) -> open_cuda (mod.rs:882-917). */
+int sparsl_device_open(int ordinal, sparsl_dev **out);
+void sparsl_device_close(sparsl_dev *dev);
+/* Device::device_name (mod.rs:948-954). */
+int sparsl_device_name(sparsl_dev *dev, char *buf, size_t cap);
+/* Device::reset_metal analogue (mod.rs:825-843): clears the process-wide
+ * quarantine only when no call is admitted. */
+int sparsl_device_reset(void);
+int sparsl_quarantined(void);
+/* Device::assoc_scan (mod.rs:1183-1197): in/out are n (a, b) pairs.
+ * Bit-identical to assoc_scan_sequential (scan.rs:298-313). */
+int sparsl_dev_assoc_scan(sparsl_dev *dev, const float *in, uint64_t n, float *out);
+/* Device::lif_integrate (mod.rs:1202-1229). */
+int sparsl_dev_lif_integrate(sparsl_dev *dev, float *v, float *theta, const float *currents,
+                             uint8_t *spikes, uint64_t n, float decay, float v_reset,
+                             float delta_theta);
+
+/* ---- CSR gate: validate_csr (mod.rs:2116-2182) ---------------------------- */
+int sparsl_validate_csr(const uint32_t *row_ptr, uint64_t row_ptr_len, const uint32_t *col,
+                        uint64_t col_len, uint64_t csr_ncols, uint64_t ncols, sparsl_shape *out);
+
+/* ---- narrow codecs (src/half.rs:49-219) ---------------------------------- */
+void sparsl_f32_to_f16_bits(const float *in, uint16_t *out, uint64_t n);
+void sparsl_f32_to_bf16_bits(const float *in, uint16_t *out, uint64_t n);
+void sparsl_quantise(int precision, const float *in, float *out, uint64_t n);
+
+/* ---- SparseOp (mod.rs:1281-2108) ---------------------------------------- */
+/* SparseOp::prepare (mod.rs:1305-1371): validates (the gate above, first
+ * failure wins, reported in *shape), quantises, optionally builds the stable
+ * reverse index (sparse.rs:361-427) and uploads once. */
+int sparsl_op_prepare(sparsl_dev *dev, const uint32_t *row_ptr, uint64_t row_ptr_len,
+                      const uint32_t *col, uint64_t col_len, uint64_t csr_ncols, uint64_t ncols,
+                      const float *weights, uint64_t weights_len, int precision, int with_transpose,
+                      sparsl_shape *shape, sparsl_op **out);
+void sparsl_op_destroy(sparsl_op *op);
+int sparsl_op_shape(sparsl_op *op, sparsl_shape *out);
+int sparsl_op_weight_precision(sparsl_op *op);    /* mod.rs:1582 */
+int sparsl_op_has_transpose(sparsl_op *op);       /* mod.rs:1594 */
+/* SparseOp::set_weights (mod.rs:1392-1409). */
+int sparsl_op_set_weights(sparsl_op *op, const float *weights, uint64_t n);
+/* SparseOp::spmv (mod.rs:1411-1429): y += A x. */
+int sparsl_op_spmv(sparsl_op *op, const float *x, uint64_t x_len, float *y, uint64_t y_len);
+/* SparseOp::spmv_spikes (mod.rs:1449-1468). */
+int sparsl_op_spmv_spikes(sparsl_op *op, const uint32_t *spikes, uint64_t words, float *y,
+                          uint64_t y_len);
+/* SparseOp::spmv_t (mod.rs:1486-1505): y += A^T x. */
+int sparsl_op_spmv_t(sparsl_op *op, const float *x, uint64_t x_len, float *y, uint64_t y_len);
+/* SparseOp::spmm (mod.rs:1528-1571): batch-minor X[ncols][n_vec], Y[nrows][n_vec]. */
+int sparsl_op_spmm(sparsl_op *op, const float *x, uint64_t x_len, uint64_t n_vec, float *y,
+                   uint64_t y_len);
+/* SparseOp::fused_spmv_lif (mod.rs:1609-1636). */
+int sparsl_op_fused_lif(sparsl_op *op, const float *x, uint64_t x_len, float *v, float *theta,
+                        uint8_t *spikes, uint64_t n, float decay, float v_reset, float delta_theta);
+/* SparseOp::fused_spmv_spikes_lif (mod.rs:1644-1678). */
+int sparsl_op_fused_spikes_lif(sparsl_op *op, const uint32_t *spikes_in, uint64_t words, float *v,
+                               float *theta, uint8_t *spikes_out, uint64_t n, float decay,
+                               float v_reset, float delta_theta);
+
+/* ---- resident API (mod.rs:1680-1973) ------------------------------------ */
+int sparsl_op_write_x(sparsl_op *op, const float *x, uint64_t len);              /* :1687 */
+int sparsl_op_write_x_spikes(sparsl_op *op, const uint32_t *s, uint64_t words);  /* :1704 */
+int sparsl_op_write_y(sparsl_op *op, const float *y, uint64_t len);              /* :1720 */
+int sparsl_op_write_lif_state(sparsl_op *op, const float *v, const float *theta,
+                              uint64_t n);                                        /* :1737 */
+int sparsl_op_spmv_resident(sparsl_op *op);                                       /* :1756 */
+int sparsl_op_fused_lif_resident(sparsl_op *op, float decay, float v_reset,
+                                 float delta_theta);                              /* :1792 */
+int sparsl_op_fused_spikes_lif_resident(sparsl_op *op, float decay, float v_reset,
+                                        float delta_theta);                       /* :1827 */
+int sparsl_op_pack_resident_spikes(sparsl_op *op);                                /* :1865 */
+/* fused_spmv_spikes_lif_recurrent_steps (mod.rs:1889-1932).  Also records
+ * the spike count of every tick in a device-side trace (see below). */
+int sparsl_op_recurrent_steps(sparsl_op *op, float decay, float v_reset, float delta_theta,
+                              uint64_t steps);
+int sparsl_op_sync_y(sparsl_op *op, float *y, uint64_t len);                      /* :1937 */
+int sparsl_op_sync_lif_state(sparsl_op *op, float *v, float *theta, uint8_t *spikes,
+                             uint64_t n);                                         /* :1960 */
+int sparsl_op_sync_x_spikes(sparsl_op *op, uint32_t *s, uint64_t words);
+
+/* ---- tick trace (extension; no reference counterpart) -------------------- */
+/* Spike counts of the ticks run by the last sparsl_op_recurrent_steps call. */
+int sparsl_op_spike_trace(sparsl_op *op, uint32_t *out, uint64_t cap, uint64_t *n_out);
+/* Ascending indices of the cells that fired in the last recurrent tick, as
+ * compacted on the device by warp ballots and a decoupled look-back. */
+int sparsl_op_spike_indices(sparsl_op *op, uint32_t *out, uint64_t cap, uint64_t *count);
+
+/* ---- zero-copy device-pointer entry points (extension) ------------------- */
+/* CUDA analogue of bind_mtl_x / bind_mtl_y (mod.rs:1975-2098): operands are
+ * device pointers and the work is only enqueued on `stream` (cudaStream_t, or
+ * NULL for the operator's own stream).  No wait, no canary check. */
+int sparsl_op_spmv_device(sparsl_op *op, const float *d_x, float *d_y, void *stream);
+int sparsl_op_spmv_spikes_device(sparsl_op *op, const uint32_t *d_spikes, float *d_y, void *stream);
+int sparsl_op_spmv_t_device(sparsl_op *op, const float *d_x, float *d_y, void *stream);
+int sparsl_op_spmm_device(sparsl_op *op, const float *d_x, uint64_t n_vec, float *d_y, void *stream);
+int sparsl_dev_assoc_scan_device(sparsl_dev *dev, const float *d_in, uint64_t n, float *d_out,
+                                 void *stream);
+/* Enqueue recurrent ticks on the operator's stream without waiting. */
+int sparsl_op_recurrent_steps_async(sparsl_op *op, float decay, float v_reset, float delta_theta,
+                                    uint64_t steps);
+void *sparsl_op_stream(sparsl_op *op);
+void *sparsl_dev_stream(sparsl_dev *dev);
+int sparsl_op_wait(sparsl_op *op);   /* bounded wait + device error word check */
+int sparsl_dev_wait(sparsl_dev *dev);
+/* Elements the last device scan had to replay serially (repair statistics). */
+int sparsl_dev_scan_stats(sparsl_dev *dev, uint64_t *repaired, uint64_t *segments);
+
+/* ---- pinned host memory (for end-to-end copies at DMA speed) ------------- */
+void *sparsl_host_alloc(uint64_t bytes);
+void sparsl_host_free(void *p);
+void *sparsl_device_alloc(sparsl_dev *dev, uint64_t bytes);
+void sparsl_device_free(void *p);
+int sparsl_memcpy(void *dst, const void *src, uint64_t bytes); /* cudaMemcpyDefault, synchronous */
+
+/* ---- multi-GPU network tick (extension; the reference is single device) -- */
+/* One rank's share of a recurrent LIF network: `blocks` are row-block
+ * operators over the global spike vector (ncols == n_global), together
+ * covering rows [row_offset, row_offset + local_rows), each starting on a
+ * multiple of 32.  Every tick runs the fused spike kernel on each block, then
+ * all-gathers the packed spike words of all ranks with NCCL (in place, one
+ * ncclAllGather per tick), then counts the global spikes into a trace.  With
+ * nranks == 1 no NCCL is loaded.  nccl_id is 128 bytes from
+ * sparsl_nccl_unique_id on rank 0, distributed by the caller. */
+int sparsl_nccl_unique_id(uint8_t out[128]);
+int sparsl_net_create(sparsl_dev *dev, sparsl_op *const *blocks, uint32_t n_blocks,
+                      uint64_t row_offset, uint64_t n_global, int rank, int nranks,
+                      const uint8_t *nccl_id, sparsl_net **out);
+void sparsl_net_destroy(sparsl_net *net);
+int sparsl_net_write_state(sparsl_net *net, const uint32_t *x_spikes_global, uint64_t words,
+                           const float *v_local, const float *theta_local, uint64_t local_rows);
+int sparsl_net_steps(sparsl_net *net, float decay, float v_reset, float delta_theta,
+                     uint64_t steps);
+int sparsl_net_steps_async(sparsl_net *net, float decay, float v_reset, float delta_theta,
+                           uint64_t steps);
+int sparsl_net_wait(sparsl_net *net);
+void *sparsl_net_stream(sparsl_net *net);
+int sparsl_net_read_state(sparsl_net *net, uint32_t *x_spikes_global, uint64_t words, float *v_local,
+                          float *theta_local, uint64_t local_rows);
+int sparsl_net_trace(sparsl_net *net, uint32_t *out, uint64_t cap, uint64_t *n_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SPARSL_CUDA_H */

@@ -1,0 +1,1406 @@
+// Runtime and C ABI of libsparsl_cuda (declared in include/sparsl_cuda.h).
+//
+// Mirrors the reference's substrate contract (src/backend/metal.rs):
+//  * one stream, one event and one mutex per operator (metal.rs:30-34);
+//  * every device buffer a kernel writes carries a 64-word canary tail that is
+//    checked after each host-facing dispatch (metal.rs:321-344);
+//  * completion is awaited with a deadline, never unbounded; a timeout or a
+//    sticky device error quarantines the backend process-wide and new calls
+//    are refused until sparsl_device_reset (metal.rs:346-445);
+//  * no CPU fallback: every entry point either runs on the GPU or fails.
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include <nccl.h>
+
+#include "../../include/sparsl_cuda.h"
+#include "common.cuh"
+#include "host.hpp"
+#include "misc.cuh"
+#include "rows.cuh"
+#include "scan.cuh"
+
+using namespace sparsl;
+
+namespace {
+
+thread_local std::string t_err;
+thread_local const char* t_reason = "";
+std::atomic<uint64_t> g_timeout_ms{60000};
+std::atomic<bool> g_quarantine{false};
+std::atomic<int> g_admitted{0};
+
+int fail(int code, const char* reason, const std::string& detail) {
+  t_reason = reason;
+  t_err = detail;
+  return code;
+}
+
+int fail_cuda(const char* operation, cudaError_t e) {
+  return fail(SPARSL_ERR_EXECUTION, operation, std::string(operation) + ": " + cudaGetErrorString(e));
+}
+
+// Admission: refuse new work while quarantined, count work in flight.
+struct Admission {
+  bool ok;
+  Admission() {
+    g_admitted.fetch_add(1);
+    ok = !g_quarantine.load();
+  }
+  ~Admission() { g_admitted.fetch_sub(1); }
+};
+
+#define ADMIT()                                                                                   \
+  Admission adm_;                                                                                 \
+  if (!adm_.ok)                                                                                   \
+    return fail(SPARSL_ERR_BACKEND, "CUDA backend is quarantined after a failed or timed-out dispatch", \
+                "CUDA backend is quarantined; call sparsl_device_reset once no work is in flight")
+
+#define CK(op, expr)                        \
+  do {                                      \
+    cudaError_t ck_e_ = (expr);             \
+    if (ck_e_ != cudaSuccess) return fail_cuda(op, ck_e_); \
+  } while (0)
+
+constexpr size_t kAlign = 256;
+inline size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+inline uint64_t packed_len(uint64_t n) { return (n + 31) / 32; }
+
+// A device allocation with an optional canary tail after its payload.
+struct DBuf {
+  void* p = nullptr;
+  size_t bytes = 0;  // payload capacity
+  bool guarded = false;
+  template <class T>
+  T* as() const {
+    return static_cast<T*>(p);
+  }
+  const uint32_t* canary() const { return reinterpret_cast<const uint32_t*>(static_cast<char*>(p) + round_up(bytes, kAlign)); }
+};
+
+cudaError_t dalloc(DBuf& b, size_t bytes, bool guard, cudaStream_t s) {
+  b.bytes = std::max<size_t>(bytes, 16);
+  b.guarded = guard;
+  const size_t total = round_up(b.bytes, kAlign) + (guard ? kCanaryWords * 4 : 0) + kAlign;
+  cudaError_t e = cudaMalloc(&b.p, total);
+  if (e != cudaSuccess) {
+    b.p = nullptr;
+    return e;
+  }
+  if (guard) {
+    e = launch_fill(const_cast<uint32_t*>(b.canary()), kCanaryWords, kCanaryBits, s);
+  }
+  return e;
+}
+
+void dfree(DBuf& b) {
+  if (b.p) cudaFree(b.p);
+  b.p = nullptr;
+  b.bytes = 0;
+}
+
+// Grow-only buffer.
+cudaError_t ensure(DBuf& b, size_t bytes, bool guard, cudaStream_t s) {
+  if (b.p && b.bytes >= bytes) return cudaSuccess;
+  if (b.p) {
+    cudaStreamSynchronize(s);
+    dfree(b);
+  }
+  return dalloc(b, bytes, guard, s);
+}
+
+std::string describe_dev_err(uint32_t bits) {
+  std::string d;
+  if (bits & DEVERR_LOOKBACK_TIMEOUT) d += "a bounded look-back wait expired; ";
+  if (bits & DEVERR_CANARY) d += "a canary tail was overwritten (out-of-bounds device write); ";
+  if (bits & DEVERR_REPAIR_LIMIT) d += "scan repair exceeded its bound; ";
+  return d.empty() ? std::string("device error word set") : d;
+}
+
+// Bounded wait for everything enqueued on `s` so far, then the device error
+// word.  `err_h` is pinned host memory the error word was copied into.
+int wait_bounded(cudaStream_t s, cudaEvent_t ev, uint32_t* err_d, uint32_t* err_h, const char* operation) {
+  cudaError_t e = cudaMemcpyAsync(err_h, err_d, sizeof(uint32_t), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaEventRecord(ev, s);
+  if (e != cudaSuccess) {
+    g_quarantine.store(true);
+    return fail_cuda(operation, e);
+  }
+  const auto t0 = std::chrono::steady_clock::now();
+  const auto limit = std::chrono::milliseconds(g_timeout_ms.load());
+  uint64_t polls = 0;
+  for (;;) {
+    e = cudaEventQuery(ev);
+    if (e == cudaSuccess) break;
+    if (e != cudaErrorNotReady) {
+      g_quarantine.store(true);
+      return fail(SPARSL_ERR_EXECUTION, operation,
+                  std::string(operation) + ": device execution failed: " + cudaGetErrorString(e) +
+                      "; backend quarantined");
+    }
+    if (std::chrono::steady_clock::now() - t0 > limit) {
+      g_quarantine.store(true);
+      return fail(SPARSL_ERR_EXECUTION, operation,
+                  std::string(operation) + ": did not complete within " + std::to_string(g_timeout_ms.load()) +
+                      " ms; backend quarantined");
+    }
+    // ~100 us of spinning, then short sleeps (metal.rs:3108-3152).
+    if (++polls > 200) std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+  const uint32_t bits = *err_h;
+  if (bits) {
+    *err_h = 0;
+    cudaMemsetAsync(err_d, 0, sizeof(uint32_t), s);
+    cudaStreamSynchronize(s);
+    return fail(SPARSL_ERR_EXECUTION, operation, std::string(operation) + ": " + describe_dev_err(bits));
+  }
+  return SPARSL_OK;
+}
+
+struct ErrWord {
+  uint32_t* d = nullptr;
+  uint32_t* h = nullptr;
+  cudaError_t init() {
+    cudaError_t e = cudaMalloc(&d, 64);
+    if (e != cudaSuccess) return e;
+    e = cudaMemset(d, 0, 64);
+    if (e != cudaSuccess) return e;
+    return cudaHostAlloc(&h, 64, cudaHostAllocDefault);
+  }
+  void release() {
+    if (d) cudaFree(d);
+    if (h) cudaFreeHost(h);
+    d = h = nullptr;
+  }
+};
+
+// ---- NCCL, loaded on demand so single-GPU users never need it ----
+struct NcclApi {
+  bool loaded = false;
+  void* handle = nullptr;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+std::mutex g_nccl_mu;
+NcclApi g_nccl;
+
+const char* nccl_load() {
+  std::lock_guard<std::mutex> lk(g_nccl_mu);
+  if (g_nccl.loaded) return nullptr;
+  void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+  if (!h) return "libnccl.so.2 could not be loaded";
+  auto sym = [&](const char* n) { return dlsym(h, n); };
+  g_nccl.GetUniqueId = reinterpret_cast<decltype(g_nccl.GetUniqueId)>(sym("ncclGetUniqueId"));
+  g_nccl.CommInitRankConfig = reinterpret_cast<decltype(g_nccl.CommInitRankConfig)>(sym("ncclCommInitRankConfig"));
+  g_nccl.CommGetAsyncError = reinterpret_cast<decltype(g_nccl.CommGetAsyncError)>(sym("ncclCommGetAsyncError"));
+  g_nccl.AllGather = reinterpret_cast<decltype(g_nccl.AllGather)>(sym("ncclAllGather"));
+  g_nccl.CommDestroy = reinterpret_cast<decltype(g_nccl.CommDestroy)>(sym("ncclCommDestroy"));
+  g_nccl.CommAbort = reinterpret_cast<decltype(g_nccl.CommAbort)>(sym("ncclCommAbort"));
+  g_nccl.GetErrorString = reinterpret_cast<decltype(g_nccl.GetErrorString)>(sym("ncclGetErrorString"));
+  if (!g_nccl.GetUniqueId || !g_nccl.CommInitRankConfig || !g_nccl.CommGetAsyncError || !g_nccl.AllGather ||
+      !g_nccl.CommDestroy || !g_nccl.CommAbort || !g_nccl.GetErrorString)
+    return "libnccl.so.2 lacks a required symbol";
+  g_nccl.handle = h;
+  g_nccl.loaded = true;
+  return nullptr;
+}
+
+}  // namespace
+
+// ==========================================================================
+// Device
+// ==========================================================================
+struct sparsl_dev {
+  int ordinal = 0;
+  std::string name;
+  int sm_count = 0;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev = nullptr;
+  std::mutex mu;
+  ErrWord err;
+  DBuf scan_in, scan_out, scan_scr;
+  uint64_t scan_cap = 0;
+  ScanScratch sc{};
+  bool scan_dirty = false;
+  DBuf lv, lth, lcur, lspk;
+};
+
+namespace {
+int dev_scan_prepare(sparsl_dev* d, uint64_t n) {
+  if (d->scan_cap >= n && !d->scan_dirty && d->scan_scr.p) return SPARSL_OK;
+  const uint64_t cap = std::max<uint64_t>(n, d->scan_cap);
+  const size_t bytes = scan_scratch_bytes(cap);
+  if (!d->scan_scr.p || d->scan_scr.bytes < bytes) {
+    cudaStreamSynchronize(d->stream);
+    dfree(d->scan_scr);
+    if (dalloc(d->scan_scr, bytes, false, d->stream) != cudaSuccess)
+      return fail(SPARSL_ERR_ALLOCATION, "scan scratch", "device allocation failed for scan scratch");
+  }
+  CK("assoc_scan", cudaMemsetAsync(d->scan_scr.p, 0, d->scan_scr.bytes, d->stream));
+  d->sc = scan_scratch_carve(d->scan_scr.p, cap);
+  d->scan_cap = cap;
+  d->scan_dirty = false;
+  return SPARSL_OK;
+}
+}  // namespace
+
+// ==========================================================================
+// Operator
+// ==========================================================================
+struct sparsl_op {
+  sparsl_dev* dev = nullptr;
+  uint32_t nrows = 0, ncols = 0, nnz = 0, max_row_nnz = 0;
+  int precision = 0;
+  bool has_t = false;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev = nullptr;
+  std::mutex mu;
+  ErrWord err;
+  DBuf row_ptr, col, w;
+  DBuf col_ptr, csc_row, csc_eidx;
+  // resident scratch (the write / step / sync API)
+  DBuf rx, rxs[2], ry, rv, rth, rspk;
+  int cur = 0;
+  // compaction + trace
+  DBuf idx_list, tile_flags, ticket, trace;
+  uint64_t trace_cap = 0, last_steps = 0;
+  // staging for host-slice calls (kept apart from resident state, as the
+  // reference CPU arm's slice API never touches its resident scratch)
+  DBuf sx, sbits, sy, sv, sth, sspk;
+  uint64_t words() const { return packed_len(ncols); }
+};
+
+namespace {
+
+int wait_op(sparsl_op* op, const char* operation) {
+  return wait_bounded(op->stream, op->ev, op->err.d, op->err.h, operation);
+}
+
+// Check every guarded buffer of the operator on its stream.
+cudaError_t check_canaries(sparsl_op* op) {
+  CanarySet set;
+  auto add = [&](const DBuf& b) {
+    if (b.p && b.guarded && set.count < CanarySet::kMax) set.ptr[set.count++] = b.canary();
+  };
+  add(op->ry);
+  add(op->rv);
+  add(op->rth);
+  add(op->rspk);
+  add(op->rxs[0]);
+  add(op->rxs[1]);
+  add(op->idx_list);
+  add(op->trace);
+  add(op->sy);
+  add(op->sv);
+  add(op->sth);
+  add(op->sspk);
+  return launch_canary_check(set, op->err.d, op->stream);
+}
+
+int finish(sparsl_op* op, const char* operation) {
+  cudaError_t e = check_canaries(op);
+  if (e != cudaSuccess) return fail_cuda(operation, e);
+  return wait_op(op, operation);
+}
+
+int wkind_of(int precision) { return precision == 1 ? W_F16 : precision == 2 ? W_BF16 : W_F32; }
+
+RowLaunch fwd_launch(sparsl_op* op) {
+  RowLaunch p;
+  p.ptr = op->row_ptr.as<uint32_t>();
+  p.idx = op->col.as<uint32_t>();
+  p.w = op->w.p;
+  p.wkind = wkind_of(op->precision);
+  p.nlines = op->nrows;
+  p.err = op->err.d;
+  return p;
+}
+
+void set_bits_mode(RowLaunch& p, const uint32_t* bits, uint64_t words) {
+  p.xbits = bits;
+  p.xbits_words = (uint32_t)words;
+  p.xmode = words <= kBitsSmemMaxWords ? X_BITS_SMEM : X_BITS_GLOBAL;
+}
+
+int check_len(const char* what, uint64_t got, uint64_t expected) {
+  if (got == expected) return SPARSL_OK;
+  return fail(SPARSL_ERR_LENGTH, what,
+              std::string("`") + what + "` must have length " + std::to_string(expected) + ", got " +
+                  std::to_string(got));
+}
+int check_min(const char* what, uint64_t got, uint64_t min) {
+  if (got >= min) return SPARSL_OK;
+  return fail(SPARSL_ERR_LENGTH, what,
+              std::string("`") + what + "` must have length >= " + std::to_string(min) + ", got " +
+                  std::to_string(got));
+}
+
+#define TRY(expr)                 \
+  do {                            \
+    int try_rc_ = (expr);         \
+    if (try_rc_ != SPARSL_OK) return try_rc_; \
+  } while (0)
+
+#define ALLOC(buf, bytes, guard, what)                                                     \
+  do {                                                                                     \
+    if (ensure((buf), (bytes), (guard), op->stream) != cudaSuccess)                        \
+      return fail(SPARSL_ERR_ALLOCATION, what, std::string("device allocation failed for ") + what); \
+  } while (0)
+
+int ensure_trace(sparsl_op* op, uint64_t steps) {
+  if (op->trace.p && op->trace_cap >= steps) return SPARSL_OK;
+  uint64_t cap = std::max<uint64_t>(steps, std::max<uint64_t>(1024, op->trace_cap * 2));
+  ALLOC(op->trace, cap * 4, true, "spike trace");
+  op->trace_cap = cap;
+  return SPARSL_OK;
+}
+
+}  // namespace
+
+// ==========================================================================
+// C ABI
+// ==========================================================================
+extern "C" {
+
+const char* sparsl_last_error(void) { return t_err.c_str(); }
+const char* sparsl_last_reason(void) { return t_reason; }
+const char* sparsl_version(void) { return "sparsl-cuda 0.1.0 (sm_100a)"; }
+void sparsl_set_timeout_ms(uint64_t ms) { g_timeout_ms.store(ms ? ms : 1); }
+
+int sparsl_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) return 0;
+  return n;
+}
+
+int sparsl_cuda_probe(const char** reason) {
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  const char* why = nullptr;
+  if (e != cudaSuccess || n == 0) {
+    why = "no CUDA device is visible to this process";
+  } else {
+    int sm100 = 0;
+    for (int i = 0; i < n; ++i) {
+      int major = 0, minor = 0;
+      cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, i);
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, i);
+      if (major == 10 && minor == 0) sm100 = 1;
+    }
+    if (!sm100) why = "no sm_100 (B200-class) device: this library is built for sm_100a only";
+  }
+  if (!why && g_quarantine.load()) why = "CUDA backend is quarantined after a failed or timed-out dispatch";
+  if (reason) *reason = why;
+  if (why) return fail(SPARSL_ERR_BACKEND, why, why);
+  return SPARSL_OK;
+}
+
+int sparsl_device_open(int ordinal, sparsl_dev** out) {
+  if (!out) return fail(SPARSL_ERR_INVALID, "null output", "sparsl_device_open: out is null");
+  *out = nullptr;
+  const char* why = nullptr;
+  TRY(sparsl_cuda_probe(&why));
+  int n = 0;
+  cudaGetDeviceCount(&n);
+  if (ordinal < 0 || ordinal >= n) return fail(SPARSL_ERR_BACKEND, "no such CUDA device", "ordinal out of range");
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, ordinal);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, ordinal);
+  if (major != 10 || minor != 0)
+    return fail(SPARSL_ERR_BACKEND, "device is not sm_100", "the requested device is not sm_100 (B200-class)");
+  CK("device_open", cudaSetDevice(ordinal));
+  auto* d = new sparsl_dev();
+  d->ordinal = ordinal;
+  cudaDeviceProp prop{};
+  cudaGetDeviceProperties(&prop, ordinal);
+  d->name = prop.name;
+  d->sm_count = prop.multiProcessorCount;
+  cudaError_t e = cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&d->ev, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = d->err.init();
+  if (e != cudaSuccess) {
+    delete d;
+    return fail_cuda("device_open", e);
+  }
+  *out = d;
+  return SPARSL_OK;
+}
+
+void sparsl_device_close(sparsl_dev* d) {
+  if (!d) return;
+  cudaSetDevice(d->ordinal);
+  cudaStreamSynchronize(d->stream);
+  dfree(d->scan_in);
+  dfree(d->scan_out);
+  dfree(d->scan_scr);
+  dfree(d->lv);
+  dfree(d->lth);
+  dfree(d->lcur);
+  dfree(d->lspk);
+  d->err.release();
+  cudaEventDestroy(d->ev);
+  cudaStreamDestroy(d->stream);
+  delete d;
+}
+
+int sparsl_device_name(sparsl_dev* d, char* buf, size_t cap) {
+  if (!d || !buf || cap == 0) return fail(SPARSL_ERR_INVALID, "null argument", "sparsl_device_name");
+  std::snprintf(buf, cap, "%s", d->name.c_str());
+  return SPARSL_OK;
+}
+
+int sparsl_device_reset(void) {
+  // Refuse while any call is admitted (mod.rs:825-843).
+  if (g_admitted.load() > 0)
+    return fail(SPARSL_ERR_BACKEND, "reset refused: admissions outstanding",
+                "reset refused: a call is still admitted");
+  g_quarantine.store(false);
+  return SPARSL_OK;
+}
+
+int sparsl_quarantined(void) { return g_quarantine.load() ? 1 : 0; }
+
+int sparsl_validate_csr(const uint32_t* row_ptr, uint64_t row_ptr_len, const uint32_t* col, uint64_t col_len,
+                        uint64_t csr_ncols, uint64_t ncols, sparsl_shape* out) {
+  PlanResult r = validate_csr(row_ptr, row_ptr_len, col, col_len, csr_ncols, ncols);
+  if (out) {
+    out->code = r.code;
+    out->a = r.a;
+    out->b = r.b;
+    out->c = r.c;
+    out->nrows = r.nrows;
+    out->ncols = r.ncols;
+    out->nnz = r.nnz;
+    out->max_row_nnz = r.max_row_nnz;
+  }
+  if (r.code != PLAN_OK) return fail(SPARSL_ERR_INVALID, "invalid CSR", "CSR failed validation");
+  return SPARSL_OK;
+}
+
+void sparsl_f32_to_f16_bits(const float* in, uint16_t* out, uint64_t n) { encode_narrow(1, in, out, n); }
+void sparsl_f32_to_bf16_bits(const float* in, uint16_t* out, uint64_t n) { encode_narrow(2, in, out, n); }
+void sparsl_quantise(int precision, const float* in, float* out, uint64_t n) { quantise(precision, in, out, n); }
+
+// ---- device-level ops ----------------------------------------------------
+int sparsl_dev_assoc_scan(sparsl_dev* d, const float* in, uint64_t n, float* out) {
+  ADMIT();
+  if (!d) return fail(SPARSL_ERR_INVALID, "null device", "assoc_scan: null device");
+  if (n == 0) return SPARSL_OK;
+  std::lock_guard<std::mutex> lk(d->mu);
+  CK("assoc_scan", cudaSetDevice(d->ordinal));
+  const size_t bytes = n * 8;
+  if (ensure(d->scan_in, bytes, false, d->stream) != cudaSuccess ||
+      ensure(d->scan_out, bytes, true, d->stream) != cudaSuccess)
+    return fail(SPARSL_ERR_ALLOCATION, "scan buffers", "device allocation failed for scan buffers");
+  TRY(dev_scan_prepare(d, n));
+  CK("assoc_scan", cudaMemcpyAsync(d->scan_in.p, in, bytes, cudaMemcpyHostToDevice, d->stream));
+  CK("assoc_scan", launch_scan(d->scan_in.as<float>(), d->scan_out.as<float>(), n, d->sc, d->err.d, d->stream));
+  CK("assoc_scan", cudaMemcpyAsync(out, d->scan_out.p, bytes, cudaMemcpyDeviceToHost, d->stream));
+  CanarySet set;
+  set.ptr[set.count++] = d->scan_out.canary();
+  CK("assoc_scan", launch_canary_check(set, d->err.d, d->stream));
+  int rc = wait_bounded(d->stream, d->ev, d->err.d, d->err.h, "assoc_scan");
+  if (rc != SPARSL_OK) d->scan_dirty = true;
+  return rc;
+}
+
+int sparsl_dev_assoc_scan_device(sparsl_dev* d, const float* d_in, uint64_t n, float* d_out, void* stream) {
+  ADMIT();
+  if (!d) return fail(SPARSL_ERR_INVALID, "null device", "assoc_scan: null device");
+  if (n == 0) return SPARSL_OK;
+  std::lock_guard<std::mutex> lk(d->mu);
+  CK("assoc_scan", cudaSetDevice(d->ordinal));
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : d->stream;
+  if (d->scan_cap < n || d->scan_dirty) {
+    cudaStreamSynchronize(s);
+    TRY(dev_scan_prepare(d, n));
+    CK("assoc_scan", cudaStreamSynchronize(d->stream));
+  }
+  CK("assoc_scan", launch_scan(d_in, d_out, n, d->sc, d->err.d, s));
+  return SPARSL_OK;
+}
+
+int sparsl_dev_scan_stats(sparsl_dev* d, uint64_t* repaired, uint64_t* segments) {
+  if (!d || !d->scan_scr.p) return fail(SPARSL_ERR_INVALID, "no scan has run", "no scan has run");
+  std::lock_guard<std::mutex> lk(d->mu);
+  uint32_t st[2] = {0, 0};
+  CK("scan_stats", cudaSetDevice(d->ordinal));
+  CK("scan_stats", cudaMemcpyAsync(st, d->sc.repair_stats, 8, cudaMemcpyDeviceToHost, d->stream));
+  CK("scan_stats", cudaStreamSynchronize(d->stream));
+  if (repaired) *repaired = st[0];
+  if (segments) *segments = st[1];
+  return SPARSL_OK;
+}
+
+int sparsl_dev_lif_integrate(sparsl_dev* d, float* v, float* theta, const float* cur, uint8_t* spk, uint64_t n,
+                             float decay, float v_reset, float dtheta) {
+  ADMIT();
+  if (!d) return fail(SPARSL_ERR_INVALID, "null device", "lif_integrate: null device");
+  if (n == 0) return SPARSL_OK;
+  std::lock_guard<std::mutex> lk(d->mu);
+  CK("lif_integrate", cudaSetDevice(d->ordinal));
+  if (ensure(d->lv, n * 4, true, d->stream) != cudaSuccess || ensure(d->lth, n * 4, true, d->stream) != cudaSuccess ||
+      ensure(d->lcur, n * 4, false, d->stream) != cudaSuccess || ensure(d->lspk, n, true, d->stream) != cudaSuccess)
+    return fail(SPARSL_ERR_ALLOCATION, "lif buffers", "device allocation failed for LIF buffers");
+  CK("lif_integrate", cudaMemcpyAsync(d->lv.p, v, n * 4, cudaMemcpyHostToDevice, d->stream));
+  CK("lif_integrate", cudaMemcpyAsync(d->lth.p, theta, n * 4, cudaMemcpyHostToDevice, d->stream));
+  CK("lif_integrate", cudaMemcpyAsync(d->lcur.p, cur, n * 4, cudaMemcpyHostToDevice, d->stream));
+  CK("lif_integrate", launch_lif_integrate(d->lv.as<float>(), d->lth.as<float>(), d->lcur.as<float>(),
+                                           d->lspk.as<uint8_t>(), n, decay, v_reset, dtheta, d->stream));
+  CK("lif_integrate", cudaMemcpyAsync(v, d->lv.p, n * 4, cudaMemcpyDeviceToHost, d->stream));
+  CK("lif_integrate", cudaMemcpyAsync(theta, d->lth.p, n * 4, cudaMemcpyDeviceToHost, d->stream));
+  CK("lif_integrate", cudaMemcpyAsync(spk, d->lspk.p, n, cudaMemcpyDeviceToHost, d->stream));
+  CanarySet set;
+  set.ptr[set.count++] = d->lv.canary();
+  set.ptr[set.count++] = d->lth.canary();
+  set.ptr[set.count++] = d->lspk.canary();
+  CK("lif_integrate", launch_canary_check(set, d->err.d, d->stream));
+  return wait_bounded(d->stream, d->ev, d->err.d, d->err.h, "lif_integrate");
+}
+
+void* sparsl_dev_stream(sparsl_dev* d) { return d ? d->stream : nullptr; }
+int sparsl_dev_wait(sparsl_dev* d) {
+  if (!d) return fail(SPARSL_ERR_INVALID, "null device", "null device");
+  cudaSetDevice(d->ordinal);
+  return wait_bounded(d->stream, d->ev, d->err.d, d->err.h, "device wait");
+}
+
+// ---- operator ------------------------------------------------------------
+int sparsl_op_prepare(sparsl_dev* d, const uint32_t* row_ptr, uint64_t row_ptr_len, const uint32_t* col,
+                      uint64_t col_len, uint64_t csr_ncols, uint64_t ncols, const float* weights,
+                      uint64_t weights_len, int precision, int with_transpose, sparsl_shape* shape,
+                      sparsl_op** out) {
+  ADMIT();
+  if (!out || !d) return fail(SPARSL_ERR_INVALID, "null argument", "sparsl_op_prepare: null argument");
+  *out = nullptr;
+  sparsl_shape sh{};
+  int rc = sparsl_validate_csr(row_ptr, row_ptr_len, col, col_len, csr_ncols, ncols, &sh);
+  if (shape) *shape = sh;
+  if (rc != SPARSL_OK) return rc;
+  if (weights_len != sh.nnz) {
+    if (shape) {
+      shape->code = SPARSL_PLAN_WEIGHTS_LEN;
+      shape->a = sh.nnz;
+      shape->b = weights_len;
+    }
+    return fail(SPARSL_ERR_INVALID, "weights length", "weights must have one entry per non-zero");
+  }
+  if (precision < 0 || precision > 2) return fail(SPARSL_ERR_INVALID, "precision", "unknown weight precision");
+  CK("prepare", cudaSetDevice(d->ordinal));
+  auto* op = new sparsl_op();
+  op->dev = d;
+  op->nrows = (uint32_t)sh.nrows;
+  op->ncols = (uint32_t)sh.ncols;
+  op->nnz = (uint32_t)sh.nnz;
+  op->max_row_nnz = (uint32_t)sh.max_row_nnz;
+  op->precision = precision;
+  op->has_t = with_transpose != 0;
+  auto bail = [&](int code) {
+    sparsl_op_destroy(op);
+    return code;
+  };
+  if (cudaStreamCreateWithFlags(&op->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&op->ev, cudaEventDisableTiming) != cudaSuccess || op->err.init() != cudaSuccess)
+    return bail(fail(SPARSL_ERR_BACKEND, "stream creation failed", "could not create operator stream"));
+  const uint64_t nnz = sh.nnz, nrows = sh.nrows, nc = sh.ncols;
+  const uint64_t words = packed_len(nc);
+  const size_t wbytes = precision == 0 ? 4 : 2;
+  // Every array gets 16 bytes of slack so vector loads near the end stay in bounds.
+#define PALLOC(buf, bytes, guard, what)                                                    \
+  do {                                                                                     \
+    if (dalloc((buf), (bytes) + 16, (guard), op->stream) != cudaSuccess)                   \
+      return bail(fail(SPARSL_ERR_ALLOCATION, what, std::string("device allocation failed for ") + what)); \
+  } while (0)
+  PALLOC(op->row_ptr, (nrows + 1) * 4, false, "row_ptr");
+  PALLOC(op->col, nnz * 4, false, "col");
+  PALLOC(op->w, nnz * wbytes, false, "values");
+  PALLOC(op->rx, nc * 4, false, "x");
+  PALLOC(op->rxs[0], words * 4, true, "x_spikes");
+  PALLOC(op->rxs[1], words * 4, true, "x_spikes");
+  PALLOC(op->ry, nrows * 4, true, "y");
+  PALLOC(op->rv, nrows * 4, true, "v");
+  PALLOC(op->rth, nrows * 4, true, "theta");
+  PALLOC(op->rspk, nrows, true, "spikes");
+  PALLOC(op->idx_list, nrows * 4, true, "spike index list");
+  PALLOC(op->tile_flags, ((uint64_t)row_tiles(op->nrows) + 1) * 8, false, "tile flags");
+  PALLOC(op->ticket, 64, false, "tile ticket");
+  if (cudaMemcpyAsync(op->row_ptr.p, row_ptr, (nrows + 1) * 4, cudaMemcpyHostToDevice, op->stream) != cudaSuccess)
+    return bail(fail_cuda("prepare", cudaGetLastError()));
+  if (nnz) {
+    if (cudaMemcpyAsync(op->col.p, col, nnz * 4, cudaMemcpyHostToDevice, op->stream) != cudaSuccess)
+      return bail(fail_cuda("prepare", cudaGetLastError()));
+  }
+  std::vector<uint16_t> narrow;
+  if (nnz) {
+    if (precision == 0) {
+      if (cudaMemcpyAsync(op->w.p, weights, nnz * 4, cudaMemcpyHostToDevice, op->stream) != cudaSuccess)
+        return bail(fail_cuda("prepare", cudaGetLastError()));
+    } else {
+      narrow.resize(nnz);
+      encode_narrow(precision, weights, narrow.data(), nnz);
+      if (cudaMemcpyAsync(op->w.p, narrow.data(), nnz * 2, cudaMemcpyHostToDevice, op->stream) != cudaSuccess)
+        return bail(fail_cuda("prepare", cudaGetLastError()));
+    }
+  }
+  std::vector<uint32_t> cp, cr, ce;
+  if (op->has_t) {
+    cp.resize(nc + 1);
+    cr.resize(nnz);
+    ce.resize(nnz);
+    build_csc(row_ptr, nrows, col, nnz, nc, cp.data(), cr.data(), ce.data());
+    PALLOC(op->col_ptr, (nc + 1) * 4, false, "csc col_ptr");
+    PALLOC(op->csc_row, nnz * 4, false, "csc row");
+    PALLOC(op->csc_eidx, nnz * 4, false, "csc edge_idx");
+    cudaMemcpyAsync(op->col_ptr.p, cp.data(), (nc + 1) * 4, cudaMemcpyHostToDevice, op->stream);
+    if (nnz) {
+      cudaMemcpyAsync(op->csc_row.p, cr.data(), nnz * 4, cudaMemcpyHostToDevice, op->stream);
+      cudaMemcpyAsync(op->csc_eidx.p, ce.data(), nnz * 4, cudaMemcpyHostToDevice, op->stream);
+    }
+  }
+  cudaMemsetAsync(op->rx.p, 0, op->rx.bytes, op->stream);
+  cudaMemsetAsync(op->rxs[0].p, 0, op->rxs[0].bytes, op->stream);
+  cudaMemsetAsync(op->rxs[1].p, 0, op->rxs[1].bytes, op->stream);
+  cudaMemsetAsync(op->ry.p, 0, op->ry.bytes, op->stream);
+  cudaMemsetAsync(op->rv.p, 0, op->rv.bytes, op->stream);
+  cudaMemsetAsync(op->rth.p, 0, op->rth.bytes, op->stream);
+  cudaMemsetAsync(op->rspk.p, 0, op->rspk.bytes, op->stream);
+  cudaMemsetAsync(op->tile_flags.p, 0, op->tile_flags.bytes, op->stream);
+  cudaMemsetAsync(op->ticket.p, 0, op->ticket.bytes, op->stream);
+  rc = wait_op(op, "prepare");  // host vectors above must outlive the copies
+  if (rc != SPARSL_OK) return bail(rc);
+#undef PALLOC
+  *out = op;
+  return SPARSL_OK;
+}
+
+void sparsl_op_destroy(sparsl_op* op) {
+  if (!op) return;
+  cudaSetDevice(op->dev->ordinal);
+  if (op->stream) cudaStreamSynchronize(op->stream);
+  DBuf* bufs[] = {&op->row_ptr, &op->col,     &op->w,       &op->col_ptr, &op->csc_row, &op->csc_eidx,
+                  &op->rx,      &op->rxs[0],  &op->rxs[1],  &op->ry,      &op->rv,      &op->rth,
+                  &op->rspk,    &op->idx_list, &op->tile_flags, &op->ticket, &op->trace, &op->sx,
+                  &op->sbits,   &op->sy,      &op->sv,      &op->sth,     &op->sspk};
+  for (DBuf* b : bufs) dfree(*b);
+  op->err.release();
+  if (op->ev) cudaEventDestroy(op->ev);
+  if (op->stream) cudaStreamDestroy(op->stream);
+  delete op;
+}
+
+int sparsl_op_shape(sparsl_op* op, sparsl_shape* out) {
+  if (!op || !out) return fail(SPARSL_ERR_INVALID, "null argument", "sparsl_op_shape");
+  *out = sparsl_shape{};
+  out->nrows = op->nrows;
+  out->ncols = op->ncols;
+  out->nnz = op->nnz;
+  out->max_row_nnz = op->max_row_nnz;
+  return SPARSL_OK;
+}
+
+int sparsl_op_weight_precision(sparsl_op* op) { return op ? op->precision : -1; }
+int sparsl_op_has_transpose(sparsl_op* op) { return op && op->has_t ? 1 : 0; }
+
+int sparsl_op_set_weights(sparsl_op* op, const float* weights, uint64_t n) {
+  ADMIT();
+  TRY(check_len("weights", n, op->nnz));
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("set_weights", cudaSetDevice(op->dev->ordinal));
+  if (n == 0) return SPARSL_OK;
+  std::vector<uint16_t> narrow;
+  if (op->precision == 0) {
+    CK("set_weights", cudaMemcpyAsync(op->w.p, weights, n * 4, cudaMemcpyHostToDevice, op->stream));
+  } else {
+    narrow.resize(n);
+    encode_narrow(op->precision, weights, narrow.data(), n);
+    CK("set_weights", cudaMemcpyAsync(op->w.p, narrow.data(), n * 2, cudaMemcpyHostToDevice, op->stream));
+  }
+  return wait_op(op, "set_weights");
+}
+
+int sparsl_op_spmv(sparsl_op* op, const float* x, uint64_t x_len, float* y, uint64_t y_len) {
+  ADMIT();
+  TRY(check_min("x", x_len, op->ncols));
+  TRY(check_len("y", y_len, op->nrows));
+  if (op->nrows == 0) return SPARSL_OK;
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("spmv", cudaSetDevice(op->dev->ordinal));
+  ALLOC(op->sx, (uint64_t)op->ncols * 4 + 16, false, "x staging");
+  ALLOC(op->sy, (uint64_t)op->nrows * 4 + 16, true, "y staging");
+  if (op->ncols) CK("spmv", cudaMemcpyAsync(op->sx.p, x, (uint64_t)op->ncols * 4, cudaMemcpyHostToDevice, op->stream));
+  CK("spmv", cudaMemcpyAsync(op->sy.p, y, (uint64_t)op->nrows * 4, cudaMemcpyHostToDevice, op->stream));
+  RowLaunch p = fwd_launch(op);
+  p.x = op->sx.as<float>();
+  p.y = op->sy.as<float>();
+  CK("spmv", launch_rows(p, op->stream));
+  CK("spmv", cudaMemcpyAsync(y, op->sy.p, (uint64_t)op->nrows * 4, cudaMemcpyDeviceToHost, op->stream));
+  return finish(op, "spmv");
+}
+
+int sparsl_op_spmv_spikes(sparsl_op* op, const uint32_t* spikes, uint64_t words, float* y, uint64_t y_len) {
+  ADMIT();
+  TRY(check_min("spikes", words, op->words()));
+  TRY(check_len("y", y_len, op->nrows));
+  if (op->nrows == 0) return SPARSL_OK;
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("spmv_spikes", cudaSetDevice(op->dev->ordinal));
+  ALLOC(op->sbits, op->words() * 4 + 16, false, "spike staging");
+  ALLOC(op->sy, (uint64_t)op->nrows * 4 + 16, true, "y staging");
+  if (op->words())
+    CK("spmv_spikes", cudaMemcpyAsync(op->sbits.p, spikes, op->words() * 4, cudaMemcpyHostToDevice, op->stream));
+  CK("spmv_spikes", cudaMemcpyAsync(op->sy.p, y, (uint64_t)op->nrows * 4, cudaMemcpyHostToDevice, op->stream));
+  RowLaunch p = fwd_launch(op);
+  set_bits_mode(p, op->sbits.as<uint32_t>(), op->words());
+  p.y = op->sy.as<float>();
+  CK("spmv_spikes", launch_rows(p, op->stream));
+  CK("spmv_spikes", cudaMemcpyAsync(y, op->sy.p, (uint64_t)op->nrows * 4, cudaMemcpyDeviceToHost, op->stream));
+  return finish(op, "spmv_spikes");
+}
+
+int sparsl_op_spmv_t(sparsl_op* op, const float* x, uint64_t x_len, float* y, uint64_t y_len) {
+  ADMIT();
+  TRY(check_min("x", x_len, op->nrows));
+  TRY(check_len("y", y_len, op->ncols));
+  if (op->ncols == 0) return SPARSL_OK;
+  if (!op->has_t)
+    return fail(SPARSL_ERR_NO_TRANSPOSE, "transpose not prepared",
+                "this operator has no reverse index; build it with prepare_with_transpose to use spmv_t");
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("spmv_t", cudaSetDevice(op->dev->ordinal));
+  ALLOC(op->sx, (uint64_t)std::max(op->nrows, op->ncols) * 4 + 16, false, "x staging");
+  ALLOC(op->sy, (uint64_t)std::max(op->nrows, op->ncols) * 4 + 16, true, "y staging");
+  if (op->nrows) CK("spmv_t", cudaMemcpyAsync(op->sx.p, x, (uint64_t)op->nrows * 4, cudaMemcpyHostToDevice, op->stream));
+  CK("spmv_t", cudaMemcpyAsync(op->sy.p, y, (uint64_t)op->ncols * 4, cudaMemcpyHostToDevice, op->stream));
+  RowLaunch p;
+  p.ptr = op->col_ptr.as<uint32_t>();
+  p.idx = op->csc_row.as<uint32_t>();
+  p.eidx = op->csc_eidx.as<uint32_t>();
+  p.w = op->w.p;
+  p.wkind = wkind_of(op->precision);
+  p.nlines = op->ncols;
+  p.x = op->sx.as<float>();
+  p.y = op->sy.as<float>();
+  p.err = op->err.d;
+  CK("spmv_t", launch_rows(p, op->stream));
+  CK("spmv_t", cudaMemcpyAsync(y, op->sy.p, (uint64_t)op->ncols * 4, cudaMemcpyDeviceToHost, op->stream));
+  return finish(op, "spmv_t");
+}
+
+int sparsl_op_spmm(sparsl_op* op, const float* x, uint64_t x_len, uint64_t n_vec, float* y, uint64_t y_len) {
+  ADMIT();
+  if (n_vec == 0) return fail(SPARSL_ERR_LENGTH, "n_vec", "`n_vec` must have length 1, got 0");
+  if (op->ncols && n_vec > UINT64_MAX / op->ncols)
+    return fail(SPARSL_ERR_LENGTH, "SpMM input element count", "SpMM input element count overflowed");
+  if (op->nrows && n_vec > UINT64_MAX / op->nrows)
+    return fail(SPARSL_ERR_LENGTH, "SpMM output element count", "SpMM output element count overflowed");
+  const uint64_t need_x = (uint64_t)op->ncols * n_vec, need_y = (uint64_t)op->nrows * n_vec;
+  TRY(check_min("x", x_len, need_x));
+  TRY(check_len("y", y_len, need_y));
+  if (op->nrows == 0) return SPARSL_OK;
+  if (n_vec == 1) return sparsl_op_spmv(op, x, x_len, y, y_len);  // mod.rs:2370-2373
+  if (n_vec > 0xffffffffull) return fail(SPARSL_ERR_LENGTH, "n_vec", "n_vec exceeds the u32 kernel range");
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("spmm", cudaSetDevice(op->dev->ordinal));
+  ALLOC(op->sx, need_x * 4 + 16, false, "X staging");
+  ALLOC(op->sy, need_y * 4 + 16, true, "Y staging");
+  if (need_x) CK("spmm", cudaMemcpyAsync(op->sx.p, x, need_x * 4, cudaMemcpyHostToDevice, op->stream));
+  CK("spmm", cudaMemcpyAsync(op->sy.p, y, need_y * 4, cudaMemcpyHostToDevice, op->stream));
+  CK("spmm", launch_spmm(op->row_ptr.as<uint32_t>(), op->col.as<uint32_t>(), op->w.p, wkind_of(op->precision),
+                         op->sx.as<float>(), op->sy.as<float>(), op->nrows, (uint32_t)n_vec, op->dev->sm_count,
+                         op->stream));
+  CK("spmm", cudaMemcpyAsync(y, op->sy.p, need_y * 4, cudaMemcpyDeviceToHost, op->stream));
+  return finish(op, "spmm");
+}
+
+static int fused_common(sparsl_op* op, const float* x, const uint32_t* bits, float* v, float* theta, uint8_t* spk,
+                        float decay, float v_reset, float dtheta, const char* name) {
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK(name, cudaSetDevice(op->dev->ordinal));
+  const uint64_t nr = op->nrows;
+  ALLOC(op->sv, nr * 4 + 16, true, "v staging");
+  ALLOC(op->sth, nr * 4 + 16, true, "theta staging");
+  ALLOC(op->sspk, nr + 16, true, "spike staging");
+  RowLaunch p = fwd_launch(op);
+  if (x) {
+    ALLOC(op->sx, (uint64_t)op->ncols * 4 + 16, false, "x staging");
+    if (op->ncols) CK(name, cudaMemcpyAsync(op->sx.p, x, (uint64_t)op->ncols * 4, cudaMemcpyHostToDevice, op->stream));
+    p.x = op->sx.as<float>();
+  } else {
+    ALLOC(op->sbits, op->words() * 4 + 16, false, "spike staging");
+    if (op->words()) CK(name, cudaMemcpyAsync(op->sbits.p, bits, op->words() * 4, cudaMemcpyHostToDevice, op->stream));
+    set_bits_mode(p, op->sbits.as<uint32_t>(), op->words());
+  }
+  CK(name, cudaMemcpyAsync(op->sv.p, v, nr * 4, cudaMemcpyHostToDevice, op->stream));
+  CK(name, cudaMemcpyAsync(op->sth.p, theta, nr * 4, cudaMemcpyHostToDevice, op->stream));
+  p.epilogue = EPI_LIF;
+  p.v = op->sv.as<float>();
+  p.theta = op->sth.as<float>();
+  p.spikes = op->sspk.as<uint8_t>();
+  p.decay = decay;
+  p.v_reset = v_reset;
+  p.dtheta = dtheta;
+  CK(name, launch_rows(p, op->stream));
+  CK(name, cudaMemcpyAsync(v, op->sv.p, nr * 4, cudaMemcpyDeviceToHost, op->stream));
+  CK(name, cudaMemcpyAsync(theta, op->sth.p, nr * 4, cudaMemcpyDeviceToHost, op->stream));
+  CK(name, cudaMemcpyAsync(spk, op->sspk.p, nr, cudaMemcpyDeviceToHost, op->stream));
+  return finish(op, name);
+}
+
+int sparsl_op_fused_lif(sparsl_op* op, const float* x, uint64_t x_len, float* v, float* theta, uint8_t* spikes,
+                        uint64_t n, float decay, float v_reset, float dtheta) {
+  ADMIT();
+  TRY(check_min("x", x_len, op->ncols));
+  TRY(check_len("v", n, op->nrows));
+  if (op->nrows == 0) return SPARSL_OK;
+  return fused_common(op, x, nullptr, v, theta, spikes, decay, v_reset, dtheta, "fused_spmv_lif");
+}
+
+int sparsl_op_fused_spikes_lif(sparsl_op* op, const uint32_t* s_in, uint64_t words, float* v, float* theta,
+                               uint8_t* s_out, uint64_t n, float decay, float v_reset, float dtheta) {
+  ADMIT();
+  TRY(check_min("spikes_in", words, op->words()));
+  TRY(check_len("v", n, op->nrows));
+  if (op->nrows == 0) return SPARSL_OK;
+  return fused_common(op, nullptr, s_in, v, theta, s_out, decay, v_reset, dtheta, "fused_spmv_spikes_lif");
+}
+
+// ---- resident ------------------------------------------------------------
+int sparsl_op_write_x(sparsl_op* op, const float* x, uint64_t len) {
+  ADMIT();
+  TRY(check_min("x", len, op->ncols));
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("write_x", cudaSetDevice(op->dev->ordinal));
+  if (op->ncols) CK("write_x", cudaMemcpyAsync(op->rx.p, x, (uint64_t)op->ncols * 4, cudaMemcpyHostToDevice, op->stream));
+  return wait_op(op, "write_x");
+}
+
+int sparsl_op_write_x_spikes(sparsl_op* op, const uint32_t* s, uint64_t words) {
+  ADMIT();
+  TRY(check_min("spikes", words, op->words()));
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("write_x_spikes", cudaSetDevice(op->dev->ordinal));
+  if (op->words())
+    CK("write_x_spikes", cudaMemcpyAsync(op->rxs[op->cur].p, s, op->words() * 4, cudaMemcpyHostToDevice, op->stream));
+  return wait_op(op, "write_x_spikes");
+}
+
+int sparsl_op_write_y(sparsl_op* op, const float* y, uint64_t len) {
+  ADMIT();
+  TRY(check_len("y", len, op->nrows));
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("write_y", cudaSetDevice(op->dev->ordinal));
+  if (op->nrows) CK("write_y", cudaMemcpyAsync(op->ry.p, y, (uint64_t)op->nrows * 4, cudaMemcpyHostToDevice, op->stream));
+  return wait_op(op, "write_y");
+}
+
+int sparsl_op_write_lif_state(sparsl_op* op, const float* v, const float* theta, uint64_t n) {
+  ADMIT();
+  TRY(check_len("v", n, op->nrows));
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("write_lif_state", cudaSetDevice(op->dev->ordinal));
+  if (n) {
+    CK("write_lif_state", cudaMemcpyAsync(op->rv.p, v, n * 4, cudaMemcpyHostToDevice, op->stream));
+    CK("write_lif_state", cudaMemcpyAsync(op->rth.p, theta, n * 4, cudaMemcpyHostToDevice, op->stream));
+  }
+  return wait_op(op, "write_lif_state");
+}
+
+int sparsl_op_spmv_resident(sparsl_op* op) {
+  ADMIT();
+  if (op->nrows == 0) return SPARSL_OK;
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("spmv_resident", cudaSetDevice(op->dev->ordinal));
+  RowLaunch p = fwd_launch(op);
+  p.x = op->rx.as<float>();
+  p.y = op->ry.as<float>();
+  CK("spmv_resident", launch_rows(p, op->stream));
+  return wait_op(op, "spmv_resident");
+}
+
+static void lif_resident_launch(sparsl_op* op, RowLaunch& p, float decay, float v_reset, float dtheta) {
+  p.epilogue = EPI_LIF;
+  p.v = op->rv.as<float>();
+  p.theta = op->rth.as<float>();
+  p.spikes = op->rspk.as<uint8_t>();
+  p.decay = decay;
+  p.v_reset = v_reset;
+  p.dtheta = dtheta;
+}
+
+int sparsl_op_fused_lif_resident(sparsl_op* op, float decay, float v_reset, float dtheta) {
+  ADMIT();
+  if (op->nrows == 0) return SPARSL_OK;
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("fused_spmv_lif_resident", cudaSetDevice(op->dev->ordinal));
+  RowLaunch p = fwd_launch(op);
+  p.x = op->rx.as<float>();
+  lif_resident_launch(op, p, decay, v_reset, dtheta);
+  CK("fused_spmv_lif_resident", launch_rows(p, op->stream));
+  return wait_op(op, "fused_spmv_lif_resident");
+}
+
+int sparsl_op_fused_spikes_lif_resident(sparsl_op* op, float decay, float v_reset, float dtheta) {
+  ADMIT();
+  if (op->nrows == 0) return SPARSL_OK;
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("fused_spmv_spikes_lif_resident", cudaSetDevice(op->dev->ordinal));
+  RowLaunch p = fwd_launch(op);
+  set_bits_mode(p, op->rxs[op->cur].as<uint32_t>(), op->words());
+  lif_resident_launch(op, p, decay, v_reset, dtheta);
+  CK("fused_spmv_spikes_lif_resident", launch_rows(p, op->stream));
+  return wait_op(op, "fused_spmv_spikes_lif_resident");
+}
+
+int sparsl_op_pack_resident_spikes(sparsl_op* op) {
+  ADMIT();
+  TRY(check_len("recurrent nrows", op->nrows, op->ncols));
+  if (op->nrows == 0) return SPARSL_OK;
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("pack_resident_spikes_to_x_spikes", cudaSetDevice(op->dev->ordinal));
+  CK("pack_resident_spikes_to_x_spikes",
+     launch_pack(op->rspk.as<uint8_t>(), op->nrows, op->rxs[op->cur].as<uint32_t>(), op->words(), op->stream));
+  return wait_op(op, "pack_resident_spikes_to_x_spikes");
+}
+
+static int enqueue_recurrent(sparsl_op* op, float decay, float v_reset, float dtheta, uint64_t steps) {
+  TRY(ensure_trace(op, steps));
+  for (uint64_t t = 0; t < steps; ++t) {
+    RowLaunch p = fwd_launch(op);
+    set_bits_mode(p, op->rxs[op->cur].as<uint32_t>(), op->words());
+    lif_resident_launch(op, p, decay, v_reset, dtheta);
+    p.out_bits = op->rxs[op->cur ^ 1].as<uint32_t>();
+    p.idx_list = op->idx_list.as<uint32_t>();
+    p.idx_count = op->trace.as<uint32_t>() + t;
+    p.tile_flags = op->tile_flags.as<unsigned long long>();
+    p.tile_ticket = op->ticket.as<uint32_t>();
+    CK("fused_spmv_spikes_lif_recurrent_steps", launch_rows(p, op->stream));
+    op->cur ^= 1;
+  }
+  op->last_steps = steps;
+  return SPARSL_OK;
+}
+
+int sparsl_op_recurrent_steps(sparsl_op* op, float decay, float v_reset, float dtheta, uint64_t steps) {
+  ADMIT();
+  TRY(check_len("recurrent nrows", op->nrows, op->ncols));
+  if (steps == 0 || op->nrows == 0) return SPARSL_OK;
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("fused_spmv_spikes_lif_recurrent_steps", cudaSetDevice(op->dev->ordinal));
+  TRY(enqueue_recurrent(op, decay, v_reset, dtheta, steps));
+  return wait_op(op, "fused_spmv_spikes_lif_recurrent_steps");
+}
+
+int sparsl_op_recurrent_steps_async(sparsl_op* op, float decay, float v_reset, float dtheta, uint64_t steps) {
+  ADMIT();
+  TRY(check_len("recurrent nrows", op->nrows, op->ncols));
+  if (steps == 0 || op->nrows == 0) return SPARSL_OK;
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("fused_spmv_spikes_lif_recurrent_steps", cudaSetDevice(op->dev->ordinal));
+  return enqueue_recurrent(op, decay, v_reset, dtheta, steps);
+}
+
+int sparsl_op_sync_y(sparsl_op* op, float* y, uint64_t len) {
+  ADMIT();
+  TRY(check_len("y", len, op->nrows));
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("sync_y", cudaSetDevice(op->dev->ordinal));
+  if (op->nrows) CK("sync_y", cudaMemcpyAsync(y, op->ry.p, (uint64_t)op->nrows * 4, cudaMemcpyDeviceToHost, op->stream));
+  return finish(op, "sync_y");
+}
+
+int sparsl_op_sync_lif_state(sparsl_op* op, float* v, float* theta, uint8_t* spikes, uint64_t n) {
+  ADMIT();
+  TRY(check_len("v", n, op->nrows));
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("sync_lif_state", cudaSetDevice(op->dev->ordinal));
+  if (n) {
+    CK("sync_lif_state", cudaMemcpyAsync(v, op->rv.p, n * 4, cudaMemcpyDeviceToHost, op->stream));
+    CK("sync_lif_state", cudaMemcpyAsync(theta, op->rth.p, n * 4, cudaMemcpyDeviceToHost, op->stream));
+    CK("sync_lif_state", cudaMemcpyAsync(spikes, op->rspk.p, n, cudaMemcpyDeviceToHost, op->stream));
+  }
+  return finish(op, "sync_lif_state");
+}
+
+int sparsl_op_sync_x_spikes(sparsl_op* op, uint32_t* s, uint64_t words) {
+  ADMIT();
+  TRY(check_min("spikes", words, op->words()));
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("sync_x_spikes", cudaSetDevice(op->dev->ordinal));
+  if (op->words())
+    CK("sync_x_spikes", cudaMemcpyAsync(s, op->rxs[op->cur].p, op->words() * 4, cudaMemcpyDeviceToHost, op->stream));
+  return finish(op, "sync_x_spikes");
+}
+
+int sparsl_op_spike_trace(sparsl_op* op, uint32_t* out, uint64_t cap, uint64_t* n_out) {
+  ADMIT();
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("spike_trace", cudaSetDevice(op->dev->ordinal));
+  const uint64_t n = std::min<uint64_t>(cap, op->last_steps);
+  if (n_out) *n_out = op->last_steps;
+  if (n) CK("spike_trace", cudaMemcpyAsync(out, op->trace.p, n * 4, cudaMemcpyDeviceToHost, op->stream));
+  return finish(op, "spike_trace");
+}
+
+int sparsl_op_spike_indices(sparsl_op* op, uint32_t* out, uint64_t cap, uint64_t* count) {
+  ADMIT();
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("spike_indices", cudaSetDevice(op->dev->ordinal));
+  if (op->last_steps == 0) {
+    if (count) *count = 0;
+    return SPARSL_OK;
+  }
+  uint32_t c = 0;
+  CK("spike_indices", cudaMemcpyAsync(&c, op->trace.as<uint32_t>() + (op->last_steps - 1), 4, cudaMemcpyDeviceToHost,
+                                      op->stream));
+  CK("spike_indices", cudaStreamSynchronize(op->stream));
+  if (count) *count = c;
+  const uint64_t n = std::min<uint64_t>(cap, c);
+  if (n) CK("spike_indices", cudaMemcpyAsync(out, op->idx_list.p, n * 4, cudaMemcpyDeviceToHost, op->stream));
+  return finish(op, "spike_indices");
+}
+
+// ---- device-pointer entry points ------------------------------------------
+static cudaStream_t pick(sparsl_op* op, void* stream) {
+  return stream ? static_cast<cudaStream_t>(stream) : op->stream;
+}
+
+int sparsl_op_spmv_device(sparsl_op* op, const float* d_x, float* d_y, void* stream) {
+  ADMIT();
+  if (op->nrows == 0) return SPARSL_OK;
+  CK("spmv", cudaSetDevice(op->dev->ordinal));
+  RowLaunch p = fwd_launch(op);
+  p.x = d_x;
+  p.y = d_y;
+  CK("spmv", launch_rows(p, pick(op, stream)));
+  return SPARSL_OK;
+}
+
+int sparsl_op_spmv_spikes_device(sparsl_op* op, const uint32_t* d_spikes, float* d_y, void* stream) {
+  ADMIT();
+  if (op->nrows == 0) return SPARSL_OK;
+  CK("spmv_spikes", cudaSetDevice(op->dev->ordinal));
+  RowLaunch p = fwd_launch(op);
+  set_bits_mode(p, d_spikes, op->words());
+  p.y = d_y;
+  CK("spmv_spikes", launch_rows(p, pick(op, stream)));
+  return SPARSL_OK;
+}
+
+int sparsl_op_spmv_t_device(sparsl_op* op, const float* d_x, float* d_y, void* stream) {
+  ADMIT();
+  if (op->ncols == 0) return SPARSL_OK;
+  if (!op->has_t) return fail(SPARSL_ERR_NO_TRANSPOSE, "transpose not prepared", "no reverse index");
+  CK("spmv_t", cudaSetDevice(op->dev->ordinal));
+  RowLaunch p;
+  p.ptr = op->col_ptr.as<uint32_t>();
+  p.idx = op->csc_row.as<uint32_t>();
+  p.eidx = op->csc_eidx.as<uint32_t>();
+  p.w = op->w.p;
+  p.wkind = wkind_of(op->precision);
+  p.nlines = op->ncols;
+  p.x = d_x;
+  p.y = d_y;
+  p.err = op->err.d;
+  CK("spmv_t", launch_rows(p, pick(op, stream)));
+  return SPARSL_OK;
+}
+
+int sparsl_op_spmm_device(sparsl_op* op, const float* d_x, uint64_t n_vec, float* d_y, void* stream) {
+  ADMIT();
+  if (op->nrows == 0) return SPARSL_OK;
+  if (n_vec == 0 || n_vec > 0xffffffffull) return fail(SPARSL_ERR_LENGTH, "n_vec", "n_vec out of range");
+  CK("spmm", cudaSetDevice(op->dev->ordinal));
+  if (n_vec == 1) return sparsl_op_spmv_device(op, d_x, d_y, stream);
+  CK("spmm", launch_spmm(op->row_ptr.as<uint32_t>(), op->col.as<uint32_t>(), op->w.p, wkind_of(op->precision), d_x,
+                         d_y, op->nrows, (uint32_t)n_vec, op->dev->sm_count, pick(op, stream)));
+  return SPARSL_OK;
+}
+
+void* sparsl_op_stream(sparsl_op* op) { return op ? op->stream : nullptr; }
+int sparsl_op_wait(sparsl_op* op) {
+  if (!op) return fail(SPARSL_ERR_INVALID, "null operator", "null operator");
+  cudaSetDevice(op->dev->ordinal);
+  return wait_op(op, "wait");
+}
+
+// ---- memory helpers --------------------------------------------------------
+void* sparsl_host_alloc(uint64_t bytes) {
+  void* p = nullptr;
+  if (cudaHostAlloc(&p, std::max<uint64_t>(bytes, 16), cudaHostAllocDefault) != cudaSuccess) return nullptr;
+  return p;
+}
+void sparsl_host_free(void* p) {
+  if (p) cudaFreeHost(p);
+}
+void* sparsl_device_alloc(sparsl_dev* d, uint64_t bytes) {
+  if (!d) return nullptr;
+  cudaSetDevice(d->ordinal);
+  void* p = nullptr;
+  if (cudaMalloc(&p, round_up(std::max<uint64_t>(bytes, 16), kAlign) + kAlign) != cudaSuccess) return nullptr;
+  return p;
+}
+void sparsl_device_free(void* p) {
+  if (p) cudaFree(p);
+}
+int sparsl_memcpy(void* dst, const void* src, uint64_t bytes) {
+  CK("memcpy", cudaMemcpy(dst, src, bytes, cudaMemcpyDefault));
+  return SPARSL_OK;
+}
+
+// ==========================================================================
+// Multi-GPU network tick
+// ==========================================================================
+}  // extern "C"
+
+struct sparsl_net {
+  sparsl_dev* dev = nullptr;
+  std::vector<sparsl_op*> blocks;
+  std::vector<uint64_t> block_off;  // local row offset of each block
+  uint64_t row_offset = 0, n_global = 0, local_rows = 0, words = 0;
+  int rank = 0, nranks = 1;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev = nullptr;
+  ErrWord err;
+  DBuf xs[2], trace;
+  int cur = 0;
+  uint64_t trace_cap = 0, last_steps = 0;
+  ncclComm_t comm = nullptr;
+};
+
+extern "C" {
+
+int sparsl_nccl_unique_id(uint8_t out[128]) {
+  if (const char* why = nccl_load()) return fail(SPARSL_ERR_BACKEND, why, why);
+  ncclUniqueId id;
+  ncclResult_t r = g_nccl.GetUniqueId(&id);
+  if (r != ncclSuccess) return fail(SPARSL_ERR_BACKEND, "ncclGetUniqueId failed", g_nccl.GetErrorString(r));
+  static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId is 128 bytes");
+  std::memcpy(out, &id, 128);
+  return SPARSL_OK;
+}
+
+int sparsl_net_create(sparsl_dev* d, sparsl_op* const* blocks, uint32_t n_blocks, uint64_t row_offset,
+                      uint64_t n_global, int rank, int nranks, const uint8_t* nccl_id, sparsl_net** out) {
+  ADMIT();
+  if (!d || !out || (n_blocks && !blocks)) return fail(SPARSL_ERR_INVALID, "null argument", "sparsl_net_create");
+  *out = nullptr;
+  if (nranks < 1 || rank < 0 || rank >= nranks) return fail(SPARSL_ERR_INVALID, "rank", "rank out of range");
+  if (row_offset % 32) return fail(SPARSL_ERR_INVALID, "row_offset", "row_offset must be a multiple of 32");
+  if (n_global % 32 || (n_global / 32) % nranks)
+    return fail(SPARSL_ERR_INVALID, "n_global", "n_global must split into equal 32-aligned rank slices");
+  uint64_t local = 0;
+  std::vector<uint64_t> offs;
+  for (uint32_t b = 0; b < n_blocks; ++b) {
+    sparsl_op* op = blocks[b];
+    if (op->dev != d) return fail(SPARSL_ERR_INVALID, "block device", "all blocks must live on the net's device");
+    if (op->ncols != n_global) return fail(SPARSL_ERR_INVALID, "block ncols", "every block must have ncols == n_global");
+    if (local % 32) return fail(SPARSL_ERR_INVALID, "block rows", "every block but the last must hold a multiple of 32 rows");
+    offs.push_back(local);
+    local += op->nrows;
+  }
+  if (nranks > 1 && local != n_global / nranks)
+    return fail(SPARSL_ERR_INVALID, "local rows", "each rank must hold n_global / nranks rows");
+  if (row_offset + local > n_global) return fail(SPARSL_ERR_INVALID, "local rows", "rows exceed n_global");
+  CK("net_create", cudaSetDevice(d->ordinal));
+  auto* net = new sparsl_net();
+  net->dev = d;
+  net->blocks.assign(blocks, blocks + n_blocks);
+  net->block_off = offs;
+  net->row_offset = row_offset;
+  net->n_global = n_global;
+  net->local_rows = local;
+  net->words = n_global / 32;
+  net->rank = rank;
+  net->nranks = nranks;
+  auto bail = [&](int code) {
+    sparsl_net_destroy(net);
+    return code;
+  };
+  if (cudaStreamCreateWithFlags(&net->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&net->ev, cudaEventDisableTiming) != cudaSuccess || net->err.init() != cudaSuccess)
+    return bail(fail(SPARSL_ERR_BACKEND, "stream creation failed", "could not create net stream"));
+  for (int i = 0; i < 2; ++i) {
+    if (dalloc(net->xs[i], net->words * 4 + 16, true, net->stream) != cudaSuccess)
+      return bail(fail(SPARSL_ERR_ALLOCATION, "x_spikes", "device allocation failed for x_spikes"));
+    cudaMemsetAsync(net->xs[i].p, 0, net->xs[i].bytes, net->stream);
+  }
+  if (nranks > 1) {
+    if (!nccl_id) return bail(fail(SPARSL_ERR_INVALID, "nccl id", "nccl_id is required when nranks > 1"));
+    if (const char* why = nccl_load()) return bail(fail(SPARSL_ERR_BACKEND, why, why));
+    ncclUniqueId id;
+    std::memcpy(&id, nccl_id, 128);
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclResult_t r = g_nccl.CommInitRankConfig(&net->comm, nranks, id, rank, &cfg);
+    const auto t0 = std::chrono::steady_clock::now();
+    while (r == ncclInProgress || r == ncclSuccess) {
+      ncclResult_t st = ncclSuccess;
+      g_nccl.CommGetAsyncError(net->comm, &st);
+      if (st == ncclSuccess) {
+        r = ncclSuccess;
+        break;
+      }
+      if (st != ncclInProgress) {
+        r = st;
+        break;
+      }
+      if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(g_timeout_ms.load())) {
+        g_nccl.CommAbort(net->comm);
+        net->comm = nullptr;
+        return bail(fail(SPARSL_ERR_EXECUTION, "NCCL init timed out", "ncclCommInitRank did not complete in time"));
+      }
+      std::this_thread::sleep_for(std::chrono::milliseconds(1));
+    }
+    if (r != ncclSuccess) {
+      if (net->comm) g_nccl.CommAbort(net->comm);
+      net->comm = nullptr;
+      return bail(fail(SPARSL_ERR_BACKEND, "NCCL init failed", g_nccl.GetErrorString(r)));
+    }
+  }
+  int rc = wait_bounded(net->stream, net->ev, net->err.d, net->err.h, "net_create");
+  if (rc != SPARSL_OK) return bail(rc);
+  *out = net;
+  return SPARSL_OK;
+}
+
+void sparsl_net_destroy(sparsl_net* net) {
+  if (!net) return;
+  cudaSetDevice(net->dev->ordinal);
+  if (net->stream) cudaStreamSynchronize(net->stream);
+  if (net->comm) {
+    if (g_quarantine.load())
+      g_nccl.CommAbort(net->comm);
+    else
+      g_nccl.CommDestroy(net->comm);
+  }
+  dfree(net->xs[0]);
+  dfree(net->xs[1]);
+  dfree(net->trace);
+  net->err.release();
+  if (net->ev) cudaEventDestroy(net->ev);
+  if (net->stream) cudaStreamDestroy(net->stream);
+  delete net;
+}
+
+void* sparsl_net_stream(sparsl_net* net) { return net ? net->stream : nullptr; }
+
+int sparsl_net_write_state(sparsl_net* net, const uint32_t* xs, uint64_t words, const float* v, const float* theta,
+                           uint64_t local_rows) {
+  ADMIT();
+  TRY(check_min("x_spikes", words, net->words));
+  TRY(check_len("v", local_rows, net->local_rows));
+  CK("net_write_state", cudaSetDevice(net->dev->ordinal));
+  CK("net_write_state", cudaMemcpyAsync(net->xs[net->cur].p, xs, net->words * 4, cudaMemcpyHostToDevice, net->stream));
+  for (size_t b = 0; b < net->blocks.size(); ++b) {
+    sparsl_op* op = net->blocks[b];
+    const uint64_t o = net->block_off[b];
+    if (!op->nrows) continue;
+    CK("net_write_state", cudaMemcpyAsync(op->rv.p, v + o, (uint64_t)op->nrows * 4, cudaMemcpyHostToDevice, net->stream));
+    CK("net_write_state", cudaMemcpyAsync(op->rth.p, theta + o, (uint64_t)op->nrows * 4, cudaMemcpyHostToDevice, net->stream));
+  }
+  return wait_bounded(net->stream, net->ev, net->err.d, net->err.h, "net_write_state");
+}
+
+static int net_enqueue(sparsl_net* net, float decay, float v_reset, float dtheta, uint64_t steps) {
+  if (!net->trace.p || net->trace_cap < steps) {
+    const uint64_t cap = std::max<uint64_t>(steps, 1024);
+    if (ensure(net->trace, cap * 4, true, net->stream) != cudaSuccess)
+      return fail(SPARSL_ERR_ALLOCATION, "trace", "device allocation failed for the spike trace");
+    net->trace_cap = cap;
+  }
+  const uint64_t slice = net->words / net->nranks;
+  for (uint64_t t = 0; t < steps; ++t) {
+    uint32_t* src = net->xs[net->cur].as<uint32_t>();
+    uint32_t* dst = net->xs[net->cur ^ 1].as<uint32_t>();
+    for (size_t b = 0; b < net->blocks.size(); ++b) {
+      sparsl_op* op = net->blocks[b];
+      if (!op->nrows) continue;
+      RowLaunch p = fwd_launch(op);
+      set_bits_mode(p, src, net->words);
+      lif_resident_launch(op, p, decay, v_reset, dtheta);
+      p.out_bits = dst + (net->row_offset + net->block_off[b]) / 32;
+      p.err = net->err.d;
+      CK("net_steps", launch_rows(p, net->stream));
+    }
+    if (net->nranks > 1) {
+      ncclResult_t r = g_nccl.AllGather(dst + (uint64_t)net->rank * slice, dst, slice, ncclUint32, net->comm, net->stream);
+      if (r != ncclSuccess) return fail(SPARSL_ERR_EXECUTION, "ncclAllGather failed", g_nccl.GetErrorString(r));
+    }
+    CK("net_steps", launch_popcount(dst, net->words, net->trace.as<uint32_t>() + t, net->stream));
+    net->cur ^= 1;
+  }
+  net->last_steps = steps;
+  return SPARSL_OK;
+}
+
+int sparsl_net_steps_async(sparsl_net* net, float decay, float v_reset, float dtheta, uint64_t steps) {
+  ADMIT();
+  if (steps == 0) return SPARSL_OK;
+  CK("net_steps", cudaSetDevice(net->dev->ordinal));
+  return net_enqueue(net, decay, v_reset, dtheta, steps);
+}
+
+int sparsl_net_wait(sparsl_net* net) {
+  ADMIT();
+  CK("net_wait", cudaSetDevice(net->dev->ordinal));
+  int rc = wait_bounded(net->stream, net->ev, net->err.d, net->err.h, "net_steps");
+  if (rc != SPARSL_OK && net->comm && g_quarantine.load()) {
+    g_nccl.CommAbort(net->comm);
+    net->comm = nullptr;
+  }
+  return rc;
+}
+
+int sparsl_net_steps(sparsl_net* net, float decay, float v_reset, float dtheta, uint64_t steps) {
+  TRY(sparsl_net_steps_async(net, decay, v_reset, dtheta, steps));
+  return sparsl_net_wait(net);
+}
+
+int sparsl_net_read_state(sparsl_net* net, uint32_t* xs, uint64_t words, float* v, float* theta, uint64_t local_rows) {
+  ADMIT();
+  TRY(check_min("x_spikes", words, net->words));
+  TRY(check_len("v", local_rows, net->local_rows));
+  CK("net_read_state", cudaSetDevice(net->dev->ordinal));
+  CK("net_read_state", cudaMemcpyAsync(xs, net->xs[net->cur].p, net->words * 4, cudaMemcpyDeviceToHost, net->stream));
+  CanarySet set;
+  set.ptr[set.count++] = net->xs[0].canary();
+  set.ptr[set.count++] = net->xs[1].canary();
+  for (size_t b = 0; b < net->blocks.size(); ++b) {
+    sparsl_op* op = net->blocks[b];
+    const uint64_t o = net->block_off[b];
+    if (!op->nrows) continue;
+    CK("net_read_state", cudaMemcpyAsync(v + o, op->rv.p, (uint64_t)op->nrows * 4, cudaMemcpyDeviceToHost, net->stream));
+    CK("net_read_state", cudaMemcpyAsync(theta + o, op->rth.p, (uint64_t)op->nrows * 4, cudaMemcpyDeviceToHost, net->stream));
+    if (set.count + 2 <= CanarySet::kMax) {
+      set.ptr[set.count++] = op->rv.canary();
+      set.ptr[set.count++] = op->rth.canary();
+    }
+  }
+  CK("net_read_state", launch_canary_check(set, net->err.d, net->stream));
+  return wait_bounded(net->stream, net->ev, net->err.d, net->err.h, "net_read_state");
+}
+
+int sparsl_net_trace(sparsl_net* net, uint32_t* out, uint64_t cap, uint64_t* n_out) {
+  ADMIT();
+  CK("net_trace", cudaSetDevice(net->dev->ordinal));
+  const uint64_t n = std::min<uint64_t>(cap, net->last_steps);
+  if (n_out) *n_out = net->last_steps;
+  if (n) CK("net_trace", cudaMemcpyAsync(out, net->trace.p, n * 4, cudaMemcpyDeviceToHost, net->stream));
+  return wait_bounded(net->stream, net->ev, net->err.d, net->err.h, "net_trace");
+}
+
+}  // extern "C"

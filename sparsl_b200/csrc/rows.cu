@@ -1,0 +1,246 @@
+// Row-fold engine: SpMV, spike SpMV, transpose SpMV and the fused LIF tick.
+//
+// Bit-exactness rule: each output line (CSR row or CSC column) is a strict
+// left fold from 0.0 with separate round-to-nearest multiply and add, then
+// combined with the old value exactly as the reference does:
+//   y[r] = y[r] + (((0 + w0*x0) + w1*x1) + ...)     (src/backend/mod.rs:2259-2267)
+// so one lane owns one line and a line is never split across lanes.
+//
+// Layout: a warp owns 32 consecutive lines.  Their CSR segments are staged
+// chunk by chunk (kChunk entries per line) into a padded shared-memory tile by
+// coalesced loads -- one 128-byte load per line per array -- and each lane
+// then folds its own line out of shared memory.  The padding (stride kChunk+1)
+// makes the transposed per-lane reads bank-conflict free.
+#include "common.cuh"
+#include "rows.cuh"
+
+namespace sparsl {
+namespace {
+
+constexpr int kChunk = 32;
+constexpr int kStride = kChunk + 1;
+
+struct WarpStage {
+  uint32_t idx[32][kStride];
+  float w[32][kStride];
+  uint32_t start[32];
+  uint32_t len[32];
+};
+
+// Decoupled look-back over integer tile counts (exact, so the result is the
+// same whichever predecessors are summed).  Run by one thread per tile.
+__device__ uint32_t lookback_count(unsigned long long* flags, uint32_t tile, uint32_t agg,
+                                   uint32_t* err) {
+  if (tile == 0) {
+    st_release_u64(flags, (2ull << 32) | agg);
+    return 0;
+  }
+  st_release_u64(flags + tile, (1ull << 32) | agg);
+  uint32_t excl = 0;
+  int64_t j = (int64_t)tile - 1;
+  uint32_t spins = 0;
+  while (j >= 0) {
+    unsigned long long f = ld_acquire_u64(flags + j);
+    uint32_t st = (uint32_t)(f >> 32);
+    if (st == 0) {
+      if (++spins > kSpinLimit) {
+        set_err(err, DEVERR_LOOKBACK_TIMEOUT);
+        break;
+      }
+      __nanosleep(64);
+      continue;
+    }
+    excl += (uint32_t)f;
+    if (st == 2) break;
+    --j;
+  }
+  st_release_u64(flags + tile, (2ull << 32) | (excl + agg));
+  return excl;
+}
+
+template <int WK, int XM, bool CSC, int EPI, bool COMPACT>
+__global__ void __launch_bounds__(kRowWarps * 32) row_fold_kernel(const RowLaunch p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ uint32_t s_tile, s_base, s_last;
+  __shared__ uint32_t s_wc[kRowWarps];
+  const int lane = threadIdx.x & 31;
+  const int wid = threadIdx.x >> 5;
+  uint32_t* s_bits = reinterpret_cast<uint32_t*>(smem);
+  const size_t bits_bytes = (XM == X_BITS_SMEM) ? (((size_t)p.xbits_words * 4 + 15) & ~(size_t)15) : 0;
+  WarpStage* st = reinterpret_cast<WarpStage*>(smem + bits_bytes) + wid;
+
+  uint32_t tile;
+  if constexpr (COMPACT) {
+    // Tiles are numbered in start order so a tile only ever waits on tiles
+    // that are already resident.
+    if (threadIdx.x == 0) s_tile = atomicAdd(p.tile_ticket, 1u);
+    __syncthreads();
+    tile = s_tile;
+  } else {
+    tile = blockIdx.x;
+  }
+
+  if constexpr (XM == X_BITS_SMEM) {
+    const uint4* src = reinterpret_cast<const uint4*>(p.xbits);
+    const uint32_t nvec = p.xbits_words >> 2;
+    for (uint32_t i = threadIdx.x; i < nvec; i += blockDim.x)
+      reinterpret_cast<uint4*>(s_bits)[i] = __ldg(src + i);
+    for (uint32_t i = (nvec << 2) + threadIdx.x; i < p.xbits_words; i += blockDim.x)
+      s_bits[i] = __ldg(p.xbits + i);
+    __syncthreads();
+  }
+
+  const uint32_t line0 = tile * kRowLines + wid * 32;
+  const uint32_t line = line0 + lane;
+  const bool valid = line < p.nlines;
+  uint32_t start = 0, len = 0;
+  if (valid) {
+    start = __ldg(p.ptr + line);
+    len = __ldg(p.ptr + line + 1) - start;
+  }
+  st->start[lane] = start;
+  st->len[lane] = len;
+  const uint32_t maxlen = __reduce_max_sync(0xffffffffu, len);
+  __syncwarp();
+
+  float sum = 0.0f;
+  for (uint32_t k = 0; k < maxlen; k += kChunk) {
+    const uint32_t off = k + lane;
+#pragma unroll 8
+    for (int rr = 0; rr < 32; ++rr) {
+      if (off < st->len[rr]) {
+        const uint32_t e = st->start[rr] + off;
+        st->idx[rr][lane] = __ldg(p.idx + e);
+        if constexpr (CSC) {
+          st->w[rr][lane] = load_weight<WK>(p.w, __ldg(p.eidx + e));
+        } else {
+          st->w[rr][lane] = load_weight<WK>(p.w, e);
+        }
+      }
+    }
+    __syncwarp();
+    const uint32_t cnt = len > k ? min((uint32_t)kChunk, len - k) : 0u;
+#pragma unroll 4
+    for (uint32_t j = 0; j < cnt; ++j) {
+      const uint32_t c = st->idx[lane][j];
+      const float wv = st->w[lane][j];
+      float xv;
+      if constexpr (XM == X_DENSE) {
+        xv = __ldg(p.x + c);
+      } else if constexpr (XM == X_BITS_SMEM) {
+        xv = (float)((s_bits[c >> 5] >> (c & 31)) & 1u);  // multiply, never branch
+      } else {
+        xv = (float)((__ldg(p.xbits + (c >> 5)) >> (c & 31)) & 1u);
+      }
+      sum = fadd(sum, fmul(wv, xv));
+    }
+    __syncwarp();
+  }
+
+  if constexpr (EPI == EPI_ACCUM) {
+    if (valid) p.y[line] = fadd(p.y[line], sum);
+  } else {
+    // lif_step (src/backend/mod.rs:2461-2472): two roundings, then >= theta.
+    bool spike = false;
+    if (valid) {
+      float vv = p.v[line];
+      float th = p.theta[line];
+      const float vol = fadd(fmul(vv, p.decay), sum);
+      if (vol >= th) {
+        spike = true;
+        vv = p.v_reset;
+        th = fadd(th, p.dtheta);
+      } else {
+        vv = vol;
+      }
+      p.v[line] = vv;
+      p.theta[line] = th;
+      p.spikes[line] = spike ? 1 : 0;
+    }
+    // Lane i of the ballot is line 32w+i: exactly the LSB-first packing of
+    // src/spikes.rs:237-262, with tail bits of a partial word left zero.
+    const uint32_t ballot = __ballot_sync(0xffffffffu, spike);
+    if (p.out_bits && lane == 0 && line0 < p.nlines) p.out_bits[line0 >> 5] = ballot;
+
+    if constexpr (COMPACT) {
+      const uint32_t ntiles = row_tiles(p.nlines);
+      if (lane == 0) s_wc[wid] = __popc(ballot);
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        uint32_t agg = 0;
+        for (int w2 = 0; w2 < kRowWarps; ++w2) agg += s_wc[w2];
+        const uint32_t excl = lookback_count(p.tile_flags, tile, agg, p.err);
+        s_base = excl;
+        if (tile == ntiles - 1) *p.idx_count = excl + agg;
+      }
+      __syncthreads();
+      uint32_t wexcl = s_base;
+      for (int w2 = 0; w2 < wid; ++w2) wexcl += s_wc[w2];
+      if (spike) {
+        const uint32_t lt = ballot & ((1u << lane) - 1u);
+        p.idx_list[wexcl + __popc(lt)] = p.idx_base + line;
+      }
+      // The last tile to finish clears the look-back state for the next launch.
+      if (threadIdx.x == 0) {
+        __threadfence();
+        s_last = (atomicAdd(p.tile_ticket + 1, 1u) == ntiles - 1) ? 1u : 0u;
+      }
+      __syncthreads();
+      if (s_last) {
+        for (uint32_t i = threadIdx.x; i < ntiles; i += blockDim.x) p.tile_flags[i] = 0ull;
+        if (threadIdx.x == 0) {
+          p.tile_ticket[0] = 0;
+          p.tile_ticket[1] = 0;
+        }
+      }
+    }
+  }
+}
+
+template <int WK, int XM, bool CSC, int EPI, bool COMPACT>
+cudaError_t launch_t(const RowLaunch& p, cudaStream_t stream) {
+  auto kern = row_fold_kernel<WK, XM, CSC, EPI, COMPACT>;
+  const size_t bits_bytes = (XM == X_BITS_SMEM) ? (((size_t)p.xbits_words * 4 + 15) & ~(size_t)15) : 0;
+  const size_t smem = bits_bytes + sizeof(WarpStage) * kRowWarps;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const uint32_t tiles = row_tiles(p.nlines);
+  kern<<<tiles, kRowWarps * 32, smem, stream>>>(p);
+  return cudaGetLastError();
+}
+
+template <int WK>
+cudaError_t dispatch_x(const RowLaunch& p, cudaStream_t s) {
+  const bool csc = p.eidx != nullptr;
+  const bool compact = p.idx_list != nullptr;
+  if (p.epilogue == EPI_ACCUM) {
+    if (csc) return launch_t<WK, X_DENSE, true, EPI_ACCUM, false>(p, s);
+    switch (p.xmode) {
+      case X_DENSE: return launch_t<WK, X_DENSE, false, EPI_ACCUM, false>(p, s);
+      case X_BITS_SMEM: return launch_t<WK, X_BITS_SMEM, false, EPI_ACCUM, false>(p, s);
+      default: return launch_t<WK, X_BITS_GLOBAL, false, EPI_ACCUM, false>(p, s);
+    }
+  }
+  switch (p.xmode) {
+    case X_DENSE: return launch_t<WK, X_DENSE, false, EPI_LIF, false>(p, s);
+    case X_BITS_SMEM:
+      return compact ? launch_t<WK, X_BITS_SMEM, false, EPI_LIF, true>(p, s)
+                     : launch_t<WK, X_BITS_SMEM, false, EPI_LIF, false>(p, s);
+    default:
+      return compact ? launch_t<WK, X_BITS_GLOBAL, false, EPI_LIF, true>(p, s)
+                     : launch_t<WK, X_BITS_GLOBAL, false, EPI_LIF, false>(p, s);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_rows(const RowLaunch& p, cudaStream_t stream) {
+  if (p.nlines == 0) return cudaSuccess;
+  switch (p.wkind) {
+    case W_F16: return dispatch_x<W_F16>(p, stream);
+    case W_BF16: return dispatch_x<W_BF16>(p, stream);
+    default: return dispatch_x<W_F32>(p, stream);
+  }
+}
+
+}  // namespace sparsl

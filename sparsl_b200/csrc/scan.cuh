@@ -1,0 +1,48 @@
+// Launch interface of the exact affine-map scan (scan.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sparsl {
+
+constexpr int kScanThreads = 256;  // threads per tile
+constexpr int kScanK = 16;         // elements per thread (one sub-chunk)
+constexpr int kScanTile = kScanThreads * kScanK;
+constexpr int kScanWarmSub = 8;    // warm-up length in sub-chunks
+constexpr int kScanWarm = kScanWarmSub * kScanK;
+
+// Per-tile look-back record.  Written by the tile, read by its successors.
+struct ScanTileRecord {
+  uint32_t status;  // 0 none, 1 aggregate, 2 inclusive
+  uint32_t tab;     // transfer table of the multiplier chain (8 x 4 bits)
+  uint32_t pad;
+  float av;         // inclusive: multiplier value of the tile's last element
+  float agg[4];     // aggregate: full (a, b), head (a, b)
+  float inc[4];     // inclusive: full (a, b), head (a, b)
+};
+
+// Scratch the scan needs, sized by scan_scratch_bytes(n).  All of it is
+// left in its zero state (or self-resetting) after each call.
+struct ScanScratch {
+  ScanTileRecord* rec;      // ntiles
+  uint32_t* ticket;         // [0] tile ticket, [1] done counter
+  uint32_t* arrive;         // ntiles: boundary arrival counters (self-resetting)
+  float* assumed;           // 2 * ntiles: thread 0's assumed incoming state
+  float* last;              // 2 * ntiles: each tile's last output state
+  uint32_t* mis_bits;       // ntiles * 8 words: in-tile sub-chunk mismatches
+  uint32_t* xmis;           // ntiles: tile-boundary mismatch
+  uint32_t* tile_bits;      // ceil(ntiles / 32) words: any mismatch in tile
+  uint32_t* repair_stats;   // [0] repaired elements, [1] repair segments
+};
+
+size_t scan_scratch_bytes(uint64_t n);
+ScanScratch scan_scratch_carve(void* base, uint64_t n);
+
+// out[i] = in[0] o in[1] o ... o in[i] as an exact sequential left fold
+// (src/scan.rs:298-313).  `in` and `out` hold n (a, b) pairs and must not
+// alias.  scratch must be zeroed once before first use.
+cudaError_t launch_scan(const float* in, float* out, uint64_t n, const ScanScratch& s,
+                        uint32_t* err, cudaStream_t stream);
+
+}  // namespace sparsl
