@@ -1,0 +1,501 @@
+#!/usr/bin/env python
+"""Benchmark of the sparsl CUDA substrate on B200.
+
+Headline workload (``--workload lif_net``, the default): the recurrent LIF
+network tick -- 4,194,304 neurons, fixed fan-in 1,024 (4.29e9 synapses, f32
+weights N(0, 0.03^2)), decay 0.95, threshold 1.0, reset 0, Bernoulli(0.01)
+initial spikes.  One step is one tick of the whole network: the fused
+spike-SpMV + LIF kernel over every row block, the in-place NCCL all-gather of
+the packed spike words across ranks, and the global spike count.  Neurons are
+row-block sharded over the ranks, so the total work is fixed as N grows
+(strong scaling).  Rows are split into operators of at most 2^31 synapses
+(u32 offsets), so one GPU holds two blocks.
+
+Inputs are generated on the GPU from seeded ChaCha12 streams (one per row),
+resident in HBM before timing; each rank's synapse arrays (34.4 GB / N) far
+exceed the 126 MB L2, so no flush is needed between ticks.
+
+Other workloads (``--workload``): ``spmv`` (100k x 100k, 64 distinct sorted
+columns per row), ``scan`` (2^26 affine maps, a ~ U[0.9, 1], b ~ N(0, 1)),
+``lif`` (262,144 neurons x fan-in 512, 1000-tick network on one GPU),
+``spmm`` (1M x 1M Zipf(1.5) rows clipped to [1, 4096], 64 vectors).
+
+``--impl reference`` times the CPU restatement of the reference crate's
+CpuParallel arm (the oracle) on this host's cores on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0}
+
+# Workload constants (see module docstring)
+NET_N = 4_194_304
+NET_FANIN = 1024
+NET_SIGMA = 0.03
+NET_DECAY, NET_VRESET, NET_DTHETA = 0.95, 0.0, 0.0
+NET_THETA0 = 1.0
+NET_DENSITY = 0.01
+NET_SEED = 0x5EED_0005
+BLOCK_NNZ_MAX = 1 << 31
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+# --------------------------------------------------------------------------
+# process plumbing
+# --------------------------------------------------------------------------
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", str(self.rank)))
+        self.pg = None
+        if self.world > 1:
+            import torch.distributed as td
+
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            td.init_process_group("gloo", rank=self.rank, world_size=self.world,
+                                  timeout=datetime.timedelta(seconds=300))
+            self.pg = td
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+
+        t = torch.tensor([v], dtype=torch.float64)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def bcast_bytes(self, b: bytes | None) -> bytes:
+        if not self.pg:
+            return b
+        obj = [b]
+        self.pg.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    def gather(self, obj):
+        if not self.pg:
+            return [obj]
+        out = [None] * self.world
+        self.pg.all_gather_object(out, obj)
+        return out
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# --------------------------------------------------------------------------
+# helpers over the C ABI
+# --------------------------------------------------------------------------
+def lib():
+    from sparsl_b200 import _lib
+
+    return _lib.load()
+
+
+def check(rc, what):
+    if rc != 0:
+        from sparsl_b200 import _lib
+
+        raise RuntimeError(f"{what} failed: {_lib.last_error()}")
+
+
+class DevArray:
+    def __init__(self, dev, nbytes):
+        self.nbytes = int(nbytes)
+        self.ptr = lib().sparsl_device_alloc(dev.handle, self.nbytes)
+        if not self.ptr:
+            raise MemoryError(f"device allocation of {nbytes} bytes failed")
+
+    def to_host(self, dtype, count):
+        out = np.empty(count, dtype)
+        if count:
+            check(lib().sparsl_memcpy(out.ctypes.data, self.ptr, out.nbytes), "memcpy D2H")
+        return out
+
+    def free(self):
+        if self.ptr:
+            lib().sparsl_device_free(self.ptr)
+            self.ptr = None
+
+
+class Pinned:
+    def __init__(self, dtype, count):
+        self.count = int(count)
+        nbytes = max(np.dtype(dtype).itemsize * self.count, 16)
+        self.ptr = lib().sparsl_host_alloc(nbytes)
+        buf = (ctypes.c_char * nbytes).from_address(self.ptr)
+        self.a = np.frombuffer(buf, dtype=dtype, count=self.count)
+
+    def free(self):
+        lib().sparsl_host_free(self.ptr)
+
+
+def torch_stream(ptr, device_index):
+    import torch
+
+    return torch.cuda.ExternalStream(ptr, device=torch.device("cuda", device_index))
+
+
+def events_ms(stream_ptr, device_index, fn):
+    """Device time of whatever fn enqueues on the stream, by CUDA events."""
+    import torch
+
+    s = torch_stream(stream_ptr, device_index)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(s)
+    fn()
+    b.record(s)
+    b.synchronize()
+    return a.elapsed_time(b)
+
+
+# --------------------------------------------------------------------------
+# LIF network (headline)
+# --------------------------------------------------------------------------
+def net_blocks(local_rows, fan_in):
+    rows_per = BLOCK_NNZ_MAX // fan_in
+    out, r = [], 0
+    while r < local_rows:
+        n = min(rows_per, local_rows - r)
+        out.append((r, n))
+        r += n
+    return out
+
+
+def build_lif_net(S, dev, dist, n_total, fan_in, keep_sample_rows=0):
+    world, rank = dist.world, dist.rank
+    local = n_total // world
+    row0 = rank * local
+    ops, sample = [], None
+    t0 = time.time()
+    for (off, nrows) in net_blocks(local, fan_in):
+        nnz = nrows * fan_in
+        dcol = DevArray(dev, nnz * 4)
+        dw = DevArray(dev, nnz * 4)
+        check(lib().sparsl_workload_fixed_fanin(NET_SEED, row0 + off, nrows, n_total, fan_in, NET_SIGMA, dcol.ptr,
+                                                dw.ptr, None), "workload")
+        col = dcol.to_host(np.uint32, nnz)
+        w = dw.to_host(np.float32, nnz)
+        dcol.free()
+        dw.free()
+        rp = (np.arange(nrows + 1, dtype=np.uint64) * fan_in).astype(np.uint32)
+        ops.append(dev.prepare(S.Csr(rp, col, n_total), n_total, w))
+        if keep_sample_rows and sample is None:
+            k = min(keep_sample_rows, nrows)
+            sample = (rp[: k + 1].copy(), col[: k * fan_in].copy(), w[: k * fan_in].copy())
+        del col, w
+    # initial state for every cell (the spike vector is global)
+    dv = DevArray(dev, n_total * 4)
+    dth = DevArray(dev, n_total * 4)
+    dpk = DevArray(dev, (n_total // 32) * 4)
+    check(lib().sparsl_workload_lif_state(NET_SEED ^ 0x57A7E, 0, n_total, 0.0, 1.0, NET_THETA0, NET_DENSITY, dv.ptr,
+                                          dth.ptr, dpk.ptr, None), "state")
+    v = dv.to_host(np.float32, n_total)
+    th = dth.to_host(np.float32, n_total)
+    pk = dpk.to_host(np.uint32, n_total // 32)
+    for a in (dv, dth, dpk):
+        a.free()
+    setup_s = time.time() - t0
+    return ops, (row0, local), (v, th, pk), sample, setup_s
+
+
+def make_net(S, dev, dist, ops, row0, n_total):
+    L = lib()
+    nid = None
+    if dist.world > 1:
+        buf = (ctypes.c_uint8 * 128)()
+        if dist.rank == 0:
+            check(L.sparsl_nccl_unique_id(buf), "nccl id")
+        nid_bytes = dist.bcast_bytes(bytes(buf) if dist.rank == 0 else None)
+        nid = (ctypes.c_uint8 * 128).from_buffer_copy(nid_bytes)
+    arr = (ctypes.c_void_p * len(ops))(*[op.handle.value for op in ops])
+    h = ctypes.c_void_p()
+    check(L.sparsl_net_create(dev.handle, arr, len(ops), row0, n_total, dist.rank, dist.world, nid,
+                              ctypes.byref(h)), "net_create")
+    return h
+
+
+def net_bytes_per_tick_per_gpu(n_total, fan_in, world):
+    # Algorithmic bytes (per GPU per tick): col + weight per synapse, row
+    # offsets, v read+write, theta read, packed spikes in and out.
+    local = n_total // world
+    return local * fan_in * 8 + (local + 1) * 4 + local * 8 + local * 4 + 2 * (n_total // 8) // world
+
+
+def cpu_sample_rate(sample, n_total, pk, v, th, seconds=10.0):
+    """Synapses/s of the oracle's CpuParallel fused tick on a sample row block."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    rp, col, w = sample
+    csr = O.Csr(rp, col, n_total)
+    k = csr.nrows
+    vv, tt, sp = v[:k].copy(), th[:k].copy(), np.zeros(k, np.uint8)
+    O.fused_spikes_lif(csr, w, pk, vv, tt, sp, NET_DECAY, NET_VRESET, NET_DTHETA, par=True)  # warm
+    t0 = time.perf_counter()
+    ticks = 0
+    while True:
+        O.fused_spikes_lif(csr, w, pk, vv, tt, sp, NET_DECAY, NET_VRESET, NET_DTHETA, par=True)
+        ticks += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = time.perf_counter() - t0
+    return ticks * csr.nnz / dt, O.num_threads(), f"{ticks} fused ticks over a {k}-row x {NET_FANIN} block " \
+        f"({csr.nnz} synapses) of the same network, {dt:.1f} s"
+
+
+def bench_lif_net(args, dist):
+    import torch
+    import sparsl_b200 as S
+
+    torch.cuda.set_device(dist.local)
+    dev = S.Device.try_new(S.Backend.Cuda, dist.local)
+    n_total, fan_in = NET_N, NET_FANIN
+    want_cpu = dist.world == 1 and dist.rank == 0 and not args.no_cpu
+    ops, (row0, local), (v, th, pk), sample, setup_s = build_lif_net(S, dev, dist, n_total, fan_in,
+                                                                     keep_sample_rows=4096 if want_cpu else 0)
+    net = make_net(S, dev, dist, ops, row0, n_total)
+    L = lib()
+    stream = L.sparsl_net_stream(net)
+    check(L.sparsl_net_write_state(net, pk.ctypes.data, pk.size, v[row0:row0 + local].ctypes.data,
+                                   th[row0:row0 + local].ctypes.data, local), "write_state")
+    p = (NET_DECAY, NET_VRESET, NET_DTHETA)
+    # warm-up (untimed)
+    check(L.sparsl_net_steps(net, *p, args.warmup), "warmup")
+    dist.barrier()
+    clocks = Clocks(dist.local)
+    if dist.rank == 0:
+        clocks.start()
+    check(L.sparsl_net_set_timing(net, args.steps), "timing")
+    dist.barrier()
+    ms = events_ms(stream, dist.local, lambda: check(L.sparsl_net_steps_async(net, *p, args.steps), "steps"))
+    check(L.sparsl_net_wait(net), "wait")
+    dist.barrier()
+    ck = clocks.stop() if dist.rank == 0 else None
+    ms_max = dist.max(ms)
+    kms = ctypes.c_double()
+    kt = ctypes.c_uint64()
+    check(L.sparsl_net_kernel_ms(net, ctypes.byref(kms), ctypes.byref(kt)), "kernel ms")
+    kernel_ms_tick = kms.value / max(kt.value, 1)
+    trace = np.zeros(args.steps, np.uint32)
+    n = ctypes.c_uint64()
+    check(L.sparsl_net_trace(net, trace.ctypes.data, trace.size, ctypes.byref(n)), "trace")
+    traces = dist.gather(trace.tolist())
+    consistent = all(t == traces[0] for t in traces)
+
+    # End to end through the C ABI with pinned host buffers: every step writes
+    # the spike vector and this rank's membrane state from the host, runs one
+    # tick, and reads them back.
+    check(L.sparsl_net_set_timing(net, 0), "timing off")
+    e2e_steps = max(1, min(args.steps, 20))
+    hp = Pinned(np.uint32, pk.size)
+    hv = Pinned(np.float32, local)
+    ht = Pinned(np.float32, local)
+    hp.a[:] = pk
+    hv.a[:] = v[row0:row0 + local]
+    ht.a[:] = th[row0:row0 + local]
+    dist.barrier()
+
+    def e2e():
+        for _ in range(e2e_steps):
+            check(L.sparsl_net_write_state(net, hp.ptr, hp.count, hv.ptr, ht.ptr, local), "e2e write")
+            check(L.sparsl_net_steps(net, *p, 1), "e2e step")
+            check(L.sparsl_net_read_state(net, hp.ptr, hp.count, hv.ptr, ht.ptr, local), "e2e read")
+
+    e2e_ms = dist.max(events_ms(stream, dist.local, e2e))
+    h2d = pk.nbytes + 2 * local * 4
+    d2h = h2d
+
+    cpu = None
+    if want_cpu and sample is not None:
+        rate, cores, desc = cpu_sample_rate(sample, n_total, pk, v, th, seconds=args.cpu_seconds)
+        cpu = {"value": rate / (n_total * fan_in), "unit": "ticks/s", "cores": cores, "kind": "port",
+               "sample": desc + "; C restatement of the reference's CpuParallel arm, full-network ticks/s = "
+                                "sample synapses/s / 4.29e9 synapses"}
+    kernels_per_tick = len(ops) + 1  # fused tick kernel per block + global spike count
+    pk_, how = peaks()
+    peak = float(pk_.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+    algo = net_bytes_per_tick_per_gpu(n_total, fan_in, dist.world)
+    achieved = algo / (kernel_ms_tick * 1e-3) / 1e9
+    traffic = os.environ.get("SPARSL_NCU_TRAFFIC_PER_TICK")
+    value = args.steps / (ms_max * 1e-3)
+    line = {
+        "metric": "LIF net ticks/sec", "value": value, "unit": "ticks/s", "n_gpus": dist.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded ChaCha12 per row, generated on the GPU)",
+        "config": {"workload": "lif_net: 4,194,304 neurons x fan-in 1024 (4.29e9 synapses), f32 weights "
+                               "N(0,0.03^2), decay 0.95, theta 1.0, reset 0, Bernoulli(0.01) initial spikes",
+                   "parallelism": f"row-block shards x{dist.world}, NCCL all-gather of packed spikes per tick",
+                   "blocks_per_gpu": len(ops), "l2": "inputs per GPU >> 126 MB L2 (no flush needed)",
+                   "setup_s": round(setup_s, 1)},
+        "clocks": ck,
+        "e2e": {"value": e2e_steps / (e2e_ms * 1e-3), "unit": "ticks/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h),
+                "path": "sparsl_net_write_state + sparsl_net_steps(1) + sparsl_net_read_state, pinned host"},
+        "gpu_launches": kernels_per_tick * args.steps,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": float(traffic) if traffic else None,
+                     "kernel": "row_fold_kernel<f32, bits, LIF> (fused spike SpMV + LIF + ballot pack)",
+                     "algorithmic_bytes_per_tick_per_gpu": algo, "kernel_ms_per_tick": kernel_ms_tick,
+                     "peak_source": how},
+        "cpu_baseline": cpu,
+        "check": {"spike_trace_sum": int(trace.sum()), "trace_identical_on_all_ranks": consistent},
+    }
+    for h in (hp, hv, ht):
+        h.free()
+    L.sparsl_net_destroy(net)
+    del ops
+    return line
+
+
+# --------------------------------------------------------------------------
+# reference arm: the oracle's CpuParallel restatement on the host cores
+# --------------------------------------------------------------------------
+def bench_reference(args, dist):
+    if dist.rank != 0:
+        return None
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    n_total, fan_in = NET_N, NET_FANIN
+    k = 8192  # sample rows
+    r = np.random.default_rng(NET_SEED)
+    col = np.sort(r.integers(0, n_total, size=(k, fan_in), dtype=np.uint32), axis=1).reshape(-1)
+    w = (r.standard_normal(k * fan_in) * NET_SIGMA).astype(np.float32)
+    rp = (np.arange(k + 1, dtype=np.uint64) * fan_in).astype(np.uint32)
+    pk = O.pack_spikes((r.random(n_total) < NET_DENSITY).astype(np.uint8))
+    v = r.random(k).astype(np.float32)
+    th = np.full(k, NET_THETA0, np.float32)
+    sp = np.zeros(k, np.uint8)
+    csr = O.Csr(rp, col, n_total)
+    for _ in range(max(args.warmup, 1)):
+        O.fused_spikes_lif(csr, w, pk, v, th, sp, NET_DECAY, NET_VRESET, NET_DTHETA, par=True)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.fused_spikes_lif(csr, w, pk, v, th, sp, NET_DECAY, NET_VRESET, NET_DTHETA, par=True)
+    dt = time.perf_counter() - t0
+    rate = args.steps * csr.nnz / dt
+    value = rate / (n_total * fan_in)
+    desc = (f"{args.steps} fused ticks over a {k}-row x {fan_in} sample block ({csr.nnz} synapses) of the "
+            f"network, {dt:.2f} s; full-network ticks/s = sample synapses/s / 4.29e9")
+    return {
+        "impl": "reference", "metric": "LIF net ticks/sec", "value": value, "unit": "ticks/s",
+        "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / value,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (numpy PCG64 sample of the same distribution)",
+        "config": {"workload": "lif_net: 4,194,304 neurons x fan-in 1024 (4.29e9 synapses)",
+                   "arm": "C restatement of sparsl's CpuParallel arm (Rust toolchain absent here)"},
+        "cpu_baseline": {"value": value, "unit": "ticks/s", "cores": O.num_threads(), "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": "ticks/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="sparsl", choices=["sparsl", "reference"])
+    ap.add_argument("--workload", default="lif_net", choices=["lif_net"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 10 if args.impl == "reference" else 200
+    args.warmup = max(args.warmup, 1)
+    dist = Dist()
+    try:
+        if args.impl == "reference":
+            line = bench_reference(args, dist)
+        else:
+            line = bench_lif_net(args, dist)
+        if dist.rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -233,6 +233,11 @@ void *sparsl_net_stream(sparsl_net *net);
 int sparsl_net_read_state(sparsl_net *net, uint32_t *x_spikes_global, uint64_t words, float *v_local,
                           float *theta_local, uint64_t local_rows);
 int sparsl_net_trace(sparsl_net *net, uint32_t *out, uint64_t cap, uint64_t *n_out);
+/* Bracket the fused tick kernels of each of the next (up to max_ticks) ticks
+ * with CUDA events on the net's stream; 0 turns timing off. */
+int sparsl_net_set_timing(sparsl_net *net, uint64_t max_ticks);
+/* Sum of those kernel durations over the ticks of the last steps call. */
+int sparsl_net_kernel_ms(sparsl_net *net, double *total_ms, uint64_t *ticks);
 
 #ifdef __cplusplus
 }

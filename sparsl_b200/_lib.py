@@ -37,7 +37,7 @@ class Shape(ctypes.Structure):
                 ("nnz", u64), ("max_row_nnz", u64)]
 
 
-# name -> (restype, argtypes); every symbol include/sparsl_cuda.h declares.
+# name -> (restype, argtypes); every symbol include/*.h declares.
 SIGNATURES = {
     "sparsl_last_error": (ctypes.c_char_p, []),
     "sparsl_last_reason": (ctypes.c_char_p, []),
@@ -109,6 +109,12 @@ SIGNATURES = {
     "sparsl_net_stream": (vp, [vp]),
     "sparsl_net_read_state": (i32, [vp, vp, u64, vp, vp, u64]),
     "sparsl_net_trace": (i32, [vp, vp, u64, ctypes.POINTER(u64)]),
+    "sparsl_net_set_timing": (i32, [vp, u64]),
+    "sparsl_net_kernel_ms": (i32, [vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(u64)]),
+    # include/sparsl_workload.h
+    "sparsl_workload_fixed_fanin": (i32, [u64, u64, u64, u64, ctypes.c_uint32, f32, vp, vp, vp]),
+    "sparsl_workload_uniform_row_ptr": (i32, [u64, ctypes.c_uint32, vp, vp]),
+    "sparsl_workload_lif_state": (i32, [u64, u64, u64, f32, f32, f32, f32, vp, vp, vp, vp]),
 }
 
 

@@ -14,6 +14,7 @@
 #include <atomic>
 #include <chrono>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -514,7 +515,16 @@ int sparsl_dev_assoc_scan(sparsl_dev* d, const float* in, uint64_t n, float* out
   set.ptr[set.count++] = d->scan_out.canary();
   CK("assoc_scan", launch_canary_check(set, d->err.d, d->stream));
   int rc = wait_bounded(d->stream, d->ev, d->err.d, d->err.h, "assoc_scan");
-  if (rc != SPARSL_OK) d->scan_dirty = true;
+  if (rc != SPARSL_OK) {
+    d->scan_dirty = true;
+    if (std::getenv("SPARSL_SCAN_DEBUG")) {
+      uint32_t st[16] = {0};
+      cudaMemcpy(st, d->sc.repair_stats, sizeof st, cudaMemcpyDeviceToHost);
+      std::fprintf(stderr, "scan debug:");
+      for (uint32_t v : st) std::fprintf(stderr, " %u", v);
+      std::fprintf(stderr, "\n");
+    }
+  }
   return rc;
 }
 
@@ -1179,6 +1189,11 @@ struct sparsl_net {
   int cur = 0;
   uint64_t trace_cap = 0, last_steps = 0;
   ncclComm_t comm = nullptr;
+  // Optional per-tick timing of the fused tick kernels (events bracket the
+  // block kernels of each tick, excluding the all-gather and the count).
+  bool timing = false;
+  std::vector<cudaEvent_t> ev_a, ev_b;
+  uint64_t timed_ticks = 0;
 };
 
 extern "C" {
@@ -1287,6 +1302,8 @@ void sparsl_net_destroy(sparsl_net* net) {
     else
       g_nccl.CommDestroy(net->comm);
   }
+  for (cudaEvent_t e : net->ev_a) cudaEventDestroy(e);
+  for (cudaEvent_t e : net->ev_b) cudaEventDestroy(e);
   dfree(net->xs[0]);
   dfree(net->xs[1]);
   dfree(net->trace);
@@ -1326,6 +1343,8 @@ static int net_enqueue(sparsl_net* net, float decay, float v_reset, float dtheta
   for (uint64_t t = 0; t < steps; ++t) {
     uint32_t* src = net->xs[net->cur].as<uint32_t>();
     uint32_t* dst = net->xs[net->cur ^ 1].as<uint32_t>();
+    const bool tm = net->timing && t < net->ev_a.size();
+    if (tm) CK("net_steps", cudaEventRecord(net->ev_a[t], net->stream));
     for (size_t b = 0; b < net->blocks.size(); ++b) {
       sparsl_op* op = net->blocks[b];
       if (!op->nrows) continue;
@@ -1336,6 +1355,7 @@ static int net_enqueue(sparsl_net* net, float decay, float v_reset, float dtheta
       p.err = net->err.d;
       CK("net_steps", launch_rows(p, net->stream));
     }
+    if (tm) CK("net_steps", cudaEventRecord(net->ev_b[t], net->stream));
     if (net->nranks > 1) {
       ncclResult_t r = g_nccl.AllGather(dst + (uint64_t)net->rank * slice, dst, slice, ncclUint32, net->comm, net->stream);
       if (r != ncclSuccess) return fail(SPARSL_ERR_EXECUTION, "ncclAllGather failed", g_nccl.GetErrorString(r));
@@ -1344,6 +1364,7 @@ static int net_enqueue(sparsl_net* net, float decay, float v_reset, float dtheta
     net->cur ^= 1;
   }
   net->last_steps = steps;
+  net->timed_ticks = net->timing ? std::min<uint64_t>(steps, net->ev_a.size()) : 0;
   return SPARSL_OK;
 }
 
@@ -1392,6 +1413,40 @@ int sparsl_net_read_state(sparsl_net* net, uint32_t* xs, uint64_t words, float* 
   }
   CK("net_read_state", launch_canary_check(set, net->err.d, net->stream));
   return wait_bounded(net->stream, net->ev, net->err.d, net->err.h, "net_read_state");
+}
+
+int sparsl_net_set_timing(sparsl_net* net, uint64_t max_ticks) {
+  if (!net) return fail(SPARSL_ERR_INVALID, "null net", "null net");
+  CK("net_set_timing", cudaSetDevice(net->dev->ordinal));
+  CK("net_set_timing", cudaStreamSynchronize(net->stream));
+  for (cudaEvent_t e : net->ev_a) cudaEventDestroy(e);
+  for (cudaEvent_t e : net->ev_b) cudaEventDestroy(e);
+  net->ev_a.clear();
+  net->ev_b.clear();
+  net->timing = max_ticks > 0;
+  for (uint64_t i = 0; i < max_ticks; ++i) {
+    cudaEvent_t a, b;
+    CK("net_set_timing", cudaEventCreate(&a));
+    CK("net_set_timing", cudaEventCreate(&b));
+    net->ev_a.push_back(a);
+    net->ev_b.push_back(b);
+  }
+  return SPARSL_OK;
+}
+
+int sparsl_net_kernel_ms(sparsl_net* net, double* total_ms, uint64_t* ticks) {
+  if (!net) return fail(SPARSL_ERR_INVALID, "null net", "null net");
+  CK("net_kernel_ms", cudaSetDevice(net->dev->ordinal));
+  CK("net_kernel_ms", cudaStreamSynchronize(net->stream));
+  double sum = 0.0;
+  for (uint64_t t = 0; t < net->timed_ticks; ++t) {
+    float ms = 0.f;
+    CK("net_kernel_ms", cudaEventElapsedTime(&ms, net->ev_a[t], net->ev_b[t]));
+    sum += ms;
+  }
+  if (total_ms) *total_ms = sum;
+  if (ticks) *ticks = net->timed_ticks;
+  return SPARSL_OK;
 }
 
 int sparsl_net_trace(sparsl_net* net, uint32_t* out, uint64_t cap, uint64_t* n_out) {

@@ -25,7 +25,7 @@ enum DevErr : uint32_t {
 // Iteration cap for every device-side spin.  At ~100 ns per poll this bounds a
 // wait at well under a second; a wait that runs out records DEVERR_* and
 // returns instead of hanging the GPU.
-constexpr uint32_t kSpinLimit = 1u << 22;
+constexpr uint32_t kSpinLimit = 1u << 20;
 
 __device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
 __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }

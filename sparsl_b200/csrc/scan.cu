@@ -206,12 +206,23 @@ __global__ void __launch_bounds__(kScanThreads) scan_main(const float2* __restri
       uint32_t stt = 0;
       if (j >= 0) stt = ld_acquire_u32(&rec[j].status);
       const uint32_t incl_mask = __ballot_sync(0xffffffffu, stt == 2u);
-      const uint32_t ready_mask = __ballot_sync(0xffffffffu, stt != 0u);
+      // Tile 0 has no predecessor, so the walk may only stop there, never
+      // pass through it: it counts as ready once it is inclusive.
+      const uint32_t ready_mask = __ballot_sync(0xffffffffu, stt == 2u || (stt == 1u && j > 0));
       const int L = incl_mask ? (__ffs(incl_mask) - 1) : 32;
       const uint32_t need = (L == 32) ? 0xffffffffu : ((1u << L) - 1u) | (1u << L);
       if ((ready_mask & need) != need) {
         if (++spins > kSpinLimit) {
           set_err(err, DEVERR_LOOKBACK_TIMEOUT);
+          if (lane == 0 && atomicCAS(s.repair_stats + 2, 0u, 1u) == 0u) {
+            s.repair_stats[3] = tile;
+            s.repair_stats[4] = (uint32_t)base;
+            s.repair_stats[5] = (uint32_t)L;
+            s.repair_stats[6] = ready_mask;
+            s.repair_stats[7] = incl_mask;
+            s.repair_stats[8] = s.ticket[0];
+            s.repair_stats[9] = s.ticket[1];
+          }
           break;
         }
         __nanosleep(32);
@@ -283,6 +294,11 @@ __global__ void __launch_bounds__(kScanThreads) scan_main(const float2* __restri
         while (ld_acquire_u32(&rec[tile - 1].status) != 2u) {
           if (++sp > kSpinLimit) {
             set_err(err, DEVERR_LOOKBACK_TIMEOUT);
+            if (atomicCAS(s.repair_stats + 2, 0u, 2u) == 0u) {
+              s.repair_stats[3] = tile;
+              s.repair_stats[8] = s.ticket[0];
+              s.repair_stats[9] = s.ticket[1];
+            }
             break;
           }
           __nanosleep(32);

@@ -1,0 +1,86 @@
+"""The network tick runtime (row-block operators + all-gather + trace) against
+the oracle's recurrent ticks, and the GPU workload generator against its
+definition.  Single GPU: one rank, several row blocks."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import assert_bits_equal
+
+import sparsl_b200 as S
+from sparsl_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(rc):
+    assert rc == 0, _lib.last_error()
+
+
+def _make_net(dev, ops, row0, n):
+    L = _lib.load()
+    arr = (ctypes.c_void_p * len(ops))(*[op.handle.value for op in ops])
+    h = ctypes.c_void_p()
+    _check(L.sparsl_net_create(dev.handle, arr, len(ops), row0, n, 0, 1, None, ctypes.byref(h)))
+    return h
+
+
+@pytest.mark.parametrize("n,deg,splits", [(4096, 64, [2048, 2048]), (6016, 200, [1024, 32, 4960])])
+def test_net_ticks_match_oracle_recurrent_steps(O, cuda_device, n, deg, splits):
+    rng = O.Rng(0xE7 + n)
+    csr = O.random_csr(n, n, deg, rng)
+    w = O.random_vec(csr.nnz, 0.5, rng)
+    v0 = O.random_vec(n, 1.0, rng)
+    t0 = np.full(n, 0.45, np.float32)
+    xs0 = O.pack_spikes((np.random.default_rng(n).random(n) < 0.03).astype(np.uint8))
+    ops, r = [], 0
+    for k in splits:
+        rp = (csr.row_ptr[r:r + k + 1] - csr.row_ptr[r]).astype(np.uint32)
+        col = csr.col[csr.row_ptr[r]:csr.row_ptr[r + k]]
+        ww = w[csr.row_ptr[r]:csr.row_ptr[r + k]]
+        ops.append(cuda_device.prepare(S.Csr(rp, col, n), n, ww))
+        r += k
+    L = _lib.load()
+    net = _make_net(cuda_device, ops, 0, n)
+    try:
+        _check(L.sparsl_net_write_state(net, xs0.ctypes.data, xs0.size, v0.ctypes.data, t0.ctypes.data, n))
+        steps = 30
+        _check(L.sparsl_net_steps(net, 0.95, 0.0, 0.0, steps))
+        trace = np.zeros(steps, np.uint32)
+        cnt = ctypes.c_uint64()
+        _check(L.sparsl_net_trace(net, trace.ctypes.data, steps, ctypes.byref(cnt)))
+        vw, tw, sw, xw = v0.copy(), t0.copy(), np.zeros(n, np.uint8), xs0.copy()
+        want = O.recurrent_steps(csr, w, xw, vw, tw, sw, 0.95, 0.0, 0.0, steps)
+        assert np.array_equal(trace, want)
+        xs, v, t = np.zeros_like(xs0), np.zeros(n, np.float32), np.zeros(n, np.float32)
+        _check(L.sparsl_net_read_state(net, xs.ctypes.data, xs.size, v.ctypes.data, t.ctypes.data, n))
+        assert np.array_equal(xs, xw)
+        assert_bits_equal(v, vw)
+        assert_bits_equal(t, tw)
+    finally:
+        L.sparsl_net_destroy(net)
+
+
+def test_workload_generator_matches_its_definition(O, cuda_device):
+    """Row r's columns are gen_index(ncols) draws of ChaCha12 seeded with
+    seed ^ (r * 0x9E3779B97F4A7C15), sorted -- checked with the oracle's Rng."""
+    L = _lib.load()
+    seed, row0, nrows, ncols, fan_in = 0x1234, 77, 5, 1_000_003, 300
+    dcol = L.sparsl_device_alloc(cuda_device.handle, nrows * fan_in * 4)
+    dw = L.sparsl_device_alloc(cuda_device.handle, nrows * fan_in * 4)
+    try:
+        _check(L.sparsl_workload_fixed_fanin(seed, row0, nrows, ncols, fan_in, 0.05, dcol, dw, None))
+        col = np.zeros(nrows * fan_in, np.uint32)
+        w = np.zeros(nrows * fan_in, np.float32)
+        _check(L.sparsl_memcpy(col.ctypes.data, dcol, col.nbytes))
+        _check(L.sparsl_memcpy(w.ctypes.data, dw, w.nbytes))
+    finally:
+        L.sparsl_device_free(dcol)
+        L.sparsl_device_free(dw)
+    for i in range(nrows):
+        r = row0 + i
+        rng = O.Rng(seed ^ ((r * 0x9E3779B97F4A7C15) & (2 ** 64 - 1)))
+        want = np.sort(np.array([rng.gen_index(ncols) for _ in range(fan_in)], np.uint32))
+        assert np.array_equal(col[i * fan_in:(i + 1) * fan_in], want)
+    assert abs(float(w.std()) - 0.05) < 0.01 and abs(float(w.mean())) < 0.01
