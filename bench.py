@@ -430,6 +430,256 @@ def bench_lif_net(args, dist):
 
 
 # --------------------------------------------------------------------------
+# single-kernel workloads (configs 1-3)
+# --------------------------------------------------------------------------
+SPMV_N, SPMV_DEG, SPMV_SEED = 100_000, 64, 0x5B11
+SCAN_N, SCAN_SEED = 1 << 26, 0x5CA2
+LIF_N, LIF_FANIN, LIF_SIGMA, LIF_DENSITY, LIF_SEED = 262_144, 512, 0.05, 0.02, 0x11F3
+
+
+def gen_distinct_rows(rng, nrows, ncols, deg):
+    """deg distinct sorted columns per row (rejection of repeats)."""
+    out = np.empty((nrows, deg), np.uint32)
+    todo = np.arange(nrows)
+    while todo.size:
+        cand = np.sort(rng.integers(0, ncols, size=(todo.size, deg + 16), dtype=np.uint32), axis=1)
+        dup = np.zeros_like(cand, dtype=bool)
+        dup[:, 1:] = cand[:, 1:] == cand[:, :-1]
+        key = np.where(dup, np.uint32(0xFFFFFFFF), cand)
+        key.sort(axis=1)
+        good = key[:, deg - 1] != 0xFFFFFFFF
+        out[todo[good]] = key[good, :deg]
+        todo = todo[~good]
+    return out.reshape(-1)
+
+
+def flush_l2(buf):
+    buf.zero_()
+
+
+def time_launches(stream, fn, k, flush=None):
+    """Per-launch device time (ms) of fn on `stream`, optionally flushing L2 before each."""
+    import torch
+
+    ts = []
+    for _ in range(k):
+        if flush is not None:
+            with torch.cuda.stream(stream):
+                flush()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        b.synchronize()
+        ts.append(a.elapsed_time(b))
+    return ts
+
+
+def bench_spmv(args, dev, want_cpu):
+    import torch
+    import sparsl_b200 as S
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    r = np.random.default_rng(SPMV_SEED)
+    col = gen_distinct_rows(r, SPMV_N, SPMV_N, SPMV_DEG)
+    rp = (np.arange(SPMV_N + 1, dtype=np.uint64) * SPMV_DEG).astype(np.uint32)
+    w = r.uniform(-1.0, 1.0, col.size).astype(np.float32)
+    x = r.uniform(0.0, 1.0, SPMV_N).astype(np.float32)
+    op = dev.prepare(S.Csr(rp, col, SPMV_N), SPMV_N, w)
+    L = lib()
+    s = torch.cuda.Stream()  # a real stream: a NULL handle would mean the operator's own stream
+    torch.cuda.set_stream(s)
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.zeros(SPMV_N, dtype=torch.float32, device="cuda")
+    flush = torch.empty(64 << 22, dtype=torch.float32, device="cuda")  # 1 GiB > L2
+    run = lambda: check(L.sparsl_op_spmv_device(op.handle, dx.data_ptr(), dy.data_ptr(), s.cuda_stream), "spmv")
+    for _ in range(args.warmup):
+        run()
+    dy.zero_()
+    ts = time_launches(s, run, args.kernel_iters, flush=lambda: flush_l2(flush))
+    ms = statistics.median(ts)
+    algo = col.size * 8 + (SPMV_N + 1) * 4 + SPMV_N * 4 + 2 * SPMV_N * 4
+    # bit-exact at full size: y accumulated kernel_iters times from zero vs the oracle doing the same
+    import oracle as O
+
+    got = dy.cpu().numpy()
+    want = np.zeros(SPMV_N, np.float32)
+    csr = O.Csr(rp, col, SPMV_N)
+    for _ in range(args.kernel_iters):
+        O.spmv(csr, w, x, want, par=True)
+    exact = bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))
+    # end to end: the C-ABI slice call with pinned host x and y
+    hx, hy = Pinned(np.float32, SPMV_N), Pinned(np.float32, SPMV_N)
+    hx.a[:] = x
+    hy.a[:] = 0
+    ops_stream = L.sparsl_op_stream(op.handle)
+    ets = [events_ms(ops_stream, torch.cuda.current_device(),
+                     lambda: check(L.sparsl_op_spmv(op.handle, hx.ptr, SPMV_N, hy.ptr, SPMV_N), "spmv e2e"))
+           for _ in range(max(3, args.kernel_iters // 2))]
+    e2e_ms = statistics.median(ets)
+    hx.free()
+    hy.free()
+    cpu = None
+    if want_cpu:
+        t0, k = time.perf_counter(), 0
+        yy = np.zeros(SPMV_N, np.float32)
+        while time.perf_counter() - t0 < args.cpu_seconds / 2:
+            O.spmv(csr, w, x, yy, par=True)
+            k += 1
+        dt = time.perf_counter() - t0
+        cpu = {"value": k * algo / dt / 1e9, "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
+               "sample": f"{k} full SpMVs of the same matrix, CpuParallel restatement"}
+    return {"metric": "SpMV effective HBM GB/s", "value": algo / (ms * 1e-3) / 1e9, "unit": "GB/s",
+            "ms_per_step": ms, "kernel_ms_samples": len(ts), "algorithmic_bytes": algo,
+            "config": "100,000 x 100,000, 64 distinct sorted cols/row, w U[-1,1], x U[0,1], f32; L2 flushed "
+                      "(1 GiB write) before every launch",
+            "e2e": {"value": algo / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 2 * SPMV_N * 4,
+                    "d2h_bytes_per_step": SPMV_N * 4, "path": "sparsl_op_spmv, pinned host x/y"},
+            "bit_exact_vs_oracle": exact, "cpu_baseline": cpu}
+
+
+def bench_scan(args, dev, want_cpu):
+    import torch
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    r = np.random.default_rng(SCAN_SEED)
+    xs = np.empty((SCAN_N, 2), np.float32)
+    xs[:, 0] = r.uniform(0.9, 1.0, SCAN_N).astype(np.float32)
+    xs[:, 1] = r.standard_normal(SCAN_N).astype(np.float32)
+    L = lib()
+    s = torch.cuda.Stream()
+    torch.cuda.set_stream(s)
+    din = torch.from_numpy(xs).cuda()
+    dout = torch.empty_like(din)
+    run = lambda: check(L.sparsl_dev_assoc_scan_device(dev.handle, din.data_ptr(), SCAN_N, dout.data_ptr(),
+                                                       s.cuda_stream), "scan")
+    for _ in range(args.warmup):
+        run()
+    ts = time_launches(s, run, args.kernel_iters)
+    ms = statistics.median(ts)
+    rep, seg = dev.scan_stats()
+    got = dout.cpu().numpy()
+    want = O.scan_sequential(xs)
+    exact = bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))
+    algo = 16 * SCAN_N
+    hin, hout = Pinned(np.float32, 2 * SCAN_N), Pinned(np.float32, 2 * SCAN_N)
+    hin.a[:] = xs.reshape(-1)
+    ets = [events_ms(L.sparsl_dev_stream(dev.handle), torch.cuda.current_device(),
+                     lambda: check(L.sparsl_dev_assoc_scan(dev.handle, hin.ptr, SCAN_N, hout.ptr), "scan e2e"))
+           for _ in range(3)]
+    e2e_ms = statistics.median(ets)
+    hin.free()
+    hout.free()
+    cpu = None
+    if want_cpu:
+        t0 = time.perf_counter()
+        O.scan_chunked(xs, 256)
+        dt_par = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        O.scan_sequential(xs)
+        dt_seq = time.perf_counter() - t0
+        cpu = {"value": algo / dt_par / 1e9, "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
+               "sample": f"one full 2^26 scan: chunked (CpuParallel arm) {dt_par:.2f} s, sequential {dt_seq:.2f} s"}
+    return {"metric": "affine scan effective HBM GB/s", "value": algo / (ms * 1e-3) / 1e9, "unit": "GB/s",
+            "ms_per_step": ms, "algorithmic_bytes": algo,
+            "config": "2^26 maps, a U[0.9,1.0], b N(0,1), f32; 1 GiB in+out > L2",
+            "repair": {"elements_replayed": rep, "segments": seg},
+            "e2e": {"value": algo / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 8 * SCAN_N,
+                    "d2h_bytes_per_step": 8 * SCAN_N, "path": "sparsl_dev_assoc_scan, pinned host"},
+            "bit_exact_vs_oracle": exact, "cpu_baseline": cpu}
+
+
+def bench_lif(args, dev, want_cpu):
+    import torch
+    import sparsl_b200 as S
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    n, fan = LIF_N, LIF_FANIN
+    nnz = n * fan
+    dcol, dw = DevArray(dev, nnz * 4), DevArray(dev, nnz * 4)
+    check(lib().sparsl_workload_fixed_fanin(LIF_SEED, 0, n, n, fan, LIF_SIGMA, dcol.ptr, dw.ptr, None), "gen")
+    col, w = dcol.to_host(np.uint32, nnz), dw.to_host(np.float32, nnz)
+    dcol.free()
+    dw.free()
+    rp = (np.arange(n + 1, dtype=np.uint64) * fan).astype(np.uint32)
+    dv, dth, dpk = DevArray(dev, n * 4), DevArray(dev, n * 4), DevArray(dev, n // 8)
+    check(lib().sparsl_workload_lif_state(LIF_SEED ^ 0x57A7E, 0, n, 0.0, 1.0, 1.0, LIF_DENSITY, dv.ptr, dth.ptr,
+                                          dpk.ptr, None), "state")
+    v0, th0, pk0 = dv.to_host(np.float32, n), dth.to_host(np.float32, n), dpk.to_host(np.uint32, n // 32)
+    for a in (dv, dth, dpk):
+        a.free()
+    op = dev.prepare(S.Csr(rp, col, n), n, w)
+    params = S.LifParams.new(0.95, 0.0, 0.0)
+    L = lib()
+    # bit-exact check of the first ticks against the oracle's CpuParallel arm
+    check_ticks = 5
+    op.write_x_spikes(pk0)
+    op.write_lif_state(v0, th0)
+    op.fused_spmv_spikes_lif_recurrent_steps(params, check_ticks)
+    csr = O.Csr(rp, col, n)
+    vw, tw, sw, xw = v0.copy(), th0.copy(), np.zeros(n, np.uint8), pk0.copy()
+    trace_w = O.recurrent_steps(csr, w, xw, vw, tw, sw, 0.95, 0.0, 0.0, check_ticks, par=True)
+    vg, tg, sg = np.zeros(n, np.float32), np.zeros(n, np.float32), np.zeros(n, np.bool_)
+    op.sync_lif_state(vg, tg, sg)
+    exact = bool(np.array_equal(op.spike_trace(), trace_w) and np.array_equal(vg.view(np.uint32), vw.view(np.uint32))
+                 and np.array_equal(op.sync_x_spikes(), xw))
+    # timed run: the 1000-tick network from its initial state
+    op.write_x_spikes(pk0)
+    op.write_lif_state(v0, th0)
+    check(L.sparsl_op_recurrent_steps(op.handle, 0.95, 0.0, 0.0, args.warmup), "warm")
+    op.write_x_spikes(pk0)
+    op.write_lif_state(v0, th0)
+    ticks = 1000
+    st = L.sparsl_op_stream(op.handle)
+    ms = events_ms(st, torch.cuda.current_device(),
+                   lambda: check(L.sparsl_op_recurrent_steps_async(op.handle, 0.95, 0.0, 0.0, ticks), "ticks"))
+    check(L.sparsl_op_wait(op.handle), "wait")
+    trace = op.spike_trace()
+    algo = nnz * 8 + (n + 1) * 4 + 2 * n * 4 + n * 4 + 2 * n // 8
+    # end to end: one tick per slice-API call with pinned host buffers
+    hs, hv, ht, ho = Pinned(np.uint32, n // 32), Pinned(np.float32, n), Pinned(np.float32, n), Pinned(np.uint8, n)
+    hs.a[:] = pk0
+    hv.a[:] = v0
+    ht.a[:] = th0
+    e2e_steps = 20
+
+    def e2e():
+        for _ in range(e2e_steps):
+            check(L.sparsl_op_fused_spikes_lif(op.handle, hs.ptr, n // 32, hv.ptr, ht.ptr, ho.ptr, n, 0.95, 0.0, 0.0),
+                  "e2e tick")
+            hs.a[:] = np.packbits(ho.a.reshape(-1, 32)[:, ::-1], axis=1).view(">u4").reshape(-1)
+
+    e2e_ms = events_ms(st, torch.cuda.current_device(), e2e)
+    for h in (hs, hv, ht, ho):
+        h.free()
+    cpu = None
+    if want_cpu:
+        vv, tt, ss, xx = v0.copy(), th0.copy(), np.zeros(n, np.uint8), pk0.copy()
+        t0, k = time.perf_counter(), 0
+        while time.perf_counter() - t0 < args.cpu_seconds / 2:
+            O.recurrent_steps(csr, w, xx, vv, tt, ss, 0.95, 0.0, 0.0, 1, par=True)
+            k += 1
+        dt = time.perf_counter() - t0
+        cpu = {"value": k / dt, "unit": "ticks/s", "cores": O.num_threads(), "kind": "port",
+               "sample": f"{k} full ticks of the same network, CpuParallel restatement"}
+    per_tick = ms / ticks
+    return {"metric": "LIF net ticks/sec (1 GPU)", "value": 1e3 / per_tick, "unit": "ticks/s",
+            "ms_per_step": per_tick, "ticks": ticks, "algorithmic_bytes_per_tick": algo,
+            "effective_GBs": algo / (per_tick * 1e-3) / 1e9,
+            "config": "262,144 neurons x fan-in 512, w N(0,0.05^2), decay 0.95, theta 1, reset 0, Bernoulli(0.02)",
+            "spike_trace_sum": int(trace.sum()),
+            "e2e": {"value": e2e_steps / (e2e_ms * 1e-3), "unit": "ticks/s",
+                    "h2d_bytes_per_step": n // 8 + 8 * n, "d2h_bytes_per_step": 9 * n,
+                    "path": "sparsl_op_fused_spikes_lif per tick + host repack, pinned host"},
+            "bit_exact_vs_oracle_first_ticks": exact, "cpu_baseline": cpu}
+
+
+# --------------------------------------------------------------------------
 # reference arm: the oracle's CpuParallel restatement on the host cores
 # --------------------------------------------------------------------------
 def bench_reference(args, dist):
@@ -478,7 +728,9 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="sparsl", choices=["sparsl", "reference"])
-    ap.add_argument("--workload", default="lif_net", choices=["lif_net"])
+    ap.add_argument("--workload", default="lif_net", choices=["lif_net", "spmv", "scan", "lif"])
+    ap.add_argument("--no-extras", action="store_true", help="N=1: skip the SpMV / scan / LIF-1GPU figures")
+    ap.add_argument("--kernel-iters", type=int, default=20)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
@@ -489,8 +741,29 @@ def main():
     try:
         if args.impl == "reference":
             line = bench_reference(args, dist)
+        elif args.workload != "lif_net":
+            import torch
+            import sparsl_b200 as S
+
+            torch.cuda.set_device(dist.local)
+            dev = S.Device.try_new(S.Backend.Cuda, dist.local)
+            fn = {"spmv": bench_spmv, "scan": bench_scan, "lif": bench_lif}[args.workload]
+            line = fn(args, dev, dist.rank == 0 and not args.no_cpu) if dist.rank == 0 else None
         else:
             line = bench_lif_net(args, dist)
+            if dist.world == 1 and not args.no_extras:
+                import torch
+                import sparsl_b200 as S
+
+                torch.cuda.empty_cache()
+                dev = S.Device.try_new(S.Backend.Cuda, dist.local)
+                extras = {}
+                for name, fn in (("spmv", bench_spmv), ("scan", bench_scan), ("lif", bench_lif)):
+                    try:
+                        extras[name] = fn(args, dev, not args.no_cpu)
+                    except Exception as e:  # report, never hide
+                        extras[name] = {"error": repr(e)}
+                line["workloads"] = extras
         if dist.rank == 0 and line is not None:
             print(json.dumps(line), flush=True)
     finally:

@@ -25,6 +25,7 @@
 
 #include "../../include/sparsl_cuda.h"
 #include "common.cuh"
+#include "ell.cuh"
 #include "host.hpp"
 #include "misc.cuh"
 #include "rows.cuh"
@@ -273,6 +274,8 @@ struct sparsl_op {
   ErrWord err;
   DBuf row_ptr, col, w;
   DBuf col_ptr, csc_row, csc_eidx;
+  // Uniform row length: TMA tensor maps over col / w as [nrows x L] matrices.
+  EllMaps ell;
   // resident scratch (the write / step / sync API)
   DBuf rx, rxs[2], ry, rv, rth, rspk;
   int cur = 0;
@@ -329,6 +332,13 @@ RowLaunch fwd_launch(sparsl_op* op) {
   p.nlines = op->nrows;
   p.err = op->err.d;
   return p;
+}
+
+// Forward launches take the TMA-pipelined kernel when the operator's rows all
+// have the same length, the generic row-fold kernel otherwise.
+cudaError_t launch_fwd(sparsl_op* op, const RowLaunch& p, cudaStream_t s) {
+  if (op->ell.ok) return launch_ell(op->ell, p, s);
+  return launch_rows(p, s);
 }
 
 void set_bits_mode(RowLaunch& p, const uint32_t* bits, uint64_t words) {
@@ -646,7 +656,8 @@ int sparsl_op_prepare(sparsl_dev* d, const uint32_t* row_ptr, uint64_t row_ptr_l
   PALLOC(op->rth, nrows * 4, true, "theta");
   PALLOC(op->rspk, nrows, true, "spikes");
   PALLOC(op->idx_list, nrows * 4, true, "spike index list");
-  PALLOC(op->tile_flags, ((uint64_t)row_tiles(op->nrows) + 1) * 8, false, "tile flags");
+  PALLOC(op->tile_flags, ((uint64_t)std::max(row_tiles(op->nrows), ell_tiles(op->nrows)) + 1) * 8, false,
+         "tile flags");
   PALLOC(op->ticket, 64, false, "tile ticket");
   if (cudaMemcpyAsync(op->row_ptr.p, row_ptr, (nrows + 1) * 4, cudaMemcpyHostToDevice, op->stream) != cudaSuccess)
     return bail(fail_cuda("prepare", cudaGetLastError()));
@@ -690,6 +701,13 @@ int sparsl_op_prepare(sparsl_dev* d, const uint32_t* row_ptr, uint64_t row_ptr_l
   cudaMemsetAsync(op->rspk.p, 0, op->rspk.bytes, op->stream);
   cudaMemsetAsync(op->tile_flags.p, 0, op->tile_flags.bytes, op->stream);
   cudaMemsetAsync(op->ticket.p, 0, op->ticket.bytes, op->stream);
+  // Uniform row length (fixed fan-in / fixed degree): enable the TMA path.
+  if (nrows && nnz && nnz % nrows == 0 && !std::getenv("SPARSL_NO_ELL")) {
+    const uint64_t L = nnz / nrows;
+    bool uniform = L <= 0xffffffffull;
+    for (uint64_t r = 0; uniform && r <= nrows; ++r) uniform = (uint64_t)row_ptr[r] == r * L;
+    if (uniform) ell_encode(op->ell, op->col.as<uint32_t>(), op->w.p, wkind_of(precision), nrows, (uint32_t)L);
+  }
   rc = wait_op(op, "prepare");  // host vectors above must outlive the copies
   if (rc != SPARSL_OK) return bail(rc);
 #undef PALLOC
@@ -756,7 +774,7 @@ int sparsl_op_spmv(sparsl_op* op, const float* x, uint64_t x_len, float* y, uint
   RowLaunch p = fwd_launch(op);
   p.x = op->sx.as<float>();
   p.y = op->sy.as<float>();
-  CK("spmv", launch_rows(p, op->stream));
+  CK("spmv", launch_fwd(op, p, op->stream));
   CK("spmv", cudaMemcpyAsync(y, op->sy.p, (uint64_t)op->nrows * 4, cudaMemcpyDeviceToHost, op->stream));
   return finish(op, "spmv");
 }
@@ -776,7 +794,7 @@ int sparsl_op_spmv_spikes(sparsl_op* op, const uint32_t* spikes, uint64_t words,
   RowLaunch p = fwd_launch(op);
   set_bits_mode(p, op->sbits.as<uint32_t>(), op->words());
   p.y = op->sy.as<float>();
-  CK("spmv_spikes", launch_rows(p, op->stream));
+  CK("spmv_spikes", launch_fwd(op, p, op->stream));
   CK("spmv_spikes", cudaMemcpyAsync(y, op->sy.p, (uint64_t)op->nrows * 4, cudaMemcpyDeviceToHost, op->stream));
   return finish(op, "spmv_spikes");
 }
@@ -863,7 +881,7 @@ static int fused_common(sparsl_op* op, const float* x, const uint32_t* bits, flo
   p.decay = decay;
   p.v_reset = v_reset;
   p.dtheta = dtheta;
-  CK(name, launch_rows(p, op->stream));
+  CK(name, launch_fwd(op, p, op->stream));
   CK(name, cudaMemcpyAsync(v, op->sv.p, nr * 4, cudaMemcpyDeviceToHost, op->stream));
   CK(name, cudaMemcpyAsync(theta, op->sth.p, nr * 4, cudaMemcpyDeviceToHost, op->stream));
   CK(name, cudaMemcpyAsync(spk, op->sspk.p, nr, cudaMemcpyDeviceToHost, op->stream));
@@ -937,7 +955,7 @@ int sparsl_op_spmv_resident(sparsl_op* op) {
   RowLaunch p = fwd_launch(op);
   p.x = op->rx.as<float>();
   p.y = op->ry.as<float>();
-  CK("spmv_resident", launch_rows(p, op->stream));
+  CK("spmv_resident", launch_fwd(op, p, op->stream));
   return wait_op(op, "spmv_resident");
 }
 
@@ -959,7 +977,7 @@ int sparsl_op_fused_lif_resident(sparsl_op* op, float decay, float v_reset, floa
   RowLaunch p = fwd_launch(op);
   p.x = op->rx.as<float>();
   lif_resident_launch(op, p, decay, v_reset, dtheta);
-  CK("fused_spmv_lif_resident", launch_rows(p, op->stream));
+  CK("fused_spmv_lif_resident", launch_fwd(op, p, op->stream));
   return wait_op(op, "fused_spmv_lif_resident");
 }
 
@@ -971,7 +989,7 @@ int sparsl_op_fused_spikes_lif_resident(sparsl_op* op, float decay, float v_rese
   RowLaunch p = fwd_launch(op);
   set_bits_mode(p, op->rxs[op->cur].as<uint32_t>(), op->words());
   lif_resident_launch(op, p, decay, v_reset, dtheta);
-  CK("fused_spmv_spikes_lif_resident", launch_rows(p, op->stream));
+  CK("fused_spmv_spikes_lif_resident", launch_fwd(op, p, op->stream));
   return wait_op(op, "fused_spmv_spikes_lif_resident");
 }
 
@@ -997,7 +1015,7 @@ static int enqueue_recurrent(sparsl_op* op, float decay, float v_reset, float dt
     p.idx_count = op->trace.as<uint32_t>() + t;
     p.tile_flags = op->tile_flags.as<unsigned long long>();
     p.tile_ticket = op->ticket.as<uint32_t>();
-    CK("fused_spmv_spikes_lif_recurrent_steps", launch_rows(p, op->stream));
+    CK("fused_spmv_spikes_lif_recurrent_steps", launch_fwd(op, p, op->stream));
     op->cur ^= 1;
   }
   op->last_steps = steps;
@@ -1095,7 +1113,7 @@ int sparsl_op_spmv_device(sparsl_op* op, const float* d_x, float* d_y, void* str
   RowLaunch p = fwd_launch(op);
   p.x = d_x;
   p.y = d_y;
-  CK("spmv", launch_rows(p, pick(op, stream)));
+  CK("spmv", launch_fwd(op, p, pick(op, stream)));
   return SPARSL_OK;
 }
 
@@ -1106,7 +1124,7 @@ int sparsl_op_spmv_spikes_device(sparsl_op* op, const uint32_t* d_spikes, float*
   RowLaunch p = fwd_launch(op);
   set_bits_mode(p, d_spikes, op->words());
   p.y = d_y;
-  CK("spmv_spikes", launch_rows(p, pick(op, stream)));
+  CK("spmv_spikes", launch_fwd(op, p, pick(op, stream)));
   return SPARSL_OK;
 }
 
@@ -1353,7 +1371,7 @@ static int net_enqueue(sparsl_net* net, float decay, float v_reset, float dtheta
       lif_resident_launch(op, p, decay, v_reset, dtheta);
       p.out_bits = dst + (net->row_offset + net->block_off[b]) / 32;
       p.err = net->err.d;
-      CK("net_steps", launch_rows(p, net->stream));
+      CK("net_steps", launch_fwd(op, p, net->stream));
     }
     if (tm) CK("net_steps", cudaEventRecord(net->ev_b[t], net->stream));
     if (net->nranks > 1) {

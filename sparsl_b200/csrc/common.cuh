@@ -89,4 +89,35 @@ __device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// Decoupled look-back over integer tile counts (exact, so the result is the
+// same whichever predecessors are summed).  Run by one thread per tile.
+__device__ inline uint32_t lookback_count(unsigned long long* flags, uint32_t tile, uint32_t agg,
+                                   uint32_t* err) {
+  if (tile == 0) {
+    st_release_u64(flags, (2ull << 32) | agg);
+    return 0;
+  }
+  st_release_u64(flags + tile, (1ull << 32) | agg);
+  uint32_t excl = 0;
+  int64_t j = (int64_t)tile - 1;
+  uint32_t spins = 0;
+  while (j >= 0) {
+    unsigned long long f = ld_acquire_u64(flags + j);
+    uint32_t st = (uint32_t)(f >> 32);
+    if (st == 0) {
+      if (++spins > kSpinLimit) {
+        set_err(err, DEVERR_LOOKBACK_TIMEOUT);
+        break;
+      }
+      __nanosleep(64);
+      continue;
+    }
+    excl += (uint32_t)f;
+    if (st == 2) break;
+    --j;
+  }
+  st_release_u64(flags + tile, (2ull << 32) | (excl + agg));
+  return excl;
+}
+
 }  // namespace sparsl

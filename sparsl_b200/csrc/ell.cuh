@@ -1,0 +1,31 @@
+// TMA-pipelined row-fold for operators with a uniform row length (ell.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "rows.cuh"
+
+namespace sparsl {
+
+constexpr int kEllWarps = 4;
+constexpr int kEllLines = kEllWarps * 32;  // rows per block (one compaction tile)
+
+__host__ __device__ inline uint32_t ell_tiles(uint32_t nlines) { return (nlines + kEllLines - 1) / kEllLines; }
+
+// Two encoded CUtensorMaps (column and weight matrices viewed as [nrows x L]).
+struct EllMaps {
+  alignas(64) unsigned char idx[128];
+  alignas(64) unsigned char w[128];
+  uint32_t L = 0;
+  bool ok = false;
+};
+
+// Builds the tensor maps; false when the shape or alignment does not allow
+// 2-D TMA boxes (the caller keeps the generic row-fold path).
+bool ell_encode(EllMaps& m, const uint32_t* col, const void* w, int wkind, uint64_t nrows, uint32_t L);
+
+// Same contract as launch_rows for a forward (CSR) launch; p.ptr is unused.
+cudaError_t launch_ell(const EllMaps& m, const RowLaunch& p, cudaStream_t stream);
+
+}  // namespace sparsl

@@ -27,37 +27,6 @@ struct WarpStage {
   uint32_t len[32];
 };
 
-// Decoupled look-back over integer tile counts (exact, so the result is the
-// same whichever predecessors are summed).  Run by one thread per tile.
-__device__ uint32_t lookback_count(unsigned long long* flags, uint32_t tile, uint32_t agg,
-                                   uint32_t* err) {
-  if (tile == 0) {
-    st_release_u64(flags, (2ull << 32) | agg);
-    return 0;
-  }
-  st_release_u64(flags + tile, (1ull << 32) | agg);
-  uint32_t excl = 0;
-  int64_t j = (int64_t)tile - 1;
-  uint32_t spins = 0;
-  while (j >= 0) {
-    unsigned long long f = ld_acquire_u64(flags + j);
-    uint32_t st = (uint32_t)(f >> 32);
-    if (st == 0) {
-      if (++spins > kSpinLimit) {
-        set_err(err, DEVERR_LOOKBACK_TIMEOUT);
-        break;
-      }
-      __nanosleep(64);
-      continue;
-    }
-    excl += (uint32_t)f;
-    if (st == 2) break;
-    --j;
-  }
-  st_release_u64(flags + tile, (2ull << 32) | (excl + agg));
-  return excl;
-}
-
 template <int WK, int XM, bool CSC, int EPI, bool COMPACT>
 __global__ void __launch_bounds__(kRowWarps * 32) row_fold_kernel(const RowLaunch p) {
   extern __shared__ __align__(16) unsigned char smem[];

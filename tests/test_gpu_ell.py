@@ -1,0 +1,104 @@
+"""The TMA-pipelined row fold (operators whose rows all have the same length)
+against the oracle and against the generic row-fold kernel, bit for bit."""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import assert_bits_equal
+
+import sparsl_b200 as S
+
+pytestmark = pytest.mark.gpu
+
+
+def _uniform(O, nrows, ncols, L, seed):
+    r = np.random.default_rng(seed)
+    col = np.sort(r.integers(0, ncols, size=(nrows, L), dtype=np.uint32), axis=1).reshape(-1)
+    rp = (np.arange(nrows + 1, dtype=np.uint64) * L).astype(np.uint32)
+    w = r.uniform(-1, 1, nrows * L).astype(np.float32)
+    return O.Csr(rp, col, ncols), w
+
+
+def _prepare(dev, csr, w, precision, generic):
+    if generic:
+        os.environ["SPARSL_NO_ELL"] = "1"
+    try:
+        return dev.prepare_with(S.Csr(csr.row_ptr, csr.col, csr.ncols), csr.ncols, w, precision)
+    finally:
+        os.environ.pop("SPARSL_NO_ELL", None)
+
+
+@pytest.mark.parametrize("nrows,ncols,L", [(1, 64, 8), (31, 100, 32), (33, 1000, 40), (129, 4096, 64),
+                                           (1000, 1000, 96), (5000, 70000, 512), (300, 5000, 1024)])
+@pytest.mark.parametrize("precision", [S.WeightPrecision.F32, S.WeightPrecision.F16, S.WeightPrecision.Bf16])
+def test_uniform_rows_spmv_and_fused_bit_exact(O, cuda_device, nrows, ncols, L, precision):
+    csr, w = _uniform(O, nrows, ncols, L, nrows * 7 + L)
+    wq = O.quantise(int(precision), w)
+    op = _prepare(cuda_device, csr, w, precision, generic=False)
+    ref = _prepare(cuda_device, csr, w, precision, generic=True)
+    r = np.random.default_rng(L)
+    x = r.uniform(-1, 1, ncols).astype(np.float32)
+    y0 = r.uniform(-1, 1, nrows).astype(np.float32)
+    got, gen = y0.copy(), y0.copy()
+    op.spmv(x, got)
+    ref.spmv(x, gen)
+    want = O.spmv(csr, wq, x, y0.copy())
+    assert_bits_equal(got, want, "spmv vs oracle")
+    assert_bits_equal(gen, want, "generic path vs oracle")
+    s = (r.random(ncols) < 0.3).astype(np.uint8)
+    pk = O.pack_spikes(s)
+    got = y0.copy()
+    op.spmv_spikes(pk, got)
+    assert_bits_equal(got, O.spmv_spikes(csr, wq, pk, y0.copy()), "spmv_spikes")
+    v0 = r.uniform(-1, 1, nrows).astype(np.float32)
+    t0 = np.abs(r.uniform(-1, 1, nrows)).astype(np.float32)
+    v, t, sp = v0.copy(), t0.copy(), np.zeros(nrows, np.bool_)
+    op.fused_spmv_spikes_lif(pk, v, t, sp, S.LifParams.new(0.9, 0.0, 0.1))
+    vw, tw, sw = v0.copy(), t0.copy(), np.zeros(nrows, np.uint8)
+    O.fused_spikes_lif(csr, wq, pk, vw, tw, sw, 0.9, 0.0, 0.1)
+    assert_bits_equal(v, vw, "fused v")
+    assert_bits_equal(t, tw, "fused theta")
+    assert np.array_equal(sp.astype(np.uint8), sw)
+
+
+@pytest.mark.parametrize("n,L", [(4096, 64), (32768, 512), (262144, 512)])
+def test_uniform_recurrent_network_bit_exact(O, cuda_device, n, L):
+    """The fixed fan-in network tick (trace, state, device-compacted indices)."""
+    r = np.random.default_rng(n)
+    col = np.sort(r.integers(0, n, size=(n, L), dtype=np.uint32), axis=1).reshape(-1)
+    rp = (np.arange(n + 1, dtype=np.uint64) * L).astype(np.uint32)
+    w = (r.standard_normal(n * L) * 0.05).astype(np.float32)
+    csr = O.Csr(rp, col, n)
+    v0 = r.random(n).astype(np.float32)
+    t0 = np.ones(n, np.float32)
+    pk0 = O.pack_spikes((r.random(n) < 0.02).astype(np.uint8))
+    op = cuda_device.prepare(S.Csr(rp, col, n), n, w)
+    op.write_x_spikes(pk0)
+    op.write_lif_state(v0, t0)
+    steps = 6
+    op.fused_spmv_spikes_lif_recurrent_steps(S.LifParams.new(0.95, 0.0, 0.0), steps)
+    vw, tw, sw, xw = v0.copy(), t0.copy(), np.zeros(n, np.uint8), pk0.copy()
+    trace = O.recurrent_steps(csr, w, xw, vw, tw, sw, 0.95, 0.0, 0.0, steps, par=True)
+    assert np.array_equal(op.spike_trace(), trace)
+    v, t, sp = np.zeros(n, np.float32), np.zeros(n, np.float32), np.zeros(n, np.bool_)
+    op.sync_lif_state(v, t, sp)
+    assert_bits_equal(v, vw)
+    assert np.array_equal(op.sync_x_spikes(), xw)
+    assert np.array_equal(op.spike_indices(), np.flatnonzero(sw).astype(np.uint32))
+
+
+def test_uniform_rows_with_non_finite_weights(O, cuda_device):
+    """inf * cleared spike is NaN on the TMA path too (spikes_backend.rs:48-89)."""
+    csr, w = _uniform(O, 64, 256, 32, 5)
+    w[3] = np.inf
+    w[40] = np.nan
+    s = np.ones(256, np.uint8)
+    s[csr.col[3]] = 0
+    pk = O.pack_spikes(s)
+    op = cuda_device.prepare(S.Csr(csr.row_ptr, csr.col, 256), 256, w)
+    got = np.zeros(64, np.float32)
+    op.spmv_spikes(pk, got)
+    want = O.spmv_spikes(csr, w, pk, np.zeros(64, np.float32))
+    assert_bits_equal(got, want)
+    assert np.isnan(got[0]) and np.isnan(got[1])
