@@ -404,8 +404,8 @@ def bench_lif_net(args, dist):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded ChaCha12 per row, generated on the GPU)",
-        "config": {"workload": "lif_net: 4,194,304 neurons x fan-in 1024 (4.29e9 synapses), f32 weights "
-                               "N(0,0.03^2), decay 0.95, theta 1.0, reset 0, Bernoulli(0.01) initial spikes",
+        "config": {"workload": f"lif_net: {n_total:,} neurons x fan-in {fan_in} ({n_total * fan_in:.3g} synapses), "
+                               "f32 weights N(0,0.03^2), decay 0.95, theta 1.0, reset 0, Bernoulli(0.01) initial spikes",
                    "parallelism": f"row-block shards x{dist.world}, NCCL all-gather of packed spikes per tick",
                    "blocks_per_gpu": len(ops), "l2": "inputs per GPU >> 126 MB L2 (no flush needed)",
                    "setup_s": round(setup_s, 1)},
@@ -634,7 +634,7 @@ def bench_lif(args, dev, want_cpu):
     check(L.sparsl_op_recurrent_steps(op.handle, 0.95, 0.0, 0.0, args.warmup), "warm")
     op.write_x_spikes(pk0)
     op.write_lif_state(v0, th0)
-    ticks = 1000
+    ticks = args.lif_ticks
     st = L.sparsl_op_stream(op.handle)
     ms = events_ms(st, torch.cuda.current_device(),
                    lambda: check(L.sparsl_op_recurrent_steps_async(op.handle, 0.95, 0.0, 0.0, ticks), "ticks"))
@@ -731,9 +731,21 @@ def main():
     ap.add_argument("--workload", default="lif_net", choices=["lif_net", "spmv", "scan", "lif"])
     ap.add_argument("--no-extras", action="store_true", help="N=1: skip the SpMV / scan / LIF-1GPU figures")
     ap.add_argument("--kernel-iters", type=int, default=20)
+    # Smaller instances of the same workloads (profiling captures, quick runs).
+    ap.add_argument("--scan-n", type=int, default=None, help="scan length (default 2^26)")
+    ap.add_argument("--lif-ticks", type=int, default=1000, help="timed ticks of the 1-GPU LIF network")
+    ap.add_argument("--net-n", type=int, default=None, help="neurons of the LIF network (default 4,194,304)")
+    ap.add_argument("--net-fanin", type=int, default=None, help="fan-in of the LIF network (default 1024)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
+    global SCAN_N, NET_N, NET_FANIN
+    if args.scan_n:
+        SCAN_N = args.scan_n
+    if args.net_n:
+        NET_N = args.net_n
+    if args.net_fanin:
+        NET_FANIN = args.net_fanin
     if args.steps is None:
         args.steps = 10 if args.impl == "reference" else 200
     args.warmup = max(args.warmup, 1)

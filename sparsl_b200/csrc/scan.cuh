@@ -9,8 +9,9 @@ namespace sparsl {
 constexpr int kScanThreads = 256;  // threads per tile
 constexpr int kScanK = 16;         // elements per thread (one sub-chunk)
 constexpr int kScanTile = kScanThreads * kScanK;
-constexpr int kScanWarmSub = 8;    // warm-up length in sub-chunks
-constexpr int kScanWarm = kScanWarmSub * kScanK;
+constexpr int kScanWarmSub = 8;    // warm-up of an in-tile guess, in sub-chunks
+constexpr int kScanHaloSub = 16;   // warm-up of a tile's first threads, reaching into the previous tile
+constexpr int kScanHalo = kScanHaloSub * kScanK;
 
 // Per-tile look-back record.  Written by the tile, read by its successors.
 struct ScanTileRecord {
