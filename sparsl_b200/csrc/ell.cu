@@ -170,20 +170,29 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1) ell_fold_kernel(const __gri
         }
         const uint32_t cv[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
         const uint32_t lim = min(8u, cnt - g * 8);
+        // The eight gathers and products are independent: issue them all
+        // before the dependent add chain.  Entries past the row end were
+        // zero-filled by the TMA box (column 0, weight 0), so their gathers
+        // stay in bounds; only their adds are skipped.
+        float prod[8];
 #pragma unroll
         for (uint32_t k = 0; k < 8; ++k) {
-          if (k < lim) {
-            const uint32_t col = cv[k];
-            float xv;
-            if constexpr (XM == X_DENSE) {
-              xv = __ldg(p.x + col);
-            } else if constexpr (XM == X_BITS_SMEM) {
-              xv = (float)((s_bits[col >> 5] >> (col & 31)) & 1u);
-            } else {
-              xv = (float)((__ldg(p.xbits + (col >> 5)) >> (col & 31)) & 1u);
-            }
-            sum = fadd(sum, fmul(wv[k], xv));
+          const uint32_t col = cv[k];
+          float xv;
+          if constexpr (XM == X_DENSE) {
+            xv = __ldg(p.x + col);
+          } else if constexpr (XM == X_BITS_SMEM) {
+            xv = (float)((s_bits[col >> 5] >> (col & 31)) & 1u);
+          } else {
+            xv = (float)((__ldg(p.xbits + (col >> 5)) >> (col & 31)) & 1u);
           }
+          prod[k] = fmul(wv[k], xv);
+        }
+        if (lim == 8) {
+#pragma unroll
+          for (uint32_t k = 0; k < 8; ++k) sum = fadd(sum, prod[k]);
+        } else {
+          for (uint32_t k = 0; k < lim; ++k) sum = fadd(sum, prod[k]);
         }
       }
       __syncwarp();

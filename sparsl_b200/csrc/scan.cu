@@ -73,6 +73,14 @@ __device__ __forceinline__ bool same_bits(Aff x, Aff y) {
   return __float_as_uint(x.a) == __float_as_uint(y.a) && __float_as_uint(x.b) == __float_as_uint(y.b);
 }
 
+__device__ __forceinline__ void stamp(const ScanScratch& s, uint32_t tile, int k) {
+  if (s.timeline && threadIdx.x == 0) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    s.timeline[(uint64_t)tile * 16 + k] = t;
+  }
+}
+
 __global__ void __launch_bounds__(kScanThreads) scan_main(const float2* __restrict__ in,
                                                          float2* __restrict__ out, uint64_t n,
                                                          ScanScratch s, uint32_t* err) {
@@ -87,7 +95,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_main(const float2* __restri
   __shared__ float s_AG[4];       // tile aggregate full, head
   __shared__ uint32_t s_TG[1];    // tile transfer table
   __shared__ float s_Atin;
-  __shared__ uint32_t s_tile, s_last;
+  __shared__ uint32_t s_tile, s_last, s_incl;
 
   const int t = threadIdx.x;
   const int lane = t & 31;
@@ -98,15 +106,30 @@ __global__ void __launch_bounds__(kScanThreads) scan_main(const float2* __restri
   __syncthreads();
   const uint32_t tile = s_tile;
   const uint64_t tile_start = (uint64_t)tile * kScanTile;
+  stamp(s, tile, 0);
 
   // ---- 1. stage halo + tile into padded shared memory (identity past n) ----
-  for (int li = t; li < kScanHalo + kScanTile; li += kScanThreads) {
-    const int64_t g = (int64_t)tile_start - kScanHalo + li;
-    float2 v = make_float2(1.0f, 0.0f);
-    if (g >= 0 && (uint64_t)g < n) v = __ldg(in + g);
-    sm[(li / kScanK) * kRowStride + (li % kScanK)] = v;
+  {
+    // All loads first, then all shared stores, so every thread keeps its
+    // whole share of the tile in flight at once.
+    constexpr int kPer = (kScanHalo + kScanTile) / kScanThreads;
+    static_assert((kScanHalo + kScanTile) % kScanThreads == 0, "tile staging");
+    float2 v[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int li = t + i * kScanThreads;
+      const int64_t g = (int64_t)tile_start - kScanHalo + li;
+      v[i] = make_float2(1.0f, 0.0f);
+      if (g >= 0 && (uint64_t)g < n) v[i] = __ldg(in + g);
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int li = t + i * kScanThreads;
+      sm[(li / kScanK) * kRowStride + (li % kScanK)] = v[i];
+    }
   }
   __syncthreads();
+  stamp(s, tile, 1);
 
   const float2* row = sm + (t + kScanHaloSub) * kRowStride;
 
@@ -178,6 +201,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_main(const float2* __restri
   }
   __syncthreads();
 
+  stamp(s, tile, 2);
   // ---- 4. publish the aggregate, 5. look back across tiles ----
   ScanTileRecord* rec = s.rec;
   if (t == 0) {
@@ -201,6 +225,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_main(const float2* __restri
     Aff Pf{1.f, 0.f}, Ph{1.f, 0.f};
     float atin = 0.f;
     bool atin_ok = false;
+    uint32_t windows = 0, lastL = 0;
     while (!done) {
       const int64_t j = base - lane;
       uint32_t stt = 0;
@@ -228,6 +253,8 @@ __global__ void __launch_bounds__(kScanThreads) scan_main(const float2* __restri
         __nanosleep(32);
         continue;
       }
+      ++windows;
+      lastL = (uint32_t)L;
       // Every lane <= L is published; fetch what the fold needs.
       float ga = 1.f, gb = 0.f, ha = 1.f, hb = 0.f, ia = 1.f, ib = 0.f, iha = 1.f, ihb = 0.f, av = 0.f;
       uint32_t tb = kTabId;
@@ -246,48 +273,75 @@ __global__ void __launch_bounds__(kScanThreads) scan_main(const float2* __restri
           av = r->av;
         }
       }
-      for (int k = 0; k <= min(L, 31); ++k) {
-        const Aff g{__shfl_sync(0xffffffffu, ga, k), __shfl_sync(0xffffffffu, gb, k)};
-        const Aff h{__shfl_sync(0xffffffffu, ha, k), __shfl_sync(0xffffffffu, hb, k)};
-        const uint32_t tk = __shfl_sync(0xffffffffu, tb, k);
-        if (k == L) {
-          const Aff I{__shfl_sync(0xffffffffu, ia, k), __shfl_sync(0xffffffffu, ib, k)};
-          const Aff IH{__shfl_sync(0xffffffffu, iha, k), __shfl_sync(0xffffffffu, ihb, k)};
-          const float A = __shfl_sync(0xffffffffu, av, k);
-          if (!have) {  // the nearest predecessor is inclusive
-            Pf = I;
-            Ph = IH;
-            atin = A;
-            atin_ok = true;
-          } else {
-            Pf = comb(I, Sf);
-            Ph = comb(I, Sh);
-            if (in_domain(A)) {
-              const uint32_t e = tab_at(St, __float_as_uint(A));
-              if (!(e & 8u)) {
-                atin = __uint_as_float(e);
-                atin_ok = true;
-              }
-            }
-          }
-          done = true;
-        } else {
-          if (!have) {
-            Sf = g;
-            Sh = h;
-            St = tk;
-            have = true;
-          } else {
-            Sf = comb(g, Sf);
-            Sh = comb(g, Sh);
-            St = tab_comb(tk, St);
+      // Compose this window's aggregates (lanes 0..L-1, farther lanes first)
+      // with a shuffle tree.  Lanes 1..L-1 are reduced together; lane 0 --
+      // the nearest tile -- is applied last, with its head aggregate instead of
+      // its full one on the head chain of the first window.
+      {
+        const bool mid = lane >= 1 && lane < L;
+        Aff rf = mid ? Aff{ga, gb} : Aff{1.f, 0.f};
+        uint32_t rt = mid ? tb : kTabId;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+          const Aff up{__shfl_down_sync(0xffffffffu, rf.a, d), __shfl_down_sync(0xffffffffu, rf.b, d)};
+          const uint32_t ut = __shfl_down_sync(0xffffffffu, rt, d);
+          if (lane + d < 32) {
+            rf = comb(up, rf);
+            rt = tab_comb(ut, rt);
           }
         }
+        const Aff W1{__shfl_sync(0xffffffffu, rf.a, 0), __shfl_sync(0xffffffffu, rf.b, 0)};
+        const uint32_t W1t = __shfl_sync(0xffffffffu, rt, 0);
+        if (L > 0) {
+          const Aff g0{__shfl_sync(0xffffffffu, ga, 0), __shfl_sync(0xffffffffu, gb, 0)};
+          const Aff h0{__shfl_sync(0xffffffffu, ha, 0), __shfl_sync(0xffffffffu, hb, 0)};
+          const uint32_t t0 = __shfl_sync(0xffffffffu, tb, 0);
+          const Aff wf = comb(W1, g0);
+          const uint32_t wt = tab_comb(W1t, t0);
+          if (!have) {
+            Sf = wf;
+            Sh = comb(W1, h0);
+            St = wt;
+            have = true;
+          } else {
+            Sf = comb(wf, Sf);
+            Sh = comb(wf, Sh);
+            St = tab_comb(wt, St);
+          }
+        }
+      }
+      if (L < 32) {
+        const Aff I{__shfl_sync(0xffffffffu, ia, L), __shfl_sync(0xffffffffu, ib, L)};
+        const Aff IH{__shfl_sync(0xffffffffu, iha, L), __shfl_sync(0xffffffffu, ihb, L)};
+        const float A = __shfl_sync(0xffffffffu, av, L);
+        if (!have) {  // the nearest predecessor is inclusive
+          Pf = I;
+          Ph = IH;
+          atin = A;
+          atin_ok = true;
+        } else {
+          Pf = comb(I, Sf);
+          Ph = comb(I, Sh);
+          if (in_domain(A)) {
+            const uint32_t e = tab_at(St, __float_as_uint(A));
+            if (!(e & 8u)) {
+              atin = __uint_as_float(e);
+              atin_ok = true;
+            }
+          }
+        }
+        done = true;
       }
       base -= 32;
     }
     // The exact multiplier entering this tile: if the tables could not carry
     // it, take it straight from the nearest predecessor once it is inclusive.
+    if (s.timeline && lane == 0) {
+      s.timeline[(uint64_t)tile * 16 + 11] = windows;
+      s.timeline[(uint64_t)tile * 16 + 12] = lastL;
+      s.timeline[(uint64_t)tile * 16 + 13] = atin_ok ? 1 : 0;
+      s.timeline[(uint64_t)tile * 16 + 14] = spins;
+    }
     if (!atin_ok) {
       uint32_t sp = 0;
       if (lane == 0) {
@@ -313,10 +367,31 @@ __global__ void __launch_bounds__(kScanThreads) scan_main(const float2* __restri
       s_P[2] = Ph.a;
       s_P[3] = Ph.b;
       s_Atin = atin;
+      // When the tables carry the multiplier across this tile, its inclusive
+      // record is known now: publish it before the rest of the block catches
+      // up, so successors' look-backs stop here sooner.
+      s_incl = 0;
+      if (in_domain(atin)) {
+        const uint32_t e = tab_at(s_TG[0], __float_as_uint(atin));
+        if (!(e & 8u)) {
+          ScanTileRecord* r = rec + tile;
+          const Aff f = comb(Pf, Aff{s_AG[0], s_AG[1]});
+          const Aff h = comb(Pf, Aff{s_AG[2], s_AG[3]});
+          r->inc[0] = f.a;
+          r->inc[1] = f.b;
+          r->inc[2] = h.a;
+          r->inc[3] = h.b;
+          r->av = __uint_as_float(e);
+          __threadfence();
+          st_release_u32(&r->status, 2u);
+          s_incl = 1;
+        }
+      }
     }
   }
   __syncthreads();
 
+  stamp(s, tile, 3);
   // ---- 6. exact multiplier at every sub-chunk boundary ----
   // Fast path: the multiplier entering the tile is in the table domain and
   // the tile's table keeps it there -- every prefix table then does too, and
@@ -362,7 +437,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_main(const float2* __restri
   __syncthreads();
 
   // ---- 7. publish the inclusive record (guesses for B, exact A) ----
-  if (t == 0) {
+  if (t == 0 && !(tile > 0 && s_incl)) {
     ScanTileRecord* r = rec + tile;
     Aff f{s_AG[0], s_AG[1]}, h{s_AG[2], s_AG[3]};
     if (tile > 0) {
@@ -379,6 +454,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_main(const float2* __restri
     st_release_u32(&r->status, 2u);
   }
 
+  stamp(s, tile, 4);
   // ---- 8. warm-up: replay the elements before this sub-chunk ----
   // In-tile threads replay the 128 elements before their sub-chunk from the
   // block-scan guess; the first threads of a tile replay the 256-element halo
@@ -430,6 +506,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_main(const float2* __restri
   s_fb[t] = st.b;
   __syncthreads();
 
+  stamp(s, tile, 5);
   // ---- 9b. in-tile relaxation ----
   // A thread whose assumed entry state differs from its predecessor's final
   // state replays its sub-chunk from that final state (inputs re-read from
@@ -439,7 +516,22 @@ __global__ void __launch_bounds__(kScanThreads) scan_main(const float2* __restri
   Aff used = assumed;
   {
     bool stale = t > 0 && start_t < n && !same_bits(used, Aff{s_fa[t - 1], s_fb[t - 1]});
+    if (s.timeline) {
+      const int cnt = __syncthreads_count(stale);
+      // first stale thread, for the profiling timeline
+      __shared__ int s_first;
+      if (t == 0) s_first = 1 << 30;
+      __syncthreads();
+      if (stale) atomicMin(&s_first, t);
+      __syncthreads();
+      if (t == 0) {
+        s.timeline[(uint64_t)tile * 16 + 8] = cnt;
+        s.timeline[(uint64_t)tile * 16 + 10] = s_first;
+      }
+    }
+    int rounds_done = 0;
     for (int round = 0; round < kScanThreads && __syncthreads_or(stale); ++round) {
+      ++rounds_done;
       Aff fin{0.f, 0.f};
       if (stale) {
         used = Aff{s_fa[t - 1], s_fb[t - 1]};
@@ -461,8 +553,10 @@ __global__ void __launch_bounds__(kScanThreads) scan_main(const float2* __restri
       __syncthreads();
       stale = t > 0 && start_t < n && !same_bits(used, Aff{s_fa[t - 1], s_fb[t - 1]});
     }
+    if (s.timeline && t == 0) s.timeline[(uint64_t)tile * 16 + 9] = rounds_done;
   }
 
+  stamp(s, tile, 6);
   // ---- 10. verify adjacent sub-chunks inside the tile ----
   bool mis = false;  // relaxation leaves none unless its round cap was hit
   if (t > 0 && start_t < n) mis = !same_bits(used, Aff{s_fa[t - 1], s_fb[t - 1]});
@@ -510,6 +604,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_main(const float2* __restri
     s_last = (atomicAdd(s.ticket + 1, 1u) == ntiles - 1) ? 1u : 0u;
   }
   __syncthreads();
+  stamp(s, tile, 7);
   // ---- 13. the last tile to finish clears the look-back state ----
   if (s_last) {
     for (uint64_t i = t; i < ntiles; i += kScanThreads) rec[i].status = 0u;

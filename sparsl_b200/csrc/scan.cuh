@@ -35,6 +35,7 @@ struct ScanScratch {
   uint32_t* xmis;           // ntiles: tile-boundary mismatch
   uint32_t* tile_bits;      // ceil(ntiles / 32) words: any mismatch in tile
   uint32_t* repair_stats;   // [0] repaired elements, [1] repair segments
+  unsigned long long* timeline = nullptr;  // optional: 8 globaltimer stamps per tile
 };
 
 size_t scan_scratch_bytes(uint64_t n);
