@@ -201,6 +201,22 @@ int sparsl_dev_wait(sparsl_dev *dev);
 /* Elements the last device scan had to replay serially (repair statistics). */
 int sparsl_dev_scan_stats(sparsl_dev *dev, uint64_t *repaired, uint64_t *segments);
 
+/* ---- allocation-free scan (no counterpart in the reference) -------------- */
+/* The exact affine-map scan for callers that cannot allocate device memory:
+ * a host whose allocator already owns all of HBM, or one that only lends this
+ * library buffers it holds.  Scratch lives in a static device array of about
+ * 256 KiB that every GPU loading the library keeps until exit, so n is capped
+ * at 4,194,304 maps (larger n returns SPARSL_ERR_LENGTH).  d_in / d_out are
+ * caller-owned device buffers of n (a, b) pairs on device `ordinal`; the work
+ * runs on `stream` (cudaStream_t, NULL = legacy default stream) and the call
+ * waits for it with a bounded poll (timeout_ms, 0 = 60 s).  It calls no
+ * cudaMalloc, cudaFree or allocating routine.  The first call on a device
+ * looks up the array's device address; make that call before any stream
+ * capture.  All calls share the one array: calls that overlap on a GPU race,
+ * so serialize them.  Results are bit-identical to sparsl_dev_assoc_scan. */
+int sparsl_dev_assoc_scan_noalloc(int ordinal, const float *d_in, uint64_t n, float *d_out,
+                                  void *stream, uint64_t timeout_ms);
+
 /* ---- pinned host memory (for end-to-end copies at DMA speed) ------------- */
 void *sparsl_host_alloc(uint64_t bytes);
 void sparsl_host_free(void *p);

@@ -94,6 +94,7 @@ SIGNATURES = {
     "sparsl_op_wait": (i32, [vp]),
     "sparsl_dev_wait": (i32, [vp]),
     "sparsl_dev_scan_stats": (i32, [vp, ctypes.POINTER(u64), ctypes.POINTER(u64)]),
+    "sparsl_dev_assoc_scan_noalloc": (i32, [i32, vp, u64, vp, vp, u64]),
     "sparsl_host_alloc": (vp, [u64]),
     "sparsl_host_free": (None, [vp]),
     "sparsl_device_alloc": (vp, [vp, u64]),

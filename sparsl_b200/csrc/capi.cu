@@ -223,6 +223,11 @@ const char* nccl_load() {
 
 }  // namespace
 
+namespace sparsl {
+// Lets other translation units report through sparsl_last_error.
+int record_error(int code, const char* message) { return fail(code, message, message); }
+}  // namespace sparsl
+
 // ==========================================================================
 // Device
 // ==========================================================================
