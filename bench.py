@@ -420,7 +420,9 @@ def bench_lif_net(args, dist):
                      "algorithmic_bytes_per_tick_per_gpu": algo, "kernel_ms_per_tick": kernel_ms_tick,
                      "peak_source": how},
         "cpu_baseline": cpu,
-        "check": {"spike_trace_sum": int(trace.sum()), "trace_identical_on_all_ranks": consistent},
+        "check": {"spike_trace_sum": int(trace.sum()), "trace_identical_on_all_ranks": consistent,
+                  "trace_sha1": __import__("hashlib").sha1(trace.tobytes()).hexdigest()[:16],
+                  "trace_head": trace[:8].tolist()},
     }
     for h in (hp, hv, ht):
         h.free()
