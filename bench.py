@@ -28,6 +28,7 @@ from __future__ import annotations
 import argparse
 import ctypes
 import datetime
+import faulthandler
 import json
 import os
 import statistics
@@ -725,6 +726,7 @@ def bench_reference(args, dist):
 
 
 def main():
+    faulthandler.enable()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)

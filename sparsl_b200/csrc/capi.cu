@@ -193,6 +193,7 @@ struct NcclApi {
   ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
   ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
   ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*CommFinalize)(ncclComm_t) = nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
   ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
@@ -203,22 +204,41 @@ NcclApi g_nccl;
 const char* nccl_load() {
   std::lock_guard<std::mutex> lk(g_nccl_mu);
   if (g_nccl.loaded) return nullptr;
-  void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+  // Reuse the NCCL the process already has (a framework that links it), so
+  // one communicator library serves every caller; otherwise load it.
+  void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+  if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
   if (!h) return "libnccl.so.2 could not be loaded";
   auto sym = [&](const char* n) { return dlsym(h, n); };
   g_nccl.GetUniqueId = reinterpret_cast<decltype(g_nccl.GetUniqueId)>(sym("ncclGetUniqueId"));
   g_nccl.CommInitRankConfig = reinterpret_cast<decltype(g_nccl.CommInitRankConfig)>(sym("ncclCommInitRankConfig"));
   g_nccl.CommGetAsyncError = reinterpret_cast<decltype(g_nccl.CommGetAsyncError)>(sym("ncclCommGetAsyncError"));
   g_nccl.AllGather = reinterpret_cast<decltype(g_nccl.AllGather)>(sym("ncclAllGather"));
+  g_nccl.CommFinalize = reinterpret_cast<decltype(g_nccl.CommFinalize)>(sym("ncclCommFinalize"));
   g_nccl.CommDestroy = reinterpret_cast<decltype(g_nccl.CommDestroy)>(sym("ncclCommDestroy"));
   g_nccl.CommAbort = reinterpret_cast<decltype(g_nccl.CommAbort)>(sym("ncclCommAbort"));
   g_nccl.GetErrorString = reinterpret_cast<decltype(g_nccl.GetErrorString)>(sym("ncclGetErrorString"));
   if (!g_nccl.GetUniqueId || !g_nccl.CommInitRankConfig || !g_nccl.CommGetAsyncError || !g_nccl.AllGather ||
-      !g_nccl.CommDestroy || !g_nccl.CommAbort || !g_nccl.GetErrorString)
+      !g_nccl.CommFinalize || !g_nccl.CommDestroy || !g_nccl.CommAbort || !g_nccl.GetErrorString)
     return "libnccl.so.2 lacks a required symbol";
   g_nccl.handle = h;
   g_nccl.loaded = true;
   return nullptr;
+}
+
+// The communicator is non-blocking (so a rank that never joins cannot hang
+// init), which means any NCCL call may return ncclInProgress with its work
+// still being set up on NCCL's own threads (the first collective connects the
+// peers).  Nothing else may be issued on the communicator or the stream until
+// that finishes: poll its state, bounded by the library timeout.
+ncclResult_t nccl_settle(ncclComm_t comm, ncclResult_t r) {
+  const auto t0 = std::chrono::steady_clock::now();
+  while (r == ncclInProgress) {
+    if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(g_timeout_ms.load())) return ncclInProgress;
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+    if (g_nccl.CommGetAsyncError(comm, &r) != ncclSuccess) return ncclSystemError;
+  }
+  return r;
 }
 
 }  // namespace
@@ -1303,24 +1323,14 @@ int sparsl_net_create(sparsl_dev* d, sparsl_op* const* blocks, uint32_t n_blocks
     ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
     cfg.blocking = 0;
     ncclResult_t r = g_nccl.CommInitRankConfig(&net->comm, nranks, id, rank, &cfg);
-    const auto t0 = std::chrono::steady_clock::now();
-    while (r == ncclInProgress || r == ncclSuccess) {
-      ncclResult_t st = ncclSuccess;
-      g_nccl.CommGetAsyncError(net->comm, &st);
-      if (st == ncclSuccess) {
-        r = ncclSuccess;
-        break;
-      }
-      if (st != ncclInProgress) {
-        r = st;
-        break;
-      }
-      if (std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(g_timeout_ms.load())) {
+    if (r == ncclSuccess || r == ncclInProgress) {
+      if (r == ncclSuccess) g_nccl.CommGetAsyncError(net->comm, &r);
+      r = nccl_settle(net->comm, r);
+      if (r == ncclInProgress) {
         g_nccl.CommAbort(net->comm);
         net->comm = nullptr;
         return bail(fail(SPARSL_ERR_EXECUTION, "NCCL init timed out", "ncclCommInitRank did not complete in time"));
       }
-      std::this_thread::sleep_for(std::chrono::milliseconds(1));
     }
     if (r != ncclSuccess) {
       if (net->comm) g_nccl.CommAbort(net->comm);
@@ -1339,10 +1349,12 @@ void sparsl_net_destroy(sparsl_net* net) {
   cudaSetDevice(net->dev->ordinal);
   if (net->stream) cudaStreamSynchronize(net->stream);
   if (net->comm) {
-    if (g_quarantine.load())
-      g_nccl.CommAbort(net->comm);
-    else
+    // Finalize flushes the communicator's outstanding work (polled, bounded);
+    // a quarantined process or a finalize that does not settle aborts instead.
+    if (!g_quarantine.load() && nccl_settle(net->comm, g_nccl.CommFinalize(net->comm)) == ncclSuccess)
       g_nccl.CommDestroy(net->comm);
+    else
+      g_nccl.CommAbort(net->comm);
   }
   for (cudaEvent_t e : net->ev_a) cudaEventDestroy(e);
   for (cudaEvent_t e : net->ev_b) cudaEventDestroy(e);
@@ -1399,7 +1411,9 @@ static int net_enqueue(sparsl_net* net, float decay, float v_reset, float dtheta
     }
     if (tm) CK("net_steps", cudaEventRecord(net->ev_b[t], net->stream));
     if (net->nranks > 1) {
-      ncclResult_t r = g_nccl.AllGather(dst + (uint64_t)net->rank * slice, dst, slice, ncclUint32, net->comm, net->stream);
+      ncclResult_t r = nccl_settle(
+          net->comm, g_nccl.AllGather(dst + (uint64_t)net->rank * slice, dst, slice, ncclUint32, net->comm, net->stream));
+      if (r == ncclInProgress) return fail(SPARSL_ERR_EXECUTION, "ncclAllGather", "ncclAllGather was not enqueued in time");
       if (r != ncclSuccess) return fail(SPARSL_ERR_EXECUTION, "ncclAllGather failed", g_nccl.GetErrorString(r));
     }
     CK("net_steps", launch_popcount(dst, net->words, net->trace.as<uint32_t>() + t, net->stream));
