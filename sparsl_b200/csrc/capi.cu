@@ -301,6 +301,7 @@ struct sparsl_op {
   DBuf col_ptr, csc_row, csc_eidx;
   // Uniform row length: TMA tensor maps over col / w as [nrows x L] matrices.
   EllMaps ell;
+  uint32_t ell_epoch = 0;  // tag of the last compacting TMA launch's flags
   // resident scratch (the write / step / sync API)
   DBuf rx, rxs[2], ry, rv, rth, rspk;
   int cur = 0;
@@ -362,8 +363,18 @@ RowLaunch fwd_launch(sparsl_op* op) {
 // Forward launches take the TMA-pipelined kernel when the operator's rows all
 // have the same length, the generic row-fold kernel otherwise.
 cudaError_t launch_fwd(sparsl_op* op, const RowLaunch& p, cudaStream_t s) {
-  if (op->ell.ok) return launch_ell(op->ell, p, s);
-  return launch_rows(p, s);
+  if (!op->ell.ok) return launch_rows(p, s);
+  if (!p.idx_list) return launch_ell(op->ell, p, s);
+  // Compacting launches tag their look-back flags with a fresh epoch; the
+  // flags are cleared only when the 30-bit tag wraps.
+  RowLaunch q = p;
+  if (++op->ell_epoch >= (1u << 30)) {
+    cudaError_t e = cudaMemsetAsync(op->tile_flags.p, 0, op->tile_flags.bytes, s);
+    if (e != cudaSuccess) return e;
+    op->ell_epoch = 1;
+  }
+  q.epoch = op->ell_epoch;
+  return launch_ell(op->ell, q, s);
 }
 
 void set_bits_mode(RowLaunch& p, const uint32_t* bits, uint64_t words) {

@@ -1,17 +1,29 @@
 // Row-fold engine for operators whose rows all hold the same number of
 // entries L (row_ptr[r] == r * L): fixed fan-in networks and fixed-degree
 // matrices.  Their column and weight arrays are dense [nrows x L] matrices, so
-// a warp's 32 rows x 32 entries are one 2-D TMA box.
+// a warp's 32 rows x 16 entries are one 2-D TMA box.
 //
-// Per warp: a 4-stage pipeline of (column tile, weight tile) pairs loaded by
-// cp.async.bulk.tensor into 128-byte-swizzled shared memory and signalled by
-// one mbarrier per stage; lane 0 keeps three chunks in flight while all 32
-// lanes fold the current one.  The swizzle makes the transposed reads (lane r
-// reads row r, 16 bytes at a time) bank-conflict free.  The arithmetic is the
-// row-fold engine's: one lane per row, strict left fold, separate
-// round-to-nearest multiply and add (src/backend/mod.rs:2259-2267).
+// Persistent and streaming: one CTA per SM, kEllWarps warps, and every warp
+// walks its own sequence of 32-row tiles.  Per warp a kStages-deep ring of
+// (column box, weight box) pairs is filled by cp.async.bulk.tensor into
+// swizzled shared memory and signalled by one mbarrier per stage; lane 0
+// refills a stage as soon as the warp has folded it, running ahead across
+// tile boundaries, so the pipeline never drains between tiles.  The swizzle
+// makes the transposed reads (lane r reads row r, 16 bytes at a time) bank
+// conflict free.  The arithmetic is the row-fold engine's: one lane per row,
+// strict left fold from 0.0, separate round-to-nearest multiply and add
+// (src/backend/mod.rs:2259-2267).
 //
-// No multicast, no clusters: every load reads this GPU's own memory.
+// Spike operands live in shared memory: the whole bitmask when it fits
+// (X_BITS_SMEM), otherwise (X_BITS_GLOBAL) a summary with one bit per group of
+// G columns ("some column of this group spiked") built once per CTA; a gather
+// reads the global bitmask only when its group's summary bit is set.  The
+// bitmask itself is exact, so the summary only decides which zero words need
+// not be fetched.
+//
+// Streaming loads carry an L2 evict-first policy so the gathered operand (x,
+// bitmask) stays resident in L2 while the matrix streams past it.  No
+// multicast, no clusters: every load reads this GPU's own memory.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -21,7 +33,10 @@ namespace sparsl {
 namespace {
 
 constexpr int kStages = 4;
-constexpr int kTileBytes = 32 * 32 * 4;  // one 32 x 32 box of 4-byte elements
+constexpr int kChunk = 16;                     // entries per row per stage
+constexpr int kIdxBox = 32 * kChunk * 4;       // 2 KiB column box
+constexpr uint32_t kSumMaxWords = 16384;       // 64 KiB summary
+constexpr uint32_t kFifo = 8;                  // > kStages: tiles a warp can run ahead
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -53,59 +68,136 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   return false;
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                            uint64_t pol) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-          "r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
       : "memory");
 }
 
 template <int WK>
 struct WBox {
-  // bytes of one weight box: 32 rows x 32 entries
-  static constexpr int kBytes = WK == W_F32 ? 4096 : 2048;
+  // bytes of one weight box: 32 rows x kChunk entries
+  static constexpr int kBytes = WK == W_F32 ? 32 * kChunk * 4 : 32 * kChunk * 2;
+  static constexpr int kStage = kIdxBox + kBytes;
 };
 
+// Summary bits of one bitmask word for groups of 2^gs columns, gs in [3, 5]:
+// bit j is set when bits [j*G, (j+1)*G) of the word are not all zero.
+__device__ __forceinline__ uint32_t word_groups(uint32_t w, uint32_t gs) {
+  if (gs == 3) {
+    const uint32_t t = (((w & 0x7f7f7f7fu) + 0x7f7f7f7fu) | w) & 0x80808080u;  // high bit per nonzero byte
+    return ((t >> 7) & 1u) | ((t >> 14) & 2u) | ((t >> 21) & 4u) | ((t >> 28) & 8u);
+  }
+  if (gs == 4) return ((w & 0xffffu) ? 1u : 0u) | ((w >> 16) ? 2u : 0u);
+  return w ? 1u : 0u;
+}
+
+// Builds the shared-memory summary: summary word s covers bitmask words
+// [s*G, s*G + G) (G = 2^gs), i.e. 32 groups of G columns.
+__device__ void build_summary(uint32_t* s_sum, const uint32_t* __restrict__ bits, uint32_t words, uint32_t gs,
+                              uint32_t sum_words) {
+  const uint32_t G = 1u << gs;
+  for (uint32_t s = threadIdx.x; s < sum_words; s += blockDim.x) {
+    const uint32_t w0 = s << gs;
+    uint32_t out = 0;
+    if (gs <= 5) {
+      const uint32_t per = 32u >> gs;  // summary bits per bitmask word
+      for (uint32_t k = 0; k < G; k += 8) {
+        uint32_t v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = (w0 + k + u < words) ? __ldg(bits + w0 + k + u) : 0u;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) out |= word_groups(v[u], gs) << ((k + u) * per);
+      }
+    } else {
+      const uint32_t wpb = G >> 5;  // bitmask words per summary bit
+      for (uint32_t b = 0; b < 32; ++b) {
+        uint32_t acc = 0;
+        for (uint32_t k = 0; k < wpb; ++k) {
+          const uint32_t wi = w0 + b * wpb + k;
+          acc |= (wi < words) ? __ldg(bits + wi) : 0u;
+        }
+        out |= (acc ? 1u : 0u) << b;
+      }
+    }
+    s_sum[s] = out;
+  }
+}
+
+// Warp-wide decoupled look-back over 32-row tile counts.  Flags are tagged
+// with the launch's epoch, so no launch has to clear them for the next one:
+// [63:34] epoch, [33:32] status (1 aggregate, 2 inclusive), [31:0] count.
+__device__ uint32_t lookback_warp(unsigned long long* flags, uint32_t tile, uint32_t agg, uint32_t epoch,
+                                  uint32_t* err, int lane) {
+  const unsigned long long tag = (unsigned long long)epoch << 34;
+  if (lane == 0) st_release_u64(flags + tile, tag | (tile == 0 ? 2ull : 1ull) << 32 | agg);
+  uint32_t excl = 0;
+  int64_t base = tile;  // next window covers tiles [base-32, base)
+  uint32_t spins = 0;
+  bool timed_out = false;
+  while (base > 0) {
+    const int64_t j = base - 1 - lane;
+    uint32_t st = 2, cnt = 0;
+    if (j >= 0) {
+      const unsigned long long f = ld_acquire_u64(flags + j);
+      st = ((f >> 34) == epoch) ? (uint32_t)(f >> 32) & 3u : 0u;
+      cnt = (uint32_t)f;
+    }
+    const uint32_t incl = __ballot_sync(0xffffffffu, st == 2);
+    const uint32_t ready = __ballot_sync(0xffffffffu, st != 0);
+    const uint32_t upto = incl ? ((incl & (0u - incl)) << 1) - 1u : 0xffffffffu;  // lanes up to the first inclusive
+    if ((ready & upto) == upto) {
+      uint32_t c = (upto >> lane) & 1u ? cnt : 0u;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+      excl += c;
+      if (incl) break;
+      base -= 32;
+      continue;
+    }
+    if (++spins > kSpinLimit) {
+      timed_out = true;
+      break;
+    }
+    __nanosleep(32);
+  }
+  if (lane == 0) {
+    if (timed_out) set_err(err, DEVERR_LOOKBACK_TIMEOUT);
+    if (tile != 0) st_release_u64(flags + tile, tag | 2ull << 32 | (excl + agg));
+  }
+  return excl;
+}
+
 template <int WK, int XM, int EPI, bool COMPACT>
-__global__ void __launch_bounds__(kEllWarps * 32, 1) ell_fold_kernel(const __grid_constant__ CUtensorMap tm_idx,
-                                                                 const __grid_constant__ CUtensorMap tm_w,
-                                                                 const RowLaunch p, uint32_t L) {
+__global__ void __launch_bounds__(kEllWarps * 32, 1)
+    ell_stream_kernel(const __grid_constant__ CUtensorMap tm_idx, const __grid_constant__ CUtensorMap tm_w,
+                      const RowLaunch p, uint32_t L, uint32_t gs, uint32_t sum_words) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t bars[kEllWarps][kStages];
-  __shared__ uint32_t s_tile, s_base, s_last;
-  __shared__ uint32_t s_wc[kEllWarps];
+  __shared__ uint32_t s_fifo[kEllWarps][kFifo];
   const int lane = threadIdx.x & 31;
   const int wid = threadIdx.x >> 5;
-  // 1024-byte alignment of the swizzled tiles is required by the hardware.
+  // 1024-byte alignment keeps every swizzled box on its swizzle period.
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const size_t bits_bytes = (XM == X_BITS_SMEM) ? (((size_t)p.xbits_words * 4 + 1023) & ~(size_t)1023) : 0;
-  uint32_t* s_bits = reinterpret_cast<uint32_t*>(smem);
-  constexpr int kWBytes = WBox<WK>::kBytes;
-  constexpr int kStageBytes = kTileBytes + kWBytes;
-  unsigned char* wbase = smem + bits_bytes + (size_t)wid * kStages * kStageBytes;
+  constexpr int kStageBytes = WBox<WK>::kStage;
+  unsigned char* ring = smem + (size_t)wid * kStages * kStageBytes;
+  uint32_t* s_x = reinterpret_cast<uint32_t*>(smem + (size_t)kEllWarps * kStages * kStageBytes);
 
-  uint32_t tile;
-  if constexpr (COMPACT) {
-    if (threadIdx.x == 0) s_tile = atomicAdd(p.tile_ticket, 1u);
-    __syncthreads();
-    tile = s_tile;
-  } else {
-    tile = blockIdx.x;
-  }
-  if constexpr (XM == X_BITS_SMEM) {
-    const uint4* src = reinterpret_cast<const uint4*>(p.xbits);
-    const uint32_t nvec = p.xbits_words >> 2;
-    for (uint32_t i = threadIdx.x; i < nvec; i += blockDim.x) reinterpret_cast<uint4*>(s_bits)[i] = __ldg(src + i);
-    for (uint32_t i = (nvec << 2) + threadIdx.x; i < p.xbits_words; i += blockDim.x) s_bits[i] = __ldg(p.xbits + i);
-  }
-
-  const uint32_t row0 = tile * kEllLines + wid * 32;
-  const uint32_t line = row0 + lane;
-  const bool valid = line < p.nlines;
-  const bool warp_active = row0 < p.nlines;
-  const uint32_t nchunks = (L + 31) / 32;
+  const uint32_t ntiles = (p.nlines + 31) / 32;
+  const uint32_t nch = (L + kChunk - 1) / kChunk;
+  const uint32_t gwarp = blockIdx.x * kEllWarps + wid;
+  const uint32_t nwarps = gridDim.x * kEllWarps;
+  const uint64_t pol = evict_first_policy();
 
   if (lane == 0) {
     for (int s = 0; s < kStages; ++s) mbar_init(&bars[wid][s], 1);
@@ -113,48 +205,90 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1) ell_fold_kernel(const __gri
   }
   __syncwarp();
 
-  auto issue = [&](uint32_t c) {
-    const int s = c % kStages;
-    unsigned char* st = wbase + s * kStageBytes;
-    mbar_expect_tx(&bars[wid][s], kStageBytes);
-    tma_load_2d(st, &tm_idx, (int)(c * 32), (int)row0, &bars[wid][s]);
-    tma_load_2d(st + kTileBytes, &tm_w, (int)(c * 32), (int)row0, &bars[wid][s]);
+  // Tile sequence: dynamic tickets when tiles must finish in start order for
+  // the compaction look-back (a ticket is only taken by a running warp, so a
+  // tile only ever waits on tiles whose owners are running); a fixed stride
+  // otherwise.
+  uint32_t k_next = 0;
+  auto grab = [&]() -> uint32_t {
+    if constexpr (COMPACT) {
+      uint32_t t = 0;
+      if (lane == 0) t = atomicAdd(p.tile_ticket, 1u);
+      return __shfl_sync(0xffffffffu, t, 0);
+    } else {
+      return gwarp + (k_next++) * nwarps;
+    }
   };
 
-  float sum = 0.0f;
+  // Issue state (warp-uniform).
+  uint32_t i_tile = grab(), i_ch = 0, iseq = 0, fifo_w = 0, fifo_r = 0;
+  bool i_more = i_tile < ntiles;
+  if (i_more) s_fifo[wid][fifo_w++ % kFifo] = i_tile;
+  auto issue_next = [&]() {
+    if (!i_more) return;
+    if (i_ch == nch) {
+      i_tile = grab();
+      i_ch = 0;
+      if (i_tile >= ntiles) {
+        i_more = false;
+        return;
+      }
+      s_fifo[wid][fifo_w++ % kFifo] = i_tile;
+    }
+    if (lane == 0) {
+      const uint32_t s = iseq % kStages;
+      unsigned char* st = ring + s * kStageBytes;
+      mbar_expect_tx(&bars[wid][s], kStageBytes);
+      tma_load_2d(st, &tm_idx, (int)(i_ch * kChunk), (int)(i_tile * 32), &bars[wid][s], pol);
+      tma_load_2d(st + kIdxBox, &tm_w, (int)(i_ch * kChunk), (int)(i_tile * 32), &bars[wid][s], pol);
+    }
+    ++iseq;
+    ++i_ch;
+  };
+  for (int s = 0; s < kStages; ++s) issue_next();
+
+  // Spike operand into shared memory while the first boxes are in flight.
+  if constexpr (XM == X_BITS_SMEM) {
+    const uint32_t nvec = p.xbits_words >> 2;
+    const uint4* src = reinterpret_cast<const uint4*>(p.xbits);
+    for (uint32_t i = threadIdx.x; i < nvec; i += blockDim.x) reinterpret_cast<uint4*>(s_x)[i] = __ldg(src + i);
+    for (uint32_t i = (nvec << 2) + threadIdx.x; i < p.xbits_words; i += blockDim.x) s_x[i] = __ldg(p.xbits + i);
+  } else if constexpr (XM == X_BITS_GLOBAL) {
+    build_summary(s_x, p.xbits, p.xbits_words, gs, sum_words);
+  }
+  __syncthreads();
+
   bool ok = true;
-  uint32_t issued = 0;
-  if (warp_active && lane == 0)
-    for (; issued < nchunks && issued < (uint32_t)kStages; ++issued) issue(issued);
-  __syncthreads();  // the bitmask (if any) is staged before the first fold
-  if (warp_active) {
-    issued = __shfl_sync(0xffffffffu, issued, 0);
-    uint32_t c = 0;
-    for (; c < nchunks; ++c) {
-      const int s = c % kStages;
-      if (!mbar_wait(&bars[wid][s], (c / kStages) & 1u)) {
+  uint32_t cseq = 0;
+  const uint32_t sw64 = (lane >> 1) & 3;  // 64-byte swizzle phase of row `lane`
+  const uint32_t sw32 = (lane >> 2) & 1;  // 32-byte swizzle phase
+  while (ok && fifo_r != fifo_w) {
+    const uint32_t tile = s_fifo[wid][fifo_r++ % kFifo];
+    float sum = 0.0f;
+    for (uint32_t c = 0; c < nch; ++c, ++cseq) {
+      const uint32_t s = cseq % kStages;
+      if (!mbar_wait(&bars[wid][s], (cseq / kStages) & 1u)) {
         ok = false;
         break;
       }
-      const unsigned char* st = wbase + s * kStageBytes;
-      const unsigned char* irow = st + lane * 128;
-      const uint32_t cnt = min(32u, L - c * 32);
-      const uint32_t sw = lane & 7;
+      const unsigned char* st = ring + s * kStageBytes;
+      const unsigned char* irow = st + lane * 64;
+      const uint32_t cnt = min((uint32_t)kChunk, L - c * kChunk);
 #pragma unroll
-      for (uint32_t g = 0; g < 4; ++g) {  // 8 entries per group
+      for (uint32_t g = 0; g < 2; ++g) {  // 8 entries per group
         if (g * 8 >= cnt) break;
-        const uint4 ca = *reinterpret_cast<const uint4*>(irow + (((2 * g) ^ sw) << 4));
-        const uint4 cb = *reinterpret_cast<const uint4*>(irow + (((2 * g + 1) ^ sw) << 4));
+        const uint4 ca = *reinterpret_cast<const uint4*>(irow + (((2 * g) ^ sw64) << 4));
+        const uint4 cb = *reinterpret_cast<const uint4*>(irow + (((2 * g + 1) ^ sw64) << 4));
         float wv[8];
         if constexpr (WK == W_F32) {
-          const unsigned char* wrow = st + kTileBytes + lane * 128;
-          const float4 wa = *reinterpret_cast<const float4*>(wrow + (((2 * g) ^ sw) << 4));
-          const float4 wb = *reinterpret_cast<const float4*>(wrow + (((2 * g + 1) ^ sw) << 4));
+          const unsigned char* wrow = st + kIdxBox + lane * 64;
+          const float4 wa = *reinterpret_cast<const float4*>(wrow + (((2 * g) ^ sw64) << 4));
+          const float4 wb = *reinterpret_cast<const float4*>(wrow + (((2 * g + 1) ^ sw64) << 4));
           wv[0] = wa.x; wv[1] = wa.y; wv[2] = wa.z; wv[3] = wa.w;
           wv[4] = wb.x; wv[5] = wb.y; wv[6] = wb.z; wv[7] = wb.w;
         } else {
-          const unsigned char* wrow = st + kTileBytes + lane * 64;
-          const uint4 h = *reinterpret_cast<const uint4*>(wrow + ((g ^ ((lane >> 1) & 3)) << 4));
+          const unsigned char* wrow = st + kIdxBox + lane * 32;
+          const uint4 h = *reinterpret_cast<const uint4*>(wrow + ((g ^ sw32) << 4));
           const uint32_t hw[4] = {h.x, h.y, h.z, h.w};
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
@@ -171,9 +305,10 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1) ell_fold_kernel(const __gri
         const uint32_t cv[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
         const uint32_t lim = min(8u, cnt - g * 8);
         // The eight gathers and products are independent: issue them all
-        // before the dependent add chain.  Entries past the row end were
-        // zero-filled by the TMA box (column 0, weight 0), so their gathers
-        // stay in bounds; only their adds are skipped.
+        // before the dependent add chain.  Entries past the row end (and rows
+        // past the last line) were zero-filled by the TMA box (column 0,
+        // weight 0), so their gathers stay in bounds; only their adds are
+        // skipped.
         float prod[8];
 #pragma unroll
         for (uint32_t k = 0; k < 8; ++k) {
@@ -181,10 +316,16 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1) ell_fold_kernel(const __gri
           float xv;
           if constexpr (XM == X_DENSE) {
             xv = __ldg(p.x + col);
-          } else if constexpr (XM == X_BITS_SMEM) {
-            xv = (float)((s_bits[col >> 5] >> (col & 31)) & 1u);
           } else {
-            xv = (float)((__ldg(p.xbits + (col >> 5)) >> (col & 31)) & 1u);
+            uint32_t bit;
+            if constexpr (XM == X_BITS_SMEM) {
+              bit = (s_x[col >> 5] >> (col & 31)) & 1u;
+            } else {
+              const uint32_t q = col >> gs;
+              bit = 0;
+              if ((s_x[q >> 5] >> (q & 31)) & 1u) bit = (__ldg(p.xbits + (col >> 5)) >> (col & 31)) & 1u;
+            }
+            xv = __uint_as_float(bit * 0x3f800000u);  // exactly 0.0f or 1.0f
           }
           prod[k] = fmul(wv[k], xv);
         }
@@ -196,104 +337,128 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1) ell_fold_kernel(const __gri
         }
       }
       __syncwarp();
-      if (c + kStages < nchunks) {
-        if (lane == 0) {
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          issue(c + kStages);
-        }
-        ++issued;
-      }
+      if (lane == 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      issue_next();
     }
-    if (!ok) {
-      set_err(p.err, DEVERR_LOOKBACK_TIMEOUT);
-      // Let every copy still in flight land before the shared memory is released.
-      for (uint32_t cc = c; cc < issued; ++cc) mbar_wait(&bars[wid][cc % kStages], (cc / kStages) & 1u);
+    if (!ok) break;
+
+    // Epilogue of one 32-row tile.
+    const uint32_t row0 = tile * 32;
+    const uint32_t line = row0 + lane;
+    const bool valid = line < p.nlines;
+    if constexpr (EPI == EPI_ACCUM) {
+      if (valid) p.y[line] = fadd(p.y[line], sum);
+    } else {
+      bool spike = false;
+      if (valid) {
+        float vv = p.v[line];
+        float th = p.theta[line];
+        const float vol = fadd(fmul(vv, p.decay), sum);
+        if (vol >= th) {
+          spike = true;
+          vv = p.v_reset;
+          th = fadd(th, p.dtheta);
+        } else {
+          vv = vol;
+        }
+        p.v[line] = vv;
+        p.theta[line] = th;
+        p.spikes[line] = spike ? 1 : 0;
+      }
+      const uint32_t ballot = __ballot_sync(0xffffffffu, spike);
+      if (p.out_bits && lane == 0) p.out_bits[tile] = ballot;
+      if constexpr (COMPACT) {
+        const uint32_t agg = __popc(ballot);
+        const uint32_t excl = lookback_warp(p.tile_flags, tile, agg, p.epoch, p.err, lane);
+        if (spike) p.idx_list[excl + __popc(ballot & ((1u << lane) - 1u))] = p.idx_base + line;
+        if (lane == 0 && tile == ntiles - 1) *p.idx_count = excl + agg;
+      }
     }
   }
 
-  if constexpr (EPI == EPI_ACCUM) {
-    if (valid && ok) p.y[line] = fadd(p.y[line], sum);
-  } else {
-    bool spike = false;
-    if (valid && ok) {
-      float vv = p.v[line];
-      float th = p.theta[line];
-      const float vol = fadd(fmul(vv, p.decay), sum);
-      if (vol >= th) {
-        spike = true;
-        vv = p.v_reset;
-        th = fadd(th, p.dtheta);
-      } else {
-        vv = vol;
-      }
-      p.v[line] = vv;
-      p.theta[line] = th;
-      p.spikes[line] = spike ? 1 : 0;
-    }
-    const uint32_t ballot = __ballot_sync(0xffffffffu, spike);
-    if (p.out_bits && lane == 0 && warp_active) p.out_bits[row0 >> 5] = ballot;
-    if constexpr (COMPACT) {
-      const uint32_t ntiles = (p.nlines + kEllLines - 1) / kEllLines;
-      if (lane == 0) s_wc[wid] = __popc(ballot);
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        uint32_t agg = 0;
-        for (int w2 = 0; w2 < kEllWarps; ++w2) agg += s_wc[w2];
-        const uint32_t excl = lookback_count(p.tile_flags, tile, agg, p.err);
-        s_base = excl;
-        if (tile == ntiles - 1) *p.idx_count = excl + agg;
-      }
-      __syncthreads();
-      uint32_t wexcl = s_base;
-      for (int w2 = 0; w2 < wid; ++w2) wexcl += s_wc[w2];
-      if (spike) p.idx_list[wexcl + __popc(ballot & ((1u << lane) - 1u))] = p.idx_base + line;
-      if (threadIdx.x == 0) {
-        __threadfence();
-        s_last = (atomicAdd(p.tile_ticket + 1, 1u) == ntiles - 1) ? 1u : 0u;
-      }
-      __syncthreads();
-      if (s_last) {
-        for (uint32_t i = threadIdx.x; i < ntiles; i += blockDim.x) p.tile_flags[i] = 0ull;
-        if (threadIdx.x == 0) {
-          p.tile_ticket[0] = 0;
-          p.tile_ticket[1] = 0;
-        }
+  if (!ok) {
+    if (lane == 0) set_err(p.err, DEVERR_LOOKBACK_TIMEOUT);
+    // Let every copy still in flight land before the shared memory is released.
+    for (uint32_t q = cseq; q < iseq; ++q) mbar_wait(&bars[wid][q % kStages], (q / kStages) & 1u);
+  }
+  if constexpr (COMPACT) {
+    // The last warp out rewinds the ticket counters for the next launch; the
+    // epoch-tagged flags need no clearing.
+    if (lane == 0) {
+      __threadfence();
+      if (atomicAdd(p.tile_ticket + 1, 1u) == nwarps - 1) {
+        atomicExch(p.tile_ticket, 0u);
+        atomicExch(p.tile_ticket + 1, 0u);
       }
     }
   }
 }
 
+// Shared-memory bytes of the spike operand for a launch.
+struct XPlan {
+  size_t bytes = 0;
+  uint32_t gs = 0, sum_words = 0;
+};
+
+XPlan plan_x(const RowLaunch& p) {
+  XPlan x;
+  if (p.xmode == X_BITS_SMEM) {
+    x.bytes = (size_t)p.xbits_words * 4;
+  } else if (p.xmode == X_BITS_GLOBAL) {
+    uint32_t gs = 3;
+    while (gs < 31 && (((uint64_t)p.xbits_words + (1ull << gs) - 1) >> gs) > kSumMaxWords) ++gs;
+    x.gs = gs;
+    x.sum_words = (uint32_t)(((uint64_t)p.xbits_words + (1ull << gs) - 1) >> gs);
+    x.bytes = (size_t)x.sum_words * 4;
+  }
+  x.bytes = (x.bytes + 15) & ~size_t(15);
+  return x;
+}
+
+int g_num_sms = 0;
+
 template <int WK, int XM, int EPI, bool COMPACT>
-cudaError_t launch_t(const EllMaps& m, const RowLaunch& p, uint32_t L, cudaStream_t stream) {
-  auto kern = ell_fold_kernel<WK, XM, EPI, COMPACT>;
-  const size_t bits_bytes = (XM == X_BITS_SMEM) ? (((size_t)p.xbits_words * 4 + 1023) & ~(size_t)1023) : 0;
-  const size_t smem = 1024 + bits_bytes + (size_t)kEllWarps * kStages * (kTileBytes + WBox<WK>::kBytes);
+cudaError_t launch_t(const EllMaps& m, const RowLaunch& p, cudaStream_t stream) {
+  auto kern = ell_stream_kernel<WK, XM, EPI, COMPACT>;
+  const XPlan xp = plan_x(p);
+  const size_t smem = 1024 + (size_t)kEllWarps * kStages * WBox<WK>::kStage + xp.bytes;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  const uint32_t tiles = (p.nlines + kEllLines - 1) / kEllLines;
-  kern<<<tiles, kEllWarps * 32, smem, stream>>>(*reinterpret_cast<const CUtensorMap*>(m.idx),
-                                                *reinterpret_cast<const CUtensorMap*>(m.w), p, L);
+  if (!g_num_sms) {
+    int dev = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+  }
+  int per_sm = 0;
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kEllWarps * 32, smem)) != cudaSuccess)
+    return e;
+  const uint32_t tiles = (p.nlines + 31) / 32;
+  const uint32_t want = (tiles + kEllWarps - 1) / kEllWarps;
+  const uint32_t grid = std::max(1u, std::min(want, (uint32_t)(std::max(per_sm, 1) * g_num_sms)));
+  kern<<<grid, kEllWarps * 32, smem, stream>>>(*reinterpret_cast<const CUtensorMap*>(m.idx),
+                                               *reinterpret_cast<const CUtensorMap*>(m.w), p, m.L, xp.gs,
+                                               xp.sum_words);
   return cudaGetLastError();
 }
 
 template <int WK>
-cudaError_t dispatch(const EllMaps& m, const RowLaunch& p, uint32_t L, cudaStream_t s) {
+cudaError_t dispatch(const EllMaps& m, const RowLaunch& p, cudaStream_t s) {
   const bool compact = p.idx_list != nullptr;
   if (p.epilogue == EPI_ACCUM) {
     switch (p.xmode) {
-      case X_DENSE: return launch_t<WK, X_DENSE, EPI_ACCUM, false>(m, p, L, s);
-      case X_BITS_SMEM: return launch_t<WK, X_BITS_SMEM, EPI_ACCUM, false>(m, p, L, s);
-      default: return launch_t<WK, X_BITS_GLOBAL, EPI_ACCUM, false>(m, p, L, s);
+      case X_DENSE: return launch_t<WK, X_DENSE, EPI_ACCUM, false>(m, p, s);
+      case X_BITS_SMEM: return launch_t<WK, X_BITS_SMEM, EPI_ACCUM, false>(m, p, s);
+      default: return launch_t<WK, X_BITS_GLOBAL, EPI_ACCUM, false>(m, p, s);
     }
   }
   switch (p.xmode) {
-    case X_DENSE: return launch_t<WK, X_DENSE, EPI_LIF, false>(m, p, L, s);
+    case X_DENSE: return launch_t<WK, X_DENSE, EPI_LIF, false>(m, p, s);
     case X_BITS_SMEM:
-      return compact ? launch_t<WK, X_BITS_SMEM, EPI_LIF, true>(m, p, L, s)
-                     : launch_t<WK, X_BITS_SMEM, EPI_LIF, false>(m, p, L, s);
+      return compact ? launch_t<WK, X_BITS_SMEM, EPI_LIF, true>(m, p, s)
+                     : launch_t<WK, X_BITS_SMEM, EPI_LIF, false>(m, p, s);
     default:
-      return compact ? launch_t<WK, X_BITS_GLOBAL, EPI_LIF, true>(m, p, L, s)
-                     : launch_t<WK, X_BITS_GLOBAL, EPI_LIF, false>(m, p, L, s);
+      return compact ? launch_t<WK, X_BITS_GLOBAL, EPI_LIF, true>(m, p, s)
+                     : launch_t<WK, X_BITS_GLOBAL, EPI_LIF, false>(m, p, s);
   }
 }
 
@@ -327,18 +492,18 @@ bool ell_encode(EllMaps& m, const uint32_t* col, const void* w, int wkind, uint6
   if ((reinterpret_cast<uintptr_t>(col) | reinterpret_cast<uintptr_t>(w)) & 15) return false;
   static_assert(sizeof(CUtensorMap) == sizeof(m.idx), "tensor map storage");
   cuuint64_t dims[2] = {L, nrows};
-  cuuint32_t box[2] = {32, 32};
+  cuuint32_t box[2] = {kChunk, 32};
   cuuint32_t estr[2] = {1, 1};
   cuuint64_t istride[1] = {(cuuint64_t)L * 4};
   CUresult r = enc(reinterpret_cast<CUtensorMap*>(m.idx), CU_TENSOR_MAP_DATA_TYPE_UINT32, 2,
                    const_cast<uint32_t*>(col), dims, istride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
   cuuint64_t wstride[1] = {(cuuint64_t)L * wbytes};
   r = enc(reinterpret_cast<CUtensorMap*>(m.w),
           wkind == W_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(w),
           dims, wstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-          wkind == W_F32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          wkind == W_F32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
   m.L = L;
@@ -349,9 +514,9 @@ bool ell_encode(EllMaps& m, const uint32_t* col, const void* w, int wkind, uint6
 cudaError_t launch_ell(const EllMaps& m, const RowLaunch& p, cudaStream_t stream) {
   if (p.nlines == 0) return cudaSuccess;
   switch (p.wkind) {
-    case W_F16: return dispatch<W_F16>(m, p, m.L, stream);
-    case W_BF16: return dispatch<W_BF16>(m, p, m.L, stream);
-    default: return dispatch<W_F32>(m, p, m.L, stream);
+    case W_F16: return dispatch<W_F16>(m, p, stream);
+    case W_BF16: return dispatch<W_BF16>(m, p, stream);
+    default: return dispatch<W_F32>(m, p, stream);
   }
 }
 

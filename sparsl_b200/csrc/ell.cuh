@@ -8,10 +8,10 @@
 
 namespace sparsl {
 
-constexpr int kEllWarps = 4;
-constexpr int kEllLines = kEllWarps * 32;  // rows per block (one compaction tile)
+constexpr int kEllWarps = 8;  // warps per persistent CTA
 
-__host__ __device__ inline uint32_t ell_tiles(uint32_t nlines) { return (nlines + kEllLines - 1) / kEllLines; }
+// Compaction tiles of the TMA path: one warp's 32 rows.
+__host__ __device__ inline uint32_t ell_tiles(uint32_t nlines) { return (nlines + 31) / 32; }
 
 // Two encoded CUtensorMaps (column and weight matrices viewed as [nrows x L]).
 struct EllMaps {
@@ -26,6 +26,8 @@ struct EllMaps {
 bool ell_encode(EllMaps& m, const uint32_t* col, const void* w, int wkind, uint64_t nrows, uint32_t L);
 
 // Same contract as launch_rows for a forward (CSR) launch; p.ptr is unused.
+// Compaction flags are tagged with p.epoch (nonzero, below 2^30, different
+// from the previous launch's) instead of being cleared between launches.
 cudaError_t launch_ell(const EllMaps& m, const RowLaunch& p, cudaStream_t stream);
 
 }  // namespace sparsl

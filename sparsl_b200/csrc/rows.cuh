@@ -48,6 +48,7 @@ struct RowLaunch {
   uint32_t idx_base = 0;           // added to every emitted line index
   unsigned long long* tile_flags = nullptr;  // >= tiles(nlines), zero on entry
   uint32_t* tile_ticket = nullptr;           // 2 words, zero on entry
+  uint32_t epoch = 0;              // TMA path: tag of this launch's compaction flags
   uint32_t* err = nullptr;         // device error word (host mapped)
 };
 

@@ -102,3 +102,57 @@ def test_uniform_rows_with_non_finite_weights(O, cuda_device):
     want = O.spmv_spikes(csr, w, pk, np.zeros(64, np.float32))
     assert_bits_equal(got, want)
     assert np.isnan(got[0]) and np.isnan(got[1])
+
+
+@pytest.mark.parametrize("ncols,density", [(600_000, 0.01), (600_000, 0.6), (5_000_000, 0.001),
+                                           (20_000_000, 0.05)])
+@pytest.mark.parametrize("precision", [S.WeightPrecision.F32, S.WeightPrecision.F16])
+def test_uniform_rows_spike_operand_beyond_shared_memory(O, cuda_device, ncols, density, precision):
+    """Spike bitmasks too large for shared memory are gathered through a
+    per-CTA summary of nonzero column groups; results stay bit-exact at every
+    density, including non-finite weights on cleared spikes."""
+    nrows, L = 3000, 40
+    csr, w = _uniform(O, nrows, ncols, L, ncols % 1000 + L)
+    w[5] = np.inf
+    w[L * 7 + 3] = np.nan
+    wq = O.quantise(int(precision), w)
+    op = _prepare(cuda_device, csr, w, precision, generic=False)
+    r = np.random.default_rng(ncols)
+    s = (r.random(ncols) < density).astype(np.uint8)
+    s[csr.col[5]] = 0
+    pk = O.pack_spikes(s)
+    y0 = r.uniform(-1, 1, nrows).astype(np.float32)
+    got = y0.copy()
+    op.spmv_spikes(pk, got)
+    want = O.spmv_spikes(csr, wq, pk, y0.copy())
+    assert_bits_equal(got, want, "spmv_spikes")
+    assert np.isnan(got[0]) and np.isnan(got[7])
+
+
+def test_uniform_recurrent_network_spike_operand_beyond_shared_memory(O, cuda_device):
+    """The compacting network tick with a bitmask gathered through the summary."""
+    n, L = 600_000, 16
+    r = np.random.default_rng(77)
+    col = np.sort(r.integers(0, n, size=(n, L), dtype=np.uint32), axis=1).reshape(-1)
+    rp = (np.arange(n + 1, dtype=np.uint64) * L).astype(np.uint32)
+    w = (r.standard_normal(n * L) * 0.4).astype(np.float32)
+    csr = O.Csr(rp, col, n)
+    v0 = r.random(n).astype(np.float32)
+    t0 = np.full(n, 0.8, np.float32)
+    pk0 = O.pack_spikes((r.random(n) < 0.05).astype(np.uint8))
+    op = cuda_device.prepare(S.Csr(rp, col, n), n, w)
+    vw, tw, sw, xw = v0.copy(), t0.copy(), np.zeros(n, np.uint8), pk0.copy()
+    trace = []
+    op.write_x_spikes(pk0)
+    op.write_lif_state(v0, t0)
+    for steps in (3, 4):  # two calls: the second reuses the ticket counters and flags
+        op.fused_spmv_spikes_lif_recurrent_steps(S.LifParams.new(0.95, 0.0, 0.0), steps)
+        trace += list(O.recurrent_steps(csr, w, xw, vw, tw, sw, 0.95, 0.0, 0.0, steps, par=True))
+        assert np.array_equal(op.spike_trace(), trace[-steps:])
+        assert np.array_equal(op.spike_indices(), np.flatnonzero(sw).astype(np.uint32))
+    assert sum(trace) > 1000
+    v, t, sp = np.zeros(n, np.float32), np.zeros(n, np.float32), np.zeros(n, np.bool_)
+    op.sync_lif_state(v, t, sp)
+    assert_bits_equal(v, vw)
+    assert_bits_equal(t, tw)
+    assert np.array_equal(op.sync_x_spikes(), xw)
