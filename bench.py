@@ -417,7 +417,8 @@ def bench_lif_net(args, dist):
         "gpu_launches": kernels_per_tick * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": float(traffic) if traffic else None,
-                     "kernel": "row_fold_kernel<f32, bits, LIF> (fused spike SpMV + LIF + ballot pack)",
+                     "kernel": "ell_stream_kernel<f32, spike bitmask via shared-memory summary, LIF> "
+                               "(TMA-streamed fused spike SpMV + LIF + ballot pack)",
                      "algorithmic_bytes_per_tick_per_gpu": algo, "kernel_ms_per_tick": kernel_ms_tick,
                      "peak_source": how},
         "cpu_baseline": cpu,
@@ -595,6 +596,120 @@ def bench_scan(args, dev, want_cpu):
             "bit_exact_vs_oracle": exact, "cpu_baseline": cpu}
 
 
+SPMM_N, SPMM_NVEC, SPMM_KMAX, SPMM_ALPHA, SPMM_SEED = 1_000_000, 64, 4096, 1.5, 0x5B33
+
+
+def gen_zipf_csr(n, ncols, kmax, alpha, seed):
+    """Row lengths from Zipf(alpha) restricted to [1, kmax] (inverse CDF), then
+    that many distinct sorted uniform columns per row (repeats are redrawn)."""
+    import torch
+
+    r = np.random.default_rng(seed)
+    k = np.arange(1, kmax + 1, dtype=np.float64)
+    cdf = np.cumsum(k ** -alpha)
+    cdf /= cdf[-1]
+    lens = np.minimum(np.searchsorted(cdf, r.random(n), side="right") + 1, kmax).astype(np.int64)
+    rp = np.zeros(n + 1, np.int64)
+    np.cumsum(lens, out=rp[1:])
+    nnz = int(rp[-1])
+    rows = torch.from_numpy(np.repeat(np.arange(n, dtype=np.int64), lens)).cuda()
+    cols = torch.from_numpy(r.integers(0, ncols, nnz, dtype=np.int64)).cuda()
+    while True:
+        key, _ = torch.sort(rows * ncols + cols)
+        cols = key % ncols
+        dup = torch.nonzero(key[1:] == key[:-1]).flatten() + 1
+        if dup.numel() == 0:
+            break
+        cols[dup] = torch.from_numpy(r.integers(0, ncols, dup.numel(), dtype=np.int64)).cuda()
+    col = cols.to(torch.int32).cpu().numpy().view(np.uint32)
+    del rows, cols, key
+    return rp.astype(np.uint32), col, r
+
+
+def bench_spmm(args, dev, want_cpu):
+    """SpMM with power-law rows: Y += A X, X 1M x 64 row-major, f32 and f16 weights."""
+    import torch
+    import sparsl_b200 as S
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    n, nv = SPMM_N, SPMM_NVEC
+    t0 = time.perf_counter()
+    rp, col, r = gen_zipf_csr(n, n, SPMM_KMAX, SPMM_ALPHA, SPMM_SEED)
+    nnz = col.size
+    w = r.uniform(-1.0, 1.0, nnz).astype(np.float32)
+    x = r.uniform(-1.0, 1.0, (n, nv)).astype(np.float32)
+    setup_s = time.perf_counter() - t0
+    L = lib()
+    s = torch.cuda.Stream()
+    torch.cuda.set_stream(s)
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.zeros((n, nv), dtype=torch.float32, device="cuda")
+    flush = torch.empty(64 << 22, dtype=torch.float32, device="cuda")  # 1 GiB > L2
+    sample = np.sort(np.random.default_rng(SPMM_SEED ^ 1).choice(n, 2000, replace=False))
+    sub_rp = np.zeros(sample.size + 1, np.uint64)
+    np.cumsum(rp[sample + 1].astype(np.uint64) - rp[sample], out=sub_rp[1:])
+    sel = np.concatenate([np.arange(rp[i], rp[i + 1]) for i in sample])
+    sub = O.Csr(sub_rp.astype(np.uint32), col[sel], n)
+    out = {}
+    for prec, tag in ((S.WeightPrecision.F32, "f32"), (S.WeightPrecision.F16, "f16")):
+        op = dev.prepare_with(S.Csr(rp, col, n), n, w, prec)
+        wb = 4 if tag == "f32" else 2
+        run = lambda: check(L.sparsl_op_spmm_device(op.handle, dx.data_ptr(), nv, dy.data_ptr(), s.cuda_stream),
+                            "spmm")
+        # parity on a row sample: one product from Y = 0 against the oracle
+        dy.zero_()
+        run()
+        s.synchronize()
+        got = dy.cpu().numpy()[sample]
+        want = O.spmm(sub, O.quantise(int(prec), w)[sel], x.reshape(-1), nv, np.zeros(sample.size * nv, np.float32),
+                      par=True).reshape(sample.size, nv)
+        exact = bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))
+        for _ in range(args.warmup):
+            run()
+        ts = time_launches(s, run, max(3, args.kernel_iters // 2), flush=lambda: flush_l2(flush))
+        ms = statistics.median(ts)
+        algo = nnz * (4 + wb) + (n + 1) * 4 + n * nv * 4 + 2 * n * nv * 4
+        out[tag] = {"value": algo / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms, "algorithmic_bytes": algo,
+                    "bit_exact_vs_oracle_row_sample": exact}
+        if tag == "f32":
+            hx, hy = Pinned(np.float32, n * nv), Pinned(np.float32, n * nv)
+            hx.a[:] = x.reshape(-1)
+            hy.a[:] = 0
+            ets = [events_ms(L.sparsl_op_stream(op.handle), torch.cuda.current_device(),
+                             lambda: check(L.sparsl_op_spmm(op.handle, hx.ptr, n * nv, nv, hy.ptr, n * nv), "spmm e2e"))
+                   for _ in range(3)]
+            e2e_ms = statistics.median(ets)
+            hx.free()
+            hy.free()
+            out[tag]["e2e"] = {"value": algo / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                               "h2d_bytes_per_step": 2 * n * nv * 4, "d2h_bytes_per_step": n * nv * 4,
+                               "path": "sparsl_op_spmm, pinned host X/Y"}
+        del op
+    cpu = None
+    if want_cpu:
+        wsub = w[sel]
+        yy = np.zeros(sample.size * nv, np.float32)
+        t1, k = time.perf_counter(), 0
+        while time.perf_counter() - t1 < args.cpu_seconds / 2:
+            O.spmm(sub, wsub, x.reshape(-1), nv, yy, par=True)
+            k += 1
+        dt = (time.perf_counter() - t1) / k * (nnz / sel.size)  # full-matrix seconds
+        cpu = {"value": out["f32"]["algorithmic_bytes"] / dt / 1e9, "unit": "GB/s", "cores": O.num_threads(),
+               "kind": "port", "sample": f"{k} SpMMs of a {sample.size}-row sample ({sel.size} nnz), "
+                                         "CpuParallel restatement, scaled to the full matrix by nnz"}
+    f32 = out["f32"]
+    return {"metric": "SpMM effective HBM GB/s", "value": f32["value"], "unit": "GB/s",
+            "ms_per_step": f32["ms_per_step"], "algorithmic_bytes": f32["algorithmic_bytes"],
+            "config": f"{n:,} x {n:,}, row lengths Zipf({SPMM_ALPHA}) restricted to [1,{SPMM_KMAX}] "
+                      f"(realised nnz {nnz:,}, mean {nnz / n:.1f}), distinct sorted uniform cols, w U[-1,1], "
+                      f"X {n:,} x {nv} row-major U[-1,1]; L2 flushed (1 GiB write) before every launch",
+            "setup_s": round(setup_s, 1), "e2e": f32.get("e2e"),
+            "bit_exact_vs_oracle_row_sample": f32["bit_exact_vs_oracle_row_sample"], "f16": out["f16"],
+            "cpu_baseline": cpu}
+
+
 def bench_lif(args, dev, want_cpu):
     import torch
     import sparsl_b200 as S
@@ -732,7 +847,7 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="sparsl", choices=["sparsl", "reference"])
-    ap.add_argument("--workload", default="lif_net", choices=["lif_net", "spmv", "scan", "lif"])
+    ap.add_argument("--workload", default="lif_net", choices=["lif_net", "spmv", "spmm", "scan", "lif"])
     ap.add_argument("--no-extras", action="store_true", help="N=1: skip the SpMV / scan / LIF-1GPU figures")
     ap.add_argument("--kernel-iters", type=int, default=20)
     # Smaller instances of the same workloads (profiling captures, quick runs).
@@ -763,7 +878,7 @@ def main():
 
             torch.cuda.set_device(dist.local)
             dev = S.Device.try_new(S.Backend.Cuda, dist.local)
-            fn = {"spmv": bench_spmv, "scan": bench_scan, "lif": bench_lif}[args.workload]
+            fn = {"spmv": bench_spmv, "spmm": bench_spmm, "scan": bench_scan, "lif": bench_lif}[args.workload]
             line = fn(args, dev, dist.rank == 0 and not args.no_cpu) if dist.rank == 0 else None
         else:
             line = bench_lif_net(args, dist)
@@ -774,7 +889,7 @@ def main():
                 torch.cuda.empty_cache()
                 dev = S.Device.try_new(S.Backend.Cuda, dist.local)
                 extras = {}
-                for name, fn in (("spmv", bench_spmv), ("scan", bench_scan), ("lif", bench_lif)):
+                for name, fn in (("spmv", bench_spmv), ("spmm", bench_spmm), ("scan", bench_scan), ("lif", bench_lif)):
                     try:
                         extras[name] = fn(args, dev, not args.no_cpu)
                     except Exception as e:  # report, never hide

@@ -1,10 +1,10 @@
 // Row-fold engine for operators whose rows all hold the same number of
 // entries L (row_ptr[r] == r * L): fixed fan-in networks and fixed-degree
 // matrices.  Their column and weight arrays are dense [nrows x L] matrices, so
-// a warp's 32 rows x 16 entries are one 2-D TMA box.
+// a warp's 32 rows x kChunk entries are one 2-D TMA box.
 //
 // Persistent and streaming: one CTA per SM, kEllWarps warps, and every warp
-// walks its own sequence of 32-row tiles.  Per warp a kStages-deep ring of
+// walks its own sequence of 32-row tiles.  Per warp a ring of
 // (column box, weight box) pairs is filled by cp.async.bulk.tensor into
 // swizzled shared memory and signalled by one mbarrier per stage; lane 0
 // refills a stage as soon as the warp has folded it, running ahead across
@@ -32,11 +32,31 @@
 namespace sparsl {
 namespace {
 
-constexpr int kStages = 4;
-constexpr int kChunk = 16;                     // entries per row per stage
-constexpr int kIdxBox = 32 * kChunk * 4;       // 2 KiB column box
+// Compile-time shape: kChunk entries per row per stage (16 or 32).  The
+// number of stages per warp is chosen at launch from the shared memory left
+// after the spike operand (kMinStages..kMaxStages).
+#ifndef SPARSL_ELL_CHUNK
+#define SPARSL_ELL_CHUNK 16
+#endif
+constexpr int kChunk = SPARSL_ELL_CHUNK;
+static_assert(kChunk == 16 || kChunk == 32, "chunk of 16 or 32 entries");
+constexpr int kMinStages = 2, kMaxStages = 8;
+constexpr int kIdxRow = kChunk * 4;            // bytes of one row of a column box
+constexpr int kIdxBox = 32 * kIdxRow;          // column box: 32 rows x kChunk entries
 constexpr uint32_t kSumMaxWords = 16384;       // 64 KiB summary
-constexpr uint32_t kFifo = 8;                  // > kStages: tiles a warp can run ahead
+constexpr uint32_t kFifo = 16;                 // > kMaxStages: tiles a warp can run ahead
+constexpr size_t kSmemBudget = 227 * 1024 - 4096;  // per-CTA limit less static use and alignment slack
+
+// 16-byte piece p of row `row` of a box whose rows are RB bytes, under the
+// matching TMA swizzle (RB = 32, 64 or 128 bytes: SWIZZLE_32B/64B/128B).
+template <int RB>
+__device__ __forceinline__ uint32_t swz(uint32_t row, uint32_t p) {
+  return ((p ^ (((row * RB) >> 7) & (RB / 16 - 1))) << 4);
+}
+template <int RB>
+constexpr CUtensorMapSwizzle swizzle_mode() {
+  return RB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : RB == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -85,8 +105,8 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
 
 template <int WK>
 struct WBox {
-  // bytes of one weight box: 32 rows x kChunk entries
-  static constexpr int kBytes = WK == W_F32 ? 32 * kChunk * 4 : 32 * kChunk * 2;
+  static constexpr int kRow = WK == W_F32 ? kChunk * 4 : kChunk * 2;  // bytes of one weight-box row
+  static constexpr int kBytes = 32 * kRow;
   static constexpr int kStage = kIdxBox + kBytes;
 };
 
@@ -136,10 +156,11 @@ __device__ void build_summary(uint32_t* s_sum, const uint32_t* __restrict__ bits
 // Warp-wide decoupled look-back over 32-row tile counts.  Flags are tagged
 // with the launch's epoch, so no launch has to clear them for the next one:
 // [63:34] epoch, [33:32] status (1 aggregate, 2 inclusive), [31:0] count.
+// Each flag word carries everything it publishes, so relaxed accesses do.
 __device__ uint32_t lookback_warp(unsigned long long* flags, uint32_t tile, uint32_t agg, uint32_t epoch,
                                   uint32_t* err, int lane) {
   const unsigned long long tag = (unsigned long long)epoch << 34;
-  if (lane == 0) st_release_u64(flags + tile, tag | (tile == 0 ? 2ull : 1ull) << 32 | agg);
+  if (lane == 0) st_relaxed_u64(flags + tile, tag | (tile == 0 ? 2ull : 1ull) << 32 | agg);
   uint32_t excl = 0;
   int64_t base = tile;  // next window covers tiles [base-32, base)
   uint32_t spins = 0;
@@ -148,7 +169,7 @@ __device__ uint32_t lookback_warp(unsigned long long* flags, uint32_t tile, uint
     const int64_t j = base - 1 - lane;
     uint32_t st = 2, cnt = 0;
     if (j >= 0) {
-      const unsigned long long f = ld_acquire_u64(flags + j);
+      const unsigned long long f = ld_relaxed_u64(flags + j);
       st = ((f >> 34) == epoch) ? (uint32_t)(f >> 32) & 3u : 0u;
       cnt = (uint32_t)f;
     }
@@ -172,17 +193,37 @@ __device__ uint32_t lookback_warp(unsigned long long* flags, uint32_t tile, uint
   }
   if (lane == 0) {
     if (timed_out) set_err(err, DEVERR_LOOKBACK_TIMEOUT);
-    if (tile != 0) st_release_u64(flags + tile, tag | 2ull << 32 | (excl + agg));
+    if (tile != 0) st_relaxed_u64(flags + tile, tag | 2ull << 32 | (excl + agg));
   }
   return excl;
+}
+
+// One spike bit of column `col` as 0.0f / 1.0f.
+template <int XM>
+__device__ __forceinline__ float spike_value(const uint32_t* s_x, const uint32_t* __restrict__ gbits, uint32_t col,
+                                             uint32_t gs) {
+  uint32_t bit;
+  if constexpr (XM == X_BITS_SMEM) {
+    const uint32_t w = s_x[col >> 5];
+    bit = __funnelshift_r(w, w, col) & 1u;  // the shift count is taken mod 32
+  } else {
+    const uint32_t q = col >> gs;
+    const uint32_t sw = s_x[q >> 5];
+    bit = 0;
+    if (__funnelshift_r(sw, sw, q) & 1u) {
+      const uint32_t w = __ldg(gbits + (col >> 5));
+      bit = __funnelshift_r(w, w, col) & 1u;
+    }
+  }
+  return __uint_as_float(bit * 0x3f800000u);  // exactly 0.0f or 1.0f
 }
 
 template <int WK, int XM, int EPI, bool COMPACT>
 __global__ void __launch_bounds__(kEllWarps * 32, 1)
     ell_stream_kernel(const __grid_constant__ CUtensorMap tm_idx, const __grid_constant__ CUtensorMap tm_w,
-                      const RowLaunch p, uint32_t L, uint32_t gs, uint32_t sum_words) {
+                      const RowLaunch p, uint32_t L, uint32_t gs, uint32_t sum_words, uint32_t nst) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  __shared__ __align__(8) uint64_t bars[kEllWarps][kStages];
+  __shared__ __align__(8) uint64_t bars[kEllWarps][kMaxStages];
   __shared__ uint32_t s_fifo[kEllWarps][kFifo];
   const int lane = threadIdx.x & 31;
   const int wid = threadIdx.x >> 5;
@@ -190,8 +231,8 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1)
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int kStageBytes = WBox<WK>::kStage;
-  unsigned char* ring = smem + (size_t)wid * kStages * kStageBytes;
-  uint32_t* s_x = reinterpret_cast<uint32_t*>(smem + (size_t)kEllWarps * kStages * kStageBytes);
+  unsigned char* ring = smem + (size_t)wid * nst * kStageBytes;
+  uint32_t* s_x = reinterpret_cast<uint32_t*>(smem + (size_t)kEllWarps * nst * kStageBytes);
 
   const uint32_t ntiles = (p.nlines + 31) / 32;
   const uint32_t nch = (L + kChunk - 1) / kChunk;
@@ -200,7 +241,7 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1)
   const uint64_t pol = evict_first_policy();
 
   if (lane == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(&bars[wid][s], 1);
+    for (uint32_t s = 0; s < nst; ++s) mbar_init(&bars[wid][s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncwarp();
@@ -220,8 +261,8 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1)
     }
   };
 
-  // Issue state (warp-uniform).
-  uint32_t i_tile = grab(), i_ch = 0, iseq = 0, fifo_w = 0, fifo_r = 0;
+  // Issue state (warp-uniform): next tile / chunk, ring slot, chunks issued.
+  uint32_t i_tile = grab(), i_ch = 0, i_slot = 0, issued = 0, fifo_w = 0, fifo_r = 0;
   bool i_more = i_tile < ntiles;
   if (i_more) s_fifo[wid][fifo_w++ % kFifo] = i_tile;
   auto issue_next = [&]() {
@@ -236,16 +277,16 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1)
       s_fifo[wid][fifo_w++ % kFifo] = i_tile;
     }
     if (lane == 0) {
-      const uint32_t s = iseq % kStages;
-      unsigned char* st = ring + s * kStageBytes;
-      mbar_expect_tx(&bars[wid][s], kStageBytes);
-      tma_load_2d(st, &tm_idx, (int)(i_ch * kChunk), (int)(i_tile * 32), &bars[wid][s], pol);
-      tma_load_2d(st + kIdxBox, &tm_w, (int)(i_ch * kChunk), (int)(i_tile * 32), &bars[wid][s], pol);
+      unsigned char* st = ring + i_slot * kStageBytes;
+      mbar_expect_tx(&bars[wid][i_slot], kStageBytes);
+      tma_load_2d(st, &tm_idx, (int)(i_ch * kChunk), (int)(i_tile * 32), &bars[wid][i_slot], pol);
+      tma_load_2d(st + kIdxBox, &tm_w, (int)(i_ch * kChunk), (int)(i_tile * 32), &bars[wid][i_slot], pol);
     }
-    ++iseq;
+    i_slot = (i_slot + 1 == nst) ? 0 : i_slot + 1;
+    ++issued;
     ++i_ch;
   };
-  for (int s = 0; s < kStages; ++s) issue_next();
+  for (uint32_t s = 0; s < nst; ++s) issue_next();
 
   // Spike operand into shared memory while the first boxes are in flight.
   if constexpr (XM == X_BITS_SMEM) {
@@ -259,36 +300,33 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1)
   __syncthreads();
 
   bool ok = true;
-  uint32_t cseq = 0;
-  const uint32_t sw64 = (lane >> 1) & 3;  // 64-byte swizzle phase of row `lane`
-  const uint32_t sw32 = (lane >> 2) & 1;  // 32-byte swizzle phase
+  uint32_t c_slot = 0, c_phase = 0, consumed = 0;
+  constexpr int kWRow = WBox<WK>::kRow;
   while (ok && fifo_r != fifo_w) {
     const uint32_t tile = s_fifo[wid][fifo_r++ % kFifo];
     float sum = 0.0f;
-    for (uint32_t c = 0; c < nch; ++c, ++cseq) {
-      const uint32_t s = cseq % kStages;
-      if (!mbar_wait(&bars[wid][s], (cseq / kStages) & 1u)) {
+    for (uint32_t c = 0; c < nch; ++c) {
+      if (!mbar_wait(&bars[wid][c_slot], c_phase)) {
         ok = false;
         break;
       }
-      const unsigned char* st = ring + s * kStageBytes;
-      const unsigned char* irow = st + lane * 64;
+      const unsigned char* st = ring + c_slot * kStageBytes;
+      const unsigned char* irow = st + lane * kIdxRow;
+      const unsigned char* wrow = st + kIdxBox + lane * kWRow;
       const uint32_t cnt = min((uint32_t)kChunk, L - c * kChunk);
 #pragma unroll
-      for (uint32_t g = 0; g < 2; ++g) {  // 8 entries per group
+      for (uint32_t g = 0; g < kChunk / 8; ++g) {  // 8 entries per group
         if (g * 8 >= cnt) break;
-        const uint4 ca = *reinterpret_cast<const uint4*>(irow + (((2 * g) ^ sw64) << 4));
-        const uint4 cb = *reinterpret_cast<const uint4*>(irow + (((2 * g + 1) ^ sw64) << 4));
+        const uint4 ca = *reinterpret_cast<const uint4*>(irow + swz<kIdxRow>(lane, 2 * g));
+        const uint4 cb = *reinterpret_cast<const uint4*>(irow + swz<kIdxRow>(lane, 2 * g + 1));
         float wv[8];
         if constexpr (WK == W_F32) {
-          const unsigned char* wrow = st + kIdxBox + lane * 64;
-          const float4 wa = *reinterpret_cast<const float4*>(wrow + (((2 * g) ^ sw64) << 4));
-          const float4 wb = *reinterpret_cast<const float4*>(wrow + (((2 * g + 1) ^ sw64) << 4));
+          const float4 wa = *reinterpret_cast<const float4*>(wrow + swz<kWRow>(lane, 2 * g));
+          const float4 wb = *reinterpret_cast<const float4*>(wrow + swz<kWRow>(lane, 2 * g + 1));
           wv[0] = wa.x; wv[1] = wa.y; wv[2] = wa.z; wv[3] = wa.w;
           wv[4] = wb.x; wv[5] = wb.y; wv[6] = wb.z; wv[7] = wb.w;
         } else {
-          const unsigned char* wrow = st + kIdxBox + lane * 32;
-          const uint4 h = *reinterpret_cast<const uint4*>(wrow + ((g ^ sw32) << 4));
+          const uint4 h = *reinterpret_cast<const uint4*>(wrow + swz<kWRow>(lane, g));
           const uint32_t hw[4] = {h.x, h.y, h.z, h.w};
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
@@ -312,20 +350,11 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1)
         float prod[8];
 #pragma unroll
         for (uint32_t k = 0; k < 8; ++k) {
-          const uint32_t col = cv[k];
           float xv;
           if constexpr (XM == X_DENSE) {
-            xv = __ldg(p.x + col);
+            xv = __ldg(p.x + cv[k]);
           } else {
-            uint32_t bit;
-            if constexpr (XM == X_BITS_SMEM) {
-              bit = (s_x[col >> 5] >> (col & 31)) & 1u;
-            } else {
-              const uint32_t q = col >> gs;
-              bit = 0;
-              if ((s_x[q >> 5] >> (q & 31)) & 1u) bit = (__ldg(p.xbits + (col >> 5)) >> (col & 31)) & 1u;
-            }
-            xv = __uint_as_float(bit * 0x3f800000u);  // exactly 0.0f or 1.0f
+            xv = spike_value<XM>(s_x, p.xbits, cv[k], gs);
           }
           prod[k] = fmul(wv[k], xv);
         }
@@ -338,6 +367,9 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1)
       }
       __syncwarp();
       if (lane == 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      c_slot = (c_slot + 1 == nst) ? 0 : c_slot + 1;
+      c_phase ^= (c_slot == 0);
+      ++consumed;
       issue_next();
     }
     if (!ok) break;
@@ -379,7 +411,11 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1)
   if (!ok) {
     if (lane == 0) set_err(p.err, DEVERR_LOOKBACK_TIMEOUT);
     // Let every copy still in flight land before the shared memory is released.
-    for (uint32_t q = cseq; q < iseq; ++q) mbar_wait(&bars[wid][q % kStages], (q / kStages) & 1u);
+    for (; consumed < issued; ++consumed) {
+      mbar_wait(&bars[wid][c_slot], c_phase);
+      c_slot = (c_slot + 1 == nst) ? 0 : c_slot + 1;
+      c_phase ^= (c_slot == 0);
+    }
   }
   if constexpr (COMPACT) {
     // The last warp out rewinds the ticket counters for the next launch; the
@@ -421,7 +457,11 @@ template <int WK, int XM, int EPI, bool COMPACT>
 cudaError_t launch_t(const EllMaps& m, const RowLaunch& p, cudaStream_t stream) {
   auto kern = ell_stream_kernel<WK, XM, EPI, COMPACT>;
   const XPlan xp = plan_x(p);
-  const size_t smem = 1024 + (size_t)kEllWarps * kStages * WBox<WK>::kStage + xp.bytes;
+  constexpr size_t kStage = WBox<WK>::kStage;
+  // As many stages per warp as the shared memory left by the spike operand holds.
+  size_t nst = (kSmemBudget - xp.bytes) / ((size_t)kEllWarps * kStage);
+  nst = std::min<size_t>(std::max<size_t>(nst, kMinStages), kMaxStages);
+  const size_t smem = 1024 + (size_t)kEllWarps * nst * kStage + xp.bytes;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   if (!g_num_sms) {
@@ -432,12 +472,13 @@ cudaError_t launch_t(const EllMaps& m, const RowLaunch& p, cudaStream_t stream) 
   int per_sm = 0;
   if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kEllWarps * 32, smem)) != cudaSuccess)
     return e;
+  if (per_sm < 1) return cudaErrorInvalidConfiguration;
   const uint32_t tiles = (p.nlines + 31) / 32;
   const uint32_t want = (tiles + kEllWarps - 1) / kEllWarps;
-  const uint32_t grid = std::max(1u, std::min(want, (uint32_t)(std::max(per_sm, 1) * g_num_sms)));
+  const uint32_t grid = std::max(1u, std::min(want, (uint32_t)(per_sm * g_num_sms)));
   kern<<<grid, kEllWarps * 32, smem, stream>>>(*reinterpret_cast<const CUtensorMap*>(m.idx),
                                                *reinterpret_cast<const CUtensorMap*>(m.w), p, m.L, xp.gs,
-                                               xp.sum_words);
+                                               xp.sum_words, (uint32_t)nst);
   return cudaGetLastError();
 }
 
@@ -492,18 +533,19 @@ bool ell_encode(EllMaps& m, const uint32_t* col, const void* w, int wkind, uint6
   if ((reinterpret_cast<uintptr_t>(col) | reinterpret_cast<uintptr_t>(w)) & 15) return false;
   static_assert(sizeof(CUtensorMap) == sizeof(m.idx), "tensor map storage");
   cuuint64_t dims[2] = {L, nrows};
-  cuuint32_t box[2] = {kChunk, 32};
+  cuuint32_t box[2] = {(cuuint32_t)kChunk, 32};
   cuuint32_t estr[2] = {1, 1};
   cuuint64_t istride[1] = {(cuuint64_t)L * 4};
   CUresult r = enc(reinterpret_cast<CUtensorMap*>(m.idx), CU_TENSOR_MAP_DATA_TYPE_UINT32, 2,
                    const_cast<uint32_t*>(col), dims, istride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   swizzle_mode<kIdxRow>(), CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
   cuuint64_t wstride[1] = {(cuuint64_t)L * wbytes};
   r = enc(reinterpret_cast<CUtensorMap*>(m.w),
           wkind == W_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(w),
           dims, wstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-          wkind == W_F32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          wkind == W_F32 ? swizzle_mode<WBox<W_F32>::kRow>() : swizzle_mode<WBox<W_F16>::kRow>(),
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return false;
   m.L = L;

@@ -8,7 +8,10 @@
 
 namespace sparsl {
 
-constexpr int kEllWarps = 8;  // warps per persistent CTA
+#ifndef SPARSL_ELL_WARPS
+#define SPARSL_ELL_WARPS 12
+#endif
+constexpr int kEllWarps = SPARSL_ELL_WARPS;  // warps per persistent CTA
 
 // Compaction tiles of the TMA path: one warp's 32 rows.
 __host__ __device__ inline uint32_t ell_tiles(uint32_t nlines) { return (nlines + 31) / 32; }
