@@ -307,6 +307,9 @@ struct sparsl_op {
   int cur = 0;
   // compaction + trace
   DBuf idx_list, tile_flags, ticket, trace;
+  // SpMM work units (rows by descending length unless all rows are equal)
+  DBuf spmm_order, spmm_units, spmm_ctr;
+  uint32_t spmm_nunits = 0, spmm_rows_per_unit = 1;
   uint64_t trace_cap = 0, last_steps = 0;
   // staging for host-slice calls (kept apart from resident state, as the
   // reference CPU arm's slice API never touches its resident scratch)
@@ -357,6 +360,7 @@ RowLaunch fwd_launch(sparsl_op* op) {
   p.wkind = wkind_of(op->precision);
   p.nlines = op->nrows;
   p.err = op->err.d;
+  p.tile_ticket = op->ticket.as<uint32_t>();
   return p;
 }
 
@@ -763,6 +767,50 @@ int sparsl_op_prepare(sparsl_dev* d, const uint32_t* row_ptr, uint64_t row_ptr_l
     for (uint64_t r = 0; uniform && r <= nrows; ++r) uniform = (uint64_t)row_ptr[r] == r * L;
     if (uniform) ell_encode(op->ell, op->col.as<uint32_t>(), op->w.p, wkind_of(precision), nrows, (uint32_t)L);
   }
+  // SpMM work units.  Equal rows: fixed runs of rows.  Otherwise rows by
+  // descending length (ties by index), cut into units of >= kSpmmUnitNnz
+  // entries or a single row, at most kSpmmUnitRows rows each.
+  std::vector<uint32_t> sp_order, sp_units;
+  PALLOC(op->spmm_ctr, 16, false, "spmm counters");
+  cudaMemsetAsync(op->spmm_ctr.p, 0, op->spmm_ctr.bytes, op->stream);
+  if (nrows) {
+    const uint32_t maxlen = (uint32_t)sh.max_row_nnz;
+    uint32_t minlen = maxlen;
+    for (uint64_t r = 0; r < nrows && minlen; ++r) minlen = std::min(minlen, row_ptr[r + 1] - row_ptr[r]);
+    if (minlen == maxlen) {
+      const uint32_t R = std::max(1u, std::min(kSpmmUnitRows, kSpmmUnitNnz / std::max(maxlen, 1u)));
+      op->spmm_rows_per_unit = R;
+      op->spmm_nunits = (uint32_t)((nrows + R - 1) / R);
+    } else {
+      sp_order.resize(nrows);
+      auto len = [&](uint64_t r) { return row_ptr[r + 1] - row_ptr[r]; };
+      if ((uint64_t)maxlen <= 4 * nrows + 4096) {
+        // Counting sort by length (descending, stable).
+        std::vector<uint32_t> start((size_t)maxlen + 2, 0);
+        for (uint64_t r = 0; r < nrows; ++r) ++start[maxlen - len(r) + 1];
+        for (size_t k = 1; k < start.size(); ++k) start[k] += start[k - 1];
+        for (uint64_t r = 0; r < nrows; ++r) sp_order[start[maxlen - len(r)]++] = (uint32_t)r;
+      } else {
+        for (uint64_t r = 0; r < nrows; ++r) sp_order[r] = (uint32_t)r;
+        std::stable_sort(sp_order.begin(), sp_order.end(), [&](uint32_t a, uint32_t b) { return len(a) > len(b); });
+      }
+      sp_units.push_back(0);
+      uint64_t acc = 0, rows_in = 0;
+      for (uint64_t i = 0; i < nrows; ++i) {
+        acc += row_ptr[sp_order[i] + 1] - row_ptr[sp_order[i]];
+        ++rows_in;
+        if (acc >= kSpmmUnitNnz || rows_in >= kSpmmUnitRows || i + 1 == nrows) {
+          sp_units.push_back((uint32_t)(i + 1));
+          acc = rows_in = 0;
+        }
+      }
+      op->spmm_nunits = (uint32_t)(sp_units.size() - 1);
+      PALLOC(op->spmm_order, nrows * 4, false, "spmm row order");
+      PALLOC(op->spmm_units, sp_units.size() * 4, false, "spmm units");
+      cudaMemcpyAsync(op->spmm_order.p, sp_order.data(), nrows * 4, cudaMemcpyHostToDevice, op->stream);
+      cudaMemcpyAsync(op->spmm_units.p, sp_units.data(), sp_units.size() * 4, cudaMemcpyHostToDevice, op->stream);
+    }
+  }
   rc = wait_op(op, "prepare");  // host vectors above must outlive the copies
   if (rc != SPARSL_OK) return bail(rc);
 #undef PALLOC
@@ -777,7 +825,8 @@ void sparsl_op_destroy(sparsl_op* op) {
   DBuf* bufs[] = {&op->row_ptr, &op->col,     &op->w,       &op->col_ptr, &op->csc_row, &op->csc_eidx,
                   &op->rx,      &op->rxs[0],  &op->rxs[1],  &op->ry,      &op->rv,      &op->rth,
                   &op->rspk,    &op->idx_list, &op->tile_flags, &op->ticket, &op->trace, &op->sx,
-                  &op->sbits,   &op->sy,      &op->sv,      &op->sth,     &op->sspk};
+                  &op->sbits,   &op->sy,      &op->sv,      &op->sth,     &op->sspk,
+                  &op->spmm_order, &op->spmm_units, &op->spmm_ctr};
   for (DBuf* b : bufs) dfree(*b);
   op->err.release();
   if (op->ev) cudaEventDestroy(op->ev);
@@ -883,6 +932,24 @@ int sparsl_op_spmv_t(sparsl_op* op, const float* x, uint64_t x_len, float* y, ui
   return finish(op, "spmv_t");
 }
 
+static SpmmLaunch spmm_launch(sparsl_op* op, const float* x, float* y, uint32_t n_vec) {
+  SpmmLaunch p;
+  p.ptr = op->row_ptr.as<uint32_t>();
+  p.idx = op->col.as<uint32_t>();
+  p.w = op->w.p;
+  p.wkind = wkind_of(op->precision);
+  p.x = x;
+  p.y = y;
+  p.nrows = op->nrows;
+  p.n_vec = n_vec;
+  p.order = op->spmm_order.p ? op->spmm_order.as<uint32_t>() : nullptr;
+  p.unit_start = op->spmm_units.p ? op->spmm_units.as<uint32_t>() : nullptr;
+  p.nunits = op->spmm_nunits;
+  p.rows_per_unit = op->spmm_rows_per_unit;
+  p.ctr = op->spmm_ctr.as<uint32_t>();
+  return p;
+}
+
 int sparsl_op_spmm(sparsl_op* op, const float* x, uint64_t x_len, uint64_t n_vec, float* y, uint64_t y_len) {
   ADMIT();
   if (n_vec == 0) return fail(SPARSL_ERR_LENGTH, "n_vec", "`n_vec` must have length 1, got 0");
@@ -902,9 +969,8 @@ int sparsl_op_spmm(sparsl_op* op, const float* x, uint64_t x_len, uint64_t n_vec
   ALLOC(op->sy, need_y * 4 + 16, true, "Y staging");
   if (need_x) CK("spmm", cudaMemcpyAsync(op->sx.p, x, need_x * 4, cudaMemcpyHostToDevice, op->stream));
   CK("spmm", cudaMemcpyAsync(op->sy.p, y, need_y * 4, cudaMemcpyHostToDevice, op->stream));
-  CK("spmm", launch_spmm(op->row_ptr.as<uint32_t>(), op->col.as<uint32_t>(), op->w.p, wkind_of(op->precision),
-                         op->sx.as<float>(), op->sy.as<float>(), op->nrows, (uint32_t)n_vec, op->dev->sm_count,
-                         op->stream));
+  CK("spmm", launch_spmm(spmm_launch(op, op->sx.as<float>(), op->sy.as<float>(), (uint32_t)n_vec),
+                         op->dev->sm_count, op->stream));
   CK("spmm", cudaMemcpyAsync(y, op->sy.p, need_y * 4, cudaMemcpyDeviceToHost, op->stream));
   return finish(op, "spmm");
 }
@@ -1208,8 +1274,7 @@ int sparsl_op_spmm_device(sparsl_op* op, const float* d_x, uint64_t n_vec, float
   if (n_vec == 0 || n_vec > 0xffffffffull) return fail(SPARSL_ERR_LENGTH, "n_vec", "n_vec out of range");
   CK("spmm", cudaSetDevice(op->dev->ordinal));
   if (n_vec == 1) return sparsl_op_spmv_device(op, d_x, d_y, stream);
-  CK("spmm", launch_spmm(op->row_ptr.as<uint32_t>(), op->col.as<uint32_t>(), op->w.p, wkind_of(op->precision), d_x,
-                         d_y, op->nrows, (uint32_t)n_vec, op->dev->sm_count, pick(op, stream)));
+  CK("spmm", launch_spmm(spmm_launch(op, d_x, d_y, (uint32_t)n_vec), op->dev->sm_count, pick(op, stream)));
   return SPARSL_OK;
 }
 
@@ -1257,6 +1322,10 @@ struct sparsl_net {
   int rank = 0, nranks = 1;
   cudaStream_t stream = nullptr;
   cudaEvent_t ev = nullptr;
+  // Blocks alternate between `stream` and `side` within a tick, so one
+  // block's persistent kernel starts on the SMs the other's tail frees.
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   ErrWord err;
   DBuf xs[2], trace;
   int cur = 0;
@@ -1319,7 +1388,10 @@ int sparsl_net_create(sparsl_dev* d, sparsl_op* const* blocks, uint32_t n_blocks
     return code;
   };
   if (cudaStreamCreateWithFlags(&net->stream, cudaStreamNonBlocking) != cudaSuccess ||
-      cudaEventCreateWithFlags(&net->ev, cudaEventDisableTiming) != cudaSuccess || net->err.init() != cudaSuccess)
+      cudaStreamCreateWithFlags(&net->side, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&net->ev, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&net->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&net->ev_join, cudaEventDisableTiming) != cudaSuccess || net->err.init() != cudaSuccess)
     return bail(fail(SPARSL_ERR_BACKEND, "stream creation failed", "could not create net stream"));
   for (int i = 0; i < 2; ++i) {
     if (dalloc(net->xs[i], net->words * 4 + 16, true, net->stream) != cudaSuccess)
@@ -1373,7 +1445,11 @@ void sparsl_net_destroy(sparsl_net* net) {
   dfree(net->xs[1]);
   dfree(net->trace);
   net->err.release();
+  if (net->side) cudaStreamSynchronize(net->side);
   if (net->ev) cudaEventDestroy(net->ev);
+  if (net->ev_fork) cudaEventDestroy(net->ev_fork);
+  if (net->ev_join) cudaEventDestroy(net->ev_join);
+  if (net->side) cudaStreamDestroy(net->side);
   if (net->stream) cudaStreamDestroy(net->stream);
   delete net;
 }
@@ -1410,6 +1486,11 @@ static int net_enqueue(sparsl_net* net, float decay, float v_reset, float dtheta
     uint32_t* dst = net->xs[net->cur ^ 1].as<uint32_t>();
     const bool tm = net->timing && t < net->ev_a.size();
     if (tm) CK("net_steps", cudaEventRecord(net->ev_a[t], net->stream));
+    const bool fork = net->blocks.size() > 1;
+    if (fork) {
+      CK("net_steps", cudaEventRecord(net->ev_fork, net->stream));
+      CK("net_steps", cudaStreamWaitEvent(net->side, net->ev_fork, 0));
+    }
     for (size_t b = 0; b < net->blocks.size(); ++b) {
       sparsl_op* op = net->blocks[b];
       if (!op->nrows) continue;
@@ -1418,7 +1499,11 @@ static int net_enqueue(sparsl_net* net, float decay, float v_reset, float dtheta
       lif_resident_launch(op, p, decay, v_reset, dtheta);
       p.out_bits = dst + (net->row_offset + net->block_off[b]) / 32;
       p.err = net->err.d;
-      CK("net_steps", launch_fwd(op, p, net->stream));
+      CK("net_steps", launch_fwd(op, p, (b & 1) ? net->side : net->stream));
+    }
+    if (fork) {
+      CK("net_steps", cudaEventRecord(net->ev_join, net->side));
+      CK("net_steps", cudaStreamWaitEvent(net->stream, net->ev_join, 0));
     }
     if (tm) CK("net_steps", cudaEventRecord(net->ev_b[t], net->stream));
     if (net->nranks > 1) {

@@ -236,7 +236,6 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1)
 
   const uint32_t ntiles = (p.nlines + 31) / 32;
   const uint32_t nch = (L + kChunk - 1) / kChunk;
-  const uint32_t gwarp = blockIdx.x * kEllWarps + wid;
   const uint32_t nwarps = gridDim.x * kEllWarps;
   const uint64_t pol = evict_first_policy();
 
@@ -246,19 +245,14 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1)
   }
   __syncwarp();
 
-  // Tile sequence: dynamic tickets when tiles must finish in start order for
-  // the compaction look-back (a ticket is only taken by a running warp, so a
-  // tile only ever waits on tiles whose owners are running); a fixed stride
-  // otherwise.
-  uint32_t k_next = 0;
+  // Tile sequence: dynamic tickets.  They balance the load when CTAs start
+  // at different times (another kernel's tail still holds some SMs), and they
+  // keep the compaction look-back safe: a ticket is only taken by a running
+  // warp, so a tile only ever waits on tiles whose owners are running.
   auto grab = [&]() -> uint32_t {
-    if constexpr (COMPACT) {
-      uint32_t t = 0;
-      if (lane == 0) t = atomicAdd(p.tile_ticket, 1u);
-      return __shfl_sync(0xffffffffu, t, 0);
-    } else {
-      return gwarp + (k_next++) * nwarps;
-    }
+    uint32_t t = 0;
+    if (lane == 0) t = atomicAdd(p.tile_ticket, 1u);
+    return __shfl_sync(0xffffffffu, t, 0);
   };
 
   // Issue state (warp-uniform): next tile / chunk, ring slot, chunks issued.
@@ -417,15 +411,13 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1)
       c_phase ^= (c_slot == 0);
     }
   }
-  if constexpr (COMPACT) {
-    // The last warp out rewinds the ticket counters for the next launch; the
-    // epoch-tagged flags need no clearing.
-    if (lane == 0) {
-      __threadfence();
-      if (atomicAdd(p.tile_ticket + 1, 1u) == nwarps - 1) {
-        atomicExch(p.tile_ticket, 0u);
-        atomicExch(p.tile_ticket + 1, 0u);
-      }
+  // The last warp out rewinds the ticket counters for the next launch; the
+  // epoch-tagged flags need no clearing.
+  if (lane == 0) {
+    __threadfence();
+    if (atomicAdd(p.tile_ticket + 1, 1u) == nwarps - 1) {
+      atomicExch(p.tile_ticket, 0u);
+      atomicExch(p.tile_ticket + 1, 0u);
     }
   }
 }
@@ -455,6 +447,7 @@ int g_num_sms = 0;
 
 template <int WK, int XM, int EPI, bool COMPACT>
 cudaError_t launch_t(const EllMaps& m, const RowLaunch& p, cudaStream_t stream) {
+  if (!p.tile_ticket) return cudaErrorInvalidValue;
   auto kern = ell_stream_kernel<WK, XM, EPI, COMPACT>;
   const XPlan xp = plan_x(p);
   constexpr size_t kStage = WBox<WK>::kStage;

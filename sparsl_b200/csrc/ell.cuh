@@ -28,7 +28,9 @@ struct EllMaps {
 // 2-D TMA boxes (the caller keeps the generic row-fold path).
 bool ell_encode(EllMaps& m, const uint32_t* col, const void* w, int wkind, uint64_t nrows, uint32_t L);
 
-// Same contract as launch_rows for a forward (CSR) launch; p.ptr is unused.
+// Same contract as launch_rows for a forward (CSR) launch; p.ptr is unused
+// and p.tile_ticket (two words, zero on entry, left zero) is required: tiles
+// are handed out by ticket.  Launches sharing it must be stream-ordered.
 // Compaction flags are tagged with p.epoch (nonzero, below 2^30, different
 // from the previous launch's) instead of being cleared between launches.
 cudaError_t launch_ell(const EllMaps& m, const RowLaunch& p, cudaStream_t stream);

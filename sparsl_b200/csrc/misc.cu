@@ -6,44 +6,85 @@ namespace sparsl {
 namespace {
 
 // Y += A X for batch-minor X[ncols][n_vec] / Y[nrows][n_vec].  One warp owns
-// one row; lane l folds vectors l and l + 32 of each 64-vector block, so every
-// (row, vector) output is its own left fold in edge order, as row_dot_batched
-// computes it (src/backend/mod.rs:2331-2360).  Each step loads one X row slice
-// with a coalesced 128-byte access per 32 vectors.
+// one row at a time; lane l folds vectors l and l + 32 of each 64-vector
+// block, so every (row, vector) output is its own left fold in edge order, as
+// row_dot_batched computes it (src/backend/mod.rs:2331-2360).  Each step reads
+// one X row slice with a coalesced 128-byte access per 32 vectors; eight
+// steps' gathers are issued before their dependent adds.  Warps are
+// persistent and take work units from a counter, long rows first.
 template <int WK>
-__global__ void __launch_bounds__(256) spmm_kernel(const uint32_t* __restrict__ ptr,
-                                                   const uint32_t* __restrict__ idx, const void* w,
-                                                   const float* __restrict__ x, float* __restrict__ y,
-                                                   uint32_t nrows, uint32_t n_vec) {
+__global__ void __launch_bounds__(256) spmm_kernel(const SpmmLaunch p) {
   const int lane = threadIdx.x & 31;
-  const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const uint32_t nwarps = (gridDim.x * blockDim.x) >> 5;
-  for (uint32_t r = warp; r < nrows; r += nwarps) {
-    const uint32_t s = __ldg(ptr + r), e = __ldg(ptr + r + 1);
-    for (uint32_t vb = 0; vb < n_vec; vb += 64) {
-      const uint32_t v0 = vb + lane, v1 = vb + 32 + lane;
-      const bool ok0 = v0 < n_vec, ok1 = v1 < n_vec;
-      float a0 = 0.0f, a1 = 0.0f;
-      for (uint32_t e0 = s; e0 < e; e0 += 32) {
-        const uint32_t ee = e0 + lane;
-        uint32_t c = 0;
-        float wv = 0.0f;
-        if (ee < e) {
-          c = __ldg(idx + ee);
-          wv = load_weight<WK>(w, ee);
+  const uint32_t nv = p.n_vec;
+  const float* __restrict__ x = p.x;
+  while (true) {
+    uint32_t u = 0;
+    if (lane == 0) u = atomicAdd(p.ctr, 1u);
+    u = __shfl_sync(0xffffffffu, u, 0);
+    if (u >= p.nunits) break;
+    uint32_t pb, pe;
+    if (p.order) {
+      pb = __ldg(p.unit_start + u);
+      pe = __ldg(p.unit_start + u + 1);
+    } else {
+      pb = u * p.rows_per_unit;
+      pe = min(p.nrows, pb + p.rows_per_unit);
+    }
+    for (uint32_t pos = pb; pos < pe; ++pos) {
+      const uint32_t r = p.order ? __ldg(p.order + pos) : pos;
+      const uint32_t s = __ldg(p.ptr + r), e = __ldg(p.ptr + r + 1);
+      for (uint32_t vb = 0; vb < nv; vb += 64) {
+        const uint32_t v0 = vb + lane, v1 = vb + 32 + lane;
+        const bool ok0 = v0 < nv, ok1 = v1 < nv;
+        float a0 = 0.0f, a1 = 0.0f;
+        for (uint32_t e0 = s; e0 < e; e0 += 32) {
+          const uint32_t ee = e0 + lane;
+          uint32_t c = 0;
+          float wv = 0.0f;
+          if (ee < e) {
+            c = __ldg(p.idx + ee);
+            wv = load_weight<WK>(p.w, ee);
+          }
+          const uint32_t cnt = min(32u, e - e0);
+          uint32_t j = 0;
+          for (; j + 8 <= cnt; j += 8) {
+            float xa[8], xb[8], wj[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const uint32_t cj = __shfl_sync(0xffffffffu, c, j + k);
+              wj[k] = __shfl_sync(0xffffffffu, wv, j + k);
+              const float* xr = x + (uint64_t)cj * nv;
+              xa[k] = ok0 ? __ldg(xr + v0) : 0.0f;
+              xb[k] = ok1 ? __ldg(xr + v1) : 0.0f;
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              a0 = fadd(a0, fmul(wj[k], xa[k]));
+              a1 = fadd(a1, fmul(wj[k], xb[k]));
+            }
+          }
+          for (; j < cnt; ++j) {
+            const uint32_t cj = __shfl_sync(0xffffffffu, c, j);
+            const float wj = __shfl_sync(0xffffffffu, wv, j);
+            const float* xr = x + (uint64_t)cj * nv;
+            if (ok0) a0 = fadd(a0, fmul(wj, __ldg(xr + v0)));
+            if (ok1) a1 = fadd(a1, fmul(wj, __ldg(xr + v1)));
+          }
         }
-        const uint32_t cnt = min(32u, e - e0);
-        for (uint32_t j = 0; j < cnt; ++j) {
-          const uint32_t cj = __shfl_sync(0xffffffffu, c, j);
-          const float wj = __shfl_sync(0xffffffffu, wv, j);
-          const float* xr = x + (uint64_t)cj * n_vec;
-          if (ok0) a0 = fadd(a0, fmul(wj, __ldg(xr + v0)));
-          if (ok1) a1 = fadd(a1, fmul(wj, __ldg(xr + v1)));
-        }
+        // An empty row still adds its 0.0 fold: -0.0 + 0.0 is +0.0.
+        float* yr = p.y + (uint64_t)r * nv;
+        if (ok0) yr[v0] = fadd(yr[v0], a0);
+        if (ok1) yr[v1] = fadd(yr[v1], a1);
       }
-      float* yr = y + (uint64_t)r * n_vec;
-      if (ok0) yr[v0] = fadd(yr[v0], a0);
-      if (ok1) yr[v1] = fadd(yr[v1], a1);
+    }
+  }
+  // The last warp out rewinds the counters for the next launch.
+  if (lane == 0) {
+    __threadfence();
+    if (atomicAdd(p.ctr + 1, 1u) == nwarps - 1) {
+      atomicExch(p.ctr, 0u);
+      atomicExch(p.ctr + 1, 0u);
     }
   }
 }
@@ -119,17 +160,24 @@ inline unsigned grid_for(uint64_t n, unsigned block, unsigned cap = 148 * 16) {
 
 }  // namespace
 
-cudaError_t launch_spmm(const uint32_t* ptr, const uint32_t* idx, const void* w, int wkind, const float* x,
-                        float* y, uint32_t nrows, uint32_t n_vec, int sm_count, cudaStream_t s) {
-  if (nrows == 0) return cudaSuccess;
+cudaError_t launch_spmm(const SpmmLaunch& p, int sm_count, cudaStream_t s) {
+  if (p.nrows == 0 || p.nunits == 0) return cudaSuccess;
   const unsigned block = 256;
-  uint64_t blocks = ((uint64_t)nrows * 32 + block - 1) / block;
-  const uint64_t cap = (uint64_t)sm_count * 8;
-  if (blocks > cap) blocks = cap;
-  switch (wkind) {
-    case W_F16: spmm_kernel<W_F16><<<(unsigned)blocks, block, 0, s>>>(ptr, idx, w, x, y, nrows, n_vec); break;
-    case W_BF16: spmm_kernel<W_BF16><<<(unsigned)blocks, block, 0, s>>>(ptr, idx, w, x, y, nrows, n_vec); break;
-    default: spmm_kernel<W_F32><<<(unsigned)blocks, block, 0, s>>>(ptr, idx, w, x, y, nrows, n_vec); break;
+  int per_sm = 0;
+  cudaError_t e;
+  switch (p.wkind) {
+    case W_F16: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, spmm_kernel<W_F16>, block, 0); break;
+    case W_BF16: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, spmm_kernel<W_BF16>, block, 0); break;
+    default: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, spmm_kernel<W_F32>, block, 0); break;
+  }
+  if (e != cudaSuccess) return e;
+  const uint64_t want = ((uint64_t)p.nunits * 32 + block - 1) / block;
+  const uint64_t cap = (uint64_t)sm_count * (per_sm > 0 ? per_sm : 1);
+  const unsigned blocks = (unsigned)(want < cap ? want : cap);
+  switch (p.wkind) {
+    case W_F16: spmm_kernel<W_F16><<<blocks, block, 0, s>>>(p); break;
+    case W_BF16: spmm_kernel<W_BF16><<<blocks, block, 0, s>>>(p); break;
+    default: spmm_kernel<W_F32><<<blocks, block, 0, s>>>(p); break;
   }
   return cudaGetLastError();
 }

@@ -18,8 +18,31 @@ struct CanarySet {
   int count = 0;
 };
 
-cudaError_t launch_spmm(const uint32_t* ptr, const uint32_t* idx, const void* w, int wkind, const float* x,
-                        float* y, uint32_t nrows, uint32_t n_vec, int sm_count, cudaStream_t s);
+// One SpMM launch, Y += A X (batch-minor X[ncols][n_vec], Y[nrows][n_vec]).
+// Rows are handed out in work units: unit u covers positions
+// [unit_start[u], unit_start[u+1]) of `order` (rows by descending length, so
+// the long rows start first and the short ones fill the tail), or, with no
+// order, the natural rows [u*rows_per_unit, ...).  `ctr` is two words, zero
+// on entry and left zero; launches sharing it must be stream-ordered.
+struct SpmmLaunch {
+  const uint32_t* ptr = nullptr;
+  const uint32_t* idx = nullptr;
+  const void* w = nullptr;
+  int wkind = 0;
+  const float* x = nullptr;
+  float* y = nullptr;
+  uint32_t nrows = 0, n_vec = 0;
+  const uint32_t* order = nullptr;       // nrows entries, or null
+  const uint32_t* unit_start = nullptr;  // nunits + 1 entries when order is set
+  uint32_t nunits = 0, rows_per_unit = 1;
+  uint32_t* ctr = nullptr;
+};
+
+// Work units over rows sorted by descending length: each unit holds at least
+// kSpmmUnitNnz entries or is a single row, and at most kSpmmUnitRows rows.
+constexpr uint32_t kSpmmUnitNnz = 512, kSpmmUnitRows = 256;
+
+cudaError_t launch_spmm(const SpmmLaunch& p, int sm_count, cudaStream_t s);
 cudaError_t launch_lif_integrate(float* v, float* theta, const float* cur, uint8_t* spk, uint64_t n,
                                  float decay, float v_reset, float dtheta, cudaStream_t s);
 cudaError_t launch_pack(const uint8_t* spk, uint64_t n, uint32_t* out, uint64_t out_words, cudaStream_t s);

@@ -367,3 +367,37 @@ def test_device_reports_b200(cuda_device):
     assert cuda_device.backend() is S.Backend.Cuda
     assert "B200" in cuda_device.device_name()
     assert S.Backend.Cuda in S.available_backends()
+
+
+@pytest.mark.parametrize("kind", ["power_law", "uniform"])
+@pytest.mark.parametrize("n_vec", [3, 64, 100])
+def test_spmm_work_units_bit_exact(O, cuda_device, kind, n_vec):
+    """Rows handed out in work units (longest rows first, or runs of equal
+    rows): empty and 2000-entry rows, -0.0 outputs, and two launches in a row
+    (the unit counters must rewind)."""
+    r = np.random.default_rng(n_vec + len(kind))
+    nrows, ncols = 3000, 5000
+    if kind == "power_law":
+        lens = np.minimum(r.zipf(1.5, nrows), 2000)
+        lens[::97] = 0
+    else:
+        lens = np.full(nrows, 8)
+    rp = np.zeros(nrows + 1, np.uint64)
+    np.cumsum(lens, out=rp[1:])
+    col = np.concatenate([np.sort(r.choice(ncols, k, replace=False)) for k in lens]).astype(np.uint32)
+    csr = O.Csr(rp.astype(np.uint32), col, ncols)
+    w = r.uniform(-1, 1, col.size).astype(np.float32)
+    X = r.uniform(-1, 1, ncols * n_vec).astype(np.float32)
+    Y0 = r.uniform(-1, 1, nrows * n_vec).astype(np.float32)
+    Y0[::5] = -0.0
+    op = cuda_device.prepare(_scsr(csr), ncols, w)
+    got = Y0.copy()
+    op.spmm(X, n_vec, got)
+    op.spmm(X, n_vec, got)
+    want = O.spmm(csr, w, X, n_vec, Y0.copy())
+    want = O.spmm(csr, w, X, n_vec, want)
+    assert_bits_equal(got, want, f"spmm {kind} n_vec={n_vec}")
+    empty = np.flatnonzero(lens == 0)
+    if empty.size:  # -0.0 + 0.0 + 0.0 is +0.0 on an empty row
+        row = got.reshape(nrows, n_vec)[empty]
+        assert not np.any(np.signbit(row) & (row == 0))
