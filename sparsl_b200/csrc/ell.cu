@@ -41,6 +41,12 @@ namespace {
 constexpr int kChunk = SPARSL_ELL_CHUNK;
 static_assert(kChunk == 16 || kChunk == 32, "chunk of 16 or 32 entries");
 constexpr int kMinStages = 2, kMaxStages = 8;
+// Dense x: gathers go through L1/L2, so fewer stages (and more CTAs per SM)
+// can hide more gather latency than deeper streaming does.
+#ifndef SPARSL_ELL_DENSE_STAGES
+#define SPARSL_ELL_DENSE_STAGES 3
+#endif
+constexpr int kDenseStages = SPARSL_ELL_DENSE_STAGES;
 constexpr int kIdxRow = kChunk * 4;            // bytes of one row of a column box
 constexpr int kIdxBox = 32 * kIdxRow;          // column box: 32 rows x kChunk entries
 constexpr uint32_t kSumMaxWords = 16384;       // 64 KiB summary
@@ -453,7 +459,7 @@ cudaError_t launch_t(const EllMaps& m, const RowLaunch& p, cudaStream_t stream) 
   constexpr size_t kStage = WBox<WK>::kStage;
   // As many stages per warp as the shared memory left by the spike operand holds.
   size_t nst = (kSmemBudget - xp.bytes) / ((size_t)kEllWarps * kStage);
-  nst = std::min<size_t>(std::max<size_t>(nst, kMinStages), kMaxStages);
+  nst = std::min<size_t>(std::max<size_t>(nst, kMinStages), XM == X_DENSE ? kDenseStages : kMaxStages);
   const size_t smem = 1024 + (size_t)kEllWarps * nst * kStage + xp.bytes;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;

@@ -9,9 +9,14 @@ namespace {
 // one row at a time; lane l folds vectors l and l + 32 of each 64-vector
 // block, so every (row, vector) output is its own left fold in edge order, as
 // row_dot_batched computes it (src/backend/mod.rs:2331-2360).  Each step reads
-// one X row slice with a coalesced 128-byte access per 32 vectors; eight
+// one X row slice with a coalesced 128-byte access per 32 vectors; kSpmmDepth
 // steps' gathers are issued before their dependent adds.  Warps are
 // persistent and take work units from a counter, long rows first.
+#ifndef SPARSL_SPMM_DEPTH
+#define SPARSL_SPMM_DEPTH 4
+#endif
+constexpr int kSpmmDepth = SPARSL_SPMM_DEPTH;  // gathers in flight per lane and vector
+
 template <int WK>
 __global__ void __launch_bounds__(256) spmm_kernel(const SpmmLaunch p) {
   const int lane = threadIdx.x & 31;
@@ -48,10 +53,10 @@ __global__ void __launch_bounds__(256) spmm_kernel(const SpmmLaunch p) {
           }
           const uint32_t cnt = min(32u, e - e0);
           uint32_t j = 0;
-          for (; j + 8 <= cnt; j += 8) {
-            float xa[8], xb[8], wj[8];
+          for (; j + kSpmmDepth <= cnt; j += kSpmmDepth) {
+            float xa[kSpmmDepth], xb[kSpmmDepth], wj[kSpmmDepth];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
+            for (int k = 0; k < kSpmmDepth; ++k) {
               const uint32_t cj = __shfl_sync(0xffffffffu, c, j + k);
               wj[k] = __shfl_sync(0xffffffffu, wv, j + k);
               const float* xr = x + (uint64_t)cj * nv;
@@ -59,7 +64,7 @@ __global__ void __launch_bounds__(256) spmm_kernel(const SpmmLaunch p) {
               xb[k] = ok1 ? __ldg(xr + v1) : 0.0f;
             }
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
+            for (int k = 0; k < kSpmmDepth; ++k) {
               a0 = fadd(a0, fmul(wj[k], xa[k]));
               a1 = fadd(a1, fmul(wj[k], xb[k]));
             }
