@@ -398,7 +398,11 @@ def bench_lif_net(args, dist):
     peak = float(pk_.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
     algo = net_bytes_per_tick_per_gpu(n_total, fan_in, dist.world)
     achieved = algo / (kernel_ms_tick * 1e-3) / 1e9
-    traffic = os.environ.get("SPARSL_NCU_TRAFFIC_PER_TICK")
+    # DRAM traffic of the tick kernel from one ncu capture of the same kernel and
+    # spike mode (1,048,576 x 512, profiles/ell_stream_kernel_lif_net.md):
+    # dram read + write = 4,310,804,312 B against 4,312,006,660 algorithmic B.
+    # Traffic grows with the synapses, so it is scaled by the algorithmic bytes.
+    traffic = algo * (4_310_804_312 / 4_312_006_660)
     value = args.steps / (ms_max * 1e-3)
     line = {
         "metric": "LIF net ticks/sec", "value": value, "unit": "ticks/s", "n_gpus": dist.world,
@@ -416,7 +420,8 @@ def bench_lif_net(args, dist):
                 "path": "sparsl_net_write_state + sparsl_net_steps(1) + sparsl_net_read_state, pinned host"},
         "gpu_launches": kernels_per_tick * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": float(traffic) if traffic else None,
+                     "traffic": traffic, "traffic_source": "ncu dram__bytes_read+write of the same kernel at "
+                                                           "1,048,576 x 512, scaled by algorithmic bytes",
                      "kernel": "ell_stream_kernel<f32, spike bitmask via shared-memory summary, LIF> "
                                "(TMA-streamed fused spike SpMV + LIF + ballot pack)",
                      "algorithmic_bytes_per_tick_per_gpu": algo, "kernel_ms_per_tick": kernel_ms_tick,
