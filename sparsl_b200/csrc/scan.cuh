@@ -6,36 +6,26 @@
 
 namespace sparsl {
 
-constexpr int kScanThreads = 256;  // threads per tile
+constexpr int kScanThreads = 256;  // sub-chunk threads per tile (8 warps)
+constexpr int kScanBlock = kScanThreads + 32;  // plus one look-back warp
 constexpr int kScanK = 16;         // elements per thread (one sub-chunk)
 constexpr int kScanTile = kScanThreads * kScanK;
 constexpr int kScanWarmSub = 8;    // warm-up of an in-tile guess, in sub-chunks
-constexpr int kScanHaloSub = 16;   // warm-up of a tile's first threads, reaching into the previous tile
+constexpr int kScanHaloSub = 32;   // warm-up of a tile's first warp, reaching into the previous tile
 constexpr int kScanHalo = kScanHaloSub * kScanK;
-
-// Per-tile look-back record.  Written by the tile, read by its successors.
-struct ScanTileRecord {
-  uint32_t status;  // 0 none, 1 aggregate, 2 inclusive
-  uint32_t tab;     // transfer table of the multiplier chain (8 x 4 bits)
-  uint32_t pad;
-  float av;         // inclusive: multiplier value of the tile's last element
-  float agg[4];     // aggregate: full (a, b), head (a, b)
-  float inc[4];     // inclusive: full (a, b), head (a, b)
-};
 
 // Scratch the scan needs, sized by scan_scratch_bytes(n).  All of it is
 // left in its zero state (or self-resetting) after each call.
 struct ScanScratch {
-  ScanTileRecord* rec;      // ntiles
+  unsigned long long* flags;  // ntiles look-back words: [33:32] status, [31:0] payload
   uint32_t* ticket;         // [0] tile ticket, [1] done counter
-  uint32_t* arrive;         // ntiles: boundary arrival counters (self-resetting)
   float* assumed;           // 2 * ntiles: thread 0's assumed incoming state
   float* last;              // 2 * ntiles: each tile's last output state
   uint32_t* mis_bits;       // ntiles * 8 words: in-tile sub-chunk mismatches
   uint32_t* xmis;           // ntiles: tile-boundary mismatch
   uint32_t* tile_bits;      // ceil(ntiles / 32) words: any mismatch in tile
   uint32_t* repair_stats;   // [0] repaired elements, [1] repair segments
-  unsigned long long* timeline = nullptr;  // optional: 8 globaltimer stamps per tile
+  unsigned long long* timeline = nullptr;  // optional: 16 words per tile (phase stamps, counters)
 };
 
 size_t scan_scratch_bytes(uint64_t n);
