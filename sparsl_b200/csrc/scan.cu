@@ -19,12 +19,13 @@
 //    predict.  Outside that domain one thread multiplies element by element.
 //  * Offset chain B (b' = x.a * b + x.b) -- speculated, with no look-back.
 //    The recurrence contracts: B's dependence on its value n elements earlier
-//    is a product of n multipliers.  So warp 0 replays the 512 elements before
-//    its sub-chunk from B = 0, and the other warps replay 128 elements from an
-//    in-tile block-scan guess (which leaves out only the tile's unknown entry
-//    B, already contracted over >= 384 elements).  For contracting data that
-//    lands on the sequential trajectory bit for bit; the look-back warp works
-//    meanwhile.
+//    is a product of n multipliers.  So each thread replays the elements
+//    before its sub-chunk (128; 256 for a tile's thread 0) from a
+//    tree-composed guess that assumes B = 0 at the start of the tile, or of a
+//    512-element halo reaching into the previous tile; that assumption is
+//    contracted over >= 256 elements and the replay removes the tree's
+//    rounding.  For contracting data this lands on the sequential trajectory
+//    bit for bit; the look-back warp works meanwhile.
 //  * Verify: each thread's assumed incoming state is compared bitwise with the
 //    final state its predecessor actually produced.  If every adjacent pair
 //    agrees, the whole output equals the sequential fold by induction.
@@ -172,6 +173,7 @@ __global__ void __launch_bounds__(kScanBlock, 5) scan_main(const float2* __restr
   // ---- 2. sub-chunk aggregates (guesses) and multiplier tables; block scan
   //         of the guesses (the look-back warp composes the tables) ----
   Aff inc{1.f, 0.f};
+  float w0_guess = 0.f;  // warp 0: guessed B at the start of its warm-up
   if (!lb_warp) {
     const float2* row = sm + (t + kScanHaloSub) * kRowStride;
     Aff agg{row[0].x, row[0].y};
@@ -198,9 +200,26 @@ __global__ void __launch_bounds__(kScanBlock, 5) scan_main(const float2* __restr
       s_wb[wid] = inc.b;
     }
     if (wid == 0) {  // warp 0's exclusive guesses need no other warp
-      float exb = __shfl_up_sync(0xffffffffu, inc.b, 1);
-      if (lane == 0) exb = 0.f;
-      s_Eb[t] = exb;
+      Aff ex{__shfl_up_sync(0xffffffffu, inc.a, 1), __shfl_up_sync(0xffffffffu, inc.b, 1)};
+      if (lane == 0) ex = Aff{1.f, 0.f};
+      s_Eb[t] = ex.b;
+      // Warp 0's warm-up guesses reach into the 512-element halo: lane t
+      // composes halo sub-chunk t, a warp scan chains them (from B = 0 at the
+      // halo start), and the halo total continues into the in-tile prefix.
+      const float2* hrow = sm + t * kRowStride;
+      Aff h{hrow[0].x, hrow[0].y};
+#pragma unroll
+      for (int j = 1; j < kScanK; ++j) h = comb(h, Aff{hrow[j].x, hrow[j].y});
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const Aff o = Aff{__shfl_up_sync(0xffffffffu, h.a, d), __shfl_up_sync(0xffffffffu, h.b, d)};
+        if (lane >= d) h = comb(o, h);
+      }
+      const Aff htot{__shfl_sync(0xffffffffu, h.a, 31), __shfl_sync(0xffffffffu, h.b, 31)};
+      // lane 0: the prefix through halo row 15; lanes 1-7: through row t + 23
+      const float hb = __shfl_sync(0xffffffffu, h.b, lane == 0 ? 15 : (lane + 23) & 31);
+      const Aff exw{__shfl_sync(0xffffffffu, ex.a, (lane + 24) & 31), __shfl_sync(0xffffffffu, ex.b, (lane + 24) & 31)};
+      w0_guess = lane < 8 ? hb : comb(htot, exw).b;  // exw is lane t - 8's in-tile prefix
     }
   }
   // Warp 0's warm-up needs nothing from the block scan: it only signals the
@@ -348,11 +367,13 @@ __global__ void __launch_bounds__(kScanBlock, 5) scan_main(const float2* __restr
       }
     }
   } else if (!copy_first) {
-    // Warp 0 replays the 512 elements before its sub-chunk from B = 0: by
-    // contraction the true B entering the window no longer shows after them.
-    // The other warps start 128 elements back from the in-tile block-scan
-    // guess, whose unknown tile-entry part was contracted by >= 384 elements.
-    // In tile 0 the first element is copied, so warp 0 starts there exactly.
+    // Each thread replays the elements before its sub-chunk from a tree
+    // guess that assumes B = 0 at the start of the tile (warps 1-7) or of the
+    // halo (warp 0); by contraction over >= 256 elements that no longer
+    // shows, and the replay removes the tree's rounding.  Replays are 128
+    // elements, except thread 0's, which only the cross-tile check (and a
+    // serial repair) would catch: it replays 256.  In tile 0 the first
+    // element is copied, so warp 0 starts there exactly.
     int r0, c0 = 0;
     float b;
     if (wid == 0) {
@@ -361,8 +382,8 @@ __global__ void __launch_bounds__(kScanBlock, 5) scan_main(const float2* __restr
         r0 = kScanHaloSub;
         c0 = 1;
       } else {
-        b = 0.f;
-        r0 = t;
+        b = w0_guess;
+        r0 = t == 0 ? kScanHaloSub / 2 : t + kScanHaloSub - kScanWarmSub;
       }
     } else {
       b = s_Eb[t - kScanWarmSub];
