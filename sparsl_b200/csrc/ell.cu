@@ -314,9 +314,17 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1)
       const unsigned char* irow = st + lane * kIdxRow;
       const unsigned char* wrow = st + kIdxBox + lane * kWRow;
       const uint32_t cnt = min((uint32_t)kChunk, L - c * kChunk);
+      // Gathers and products are independent of the add chain: issue them
+      // first -- all kChunk of them for spike operands (shared-memory
+      // lookups), 8 at a time for dense x (where the add chain then overlaps
+      // the next group's L1 gathers; measured faster).  Entries past the row
+      // end (and rows past the last line) were zero-filled by the TMA box
+      // (column 0, weight 0), so their gathers stay in bounds; only their
+      // adds are skipped.
+      constexpr bool kGatherAll = XM != X_DENSE;
+      float prod[kChunk];
 #pragma unroll
       for (uint32_t g = 0; g < kChunk / 8; ++g) {  // 8 entries per group
-        if (g * 8 >= cnt) break;
         const uint4 ca = *reinterpret_cast<const uint4*>(irow + swz<kIdxRow>(lane, 2 * g));
         const uint4 cb = *reinterpret_cast<const uint4*>(irow + swz<kIdxRow>(lane, 2 * g + 1));
         float wv[8];
@@ -341,13 +349,6 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1)
           }
         }
         const uint32_t cv[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
-        const uint32_t lim = min(8u, cnt - g * 8);
-        // The eight gathers and products are independent: issue them all
-        // before the dependent add chain.  Entries past the row end (and rows
-        // past the last line) were zero-filled by the TMA box (column 0,
-        // weight 0), so their gathers stay in bounds; only their adds are
-        // skipped.
-        float prod[8];
 #pragma unroll
         for (uint32_t k = 0; k < 8; ++k) {
           float xv;
@@ -356,13 +357,27 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1)
           } else {
             xv = spike_value<XM>(s_x, p.xbits, cv[k], gs);
           }
-          prod[k] = fmul(wv[k], xv);
+          prod[8 * g + k] = fmul(wv[k], xv);
         }
-        if (lim == 8) {
+        if constexpr (!kGatherAll) {
+          if (cnt >= 8 * g + 8) {
 #pragma unroll
-          for (uint32_t k = 0; k < 8; ++k) sum = fadd(sum, prod[k]);
+            for (uint32_t k = 0; k < 8; ++k) sum = fadd(sum, prod[8 * g + k]);
+          } else {
+#pragma unroll
+            for (uint32_t k = 0; k < 8; ++k)
+              if (8 * g + k < cnt) sum = fadd(sum, prod[8 * g + k]);
+          }
+        }
+      }
+      if constexpr (kGatherAll) {
+        if (cnt == (uint32_t)kChunk) {
+#pragma unroll
+          for (uint32_t k = 0; k < (uint32_t)kChunk; ++k) sum = fadd(sum, prod[k]);
         } else {
-          for (uint32_t k = 0; k < lim; ++k) sum = fadd(sum, prod[k]);
+#pragma unroll
+          for (uint32_t k = 0; k < (uint32_t)kChunk; ++k)
+            if (k < cnt) sum = fadd(sum, prod[k]);
         }
       }
       __syncwarp();

@@ -374,17 +374,16 @@ __global__ void __launch_bounds__(kScanBlock, 5) scan_main(const float2* __restr
     // elements, except thread 0's, which only the cross-tile check (and a
     // serial repair) would catch: it replays 256.  In tile 0 the first
     // element is copied, so warp 0 starts there exactly.
-    int r0, c0 = 0;
+    int r0;
     float b;
-    if (wid == 0) {
-      if (tile == 0) {
-        b = sm[kScanHaloSub * kRowStride].y;
-        r0 = kScanHaloSub;
-        c0 = 1;
-      } else {
-        b = w0_guess;
-        r0 = t == 0 ? kScanHaloSub / 2 : t + kScanHaloSub - kScanWarmSub;
-      }
+    if (wid == 0 && tile == 0) {
+      const float2* rr = sm + kScanHaloSub * kRowStride;
+      b = rr[0].y;
+      for (int j = 1; j < kScanK; ++j) b = fadd(fmul(rr[j].x, b), rr[j].y);
+      r0 = kScanHaloSub + 1;
+    } else if (wid == 0) {
+      b = w0_guess;
+      r0 = t == 0 ? kScanHaloSub / 2 : t + kScanHaloSub - kScanWarmSub;
     } else {
       b = s_Eb[t - kScanWarmSub];
       r0 = t - kScanWarmSub + kScanHaloSub;
@@ -395,8 +394,7 @@ __global__ void __launch_bounds__(kScanBlock, 5) scan_main(const float2* __restr
 #pragma unroll
       for (int j = 0; j < kScanK; ++j) x[j] = rr[j];
 #pragma unroll
-      for (int j = 0; j < kScanK; ++j)
-        if (r != r0 || j >= c0) b = fadd(fmul(x[j].x, b), x[j].y);
+      for (int j = 0; j < kScanK; ++j) b = fadd(fmul(x[j].x, b), x[j].y);
     }
     wb = b;
     if (t == 0) s_wb0 = b;
