@@ -539,13 +539,47 @@ def bench_spmv(args, dev, want_cpu):
         dt = time.perf_counter() - t0
         cpu = {"value": k * algo / dt / 1e9, "unit": "GB/s", "cores": O.num_threads(), "kind": "port",
                "sample": f"{k} full SpMVs of the same matrix, CpuParallel restatement"}
+    # The same matrix with binary16 weights (the half.rs narrow path), and the
+    # transpose product over the operator's reverse index; each checked against
+    # the oracle after kernel_iters accumulations from zero.
+    def measure(op_, fn, xin, ylen, algo_, want_fn):
+        dyy = torch.zeros(ylen, dtype=torch.float32, device="cuda")
+        run_ = lambda: check(fn(op_.handle, xin.data_ptr(), dyy.data_ptr(), s.cuda_stream), "spmv variant")
+        for _ in range(args.warmup):
+            run_()
+        dyy.zero_()
+        ts_ = time_launches(s, run_, args.kernel_iters, flush=lambda: flush_l2(flush))
+        ms_ = statistics.median(ts_)
+        ref = np.zeros(ylen, np.float32)
+        for _ in range(args.kernel_iters):
+            want_fn(ref)
+        ok_ = bool(np.array_equal(dyy.cpu().numpy().view(np.uint32), ref.view(np.uint32)))
+        return {"value": algo_ / (ms_ * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms_, "algorithmic_bytes": algo_,
+                "bit_exact_vs_oracle": ok_}
+
+    op16 = dev.prepare_with(S.Csr(rp, col, SPMV_N), SPMV_N, w, S.WeightPrecision.F16)
+    w16 = O.quantise(int(S.WeightPrecision.F16), w)
+    algo16 = col.size * 6 + (SPMV_N + 1) * 4 + SPMV_N * 4 + 2 * SPMV_N * 4
+    f16 = measure(op16, L.sparsl_op_spmv_device, dx, SPMV_N, algo16, lambda ref: O.spmv(csr, w16, x, ref, par=True))
+    del op16
+    opt = dev.prepare_with_transpose(S.Csr(rp, col, SPMV_N), SPMV_N, w)
+    xt = r.uniform(0.0, 1.0, SPMV_N).astype(np.float32)
+    dxt = torch.from_numpy(xt).cuda()
+    csc = O.csc_from_csr(csr, SPMV_N)
+    # CSC walk: row index + weight (kept in reverse-index order) per entry, x
+    # gathered by row; col_ptr, x and y once.
+    algot = col.size * 8 + (SPMV_N + 1) * 4 + SPMV_N * 4 + 2 * SPMV_N * 4
+    tr = measure(opt, L.sparsl_op_spmv_t_device, dxt, SPMV_N, algot,
+                 lambda ref: O.spmv_t(csc, w, xt, ref, par=True))
+    del opt
     return {"metric": "SpMV effective HBM GB/s", "value": algo / (ms * 1e-3) / 1e9, "unit": "GB/s",
             "ms_per_step": ms, "kernel_ms_samples": len(ts), "algorithmic_bytes": algo,
             "config": "100,000 x 100,000, 64 distinct sorted cols/row, w U[-1,1], x U[0,1], f32; L2 flushed "
                       "(1 GiB write) before every launch",
             "e2e": {"value": algo / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 2 * SPMV_N * 4,
                     "d2h_bytes_per_step": SPMV_N * 4, "path": "sparsl_op_spmv, pinned host x/y"},
-            "bit_exact_vs_oracle": exact, "cpu_baseline": cpu}
+            "bit_exact_vs_oracle": exact, "cpu_baseline": cpu,
+            "f16_weights": f16, "transpose": tr}
 
 
 def bench_scan(args, dev, want_cpu):

@@ -299,6 +299,7 @@ struct sparsl_op {
   ErrWord err;
   DBuf row_ptr, col, w;
   DBuf col_ptr, csc_row, csc_eidx;
+  DBuf w_csc;  // the weights in reverse-index order: w_csc[k] = w[csc_eidx[k]]
   // Uniform row length: TMA tensor maps over col / w as [nrows x L] matrices.
   EllMaps ell;
   uint32_t ell_epoch = 0;  // tag of the last compacting TMA launch's flags
@@ -750,6 +751,13 @@ int sparsl_op_prepare(sparsl_dev* d, const uint32_t* row_ptr, uint64_t row_ptr_l
       cudaMemcpyAsync(op->csc_row.p, cr.data(), nnz * 4, cudaMemcpyHostToDevice, op->stream);
       cudaMemcpyAsync(op->csc_eidx.p, ce.data(), nnz * 4, cudaMemcpyHostToDevice, op->stream);
     }
+    // The transpose product streams its weights in reverse-index order
+    // instead of gathering them through edge_idx (same products, same order).
+    PALLOC(op->w_csc, nnz * wbytes, false, "csc values");
+    if (nnz &&
+        launch_gather_weights(op->w.p, op->csc_eidx.as<uint32_t>(), nnz, (int)wbytes, op->w_csc.p, op->stream) !=
+            cudaSuccess)
+      return bail(fail_cuda("prepare", cudaGetLastError()));
   }
   cudaMemsetAsync(op->rx.p, 0, op->rx.bytes, op->stream);
   cudaMemsetAsync(op->rxs[0].p, 0, op->rxs[0].bytes, op->stream);
@@ -822,7 +830,7 @@ void sparsl_op_destroy(sparsl_op* op) {
   if (!op) return;
   cudaSetDevice(op->dev->ordinal);
   if (op->stream) cudaStreamSynchronize(op->stream);
-  DBuf* bufs[] = {&op->row_ptr, &op->col,     &op->w,       &op->col_ptr, &op->csc_row, &op->csc_eidx,
+  DBuf* bufs[] = {&op->row_ptr, &op->col,     &op->w,       &op->col_ptr, &op->csc_row, &op->csc_eidx, &op->w_csc,
                   &op->rx,      &op->rxs[0],  &op->rxs[1],  &op->ry,      &op->rv,      &op->rth,
                   &op->rspk,    &op->idx_list, &op->tile_flags, &op->ticket, &op->trace, &op->sx,
                   &op->sbits,   &op->sy,      &op->sv,      &op->sth,     &op->sspk,
@@ -861,6 +869,9 @@ int sparsl_op_set_weights(sparsl_op* op, const float* weights, uint64_t n) {
     encode_narrow(op->precision, weights, narrow.data(), n);
     CK("set_weights", cudaMemcpyAsync(op->w.p, narrow.data(), n * 2, cudaMemcpyHostToDevice, op->stream));
   }
+  if (op->has_t)
+    CK("set_weights", launch_gather_weights(op->w.p, op->csc_eidx.as<uint32_t>(), n, op->precision == 0 ? 4 : 2,
+                                            op->w_csc.p, op->stream));
   return wait_op(op, "set_weights");
 }
 
@@ -920,8 +931,7 @@ int sparsl_op_spmv_t(sparsl_op* op, const float* x, uint64_t x_len, float* y, ui
   RowLaunch p;
   p.ptr = op->col_ptr.as<uint32_t>();
   p.idx = op->csc_row.as<uint32_t>();
-  p.eidx = op->csc_eidx.as<uint32_t>();
-  p.w = op->w.p;
+  p.w = op->w_csc.p;  // reverse-index order: a plain row fold over the CSC lines
   p.wkind = wkind_of(op->precision);
   p.nlines = op->ncols;
   p.x = op->sx.as<float>();
@@ -1257,8 +1267,7 @@ int sparsl_op_spmv_t_device(sparsl_op* op, const float* d_x, float* d_y, void* s
   RowLaunch p;
   p.ptr = op->col_ptr.as<uint32_t>();
   p.idx = op->csc_row.as<uint32_t>();
-  p.eidx = op->csc_eidx.as<uint32_t>();
-  p.w = op->w.p;
+  p.w = op->w_csc.p;  // reverse-index order: a plain row fold over the CSC lines
   p.wkind = wkind_of(op->precision);
   p.nlines = op->ncols;
   p.x = d_x;

@@ -7,6 +7,7 @@
 // survive (tests/stress.rs:366-384).
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -30,25 +31,11 @@ constexpr uint32_t kSpinLimit = 1u << 20;
 __device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
 __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
 
-// binary16 bits -> f32, exact for every pattern including subnormals and NaN
-// payloads (same integer construction as src/half.rs:49-90).
-__device__ __forceinline__ float widen_f16(uint32_t h) {
-  uint32_t sign = (h & 0x8000u) << 16;
-  uint32_t e = (h >> 10) & 0x1fu;
-  uint32_t m = h & 0x3ffu;
-  uint32_t out;
-  if (e == 0x1f) {
-    out = sign | 0x7f800000u | (m << 13);
-  } else if (e != 0) {
-    out = sign | ((e + 112u) << 23) | (m << 13);
-  } else if (m == 0) {
-    out = sign;
-  } else {
-    uint32_t shift = __clz(m) - 21;  // leading one onto bit 10
-    out = sign | ((113u - shift) << 23) | (((m << shift) & 0x3ffu) << 13);
-  }
-  return __uint_as_float(out);
-}
+// binary16 bits -> f32 by the hardware conversion (cvt.f32.f16, no flush):
+// every binary16 value, subnormals included, is an f32 value, so for every
+// non-NaN pattern the result is the one half.rs:49-90 constructs bit for bit.
+// A NaN stays a NaN (its payload may differ, which the parity rule allows).
+__device__ __forceinline__ float widen_f16(uint32_t h) { return __half2float(__ushort_as_half((unsigned short)h)); }
 
 // bfloat16 bits -> f32: the top half of an f32 (src/half.rs:187-189).
 __device__ __forceinline__ float widen_bf16(uint32_t h) { return __uint_as_float(h << 16); }

@@ -156,6 +156,13 @@ __global__ void fill_kernel(uint32_t* p, uint64_t n, uint32_t v) {
     p[i] = v;
 }
 
+template <typename T>
+__global__ void gather_kernel(const T* __restrict__ w, const uint32_t* __restrict__ idx, uint64_t n,
+                              T* __restrict__ out) {
+  for (uint64_t k = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; k < n; k += (uint64_t)gridDim.x * blockDim.x)
+    out[k] = w[__ldg(idx + k)];
+}
+
 inline unsigned grid_for(uint64_t n, unsigned block, unsigned cap = 148 * 16) {
   uint64_t g = (n + block - 1) / block;
   if (g < 1) g = 1;
@@ -184,6 +191,18 @@ cudaError_t launch_spmm(const SpmmLaunch& p, int sm_count, cudaStream_t s) {
     case W_BF16: spmm_kernel<W_BF16><<<blocks, block, 0, s>>>(p); break;
     default: spmm_kernel<W_F32><<<blocks, block, 0, s>>>(p); break;
   }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_weights(const void* w, const uint32_t* idx, uint64_t n, int wbytes, void* out,
+                                  cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  if (wbytes == 4)
+    gather_kernel<uint32_t><<<grid_for(n, 256), 256, 0, s>>>(static_cast<const uint32_t*>(w), idx, n,
+                                                              static_cast<uint32_t*>(out));
+  else
+    gather_kernel<uint16_t><<<grid_for(n, 256), 256, 0, s>>>(static_cast<const uint16_t*>(w), idx, n,
+                                                              static_cast<uint16_t*>(out));
   return cudaGetLastError();
 }
 

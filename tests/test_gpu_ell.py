@@ -156,3 +156,26 @@ def test_uniform_recurrent_network_spike_operand_beyond_shared_memory(O, cuda_de
     assert_bits_equal(v, vw)
     assert_bits_equal(t, tw)
     assert np.array_equal(op.sync_x_spikes(), xw)
+
+
+@pytest.mark.parametrize("generic", [False, True])
+def test_f16_weights_every_binary16_pattern(O, cuda_device, generic):
+    """Every one of the 65,536 binary16 patterns as a weight, through the TMA
+    path and the generic path: each row folds one pattern followed by +0
+    entries against x = 1, so y is the widened weight (NaN patterns compare as
+    NaN, -0 becomes +0 exactly as in the reference's fold)."""
+    pats = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    wide = O.f16_bits_to_f32(pats)
+    nrows, L = 65536, 8
+    col = np.tile(np.arange(L, dtype=np.uint32), nrows)
+    rp = (np.arange(nrows + 1, dtype=np.uint64) * L).astype(np.uint32)
+    w = np.zeros((nrows, L), np.float32)
+    w[:, 0] = wide
+    w = w.reshape(-1)
+    csr = O.Csr(rp, col, L)
+    op = _prepare(cuda_device, csr, w, S.WeightPrecision.F16, generic=generic)
+    x = np.ones(L, np.float32)
+    got = np.zeros(nrows, np.float32)
+    op.spmv(x, got)
+    want = O.spmv(csr, O.quantise(int(S.WeightPrecision.F16), w), x, np.zeros(nrows, np.float32))
+    assert_bits_equal(got, want, f"all binary16 patterns generic={generic}")

@@ -401,3 +401,26 @@ def test_spmm_work_units_bit_exact(O, cuda_device, kind, n_vec):
     if empty.size:  # -0.0 + 0.0 + 0.0 is +0.0 on an empty row
         row = got.reshape(nrows, n_vec)[empty]
         assert not np.any(np.signbit(row) & (row == 0))
+
+
+@pytest.mark.parametrize("precision", [S.WeightPrecision.F32, S.WeightPrecision.F16, S.WeightPrecision.Bf16])
+def test_set_weights_refreshes_the_transpose(O, cuda_device, precision):
+    """The transpose product reads the weights in reverse-index order; after
+    set_weights both directions must use the new weights (mod.rs:1397)."""
+    nrows, ncols, deg = 1000, 700, 40
+    csr, w, x, y0 = _fixture(O, (nrows, ncols, deg), 0x7A11 + int(precision))
+    op = cuda_device.prepare_with_transpose_precision(_scsr(csr), ncols, w, precision)
+    w2 = O.random_vec(csr.nnz, 3.0, O.Rng(0x33 + int(precision)))
+    w2[::97] = np.inf
+    op.set_weights(w2)
+    wq = O.quantise(int(precision), w2)
+    csc = O.csc_from_csr(csr, ncols)
+    rng = O.Rng(0x44)
+    xt = O.random_vec(nrows, 1.0, rng)
+    yt0 = O.random_vec(ncols, 1.0, rng)
+    got = yt0.copy()
+    op.spmv_t(xt, got)
+    assert_bits_equal(got, O.spmv_t(csc, wq, xt, yt0.copy()), "spmv_t after set_weights")
+    got = y0.copy()
+    op.spmv(x, got)
+    assert_bits_equal(got, O.spmv(csr, wq, x, y0.copy()), "spmv after set_weights")
