@@ -44,7 +44,7 @@ constexpr int kMinStages = 2, kMaxStages = 8;
 // Dense x: gathers go through L1/L2, so fewer stages (and more CTAs per SM)
 // can hide more gather latency than deeper streaming does.
 #ifndef SPARSL_ELL_DENSE_STAGES
-#define SPARSL_ELL_DENSE_STAGES 3
+#define SPARSL_ELL_DENSE_STAGES 2
 #endif
 constexpr int kDenseStages = SPARSL_ELL_DENSE_STAGES;
 constexpr int kIdxRow = kChunk * 4;            // bytes of one row of a column box
@@ -487,6 +487,15 @@ cudaError_t launch_t(const EllMaps& m, const RowLaunch& p, cudaStream_t stream) 
   if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kEllWarps * 32, smem)) != cudaSuccess)
     return e;
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
+  if constexpr (XM == X_DENSE) {
+    // Dense x is gathered through L1: one CTA per SM, and a shared-memory
+    // carveout just large enough for it, so the rest of the SM's L1/shared
+    // storage caches x (a second CTA would squeeze that L1 to almost nothing).
+    per_sm = 1;
+    const int pct = (int)std::min<size_t>(100, (smem + 4096) * 100 / (228 * 1024) + 1);
+    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, pct)) != cudaSuccess)
+      return e;
+  }
   const uint32_t tiles = (p.nlines + 31) / 32;
   const uint32_t want = (tiles + kEllWarps - 1) / kEllWarps;
   const uint32_t grid = std::max(1u, std::min(want, (uint32_t)(per_sm * g_num_sms)));
