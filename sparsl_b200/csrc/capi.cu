@@ -30,6 +30,7 @@
 #include "misc.cuh"
 #include "rows.cuh"
 #include "scan.cuh"
+#include "sell.cuh"
 
 using namespace sparsl;
 
@@ -300,6 +301,13 @@ struct sparsl_op {
   DBuf row_ptr, col, w;
   DBuf col_ptr, csc_row, csc_eidx;
   DBuf w_csc;  // the weights in reverse-index order: w_csc[k] = w[csc_eidx[k]]
+  // Sliced-ELL copy of the reverse index for the transpose product (when its
+  // padding stays bounded): slice offsets, row and edge index per entry, the
+  // weights in that order, and the slice counter.
+  bool sell_ok = false;
+  uint32_t sell_slices = 0;
+  uint64_t sell_total = 0;
+  DBuf sell_ptr, sell_row, sell_eidx, w_sell, sell_ctr;
   // Uniform row length: TMA tensor maps over col / w as [nrows x L] matrices.
   EllMaps ell;
   uint32_t ell_epoch = 0;  // tag of the last compacting TMA launch's flags
@@ -737,27 +745,66 @@ int sparsl_op_prepare(sparsl_dev* d, const uint32_t* row_ptr, uint64_t row_ptr_l
         return bail(fail_cuda("prepare", cudaGetLastError()));
     }
   }
-  std::vector<uint32_t> cp, cr, ce;
+  std::vector<uint32_t> cp, cr, ce, sell_row_h, sell_eidx_h;
+  std::vector<uint64_t> sell_ptr_h;
   if (op->has_t) {
     cp.resize(nc + 1);
     cr.resize(nnz);
     ce.resize(nnz);
     build_csc(row_ptr, nrows, col, nnz, nc, cp.data(), cr.data(), ce.data());
     PALLOC(op->col_ptr, (nc + 1) * 4, false, "csc col_ptr");
-    PALLOC(op->csc_row, nnz * 4, false, "csc row");
-    PALLOC(op->csc_eidx, nnz * 4, false, "csc edge_idx");
     cudaMemcpyAsync(op->col_ptr.p, cp.data(), (nc + 1) * 4, cudaMemcpyHostToDevice, op->stream);
-    if (nnz) {
-      cudaMemcpyAsync(op->csc_row.p, cr.data(), nnz * 4, cudaMemcpyHostToDevice, op->stream);
-      cudaMemcpyAsync(op->csc_eidx.p, ce.data(), nnz * 4, cudaMemcpyHostToDevice, op->stream);
+    // Sliced ELL: slices of 32 columns, each padded to its longest column,
+    // entries column-major within the slice.  Kept only while the padding at
+    // most doubles the entries (a hub column would blow it up).
+    const uint64_t nslices = (nc + 31) / 32;
+    std::vector<uint64_t> sp(nslices + 1, 0);
+    for (uint64_t sl = 0; sl < nslices; ++sl) {
+      uint32_t depth = 0;
+      for (uint64_t c = sl * 32; c < std::min<uint64_t>(nc, sl * 32 + 32); ++c) depth = std::max(depth, cp[c + 1] - cp[c]);
+      sp[sl + 1] = sp[sl] + (uint64_t)depth * 32;
     }
-    // The transpose product streams its weights in reverse-index order
-    // instead of gathering them through edge_idx (same products, same order).
-    PALLOC(op->w_csc, nnz * wbytes, false, "csc values");
-    if (nnz &&
-        launch_gather_weights(op->w.p, op->csc_eidx.as<uint32_t>(), nnz, (int)wbytes, op->w_csc.p, op->stream) !=
-            cudaSuccess)
-      return bail(fail_cuda("prepare", cudaGetLastError()));
+    if (nnz && sp[nslices] <= 2 * nnz + 32 * nslices && nslices <= 0xffffffffull) {
+      sell_row_h.assign(sp[nslices], 0u);
+      sell_eidx_h.assign(sp[nslices], 0u);
+      for (uint64_t c = 0; c < nc; ++c) {
+        const uint64_t b = sp[c / 32] + (c % 32);
+        for (uint32_t k = cp[c]; k < cp[c + 1]; ++k) {
+          sell_row_h[b + (uint64_t)(k - cp[c]) * 32] = cr[k];
+          sell_eidx_h[b + (uint64_t)(k - cp[c]) * 32] = ce[k];
+        }
+      }
+      sell_ptr_h.swap(sp);
+      op->sell_total = sell_ptr_h[nslices];
+      op->sell_slices = (uint32_t)nslices;
+      PALLOC(op->sell_ptr, (nslices + 1) * 8, false, "sliced-ELL offsets");
+      PALLOC(op->sell_row, op->sell_total * 4, false, "sliced-ELL rows");
+      PALLOC(op->sell_eidx, op->sell_total * 4, false, "sliced-ELL edge index");
+      PALLOC(op->w_sell, op->sell_total * wbytes, false, "sliced-ELL values");
+      PALLOC(op->sell_ctr, 16, false, "sliced-ELL counter");
+      cudaMemcpyAsync(op->sell_ptr.p, sell_ptr_h.data(), (nslices + 1) * 8, cudaMemcpyHostToDevice, op->stream);
+      cudaMemcpyAsync(op->sell_row.p, sell_row_h.data(), op->sell_total * 4, cudaMemcpyHostToDevice, op->stream);
+      cudaMemcpyAsync(op->sell_eidx.p, sell_eidx_h.data(), op->sell_total * 4, cudaMemcpyHostToDevice, op->stream);
+      cudaMemsetAsync(op->sell_ctr.p, 0, op->sell_ctr.bytes, op->stream);
+      if (launch_gather_weights(op->w.p, op->sell_eidx.as<uint32_t>(), op->sell_total, (int)wbytes, op->w_sell.p,
+                                op->stream) != cudaSuccess)
+        return bail(fail_cuda("prepare", cudaGetLastError()));
+      op->sell_ok = true;
+    } else {
+      PALLOC(op->csc_row, nnz * 4, false, "csc row");
+      PALLOC(op->csc_eidx, nnz * 4, false, "csc edge_idx");
+      if (nnz) {
+        cudaMemcpyAsync(op->csc_row.p, cr.data(), nnz * 4, cudaMemcpyHostToDevice, op->stream);
+        cudaMemcpyAsync(op->csc_eidx.p, ce.data(), nnz * 4, cudaMemcpyHostToDevice, op->stream);
+      }
+      // The transpose product streams its weights in reverse-index order
+      // instead of gathering them through edge_idx (same products, same order).
+      PALLOC(op->w_csc, nnz * wbytes, false, "csc values");
+      if (nnz &&
+          launch_gather_weights(op->w.p, op->csc_eidx.as<uint32_t>(), nnz, (int)wbytes, op->w_csc.p, op->stream) !=
+              cudaSuccess)
+        return bail(fail_cuda("prepare", cudaGetLastError()));
+    }
   }
   cudaMemsetAsync(op->rx.p, 0, op->rx.bytes, op->stream);
   cudaMemsetAsync(op->rxs[0].p, 0, op->rxs[0].bytes, op->stream);
@@ -831,6 +878,7 @@ void sparsl_op_destroy(sparsl_op* op) {
   cudaSetDevice(op->dev->ordinal);
   if (op->stream) cudaStreamSynchronize(op->stream);
   DBuf* bufs[] = {&op->row_ptr, &op->col,     &op->w,       &op->col_ptr, &op->csc_row, &op->csc_eidx, &op->w_csc,
+                  &op->sell_ptr, &op->sell_row, &op->sell_eidx, &op->w_sell, &op->sell_ctr,
                   &op->rx,      &op->rxs[0],  &op->rxs[1],  &op->ry,      &op->rv,      &op->rth,
                   &op->rspk,    &op->idx_list, &op->tile_flags, &op->ticket, &op->trace, &op->sx,
                   &op->sbits,   &op->sy,      &op->sv,      &op->sth,     &op->sspk,
@@ -869,7 +917,10 @@ int sparsl_op_set_weights(sparsl_op* op, const float* weights, uint64_t n) {
     encode_narrow(op->precision, weights, narrow.data(), n);
     CK("set_weights", cudaMemcpyAsync(op->w.p, narrow.data(), n * 2, cudaMemcpyHostToDevice, op->stream));
   }
-  if (op->has_t)
+  if (op->sell_ok)
+    CK("set_weights", launch_gather_weights(op->w.p, op->sell_eidx.as<uint32_t>(), op->sell_total,
+                                            op->precision == 0 ? 4 : 2, op->w_sell.p, op->stream));
+  else if (op->has_t)
     CK("set_weights", launch_gather_weights(op->w.p, op->csc_eidx.as<uint32_t>(), n, op->precision == 0 ? 4 : 2,
                                             op->w_csc.p, op->stream));
   return wait_op(op, "set_weights");
@@ -914,6 +965,35 @@ int sparsl_op_spmv_spikes(sparsl_op* op, const uint32_t* spikes, uint64_t words,
   return finish(op, "spmv_spikes");
 }
 
+// The transpose product: the sliced-ELL fold when the operator has it, the
+// row-fold engine over the CSC lines otherwise.
+static cudaError_t launch_transpose(sparsl_op* op, const float* x, float* y, cudaStream_t s) {
+  if (op->sell_ok) {
+    SellLaunch p;
+    p.slice_ptr = op->sell_ptr.as<uint64_t>();
+    p.line_ptr = op->col_ptr.as<uint32_t>();
+    p.idx = op->sell_row.as<uint32_t>();
+    p.w = op->w_sell.p;
+    p.wkind = wkind_of(op->precision);
+    p.x = x;
+    p.y = y;
+    p.nlines = op->ncols;
+    p.nslices = op->sell_slices;
+    p.ctr = op->sell_ctr.as<uint32_t>();
+    return launch_sell(p, op->dev->sm_count, s);
+  }
+  RowLaunch p;
+  p.ptr = op->col_ptr.as<uint32_t>();
+  p.idx = op->csc_row.as<uint32_t>();
+  p.w = op->w_csc.p;  // reverse-index order: a plain row fold over the CSC lines
+  p.wkind = wkind_of(op->precision);
+  p.nlines = op->ncols;
+  p.x = x;
+  p.y = y;
+  p.err = op->err.d;
+  return launch_rows(p, s);
+}
+
 int sparsl_op_spmv_t(sparsl_op* op, const float* x, uint64_t x_len, float* y, uint64_t y_len) {
   ADMIT();
   TRY(check_min("x", x_len, op->nrows));
@@ -928,16 +1008,7 @@ int sparsl_op_spmv_t(sparsl_op* op, const float* x, uint64_t x_len, float* y, ui
   ALLOC(op->sy, (uint64_t)std::max(op->nrows, op->ncols) * 4 + 16, true, "y staging");
   if (op->nrows) CK("spmv_t", cudaMemcpyAsync(op->sx.p, x, (uint64_t)op->nrows * 4, cudaMemcpyHostToDevice, op->stream));
   CK("spmv_t", cudaMemcpyAsync(op->sy.p, y, (uint64_t)op->ncols * 4, cudaMemcpyHostToDevice, op->stream));
-  RowLaunch p;
-  p.ptr = op->col_ptr.as<uint32_t>();
-  p.idx = op->csc_row.as<uint32_t>();
-  p.w = op->w_csc.p;  // reverse-index order: a plain row fold over the CSC lines
-  p.wkind = wkind_of(op->precision);
-  p.nlines = op->ncols;
-  p.x = op->sx.as<float>();
-  p.y = op->sy.as<float>();
-  p.err = op->err.d;
-  CK("spmv_t", launch_rows(p, op->stream));
+  CK("spmv_t", launch_transpose(op, op->sx.as<float>(), op->sy.as<float>(), op->stream));
   CK("spmv_t", cudaMemcpyAsync(y, op->sy.p, (uint64_t)op->ncols * 4, cudaMemcpyDeviceToHost, op->stream));
   return finish(op, "spmv_t");
 }
@@ -1264,16 +1335,7 @@ int sparsl_op_spmv_t_device(sparsl_op* op, const float* d_x, float* d_y, void* s
   if (op->ncols == 0) return SPARSL_OK;
   if (!op->has_t) return fail(SPARSL_ERR_NO_TRANSPOSE, "transpose not prepared", "no reverse index");
   CK("spmv_t", cudaSetDevice(op->dev->ordinal));
-  RowLaunch p;
-  p.ptr = op->col_ptr.as<uint32_t>();
-  p.idx = op->csc_row.as<uint32_t>();
-  p.w = op->w_csc.p;  // reverse-index order: a plain row fold over the CSC lines
-  p.wkind = wkind_of(op->precision);
-  p.nlines = op->ncols;
-  p.x = d_x;
-  p.y = d_y;
-  p.err = op->err.d;
-  CK("spmv_t", launch_rows(p, pick(op, stream)));
+  CK("spmv_t", launch_transpose(op, d_x, d_y, pick(op, stream)));
   return SPARSL_OK;
 }
 

@@ -424,3 +424,38 @@ def test_set_weights_refreshes_the_transpose(O, cuda_device, precision):
     got = y0.copy()
     op.spmv(x, got)
     assert_bits_equal(got, O.spmv(csr, wq, x, y0.copy()), "spmv after set_weights")
+
+
+@pytest.mark.parametrize("hub", [False, True])
+def test_spmv_t_sliced_and_hub_layouts(O, cuda_device, hub):
+    """The transpose product runs over a sliced-ELL copy of the reverse index;
+    a hub column (here in every row) would pad that copy beyond twice the
+    nonzeros, so such operators keep the CSC row-fold path.  Both must equal
+    the reference's col_dot fold bit for bit, in every precision."""
+    r = np.random.default_rng(7 + hub)
+    nrows, ncols = 3000, 2000
+    rows = []
+    for i in range(nrows):
+        k = int(r.integers(0, 12))
+        cols = set(r.choice(ncols, k, replace=False).tolist())
+        if hub:
+            cols.add(5)
+        rows.append(sorted(cols))
+    lens = np.array([len(c) for c in rows])
+    rp = np.zeros(nrows + 1, np.uint64)
+    np.cumsum(lens, out=rp[1:])
+    col = np.array([c for row in rows for c in row], np.uint32)
+    csr = O.Csr(rp.astype(np.uint32), col, ncols)
+    w = r.uniform(-1, 1, col.size).astype(np.float32)
+    w[::41] = np.inf
+    csc = O.csc_from_csr(csr, ncols)
+    xt = r.uniform(-1, 1, nrows).astype(np.float32)
+    xt[::13] = 0.0
+    yt0 = r.uniform(-1, 1, ncols).astype(np.float32)
+    yt0[::7] = -0.0
+    for p in (S.WeightPrecision.F32, S.WeightPrecision.F16, S.WeightPrecision.Bf16):
+        op = cuda_device.prepare_with_transpose_precision(_scsr(csr), ncols, w, p)
+        got = yt0.copy()
+        op.spmv_t(xt, got)
+        want = O.spmv_t(csc, O.quantise(int(p), w), xt, yt0.copy())
+        assert_bits_equal(got, want, f"spmv_t hub={hub} {p}")
