@@ -192,10 +192,29 @@ class DevArray:
             check(lib().sparsl_memcpy(out.ctypes.data, self.ptr, out.nbytes), "memcpy D2H")
         return out
 
+    def span(self, count):
+        """The first `count` 4-byte elements, as the array argument of
+        Device.prepare_device."""
+        return _Span(self.ptr, int(count))
+
     def free(self):
         if self.ptr:
             lib().sparsl_device_free(self.ptr)
             self.ptr = None
+
+
+class _Span:
+    def __init__(self, ptr, count):
+        self._ptr, self._count = ptr, count
+
+    def data_ptr(self):
+        return self._ptr
+
+    def numel(self):
+        return self._count
+
+    def element_size(self):
+        return 4
 
 
 class Pinned:
@@ -247,24 +266,28 @@ def build_lif_net(S, dev, dist, n_total, fan_in, keep_sample_rows=0):
     world, rank = dist.world, dist.rank
     local = n_total // world
     row0 = rank * local
+    import torch
+
     ops, sample = [], None
     t0 = time.time()
     for (off, nrows) in net_blocks(local, fan_in):
+        # The synapses are drawn on the GPU and the operator is prepared from
+        # them there (validated and copied in HBM; no host round trip).
         nnz = nrows * fan_in
+        drp = DevArray(dev, (nrows + 1) * 4)
         dcol = DevArray(dev, nnz * 4)
         dw = DevArray(dev, nnz * 4)
+        check(lib().sparsl_workload_uniform_row_ptr(nrows, fan_in, drp.ptr, None), "row_ptr")
         check(lib().sparsl_workload_fixed_fanin(NET_SEED, row0 + off, nrows, n_total, fan_in, NET_SIGMA, dcol.ptr,
                                                 dw.ptr, None), "workload")
-        col = dcol.to_host(np.uint32, nnz)
-        w = dw.to_host(np.float32, nnz)
-        dcol.free()
-        dw.free()
-        rp = (np.arange(nrows + 1, dtype=np.uint64) * fan_in).astype(np.uint32)
-        ops.append(dev.prepare(S.Csr(rp, col, n_total), n_total, w))
+        torch.cuda.synchronize()
+        ops.append(dev.prepare_device(drp.span(nrows + 1), dcol.span(nnz), n_total, dw.span(nnz)))
         if keep_sample_rows and sample is None:
             k = min(keep_sample_rows, nrows)
-            sample = (rp[: k + 1].copy(), col[: k * fan_in].copy(), w[: k * fan_in].copy())
-        del col, w
+            sample = (drp.to_host(np.uint32, k + 1), dcol.to_host(np.uint32, k * fan_in),
+                      dw.to_host(np.float32, k * fan_in))
+        for a in (drp, dcol, dw):
+            a.free()
     # initial state for every cell (the spike vector is global)
     dv = DevArray(dev, n_total * 4)
     dth = DevArray(dev, n_total * 4)

@@ -129,6 +129,24 @@ int sparsl_op_prepare(sparsl_dev *dev, const uint32_t *row_ptr, uint64_t row_ptr
                       const uint32_t *col, uint64_t col_len, uint64_t csr_ncols, uint64_t ncols,
                       const float *weights, uint64_t weights_len, int precision, int with_transpose,
                       sparsl_shape *shape, sparsl_op **out);
+/* SparseOp::prepare (mod.rs:1305-1371) for a CSR whose arrays are already in
+ * device memory of `dev` (d_row_ptr: row_ptr_len u32, d_col: col_len u32,
+ * d_weights: weights_len f32): no extension in the reference, which only
+ * takes host slices.  The same gate runs in the same order with the same
+ * first-failure payload in *shape: the row_ptr checks on a host copy of
+ * row_ptr (O(rows) bytes), the column-range and row-order checks on the GPU.
+ * Narrow precisions are encoded on the GPU by the same encoder as
+ * sparsl_f32_to_f16_bits / sparsl_f32_to_bf16_bits, so the operator is
+ * bit-identical to one from sparsl_op_prepare on the same values.  Each
+ * array must be device memory of this GPU lying inside one allocation
+ * (else SPARSL_ERR_INVALID), and every write to it must have completed
+ * before the call.  with_transpose copies col back to build the reverse
+ * index on the host.  The caller keeps ownership of its arrays. */
+int sparsl_op_prepare_device(sparsl_dev *dev, const uint32_t *d_row_ptr, uint64_t row_ptr_len,
+                             const uint32_t *d_col, uint64_t col_len, uint64_t csr_ncols,
+                             uint64_t ncols, const float *d_weights, uint64_t weights_len,
+                             int precision, int with_transpose, sparsl_shape *shape,
+                             sparsl_op **out);
 void sparsl_op_destroy(sparsl_op *op);
 int sparsl_op_shape(sparsl_op *op, sparsl_shape *out);
 int sparsl_op_weight_precision(sparsl_op *op);    /* mod.rs:1582 */

@@ -15,7 +15,9 @@ from __future__ import annotations
 import ctypes
 import enum
 import math
+import sys
 from dataclasses import dataclass
+from typing import Optional
 
 import numpy as np
 
@@ -436,6 +438,14 @@ class Device:
     def prepare_bf16_with_transpose(self, csr: Csr, ncols: int, weights) -> "SparseOp":
         return SparseOp._prepare(self, csr, ncols, weights, True, WeightPrecision.Bf16)
 
+    def prepare_device(self, row_ptr, col, ncols: int, weights, precision: WeightPrecision = WeightPrecision.F32,
+                       transpose: bool = False, csr_ncols: Optional[int] = None) -> "SparseOp":
+        """``prepare_with`` / ``prepare_with_transpose_precision`` for a CSR whose
+        arrays already live on this GPU; the same gate, errors and operator.
+        ``csr_ncols`` is the CSR's own column count (defaults to ``ncols``)."""
+        return SparseOp._prepare_device(self, row_ptr, col, ncols if csr_ncols is None else csr_ncols, ncols,
+                                        weights, transpose, precision)
+
     # ---- device-level ops ----
     def assoc_scan(self, xs) -> np.ndarray:
         """Inclusive scan of (a, b) maps, bit-identical to assoc_scan_sequential.
@@ -505,6 +515,36 @@ class SparseOp:
         rc = _lib.load().sparsl_op_prepare(device.handle, _ptr(rp), rp.size, _ptr(col), col.size, csr.ncols(),
                                            int(ncols), _ptr(w), w.size, int(precision), int(transpose),
                                            ctypes.byref(sh), ctypes.byref(h))
+        return cls._finish(device, rc, sh, h, precision)
+
+    @classmethod
+    def _prepare_device(cls, device: Device, row_ptr, col, csr_ncols: int, ncols: int, weights, transpose: bool,
+                        precision: WeightPrecision) -> "SparseOp":
+        """``prepare`` from arrays already on the GPU (sparsl_op_prepare_device).
+
+        ``row_ptr`` and ``col`` are 32-bit integer tensors and ``weights`` a
+        float32 tensor, contiguous, on this device (torch tensors or any object
+        with ``data_ptr()``, ``numel()`` and ``element_size()``).  Torch work
+        that writes them is synchronised first.
+        """
+        for name, t, size in (("row_ptr", row_ptr, 4), ("col", col, 4), ("weights", weights, 4)):
+            if t.element_size() != size:
+                raise SparsePlanError("Backend", f"{name} must have {size}-byte elements", reason=name)
+            if hasattr(t, "is_contiguous") and not t.is_contiguous():
+                raise SparsePlanError("Backend", f"{name} must be contiguous", reason=name)
+        torch = sys.modules.get("torch")
+        if torch is not None and isinstance(weights, torch.Tensor) and weights.is_cuda:
+            torch.cuda.synchronize(weights.device)
+        sh = Shape()
+        h = ctypes.c_void_p()
+        rc = _lib.load().sparsl_op_prepare_device(device.handle, row_ptr.data_ptr(), row_ptr.numel(), col.data_ptr(),
+                                                  col.numel(), int(csr_ncols), int(ncols), weights.data_ptr(),
+                                                  weights.numel(), int(precision), int(transpose), ctypes.byref(sh),
+                                                  ctypes.byref(h))
+        return cls._finish(device, rc, sh, h, precision)
+
+    @classmethod
+    def _finish(cls, device: Device, rc: int, sh, h, precision: WeightPrecision) -> "SparseOp":
         if rc == _lib.SPARSL_ERR_INVALID and sh.code != 0:
             raise _plan_error(sh)
         if rc == _lib.SPARSL_ERR_ALLOCATION:

@@ -31,6 +31,7 @@
 #include "rows.cuh"
 #include "scan.cuh"
 #include "sell.cuh"
+#include "validate.cuh"
 
 using namespace sparsl;
 
@@ -265,6 +266,7 @@ struct sparsl_dev {
   ScanScratch sc{};
   bool scan_dirty = false;
   DBuf lv, lth, lcur, lspk;
+  DBuf vscratch;  // device CSR validation results
 };
 
 namespace {
@@ -511,6 +513,7 @@ void sparsl_device_close(sparsl_dev* d) {
   dfree(d->lth);
   dfree(d->lcur);
   dfree(d->lspk);
+  dfree(d->vscratch);
   d->err.release();
   cudaEventDestroy(d->ev);
   cudaStreamDestroy(d->stream);
@@ -668,6 +671,93 @@ int sparsl_dev_wait(sparsl_dev* d) {
 }
 
 // ---- operator ------------------------------------------------------------
+namespace {
+
+// Where an operator's CSR comes from.  row_ptr is always readable on the
+// host (the device-source entry copies it there first: O(rows) bytes);
+// col and weights are host pointers, or device pointers when `device`.
+struct PrepSrc {
+  const uint32_t* row_ptr;
+  const uint32_t* d_row_ptr;  // device row_ptr (device sources), else null
+  const uint32_t* col;
+  const float* weights;
+  bool device;
+};
+
+void to_shape(const PlanResult& r, sparsl_shape* out) {
+  out->code = r.code;
+  out->a = r.a;
+  out->b = r.b;
+  out->c = r.c;
+  out->nrows = r.nrows;
+  out->ncols = r.ncols;
+  out->nnz = r.nnz;
+  out->max_row_nnz = r.max_row_nnz;
+}
+
+// The argument checks that follow validate_csr in SparseOp::prepare
+// (src/backend/mod.rs:1305-1320): one weight per non-zero, a known precision.
+int check_prepare_args(const sparsl_shape& sh, uint64_t weights_len, int precision, sparsl_shape* shape) {
+  if (weights_len != sh.nnz) {
+    if (shape) {
+      shape->code = SPARSL_PLAN_WEIGHTS_LEN;
+      shape->a = sh.nnz;
+      shape->b = weights_len;
+    }
+    return fail(SPARSL_ERR_INVALID, "weights length", "weights must have one entry per non-zero");
+  }
+  if (precision < 0 || precision > 2) return fail(SPARSL_ERR_INVALID, "precision", "unknown weight precision");
+  return SPARSL_OK;
+}
+
+// cuMemGetAddressRange through the runtime's driver entry point.
+typedef int (*AddrRangeFn)(unsigned long long*, size_t*, unsigned long long);
+AddrRangeFn addr_range_fn() {
+  static AddrRangeFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<AddrRangeFn>(p);
+    return (AddrRangeFn) nullptr;
+  }();
+  return fn;
+}
+
+// A caller's device array must be device (or managed) memory of this GPU
+// and lie inside one allocation, so no kernel reading it leaves the
+// allocation whatever the caller passed.
+int check_device_span(const void* p, uint64_t bytes, int ordinal, const char* what) {
+  if (bytes == 0) return SPARSL_OK;
+  if (!p) return fail(SPARSL_ERR_INVALID, "null device array", std::string(what) + ": null device pointer");
+  cudaPointerAttributes at{};
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(SPARSL_ERR_INVALID, "not device memory", std::string(what) + ": not a device pointer");
+  }
+  if ((at.type != cudaMemoryTypeDevice && at.type != cudaMemoryTypeManaged) ||
+      (at.type == cudaMemoryTypeDevice && at.device != ordinal))
+    return fail(SPARSL_ERR_INVALID, "not device memory",
+                std::string(what) + ": not device memory of GPU " + std::to_string(ordinal));
+  if (at.type == cudaMemoryTypeDevice) {
+    AddrRangeFn fn = addr_range_fn();
+    unsigned long long base = 0;
+    size_t size = 0;
+    if (!fn || fn(&base, &size, reinterpret_cast<unsigned long long>(p)) != 0)
+      return fail(SPARSL_ERR_INVALID, "not device memory", std::string(what) + ": no allocation holds it");
+    const unsigned long long a = reinterpret_cast<unsigned long long>(p);
+    if (a + bytes < a || a + bytes > base + size)
+      return fail(SPARSL_ERR_INVALID, "device array too short",
+                  std::string(what) + ": the array runs past the end of its allocation");
+  }
+  return SPARSL_OK;
+}
+
+int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int precision, int with_transpose,
+                 sparsl_op** out);
+
+}  // namespace
+
 int sparsl_op_prepare(sparsl_dev* d, const uint32_t* row_ptr, uint64_t row_ptr_len, const uint32_t* col,
                       uint64_t col_len, uint64_t csr_ncols, uint64_t ncols, const float* weights,
                       uint64_t weights_len, int precision, int with_transpose, sparsl_shape* shape,
@@ -679,15 +769,47 @@ int sparsl_op_prepare(sparsl_dev* d, const uint32_t* row_ptr, uint64_t row_ptr_l
   int rc = sparsl_validate_csr(row_ptr, row_ptr_len, col, col_len, csr_ncols, ncols, &sh);
   if (shape) *shape = sh;
   if (rc != SPARSL_OK) return rc;
-  if (weights_len != sh.nnz) {
-    if (shape) {
-      shape->code = SPARSL_PLAN_WEIGHTS_LEN;
-      shape->a = sh.nnz;
-      shape->b = weights_len;
-    }
-    return fail(SPARSL_ERR_INVALID, "weights length", "weights must have one entry per non-zero");
+  TRY(check_prepare_args(sh, weights_len, precision, shape));
+  return prepare_body(d, PrepSrc{row_ptr, nullptr, col, weights, false}, sh, precision, with_transpose, out);
+}
+
+int sparsl_op_prepare_device(sparsl_dev* d, const uint32_t* d_row_ptr, uint64_t row_ptr_len, const uint32_t* d_col,
+                             uint64_t col_len, uint64_t csr_ncols, uint64_t ncols, const float* d_weights,
+                             uint64_t weights_len, int precision, int with_transpose, sparsl_shape* shape,
+                             sparsl_op** out) {
+  ADMIT();
+  if (!out || !d) return fail(SPARSL_ERR_INVALID, "null argument", "sparsl_op_prepare_device: null argument");
+  *out = nullptr;
+  CK("prepare_device", cudaSetDevice(d->ordinal));
+  TRY(check_device_span(d_row_ptr, row_ptr_len * 4, d->ordinal, "row_ptr"));
+  TRY(check_device_span(d_col, col_len * 4, d->ordinal, "col"));
+  TRY(check_device_span(d_weights, weights_len * 4, d->ordinal, "weights"));
+  std::vector<uint32_t> rp(row_ptr_len);
+  sparsl_shape sh{};
+  {
+    std::lock_guard<std::mutex> lk(d->mu);
+    if (row_ptr_len)
+      CK("prepare_device",
+         cudaMemcpyAsync(rp.data(), d_row_ptr, row_ptr_len * 4, cudaMemcpyDeviceToHost, d->stream));
+    CK("prepare_device", cudaStreamSynchronize(d->stream));
+    if (!d->vscratch.p && dalloc(d->vscratch, 32, false, d->stream) != cudaSuccess)
+      return fail(SPARSL_ERR_ALLOCATION, "validation scratch", "device allocation failed for validation scratch");
+    PlanResult r{};
+    CK("prepare_device", validate_csr_device(rp.data(), row_ptr_len, d_row_ptr, d_col, col_len, csr_ncols, ncols,
+                                             d->vscratch.as<unsigned long long>(), d->stream, &r));
+    to_shape(r, &sh);
   }
-  if (precision < 0 || precision > 2) return fail(SPARSL_ERR_INVALID, "precision", "unknown weight precision");
+  if (shape) *shape = sh;
+  if (sh.code != PLAN_OK) return fail(SPARSL_ERR_INVALID, "invalid CSR", "CSR failed validation");
+  TRY(check_prepare_args(sh, weights_len, precision, shape));
+  return prepare_body(d, PrepSrc{rp.data(), d_row_ptr, d_col, d_weights, true}, sh, precision, with_transpose, out);
+}
+
+namespace {
+int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int precision, int with_transpose,
+                 sparsl_op** out) {
+  const uint32_t* row_ptr = src.row_ptr;
+  int rc = SPARSL_OK;
   CK("prepare", cudaSetDevice(d->ordinal));
   auto* op = new sparsl_op();
   op->dev = d;
@@ -727,20 +849,26 @@ int sparsl_op_prepare(sparsl_dev* d, const uint32_t* row_ptr, uint64_t row_ptr_l
   PALLOC(op->tile_flags, ((uint64_t)std::max(row_tiles(op->nrows), ell_tiles(op->nrows)) + 1) * 8, false,
          "tile flags");
   PALLOC(op->ticket, 64, false, "tile ticket");
-  if (cudaMemcpyAsync(op->row_ptr.p, row_ptr, (nrows + 1) * 4, cudaMemcpyHostToDevice, op->stream) != cudaSuccess)
+  const cudaMemcpyKind in_kind = src.device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  if (cudaMemcpyAsync(op->row_ptr.p, src.d_row_ptr ? src.d_row_ptr : row_ptr, (nrows + 1) * 4, in_kind,
+                      op->stream) != cudaSuccess)
     return bail(fail_cuda("prepare", cudaGetLastError()));
   if (nnz) {
-    if (cudaMemcpyAsync(op->col.p, col, nnz * 4, cudaMemcpyHostToDevice, op->stream) != cudaSuccess)
+    if (cudaMemcpyAsync(op->col.p, src.col, nnz * 4, in_kind, op->stream) != cudaSuccess)
       return bail(fail_cuda("prepare", cudaGetLastError()));
   }
   std::vector<uint16_t> narrow;
   if (nnz) {
     if (precision == 0) {
-      if (cudaMemcpyAsync(op->w.p, weights, nnz * 4, cudaMemcpyHostToDevice, op->stream) != cudaSuccess)
+      if (cudaMemcpyAsync(op->w.p, src.weights, nnz * 4, in_kind, op->stream) != cudaSuccess)
+        return bail(fail_cuda("prepare", cudaGetLastError()));
+    } else if (src.device) {
+      // The same encoder as the host's, run on the GPU (codec.cuh).
+      if (launch_encode_narrow(precision, src.weights, op->w.as<uint16_t>(), nnz, op->stream) != cudaSuccess)
         return bail(fail_cuda("prepare", cudaGetLastError()));
     } else {
       narrow.resize(nnz);
-      encode_narrow(precision, weights, narrow.data(), nnz);
+      encode_narrow(precision, src.weights, narrow.data(), nnz);
       if (cudaMemcpyAsync(op->w.p, narrow.data(), nnz * 2, cudaMemcpyHostToDevice, op->stream) != cudaSuccess)
         return bail(fail_cuda("prepare", cudaGetLastError()));
     }
@@ -751,6 +879,16 @@ int sparsl_op_prepare(sparsl_dev* d, const uint32_t* row_ptr, uint64_t row_ptr_l
     cp.resize(nc + 1);
     cr.resize(nnz);
     ce.resize(nnz);
+    // The reverse index is built on the host; device sources copy col back.
+    std::vector<uint32_t> col_h;
+    const uint32_t* col = src.col;
+    if (src.device) {
+      col_h.resize(nnz);
+      if (nnz && (cudaMemcpyAsync(col_h.data(), src.col, nnz * 4, cudaMemcpyDeviceToHost, op->stream) != cudaSuccess ||
+                  cudaStreamSynchronize(op->stream) != cudaSuccess))
+        return bail(fail_cuda("prepare", cudaGetLastError()));
+      col = col_h.data();
+    }
     build_csc(row_ptr, nrows, col, nnz, nc, cp.data(), cr.data(), ce.data());
     PALLOC(op->col_ptr, (nc + 1) * 4, false, "csc col_ptr");
     cudaMemcpyAsync(op->col_ptr.p, cp.data(), (nc + 1) * 4, cudaMemcpyHostToDevice, op->stream);
@@ -872,6 +1010,7 @@ int sparsl_op_prepare(sparsl_dev* d, const uint32_t* row_ptr, uint64_t row_ptr_l
   *out = op;
   return SPARSL_OK;
 }
+}  // namespace
 
 void sparsl_op_destroy(sparsl_op* op) {
   if (!op) return;
