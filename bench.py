@@ -595,6 +595,28 @@ def bench_spmv(args, dev, want_cpu):
     tr = measure(opt, L.sparsl_op_spmv_t_device, dxt, SPMV_N, algot,
                  lambda ref: O.spmv_t(csc, w, xt, ref, par=True))
     del opt
+    # The reverse index itself, built on the GPU from device arrays (gate
+    # included; wall clock of the blocking C-ABI call) against the oracle's
+    # host counting sort.
+    drp, dcol = torch.from_numpy(rp.view(np.int32)).cuda(), torch.from_numpy(col.view(np.int32)).cuda()
+    dcp = torch.empty(SPMV_N + 1, dtype=torch.int32, device="cuda")
+    drow = torch.empty(col.size, dtype=torch.int32, device="cuda")
+    deidx = torch.empty(col.size, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    cts = []
+    for _ in range(args.warmup + 5):
+        t0 = time.perf_counter()
+        dev.csc_from_csr_device(drp, dcol, SPMV_N, dcp, drow, deidx)
+        cts.append((time.perf_counter() - t0) * 1e3)
+    csc_ms = statistics.median(cts[args.warmup:])
+    csc_ok = all(np.array_equal(g.cpu().numpy().view(np.uint32), w_) for g, w_ in zip((dcp, drow, deidx), csc))
+    t0 = time.perf_counter()
+    O.csc_from_csr(csr, SPMV_N)
+    csc_cpu_ms = (time.perf_counter() - t0) * 1e3
+    rev = {"ms": csc_ms, "edges_per_s": col.size / (csc_ms * 1e-3), "identical_to_oracle": csc_ok,
+           "cpu_ms": csc_cpu_ms, "cpu": "oracle counting sort (sparse.rs:361-427 restated), 1 thread",
+           "path": "sparsl_csc_from_csr_device: device gate + 3 radix passes + col_ptr/row"}
+    del drp, dcol, dcp, drow, deidx
     return {"metric": "SpMV effective HBM GB/s", "value": algo / (ms * 1e-3) / 1e9, "unit": "GB/s",
             "ms_per_step": ms, "kernel_ms_samples": len(ts), "algorithmic_bytes": algo,
             "config": "100,000 x 100,000, 64 distinct sorted cols/row, w U[-1,1], x U[0,1], f32; L2 flushed "
@@ -602,7 +624,7 @@ def bench_spmv(args, dev, want_cpu):
             "e2e": {"value": algo / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 2 * SPMV_N * 4,
                     "d2h_bytes_per_step": SPMV_N * 4, "path": "sparsl_op_spmv, pinned host x/y"},
             "bit_exact_vs_oracle": exact, "cpu_baseline": cpu,
-            "f16_weights": f16, "transpose": tr}
+            "f16_weights": f16, "transpose": tr, "reverse_index": rev}
 
 
 def bench_scan(args, dev, want_cpu):

@@ -123,8 +123,8 @@ void sparsl_quantise(int precision, const float *in, float *out, uint64_t n);
 
 /* ---- SparseOp (mod.rs:1281-2108) ---------------------------------------- */
 /* SparseOp::prepare (mod.rs:1305-1371): validates (the gate above, first
- * failure wins, reported in *shape), quantises, optionally builds the stable
- * reverse index (sparse.rs:361-427) and uploads once. */
+ * failure wins, reported in *shape), quantises, uploads once and optionally
+ * builds the stable reverse index (sparse.rs:361-427) on the GPU. */
 int sparsl_op_prepare(sparsl_dev *dev, const uint32_t *row_ptr, uint64_t row_ptr_len,
                       const uint32_t *col, uint64_t col_len, uint64_t csr_ncols, uint64_t ncols,
                       const float *weights, uint64_t weights_len, int precision, int with_transpose,
@@ -140,13 +140,24 @@ int sparsl_op_prepare(sparsl_dev *dev, const uint32_t *row_ptr, uint64_t row_ptr
  * bit-identical to one from sparsl_op_prepare on the same values.  Each
  * array must be device memory of this GPU lying inside one allocation
  * (else SPARSL_ERR_INVALID), and every write to it must have completed
- * before the call.  with_transpose copies col back to build the reverse
- * index on the host.  The caller keeps ownership of its arrays. */
+ * before the call.  with_transpose builds the reverse index on the GPU, as
+ * sparsl_op_prepare does.  The caller keeps ownership of its arrays. */
 int sparsl_op_prepare_device(sparsl_dev *dev, const uint32_t *d_row_ptr, uint64_t row_ptr_len,
                              const uint32_t *d_col, uint64_t col_len, uint64_t csr_ncols,
                              uint64_t ncols, const float *d_weights, uint64_t weights_len,
                              int precision, int with_transpose, sparsl_shape *shape,
                              sparsl_op **out);
+/* Csc::from_csr_slices (sparse.rs:361-427) on the GPU, for a CSR in device
+ * memory of `dev`: writes d_col_ptr[ncols + 1], and per slot d_row[col_len]
+ * and d_edge_idx[col_len] -- each column's edges in CSR order, the same
+ * arrays as the reference's counting sort.  The CSR passes the gate of
+ * sparsl_validate_csr first (payload in *shape).  Every array must be
+ * device memory of this GPU inside one allocation, with all writes to the
+ * inputs complete.  Runs on the device's stream and returns when done. */
+int sparsl_csc_from_csr_device(sparsl_dev *dev, const uint32_t *d_row_ptr, uint64_t row_ptr_len,
+                               const uint32_t *d_col, uint64_t col_len, uint64_t ncols,
+                               uint32_t *d_col_ptr, uint32_t *d_row, uint32_t *d_edge_idx,
+                               sparsl_shape *shape);
 void sparsl_op_destroy(sparsl_op *op);
 int sparsl_op_shape(sparsl_op *op, sparsl_shape *out);
 int sparsl_op_weight_precision(sparsl_op *op);    /* mod.rs:1582 */

@@ -60,6 +60,7 @@ SIGNATURES = {
                                 ctypes.POINTER(vp)]),
     "sparsl_op_prepare_device": (i32, [vp, vp, u64, vp, u64, u64, u64, vp, u64, i32, i32,
                                        ctypes.POINTER(Shape), ctypes.POINTER(vp)]),
+    "sparsl_csc_from_csr_device": (i32, [vp, vp, u64, vp, u64, u64, vp, vp, vp, ctypes.POINTER(Shape)]),
     "sparsl_op_destroy": (None, [vp]),
     "sparsl_op_shape": (i32, [vp, ctypes.POINTER(Shape)]),
     "sparsl_op_weight_precision": (i32, [vp]),

@@ -438,6 +438,25 @@ class Device:
     def prepare_bf16_with_transpose(self, csr: Csr, ncols: int, weights) -> "SparseOp":
         return SparseOp._prepare(self, csr, ncols, weights, True, WeightPrecision.Bf16)
 
+    def csc_from_csr_device(self, row_ptr, col, ncols: int, col_ptr, row, edge_idx) -> None:
+        """``Csc::from_csr_slices`` (sparse.rs:361-427) on the GPU.
+
+        Inputs and outputs are 32-bit device arrays of this GPU (torch tensors
+        or objects with ``data_ptr()`` / ``numel()``): ``col_ptr`` holds
+        ``ncols + 1`` entries, ``row`` and ``edge_idx`` one per edge.  The CSR
+        passes the same gate as ``prepare`` first (SparsePlanError)."""
+        torch = sys.modules.get("torch")
+        if torch is not None and isinstance(col, torch.Tensor) and col.is_cuda:
+            torch.cuda.synchronize(col.device)
+        sh = Shape()
+        rc = _lib.load().sparsl_csc_from_csr_device(self._h, row_ptr.data_ptr(), row_ptr.numel(), col.data_ptr(),
+                                                    col.numel(), int(ncols), col_ptr.data_ptr(), row.data_ptr(),
+                                                    edge_idx.data_ptr(), ctypes.byref(sh))
+        if rc == _lib.SPARSL_ERR_INVALID and sh.code != 0:
+            raise _plan_error(sh)
+        if rc != 0:
+            raise SparsePlanError("Backend", f"backend refused: {_lib.last_error()}", reason=_lib.last_reason())
+
     def prepare_device(self, row_ptr, col, ncols: int, weights, precision: WeightPrecision = WeightPrecision.F32,
                        transpose: bool = False, csr_ncols: Optional[int] = None) -> "SparseOp":
         """``prepare_with`` / ``prepare_with_transpose_precision`` for a CSR whose

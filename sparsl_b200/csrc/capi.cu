@@ -25,6 +25,7 @@
 
 #include "../../include/sparsl_cuda.h"
 #include "common.cuh"
+#include "csc.cuh"
 #include "ell.cuh"
 #include "host.hpp"
 #include "misc.cuh"
@@ -756,6 +757,33 @@ int check_device_span(const void* p, uint64_t bytes, int ordinal, const char* wh
 int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int precision, int with_transpose,
                  sparsl_op** out);
 
+// Device temporaries of one call, freed when it returns.
+struct TmpBufs {
+  DBuf row, eidx, keys, scratch, depth;
+  ~TmpBufs() {
+    for (DBuf* b : {&row, &eidx, &keys, &scratch, &depth}) dfree(*b);
+  }
+};
+
+// The CSR gate (validate_csr) for arrays in device memory; `rp` receives
+// the host copy of row_ptr.  Returns a status only for a CUDA failure; the
+// gate's verdict is in *sh.
+int gate_device(sparsl_dev* d, const uint32_t* d_row_ptr, uint64_t row_ptr_len, const uint32_t* d_col,
+                uint64_t col_len, uint64_t csr_ncols, uint64_t ncols, std::vector<uint32_t>& rp, sparsl_shape* sh) {
+  rp.assign(row_ptr_len, 0u);
+  std::lock_guard<std::mutex> lk(d->mu);
+  if (row_ptr_len)
+    CK("validate", cudaMemcpyAsync(rp.data(), d_row_ptr, row_ptr_len * 4, cudaMemcpyDeviceToHost, d->stream));
+  CK("validate", cudaStreamSynchronize(d->stream));
+  if (!d->vscratch.p && dalloc(d->vscratch, 32, false, d->stream) != cudaSuccess)
+    return fail(SPARSL_ERR_ALLOCATION, "validation scratch", "device allocation failed for validation scratch");
+  PlanResult r{};
+  CK("validate", validate_csr_device(rp.data(), row_ptr_len, d_row_ptr, d_col, col_len, csr_ncols, ncols,
+                                     d->vscratch.as<unsigned long long>(), d->stream, &r));
+  to_shape(r, sh);
+  return SPARSL_OK;
+}
+
 }  // namespace
 
 int sparsl_op_prepare(sparsl_dev* d, const uint32_t* row_ptr, uint64_t row_ptr_len, const uint32_t* col,
@@ -784,25 +812,39 @@ int sparsl_op_prepare_device(sparsl_dev* d, const uint32_t* d_row_ptr, uint64_t 
   TRY(check_device_span(d_row_ptr, row_ptr_len * 4, d->ordinal, "row_ptr"));
   TRY(check_device_span(d_col, col_len * 4, d->ordinal, "col"));
   TRY(check_device_span(d_weights, weights_len * 4, d->ordinal, "weights"));
-  std::vector<uint32_t> rp(row_ptr_len);
+  std::vector<uint32_t> rp;
   sparsl_shape sh{};
-  {
-    std::lock_guard<std::mutex> lk(d->mu);
-    if (row_ptr_len)
-      CK("prepare_device",
-         cudaMemcpyAsync(rp.data(), d_row_ptr, row_ptr_len * 4, cudaMemcpyDeviceToHost, d->stream));
-    CK("prepare_device", cudaStreamSynchronize(d->stream));
-    if (!d->vscratch.p && dalloc(d->vscratch, 32, false, d->stream) != cudaSuccess)
-      return fail(SPARSL_ERR_ALLOCATION, "validation scratch", "device allocation failed for validation scratch");
-    PlanResult r{};
-    CK("prepare_device", validate_csr_device(rp.data(), row_ptr_len, d_row_ptr, d_col, col_len, csr_ncols, ncols,
-                                             d->vscratch.as<unsigned long long>(), d->stream, &r));
-    to_shape(r, &sh);
-  }
+  TRY(gate_device(d, d_row_ptr, row_ptr_len, d_col, col_len, csr_ncols, ncols, rp, &sh));
   if (shape) *shape = sh;
   if (sh.code != PLAN_OK) return fail(SPARSL_ERR_INVALID, "invalid CSR", "CSR failed validation");
   TRY(check_prepare_args(sh, weights_len, precision, shape));
   return prepare_body(d, PrepSrc{rp.data(), d_row_ptr, d_col, d_weights, true}, sh, precision, with_transpose, out);
+}
+
+int sparsl_csc_from_csr_device(sparsl_dev* d, const uint32_t* d_row_ptr, uint64_t row_ptr_len, const uint32_t* d_col,
+                               uint64_t col_len, uint64_t ncols, uint32_t* d_col_ptr, uint32_t* d_row,
+                               uint32_t* d_edge_idx, sparsl_shape* shape) {
+  ADMIT();
+  if (!d) return fail(SPARSL_ERR_INVALID, "null argument", "sparsl_csc_from_csr_device: null device");
+  CK("csc_from_csr", cudaSetDevice(d->ordinal));
+  TRY(check_device_span(d_row_ptr, row_ptr_len * 4, d->ordinal, "row_ptr"));
+  TRY(check_device_span(d_col, col_len * 4, d->ordinal, "col"));
+  std::vector<uint32_t> rp;
+  sparsl_shape sh{};
+  TRY(gate_device(d, d_row_ptr, row_ptr_len, d_col, col_len, ncols, ncols, rp, &sh));
+  if (shape) *shape = sh;
+  if (sh.code != PLAN_OK) return fail(SPARSL_ERR_INVALID, "invalid CSR", "CSR failed validation");
+  // The gate bounds ncols and nnz by 2^32 - 1, so these sizes cannot overflow.
+  TRY(check_device_span(d_col_ptr, (ncols + 1) * 4, d->ordinal, "col_ptr"));
+  TRY(check_device_span(d_row, col_len * 4, d->ordinal, "row"));
+  TRY(check_device_span(d_edge_idx, col_len * 4, d->ordinal, "edge_idx"));
+  std::lock_guard<std::mutex> lk(d->mu);
+  TmpBufs tmp;
+  if (dalloc(tmp.scratch, csc_scratch_bytes(sh.nnz), false, d->stream) != cudaSuccess)
+    return fail(SPARSL_ERR_ALLOCATION, "reverse index", "device allocation failed for the reverse index");
+  CK("csc_from_csr", csc_build(d_row_ptr, sh.nrows, d_col, sh.nnz, ncols, d_col_ptr, d_row, d_edge_idx, nullptr,
+                               tmp.scratch.p, d->err.d, d->stream));
+  return wait_bounded(d->stream, d->ev, d->err.d, d->err.h, "csc_from_csr");
 }
 
 namespace {
@@ -873,45 +915,38 @@ int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int 
         return bail(fail_cuda("prepare", cudaGetLastError()));
     }
   }
-  std::vector<uint32_t> cp, cr, ce, sell_row_h, sell_eidx_h;
   std::vector<uint64_t> sell_ptr_h;
   if (op->has_t) {
-    cp.resize(nc + 1);
-    cr.resize(nnz);
-    ce.resize(nnz);
-    // The reverse index is built on the host; device sources copy col back.
-    std::vector<uint32_t> col_h;
-    const uint32_t* col = src.col;
-    if (src.device) {
-      col_h.resize(nnz);
-      if (nnz && (cudaMemcpyAsync(col_h.data(), src.col, nnz * 4, cudaMemcpyDeviceToHost, op->stream) != cudaSuccess ||
-                  cudaStreamSynchronize(op->stream) != cudaSuccess))
-        return bail(fail_cuda("prepare", cudaGetLastError()));
-      col = col_h.data();
-    }
-    build_csc(row_ptr, nrows, col, nnz, nc, cp.data(), cr.data(), ce.data());
+    // The stable reverse index, built on the GPU from the uploaded CSR
+    // (csc.cu) into temporaries; the operator keeps the sliced-ELL form or,
+    // for hub-column operators, the CSC itself.
     PALLOC(op->col_ptr, (nc + 1) * 4, false, "csc col_ptr");
-    cudaMemcpyAsync(op->col_ptr.p, cp.data(), (nc + 1) * 4, cudaMemcpyHostToDevice, op->stream);
+    TmpBufs tmp;
+    const uint64_t nslices = (nc + 31) / 32;
+    if (dalloc(tmp.row, nnz * 4, false, op->stream) != cudaSuccess ||
+        dalloc(tmp.eidx, nnz * 4, false, op->stream) != cudaSuccess ||
+        dalloc(tmp.keys, nnz * 4, false, op->stream) != cudaSuccess ||
+        dalloc(tmp.scratch, csc_scratch_bytes(nnz), false, op->stream) != cudaSuccess ||
+        dalloc(tmp.depth, nslices * 4, false, op->stream) != cudaSuccess)
+      return bail(fail(SPARSL_ERR_ALLOCATION, "reverse index", "device allocation failed for the reverse index"));
+    if (csc_build(op->row_ptr.as<uint32_t>(), nrows, op->col.as<uint32_t>(), nnz, nc, op->col_ptr.as<uint32_t>(),
+                  tmp.row.as<uint32_t>(), tmp.eidx.as<uint32_t>(), tmp.keys.as<uint32_t>(), tmp.scratch.p, op->err.d,
+                  op->stream) != cudaSuccess ||
+        launch_slice_depth(op->col_ptr.as<uint32_t>(), nc, tmp.depth.as<uint32_t>(), op->stream) != cudaSuccess)
+      return bail(fail_cuda("prepare", cudaGetLastError()));
     // Sliced ELL: slices of 32 columns, each padded to its longest column,
     // entries column-major within the slice.  Kept only while the padding at
     // most doubles the entries (a hub column would blow it up).
-    const uint64_t nslices = (nc + 31) / 32;
-    std::vector<uint64_t> sp(nslices + 1, 0);
-    for (uint64_t sl = 0; sl < nslices; ++sl) {
-      uint32_t depth = 0;
-      for (uint64_t c = sl * 32; c < std::min<uint64_t>(nc, sl * 32 + 32); ++c) depth = std::max(depth, cp[c + 1] - cp[c]);
-      sp[sl + 1] = sp[sl] + (uint64_t)depth * 32;
+    std::vector<uint32_t> depth(nslices);
+    if (nslices) {
+      if (cudaMemcpyAsync(depth.data(), tmp.depth.p, nslices * 4, cudaMemcpyDeviceToHost, op->stream) != cudaSuccess)
+        return bail(fail_cuda("prepare", cudaGetLastError()));
     }
+    rc = wait_op(op, "prepare");  // also reports a reverse-index look-back that gave up
+    if (rc != SPARSL_OK) return bail(rc);
+    std::vector<uint64_t> sp(nslices + 1, 0);
+    for (uint64_t sl = 0; sl < nslices; ++sl) sp[sl + 1] = sp[sl] + (uint64_t)depth[sl] * 32;
     if (nnz && sp[nslices] <= 2 * nnz + 32 * nslices && nslices <= 0xffffffffull) {
-      sell_row_h.assign(sp[nslices], 0u);
-      sell_eidx_h.assign(sp[nslices], 0u);
-      for (uint64_t c = 0; c < nc; ++c) {
-        const uint64_t b = sp[c / 32] + (c % 32);
-        for (uint32_t k = cp[c]; k < cp[c + 1]; ++k) {
-          sell_row_h[b + (uint64_t)(k - cp[c]) * 32] = cr[k];
-          sell_eidx_h[b + (uint64_t)(k - cp[c]) * 32] = ce[k];
-        }
-      }
       sell_ptr_h.swap(sp);
       op->sell_total = sell_ptr_h[nslices];
       op->sell_slices = (uint32_t)nslices;
@@ -921,20 +956,19 @@ int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int 
       PALLOC(op->w_sell, op->sell_total * wbytes, false, "sliced-ELL values");
       PALLOC(op->sell_ctr, 16, false, "sliced-ELL counter");
       cudaMemcpyAsync(op->sell_ptr.p, sell_ptr_h.data(), (nslices + 1) * 8, cudaMemcpyHostToDevice, op->stream);
-      cudaMemcpyAsync(op->sell_row.p, sell_row_h.data(), op->sell_total * 4, cudaMemcpyHostToDevice, op->stream);
-      cudaMemcpyAsync(op->sell_eidx.p, sell_eidx_h.data(), op->sell_total * 4, cudaMemcpyHostToDevice, op->stream);
+      cudaMemsetAsync(op->sell_row.p, 0, op->sell_total * 4, op->stream);
+      cudaMemsetAsync(op->sell_eidx.p, 0, op->sell_total * 4, op->stream);
       cudaMemsetAsync(op->sell_ctr.p, 0, op->sell_ctr.bytes, op->stream);
-      if (launch_gather_weights(op->w.p, op->sell_eidx.as<uint32_t>(), op->sell_total, (int)wbytes, op->w_sell.p,
+      if (launch_sell_fill(op->col_ptr.as<uint32_t>(), tmp.keys.as<uint32_t>(), tmp.row.as<uint32_t>(),
+                           tmp.eidx.as<uint32_t>(), nnz, op->sell_ptr.as<unsigned long long>(),
+                           op->sell_row.as<uint32_t>(), op->sell_eidx.as<uint32_t>(), op->stream) != cudaSuccess ||
+          launch_gather_weights(op->w.p, op->sell_eidx.as<uint32_t>(), op->sell_total, (int)wbytes, op->w_sell.p,
                                 op->stream) != cudaSuccess)
         return bail(fail_cuda("prepare", cudaGetLastError()));
       op->sell_ok = true;
     } else {
-      PALLOC(op->csc_row, nnz * 4, false, "csc row");
-      PALLOC(op->csc_eidx, nnz * 4, false, "csc edge_idx");
-      if (nnz) {
-        cudaMemcpyAsync(op->csc_row.p, cr.data(), nnz * 4, cudaMemcpyHostToDevice, op->stream);
-        cudaMemcpyAsync(op->csc_eidx.p, ce.data(), nnz * 4, cudaMemcpyHostToDevice, op->stream);
-      }
+      std::swap(op->csc_row, tmp.row);
+      std::swap(op->csc_eidx, tmp.eidx);
       // The transpose product streams its weights in reverse-index order
       // instead of gathering them through edge_idx (same products, same order).
       PALLOC(op->w_csc, nnz * wbytes, false, "csc values");
@@ -943,6 +977,8 @@ int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int 
               cudaSuccess)
         return bail(fail_cuda("prepare", cudaGetLastError()));
     }
+    rc = wait_op(op, "prepare");  // the temporaries are freed on return
+    if (rc != SPARSL_OK) return bail(rc);
   }
   cudaMemsetAsync(op->rx.p, 0, op->rx.bytes, op->stream);
   cudaMemsetAsync(op->rxs[0].p, 0, op->rxs[0].bytes, op->stream);

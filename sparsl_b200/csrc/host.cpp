@@ -1,5 +1,5 @@
-// Host-side pieces of the library: the CSR gate, the narrow-weight encoders
-// and the stable reverse index.  Plain C++; no CUDA calls.
+// Host-side pieces of the library: the CSR gate and the narrow-weight
+// encoders.  Plain C++; no CUDA calls.
 #include "host.hpp"
 
 #include "codec.cuh"
@@ -198,22 +198,6 @@ PlanResult validate_csr(const uint32_t* row_ptr, uint64_t row_ptr_len, const uin
   r.nnz = col_len;
   r.max_row_nnz = mx;
   return r;
-}
-
-// Stable reverse index: a counting sort by column that keeps CSR order within
-// each column (src/sparse.rs:361-427).
-void build_csc(const uint32_t* row_ptr, uint64_t nrows, const uint32_t* col, uint64_t nnz, uint64_t ncols,
-               uint32_t* col_ptr, uint32_t* row, uint32_t* edge_idx) {
-  std::vector<uint32_t> cursor(ncols + 1, 0);
-  for (uint64_t k = 0; k < nnz; ++k) cursor[col[k] + 1]++;
-  for (uint64_t c = 0; c < ncols; ++c) cursor[c + 1] += cursor[c];
-  std::memcpy(col_ptr, cursor.data(), sizeof(uint32_t) * (ncols + 1));
-  for (uint64_t r = 0; r < nrows; ++r)
-    for (uint64_t k = row_ptr[r]; k < row_ptr[r + 1]; ++k) {
-      const uint32_t slot = cursor[col[k]]++;
-      row[slot] = (uint32_t)r;
-      edge_idx[slot] = (uint32_t)k;
-    }
 }
 
 }  // namespace sparsl

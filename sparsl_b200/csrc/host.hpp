@@ -33,8 +33,4 @@ void quantise(int precision, const float* in, float* out, uint64_t n);
 
 PlanResult validate_csr(const uint32_t* row_ptr, uint64_t row_ptr_len, const uint32_t* col, uint64_t col_len,
                         uint64_t csr_ncols, uint64_t ncols);
-
-void build_csc(const uint32_t* row_ptr, uint64_t nrows, const uint32_t* col, uint64_t nnz, uint64_t ncols,
-               uint32_t* col_ptr, uint32_t* row, uint32_t* edge_idx);
-
 }  // namespace sparsl
