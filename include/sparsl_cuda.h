@@ -210,10 +210,42 @@ int sparsl_op_spike_trace(sparsl_op *op, uint32_t *out, uint64_t cap, uint64_t *
  * compacted on the device by warp ballots and a decoupled look-back. */
 int sparsl_op_spike_indices(sparsl_op *op, uint32_t *out, uint64_t cap, uint64_t *count);
 
+/* ---- zero-copy interop: bound buffers and event handoff ------------------ */
+/* CUDA analogue of SparseOp::bind_mtl_x / bind_mtl_y / unbind_mtl_* /
+ * mtl_*_gpu_address / alloc_mtl_f32 (mod.rs:1975-2066, metal.rs:1834-1916).
+ * A bound caller buffer (device memory of the operator's GPU holding at least
+ * ncols (x) or nrows (y) f32 up to the end of its allocation; else
+ * SPARSL_ERR_BACKEND or SPARSL_ERR_LENGTH, validate_external_vec
+ * metal.rs:1805-1832) replaces the operator's own x / y:
+ *  - sparsl_op_spmv and sparsl_op_fused_lif read a bound x instead of the
+ *    host slice; sparsl_op_spmv accumulates into a bound y and copies it
+ *    into the host slice afterwards;
+ *  - spmv_resident, fused_lif_resident and sync_y use the bound buffers;
+ *  - write_x / write_y are refused (SPARSL_ERR_BACKEND) while bound.
+ * The caller keeps the buffer alive while it is bound. */
+int sparsl_op_bind_x(sparsl_op *op, const float *d_x);
+int sparsl_op_bind_y(sparsl_op *op, float *d_y);
+int sparsl_op_unbind_x(sparsl_op *op);
+int sparsl_op_unbind_y(sparsl_op *op);
+int sparsl_op_x_address(sparsl_op *op, uint64_t *out); /* active x: bound or owned */
+int sparsl_op_y_address(sparsl_op *op, uint64_t *out);
+/* n f32 of device memory on the operator's GPU, filled from `data` (NULL:
+ * uninitialised); free with sparsl_device_free. */
+int sparsl_op_alloc_f32(sparsl_op *op, const float *data, uint64_t n, float **out);
+/* wait_shared_event / signal_shared_event (metal.rs:1918-1953) with a CUDA
+ * event (cudaEvent_t) in place of an MTLSharedEvent:
+ *  - wait: the operator's stream waits for the event on the device, and the
+ *    host polls it for up to timeout_ms (SPARSL_ERR_EXECUTION on expiry).
+ *    NULL returns at once, like a value of 0.
+ *  - signal: records the event on the operator's stream, so it completes
+ *    after all of the operator's work enqueued before it. */
+int sparsl_op_wait_event(sparsl_op *op, void *event, uint64_t timeout_ms);
+int sparsl_op_signal_event(sparsl_op *op, void *event);
+
 /* ---- zero-copy device-pointer entry points (extension) ------------------- */
-/* CUDA analogue of bind_mtl_x / bind_mtl_y (mod.rs:1975-2098): operands are
- * device pointers and the work is only enqueued on `stream` (cudaStream_t, or
- * NULL for the operator's own stream).  No wait, no canary check. */
+/* Operands are device pointers and the work is only enqueued on `stream`
+ * (cudaStream_t, or NULL for the operator's own stream).  No wait, no canary
+ * check. */
 int sparsl_op_spmv_device(sparsl_op *op, const float *d_x, float *d_y, void *stream);
 int sparsl_op_spmv_spikes_device(sparsl_op *op, const uint32_t *d_spikes, float *d_y, void *stream);
 int sparsl_op_spmv_t_device(sparsl_op *op, const float *d_x, float *d_y, void *stream);

@@ -12,6 +12,7 @@ from .backend import (  # noqa: F401
     BackendUnavailable,
     Csr,
     CsrError,
+    DeviceBuffer,
     Device,
     LifParams,
     LifParamsError,

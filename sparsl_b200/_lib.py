@@ -61,6 +61,15 @@ SIGNATURES = {
     "sparsl_op_prepare_device": (i32, [vp, vp, u64, vp, u64, u64, u64, vp, u64, i32, i32,
                                        ctypes.POINTER(Shape), ctypes.POINTER(vp)]),
     "sparsl_csc_from_csr_device": (i32, [vp, vp, u64, vp, u64, u64, vp, vp, vp, ctypes.POINTER(Shape)]),
+    "sparsl_op_bind_x": (i32, [vp, vp]),
+    "sparsl_op_bind_y": (i32, [vp, vp]),
+    "sparsl_op_unbind_x": (i32, [vp]),
+    "sparsl_op_unbind_y": (i32, [vp]),
+    "sparsl_op_x_address": (i32, [vp, ctypes.POINTER(u64)]),
+    "sparsl_op_y_address": (i32, [vp, ctypes.POINTER(u64)]),
+    "sparsl_op_alloc_f32": (i32, [vp, vp, u64, ctypes.POINTER(vp)]),
+    "sparsl_op_wait_event": (i32, [vp, vp, u64]),
+    "sparsl_op_signal_event": (i32, [vp, vp]),
     "sparsl_op_destroy": (None, [vp]),
     "sparsl_op_shape": (i32, [vp, ctypes.POINTER(Shape)]),
     "sparsl_op_weight_precision": (i32, [vp]),

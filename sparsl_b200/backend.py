@@ -509,6 +509,52 @@ def _spike_view(spikes):
     return spikes.view(np.uint8)
 
 
+def _dptr(buffer):
+    return None if buffer is None else buffer.data_ptr()
+
+
+def _event_handle(event):
+    if event is None:
+        return None
+    if isinstance(event, int):
+        return event
+    return getattr(event, "cuda_event")  # torch.cuda.Event
+
+
+class DeviceBuffer:
+    """Device memory returned by ``SparseOp.alloc_cuda_f32`` (freed on ``free``
+    or garbage collection)."""
+
+    def __init__(self, ptr: int, n: int):
+        self._ptr, self._n = ptr, n
+
+    def data_ptr(self) -> int:
+        return self._ptr
+
+    def numel(self) -> int:
+        return self._n
+
+    def element_size(self) -> int:
+        return 4
+
+    def to_numpy(self) -> np.ndarray:
+        out = np.empty(self._n, np.float32)
+        if self._n:
+            _check(_lib.load().sparsl_memcpy(out.ctypes.data, self._ptr, out.nbytes), "memcpy")
+        return out
+
+    def free(self) -> None:
+        if self._ptr:
+            _lib.load().sparsl_device_free(self._ptr)
+            self._ptr = 0
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
 # --------------------------------------------------------------------------
 # SparseOp (mod.rs:1281-2108)
 # --------------------------------------------------------------------------
@@ -769,6 +815,51 @@ class SparseOp:
         sp = _spike_view(spikes)
         _check(_lib.load().sparsl_op_sync_lif_state(self._h, _ptr(v), _ptr(theta), _ptr(sp), n),
                "sync_lif_state")
+
+    # ---- zero-copy interop (mod.rs:1975-2098) ----
+    def bind_cuda_x(self, buffer) -> None:
+        """``bind_mtl_x``: a caller device buffer (torch tensor, DeviceBuffer or
+        anything with ``data_ptr()``) of at least ncols f32 becomes this
+        operator's x.  The caller keeps it alive while bound."""
+        _check(_lib.load().sparsl_op_bind_x(self._h, _dptr(buffer)), "bind_x")
+
+    def bind_cuda_y(self, buffer) -> None:
+        """``bind_mtl_y``: a caller device buffer of at least nrows f32 becomes y."""
+        _check(_lib.load().sparsl_op_bind_y(self._h, _dptr(buffer)), "bind_y")
+
+    def unbind_cuda_x(self) -> None:
+        _check(_lib.load().sparsl_op_unbind_x(self._h), "unbind_x")
+
+    def unbind_cuda_y(self) -> None:
+        _check(_lib.load().sparsl_op_unbind_y(self._h), "unbind_y")
+
+    def cuda_x_gpu_address(self) -> int:
+        out = ctypes.c_uint64()
+        _check(_lib.load().sparsl_op_x_address(self._h, ctypes.byref(out)), "x_address")
+        return out.value
+
+    def cuda_y_gpu_address(self) -> int:
+        out = ctypes.c_uint64()
+        _check(_lib.load().sparsl_op_y_address(self._h, ctypes.byref(out)), "y_address")
+        return out.value
+
+    def alloc_cuda_f32(self, data) -> "DeviceBuffer":
+        """``alloc_mtl_f32``: an f32 device buffer on this operator's GPU holding ``data``."""
+        a = np.ascontiguousarray(data, dtype=np.float32)
+        out = ctypes.c_void_p()
+        _check(_lib.load().sparsl_op_alloc_f32(self._h, _ptr(a) if a.size else None, a.size, ctypes.byref(out)),
+               "alloc_f32")
+        return DeviceBuffer(out.value, a.size)
+
+    def wait_cuda_event(self, event, timeout_ms: int) -> None:
+        """``wait_shared_event`` for a CUDA event (torch.cuda.Event or a raw
+        cudaEvent_t): device-side ordering plus a bounded host wait."""
+        _check(_lib.load().sparsl_op_wait_event(self._h, _event_handle(event), int(timeout_ms)), "wait_event")
+
+    def signal_cuda_event(self, event) -> None:
+        """``signal_shared_event``: records the (already created) CUDA event on
+        this operator's stream, after all of its enqueued work."""
+        _check(_lib.load().sparsl_op_signal_event(self._h, _event_handle(event)), "signal_event")
 
     # ---- extensions: tick trace ----
     def sync_x_spikes(self) -> np.ndarray:

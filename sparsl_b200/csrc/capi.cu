@@ -326,7 +326,13 @@ struct sparsl_op {
   // staging for host-slice calls (kept apart from resident state, as the
   // reference CPU arm's slice API never touches its resident scratch)
   DBuf sx, sbits, sy, sv, sth, sspk;
+  // Caller-owned device buffers bound as the SpMV x (ncols f32) and y
+  // (nrows f32) in place of the operator's own (zero-copy interop).
+  const float* ext_x = nullptr;
+  float* ext_y = nullptr;
   uint64_t words() const { return packed_len(ncols); }
+  const float* x_active() const { return ext_x ? ext_x : rx.as<float>(); }
+  float* y_active() const { return ext_y ? ext_y : ry.as<float>(); }
 };
 
 namespace {
@@ -1108,15 +1114,26 @@ int sparsl_op_spmv(sparsl_op* op, const float* x, uint64_t x_len, float* y, uint
   if (op->nrows == 0) return SPARSL_OK;
   std::lock_guard<std::mutex> lk(op->mu);
   CK("spmv", cudaSetDevice(op->dev->ordinal));
-  ALLOC(op->sx, (uint64_t)op->ncols * 4 + 16, false, "x staging");
-  ALLOC(op->sy, (uint64_t)op->nrows * 4 + 16, true, "y staging");
-  if (op->ncols) CK("spmv", cudaMemcpyAsync(op->sx.p, x, (uint64_t)op->ncols * 4, cudaMemcpyHostToDevice, op->stream));
-  CK("spmv", cudaMemcpyAsync(op->sy.p, y, (uint64_t)op->nrows * 4, cudaMemcpyHostToDevice, op->stream));
+  // A bound x is read in place of the slice; a bound y is accumulated into
+  // and then read back into the slice (metal.rs:2143-2170).
   RowLaunch p = fwd_launch(op);
-  p.x = op->sx.as<float>();
-  p.y = op->sy.as<float>();
+  if (op->ext_x) {
+    p.x = op->ext_x;
+  } else {
+    ALLOC(op->sx, (uint64_t)op->ncols * 4 + 16, false, "x staging");
+    if (op->ncols)
+      CK("spmv", cudaMemcpyAsync(op->sx.p, x, (uint64_t)op->ncols * 4, cudaMemcpyHostToDevice, op->stream));
+    p.x = op->sx.as<float>();
+  }
+  if (op->ext_y) {
+    p.y = op->ext_y;
+  } else {
+    ALLOC(op->sy, (uint64_t)op->nrows * 4 + 16, true, "y staging");
+    CK("spmv", cudaMemcpyAsync(op->sy.p, y, (uint64_t)op->nrows * 4, cudaMemcpyHostToDevice, op->stream));
+    p.y = op->sy.as<float>();
+  }
   CK("spmv", launch_fwd(op, p, op->stream));
-  CK("spmv", cudaMemcpyAsync(y, op->sy.p, (uint64_t)op->nrows * 4, cudaMemcpyDeviceToHost, op->stream));
+  CK("spmv", cudaMemcpyAsync(y, p.y, (uint64_t)op->nrows * 4, cudaMemcpyDeviceToHost, op->stream));
   return finish(op, "spmv");
 }
 
@@ -1240,7 +1257,9 @@ static int fused_common(sparsl_op* op, const float* x, const uint32_t* bits, flo
   ALLOC(op->sth, nr * 4 + 16, true, "theta staging");
   ALLOC(op->sspk, nr + 16, true, "spike staging");
   RowLaunch p = fwd_launch(op);
-  if (x) {
+  if (x && op->ext_x) {
+    p.x = op->ext_x;  // a bound x replaces the slice (metal.rs:2686-2688)
+  } else if (x) {
     ALLOC(op->sx, (uint64_t)op->ncols * 4 + 16, false, "x staging");
     if (op->ncols) CK(name, cudaMemcpyAsync(op->sx.p, x, (uint64_t)op->ncols * 4, cudaMemcpyHostToDevice, op->stream));
     p.x = op->sx.as<float>();
@@ -1288,6 +1307,9 @@ int sparsl_op_write_x(sparsl_op* op, const float* x, uint64_t len) {
   ADMIT();
   TRY(check_min("x", len, op->ncols));
   std::lock_guard<std::mutex> lk(op->mu);
+  if (op->ext_x)
+    return fail(SPARSL_ERR_BACKEND, "write_x refused while an external buffer is bound as x; unbind first",
+                "write_x refused while an external buffer is bound as x; unbind first");
   CK("write_x", cudaSetDevice(op->dev->ordinal));
   if (op->ncols) CK("write_x", cudaMemcpyAsync(op->rx.p, x, (uint64_t)op->ncols * 4, cudaMemcpyHostToDevice, op->stream));
   return wait_op(op, "write_x");
@@ -1307,6 +1329,9 @@ int sparsl_op_write_y(sparsl_op* op, const float* y, uint64_t len) {
   ADMIT();
   TRY(check_len("y", len, op->nrows));
   std::lock_guard<std::mutex> lk(op->mu);
+  if (op->ext_y)
+    return fail(SPARSL_ERR_BACKEND, "write_y refused while an external buffer is bound as y; unbind first",
+                "write_y refused while an external buffer is bound as y; unbind first");
   CK("write_y", cudaSetDevice(op->dev->ordinal));
   if (op->nrows) CK("write_y", cudaMemcpyAsync(op->ry.p, y, (uint64_t)op->nrows * 4, cudaMemcpyHostToDevice, op->stream));
   return wait_op(op, "write_y");
@@ -1330,8 +1355,8 @@ int sparsl_op_spmv_resident(sparsl_op* op) {
   std::lock_guard<std::mutex> lk(op->mu);
   CK("spmv_resident", cudaSetDevice(op->dev->ordinal));
   RowLaunch p = fwd_launch(op);
-  p.x = op->rx.as<float>();
-  p.y = op->ry.as<float>();
+  p.x = op->x_active();
+  p.y = op->y_active();
   CK("spmv_resident", launch_fwd(op, p, op->stream));
   return wait_op(op, "spmv_resident");
 }
@@ -1352,7 +1377,7 @@ int sparsl_op_fused_lif_resident(sparsl_op* op, float decay, float v_reset, floa
   std::lock_guard<std::mutex> lk(op->mu);
   CK("fused_spmv_lif_resident", cudaSetDevice(op->dev->ordinal));
   RowLaunch p = fwd_launch(op);
-  p.x = op->rx.as<float>();
+  p.x = op->x_active();
   lif_resident_launch(op, p, decay, v_reset, dtheta);
   CK("fused_spmv_lif_resident", launch_fwd(op, p, op->stream));
   return wait_op(op, "fused_spmv_lif_resident");
@@ -1423,7 +1448,8 @@ int sparsl_op_sync_y(sparsl_op* op, float* y, uint64_t len) {
   TRY(check_len("y", len, op->nrows));
   std::lock_guard<std::mutex> lk(op->mu);
   CK("sync_y", cudaSetDevice(op->dev->ordinal));
-  if (op->nrows) CK("sync_y", cudaMemcpyAsync(y, op->ry.p, (uint64_t)op->nrows * 4, cudaMemcpyDeviceToHost, op->stream));
+  if (op->nrows)
+    CK("sync_y", cudaMemcpyAsync(y, op->y_active(), (uint64_t)op->nrows * 4, cudaMemcpyDeviceToHost, op->stream));
   return finish(op, "sync_y");
 }
 
@@ -1438,6 +1464,134 @@ int sparsl_op_sync_lif_state(sparsl_op* op, float* v, float* theta, uint8_t* spi
     CK("sync_lif_state", cudaMemcpyAsync(spikes, op->rspk.p, n, cudaMemcpyDeviceToHost, op->stream));
   }
   return finish(op, "sync_lif_state");
+}
+
+// ---- zero-copy interop (mod.rs:1975-2098, metal.rs:1805-1955) -------------
+namespace {
+
+// validate_external_vec (metal.rs:1805-1832): the buffer must be device
+// memory of the operator's GPU and hold `elems` f32 from `p` to the end of
+// its allocation.
+int check_external(sparsl_op* op, const void* p, uint64_t elems, const char* what) {
+  cudaPointerAttributes at{};
+  const bool ok = p && cudaPointerGetAttributes(&at, p) == cudaSuccess &&
+                  ((at.type == cudaMemoryTypeDevice && at.device == op->dev->ordinal) ||
+                   at.type == cudaMemoryTypeManaged);
+  if (!ok) {
+    cudaGetLastError();
+    return fail(SPARSL_ERR_BACKEND, "external buffer is not device memory of this operator's GPU",
+                std::string(what) + ": not device memory of GPU " + std::to_string(op->dev->ordinal));
+  }
+  AddrRangeFn fn = addr_range_fn();
+  unsigned long long base = 0;
+  size_t size = 0;
+  const unsigned long long a = reinterpret_cast<unsigned long long>(p);
+  if (!fn || fn(&base, &size, a) != 0)
+    return fail(SPARSL_ERR_BACKEND, "external buffer is not device memory of this operator's GPU",
+                std::string(what) + ": no allocation holds it");
+  const uint64_t need = elems * 4, got = base + size - a;
+  if (got < need)
+    return fail(SPARSL_ERR_LENGTH, "external buffer too short",
+                std::string(what) + ": needs " + std::to_string(need) + " bytes, its allocation holds " +
+                    std::to_string(got) + " from this address");
+  return SPARSL_OK;
+}
+
+}  // namespace
+
+int sparsl_op_bind_x(sparsl_op* op, const float* d_x) {
+  ADMIT();
+  if (!op) return fail(SPARSL_ERR_INVALID, "null argument", "bind_x: null operator");
+  CK("bind_x", cudaSetDevice(op->dev->ordinal));
+  TRY(check_external(op, d_x, op->ncols, "external x"));
+  std::lock_guard<std::mutex> lk(op->mu);
+  op->ext_x = d_x;
+  return SPARSL_OK;
+}
+
+int sparsl_op_bind_y(sparsl_op* op, float* d_y) {
+  ADMIT();
+  if (!op) return fail(SPARSL_ERR_INVALID, "null argument", "bind_y: null operator");
+  CK("bind_y", cudaSetDevice(op->dev->ordinal));
+  TRY(check_external(op, d_y, op->nrows, "external y"));
+  std::lock_guard<std::mutex> lk(op->mu);
+  op->ext_y = d_y;
+  return SPARSL_OK;
+}
+
+int sparsl_op_unbind_x(sparsl_op* op) {
+  if (!op) return fail(SPARSL_ERR_INVALID, "null argument", "unbind_x: null operator");
+  std::lock_guard<std::mutex> lk(op->mu);
+  op->ext_x = nullptr;
+  return SPARSL_OK;
+}
+
+int sparsl_op_unbind_y(sparsl_op* op) {
+  if (!op) return fail(SPARSL_ERR_INVALID, "null argument", "unbind_y: null operator");
+  std::lock_guard<std::mutex> lk(op->mu);
+  op->ext_y = nullptr;
+  return SPARSL_OK;
+}
+
+int sparsl_op_x_address(sparsl_op* op, uint64_t* out) {
+  if (!op || !out) return fail(SPARSL_ERR_INVALID, "null argument", "x_address: null argument");
+  std::lock_guard<std::mutex> lk(op->mu);
+  *out = reinterpret_cast<uint64_t>(op->x_active());
+  return SPARSL_OK;
+}
+
+int sparsl_op_y_address(sparsl_op* op, uint64_t* out) {
+  if (!op || !out) return fail(SPARSL_ERR_INVALID, "null argument", "y_address: null argument");
+  std::lock_guard<std::mutex> lk(op->mu);
+  *out = reinterpret_cast<uint64_t>(op->y_active());
+  return SPARSL_OK;
+}
+
+int sparsl_op_alloc_f32(sparsl_op* op, const float* data, uint64_t n, float** out) {
+  ADMIT();
+  if (!op || !out) return fail(SPARSL_ERR_INVALID, "null argument", "alloc_f32: null argument");
+  *out = nullptr;
+  CK("alloc_f32", cudaSetDevice(op->dev->ordinal));
+  void* p = sparsl_device_alloc(op->dev, n * 4);
+  if (!p)
+    return fail(SPARSL_ERR_BACKEND, "could not allocate an external buffer on the operator's GPU",
+                "alloc_f32: device allocation failed");
+  if (n && data && cudaMemcpy(p, data, n * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+    sparsl_device_free(p);
+    return fail_cuda("alloc_f32", cudaGetLastError());
+  }
+  *out = static_cast<float*>(p);
+  return SPARSL_OK;
+}
+
+int sparsl_op_wait_event(sparsl_op* op, void* event, uint64_t timeout_ms) {
+  ADMIT();
+  if (!op) return fail(SPARSL_ERR_INVALID, "null argument", "wait_event: null operator");
+  if (!event) return SPARSL_OK;  // like a shared-event value of 0: nothing to wait for
+  CK("wait_event", cudaSetDevice(op->dev->ordinal));
+  cudaEvent_t ev = static_cast<cudaEvent_t>(event);
+  // Device order first: the operator's later work follows the peer's even if
+  // the host stops waiting.
+  CK("wait_event", cudaStreamWaitEvent(op->stream, ev, 0));
+  const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(timeout_ms);
+  for (;;) {
+    const cudaError_t q = cudaEventQuery(ev);
+    if (q == cudaSuccess) return SPARSL_OK;
+    if (q != cudaErrorNotReady) return fail_cuda("wait_event", q);
+    if (std::chrono::steady_clock::now() >= deadline)
+      return fail(SPARSL_ERR_EXECUTION, "wait_event timed out",
+                  "wait_event: the peer event did not complete within " + std::to_string(timeout_ms) + " ms");
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+int sparsl_op_signal_event(sparsl_op* op, void* event) {
+  ADMIT();
+  if (!op || !event) return fail(SPARSL_ERR_INVALID, "null argument", "signal_event: null argument");
+  CK("signal_event", cudaSetDevice(op->dev->ordinal));
+  // Completes once every call enqueued on the operator before it has finished.
+  CK("signal_event", cudaEventRecord(static_cast<cudaEvent_t>(event), op->stream));
+  return SPARSL_OK;
 }
 
 int sparsl_op_sync_x_spikes(sparsl_op* op, uint32_t* s, uint64_t words) {
