@@ -627,6 +627,168 @@ def bench_spmv(args, dev, want_cpu):
             "f16_weights": f16, "transpose": tr, "reverse_index": rev}
 
 
+def bench_rowshard(args, dev, dist, kind):
+    """SpMV (config 1 shape) or SpMM (config 4 shape) sharded by rows with x
+    replicated: rank r owns a row block drawn from seed + r (weak scaling, N
+    row blocks in all), every rank holds the same x, no exchange.  Each
+    rank's kernel is timed by CUDA events with L2 flushed before every
+    launch; the step time is the max over ranks of the per-rank median."""
+    import torch
+    import sparsl_b200 as S
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    L = lib()
+    if kind == "spmv":
+        n, nv, seed = SPMV_N, 1, SPMV_SEED
+        r = np.random.default_rng(seed + dist.rank)
+        col = gen_distinct_rows(r, n, n, SPMV_DEG)
+        rp = (np.arange(n + 1, dtype=np.uint64) * SPMV_DEG).astype(np.uint32)
+        w = r.uniform(-1.0, 1.0, col.size).astype(np.float32)
+        x = np.random.default_rng(seed ^ 0x5EED).uniform(0.0, 1.0, n).astype(np.float32)
+    else:
+        n, nv, seed = SPMM_N, SPMM_NVEC, SPMM_SEED
+        rp, col, r = gen_zipf_csr(n, n, SPMM_KMAX, SPMM_ALPHA, seed + dist.rank)
+        w = r.uniform(-1.0, 1.0, col.size).astype(np.float32)
+        x = np.random.default_rng(seed ^ 0x5EED).uniform(-1.0, 1.0, n * nv).astype(np.float32)
+    nnz = col.size
+    op = dev.prepare(S.Csr(rp, col, n), n, w)
+    s = torch.cuda.Stream()
+    torch.cuda.set_stream(s)
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.zeros(n * nv, dtype=torch.float32, device="cuda")
+    flush = torch.empty(64 << 22, dtype=torch.float32, device="cuda")  # 1 GiB > L2
+    if kind == "spmv":
+        run = lambda: check(L.sparsl_op_spmv_device(op.handle, dx.data_ptr(), dy.data_ptr(), s.cuda_stream), "spmv")
+        algo = nnz * 8 + (n + 1) * 4 + n * 4 + 2 * n * 4
+    else:
+        run = lambda: check(L.sparsl_op_spmm_device(op.handle, dx.data_ptr(), nv, dy.data_ptr(), s.cuda_stream),
+                            "spmm")
+        algo = nnz * 8 + (n + 1) * 4 + n * nv * 4 + 2 * n * nv * 4
+    # parity: one product from y = 0 against the oracle (SpMM on a row sample)
+    run()
+    s.synchronize()
+    got = dy.cpu().numpy()
+    if kind == "spmv":
+        want = O.spmv(O.Csr(rp, col, n), w, x, np.zeros(n, np.float32), par=True)
+        exact = bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))
+    else:
+        sample = np.sort(np.random.default_rng(seed ^ 1).choice(n, 2000, replace=False))
+        sub_rp = np.zeros(sample.size + 1, np.uint64)
+        np.cumsum(rp[sample + 1].astype(np.uint64) - rp[sample], out=sub_rp[1:])
+        sel = np.concatenate([np.arange(rp[i], rp[i + 1]) for i in sample])
+        want = O.spmm(O.Csr(sub_rp.astype(np.uint32), col[sel], n), w[sel], x, nv,
+                      np.zeros(sample.size * nv, np.float32), par=True).reshape(sample.size, nv)
+        exact = bool(np.array_equal(got.reshape(n, nv)[sample].view(np.uint32), want.view(np.uint32)))
+    for _ in range(args.warmup):
+        run()
+    dist.barrier()
+    clocks = Clocks(dist.local)
+    if dist.rank == 0:
+        clocks.start()
+    dist.barrier()
+    ts = time_launches(s, run, args.kernel_iters, flush=lambda: flush_l2(flush))
+    dist.barrier()
+    ck = clocks.stop() if dist.rank == 0 else None
+    ms = dist.max(statistics.median(ts))
+    oks = dist.gather(exact)
+    if dist.rank != 0:
+        return None
+    shape = (f"{n:,} x {n:,} per GPU, 64 distinct sorted cols/row" if kind == "spmv" else
+             f"{n:,} x {n:,} per GPU, Zipf(1.5) rows in [1,4096], X {n:,} x {nv} row-major")
+    return {"metric": f"{'SpMV' if kind == 'spmv' else 'SpMM'} effective HBM GB/s",
+            "value": dist.world * algo / (ms * 1e-3) / 1e9, "unit": "GB/s", "n_gpus": dist.world,
+            "steps": args.kernel_iters, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, row block per rank)",
+            "config": {"workload": f"{kind}: {dist.world} row blocks of {shape}; x replicated",
+                       "parallelism": "row blocks, x replicated, no exchange",
+                       "l2": "L2 flushed (1 GiB write) before every launch"},
+            "algorithmic_bytes_per_gpu": algo, "clocks": ck, "bit_exact_vs_oracle": all(oks)}
+
+
+def bench_scan_sharded(args, dev, dist):
+    """The exact scan of a sequence split into one run of SCAN_N maps per rank
+    (weak scaling: N x SCAN_N maps in all): halo and table all-gather, entry
+    guess, local scan, boundary-state check and rejoin rounds
+    (sparsl_b200/dist_scan.py).  Each step is timed by CUDA events on the
+    device's stream around the whole procedure, host exchanges included;
+    the step time is the max over ranks.  Rank r's run is drawn from seed
+    SCAN_SEED + r (rank 0's run is exactly the 1-GPU workload)."""
+    import torch
+
+    from sparsl_b200 import dist_scan
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    r = np.random.default_rng(SCAN_SEED + dist.rank)
+    xs = np.empty((SCAN_N, 2), np.float32)
+    xs[:, 0] = r.uniform(0.9, 1.0, SCAN_N).astype(np.float32)
+    xs[:, 1] = r.standard_normal(SCAN_N).astype(np.float32)
+    din = torch.from_numpy(xs).cuda()
+    dout = torch.empty_like(din)
+    torch.cuda.synchronize()
+    gather = dist_scan.process_group_all_gather(dist.pg, dist.world)
+    run = dist_scan.DeviceRun(dev, din, dout, SCAN_N)
+    stream = lib().sparsl_dev_stream(dev.handle)
+    st = None
+
+    def step():
+        nonlocal st
+        st = dist_scan.sharded_scan(run, dist.rank, dist.world, gather)
+
+    for _ in range(args.warmup):
+        step()
+    dist.barrier()
+    clocks = Clocks(dist.local)
+    if dist.rank == 0:
+        clocks.start()
+    ts = []
+    for _ in range(args.steps):
+        dist.barrier()
+        ts.append(events_ms(stream, dist.local, step))
+    dist.barrier()
+    ck = clocks.stop() if dist.rank == 0 else None
+    ms = dist.max(statistics.median(ts))
+    # Bit-exact, checked in parallel: each rank folds its own run on the CPU
+    # from the entry state the GPU run used and compares every output; then
+    # each entry must equal the previous rank's CPU-computed exit state.  By
+    # induction from rank 0 (no entry), the whole output is the sequential
+    # fold of the concatenated sequence.
+    got = dout.cpu().numpy()
+    per = dist.gather({"last": got[-1].tobytes(), "rounds": st.rounds, "rewritten": st.rewritten,
+                       "entry_exact": st.entry_exact})
+    x2 = xs.copy()
+    if dist.rank > 0:
+        x2[0] = _comb_f32(np.frombuffer(per[dist.rank - 1]["last"], np.float32), xs[0])
+    want = O.scan_sequential(x2)
+    oks = dist.gather(bool(np.array_equal(got.view(np.uint32), want.view(np.uint32))))
+    algo = 16 * SCAN_N * dist.world
+    if dist.rank != 0:
+        return None
+    return {"metric": "affine scan effective HBM GB/s", "value": algo / (ms * 1e-3) / 1e9, "unit": "GB/s",
+            "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded numpy per rank: a U[0.9,1], b N(0,1))",
+            "config": {"workload": f"scan: {dist.world} x {SCAN_N:,} maps, one consecutive run per GPU",
+                       "parallelism": "contiguous runs; one all-gather of halos (2,048 maps) and multiplier "
+                                      "tables, entry guess, local exact scan, boundary-state all-gather "
+                                      "(rejoin rounds only on a mismatch)",
+                       "l2": "1 GiB in+out per GPU > L2"},
+            "algorithmic_bytes": algo, "clocks": ck,
+            "bit_exact_vs_oracle": all(oks),
+            "boundary": {"rounds": per[0]["rounds"], "rewritten": sum(p["rewritten"] for p in per),
+                         "entry_guess_exact": sum(1 for p in per if p["entry_exact"]), "ranks": dist.world}}
+
+
+def _comb_f32(p, q):
+    """(q.a * p.a, q.a * p.b + q.b) in f32 with two roundings (scan.rs:127-132)."""
+    a = np.float32(q[0]) * np.float32(p[0])
+    b = np.float32(q[0]) * np.float32(p[1]) + np.float32(q[1])
+    return np.array([a, b], np.float32)
+
+
 def bench_scan(args, dev, want_cpu):
     import torch
 
@@ -962,8 +1124,13 @@ def main():
 
             torch.cuda.set_device(dist.local)
             dev = S.Device.try_new(S.Backend.Cuda, dist.local)
-            fn = {"spmv": bench_spmv, "spmm": bench_spmm, "scan": bench_scan, "lif": bench_lif}[args.workload]
-            line = fn(args, dev, dist.rank == 0 and not args.no_cpu) if dist.rank == 0 else None
+            if args.workload == "scan" and dist.world > 1:
+                line = bench_scan_sharded(args, dev, dist)
+            elif args.workload in ("spmv", "spmm") and dist.world > 1:
+                line = bench_rowshard(args, dev, dist, args.workload)
+            else:
+                fn = {"spmv": bench_spmv, "spmm": bench_spmm, "scan": bench_scan, "lif": bench_lif}[args.workload]
+                line = fn(args, dev, dist.rank == 0 and not args.no_cpu) if dist.rank == 0 else None
         else:
             line = bench_lif_net(args, dist)
             if dist.world == 1 and not args.no_extras:

@@ -252,6 +252,39 @@ int sparsl_op_spmv_t_device(sparsl_op *op, const float *d_x, float *d_y, void *s
 int sparsl_op_spmm_device(sparsl_op *op, const float *d_x, uint64_t n_vec, float *d_y, void *stream);
 int sparsl_dev_assoc_scan_device(sparsl_dev *dev, const float *d_in, uint64_t n, float *d_out,
                                  void *stream);
+/* ---- a scan split into runs across devices (extension) ------------------- */
+/* The pieces of an exact scan whose maps are split into consecutive runs,
+ * one per device (the speculate/verify rule of the single-device scan,
+ * applied across devices; the host exchanges the boundary states).
+ *  - assoc_scan_from: the scan of a run that continues a longer sequence
+ *    whose state before d_in[0] is entry[0..1] (NULL: the run starts the
+ *    sequence and its first map is copied, scan.rs:280-286).
+ *  - scan_fold: the state after folding d_in[0..n) (from entry, or from a
+ *    copy of d_in[0]), into state[0..1] (host memory); used to guess a run's
+ *    entry state from the maps before it.  Synchronous, one thread.
+ *  - scan_rejoin: given a run's exact entry state, rewrites d_out from the
+ *    start until it rejoins the stored trajectory bit for bit; returns the
+ *    run's exit state and the number of rewritten maps.  Synchronous, one
+ *    thread, at most n steps. */
+int sparsl_dev_assoc_scan_from_device(sparsl_dev *dev, const float *d_in, uint64_t n, float *d_out,
+                                      const float *entry, void *stream);
+int sparsl_dev_scan_fold_device(sparsl_dev *dev, const float *d_in, uint64_t n, const float *entry,
+                                float *state, void *stream);
+int sparsl_dev_scan_rejoin_device(sparsl_dev *dev, const float *d_in, float *d_out, uint64_t n,
+                                  const float *entry, float *exit_state, uint64_t *rewritten,
+                                  void *stream);
+/*  - scan_table: the transfer table of d_in[0..n) for the multiplier chain:
+ *    nibble m (m = 0..7) is the bit pattern of the multiplier leaving the run
+ *    when m * 2^-149 entered it, or 8 when that is not one of {0..7} * 2^-149
+ *    (on multipliers in [0.9, 1] the f32 chain settles on such a value and
+ *    stays there, so runs compose by their tables).  Synchronous.
+ *  - scan_settle: the multiplier chain from a copy of d_in[0] up to the first
+ *    value in {0..7} * 2^-149 (or the end of the run): *multiplier, and in
+ *    *folded the number of maps folded so far. */
+int sparsl_dev_scan_table_device(sparsl_dev *dev, const float *d_in, uint64_t n, uint32_t *table,
+                                 void *stream);
+int sparsl_dev_scan_settle_device(sparsl_dev *dev, const float *d_in, uint64_t n, float *multiplier,
+                                  uint64_t *folded, void *stream);
 /* Enqueue recurrent ticks on the operator's stream without waiting. */
 int sparsl_op_recurrent_steps_async(sparsl_op *op, float decay, float v_reset, float delta_theta,
                                     uint64_t steps);

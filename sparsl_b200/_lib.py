@@ -70,6 +70,11 @@ SIGNATURES = {
     "sparsl_op_alloc_f32": (i32, [vp, vp, u64, ctypes.POINTER(vp)]),
     "sparsl_op_wait_event": (i32, [vp, vp, u64]),
     "sparsl_op_signal_event": (i32, [vp, vp]),
+    "sparsl_dev_assoc_scan_from_device": (i32, [vp, vp, u64, vp, vp, vp]),
+    "sparsl_dev_scan_fold_device": (i32, [vp, vp, u64, vp, vp, vp]),
+    "sparsl_dev_scan_rejoin_device": (i32, [vp, vp, vp, u64, vp, vp, ctypes.POINTER(u64), vp]),
+    "sparsl_dev_scan_table_device": (i32, [vp, vp, u64, ctypes.POINTER(ctypes.c_uint32), vp]),
+    "sparsl_dev_scan_settle_device": (i32, [vp, vp, u64, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(u64), vp]),
     "sparsl_op_destroy": (None, [vp]),
     "sparsl_op_shape": (i32, [vp, ctypes.POINTER(Shape)]),
     "sparsl_op_weight_precision": (i32, [vp]),

@@ -479,6 +479,60 @@ class Device:
                "assoc_scan")
         return out
 
+    def wait(self) -> None:
+        """Bounded wait for the device's own stream, then its error word."""
+        _check(_lib.load().sparsl_dev_wait(self._h), "device wait")
+
+    def stream_handle(self) -> int:
+        """The device's own stream (cudaStream_t) as an integer."""
+        return _lib.load().sparsl_dev_stream(self._h) or 0
+
+    # ---- a scan split into runs across devices (extension) ----
+    def assoc_scan_from_device(self, d_in, n: int, d_out, entry=None, stream=None) -> None:
+        """Exact scan of n device-resident maps that continue a sequence whose
+        state before ``d_in[0]`` is ``entry`` ((a, b), or None: the run starts
+        the sequence).  Enqueued on ``stream`` (a cudaStream_t, None = the
+        device's own)."""
+        e = None if entry is None else np.asarray(entry, np.float32)
+        _check(_lib.load().sparsl_dev_assoc_scan_from_device(self._h, _dptr(d_in), int(n), _dptr(d_out),
+                                                             None if e is None else e.ctypes.data, stream),
+               "assoc_scan")
+
+    def scan_fold_device(self, d_in, n: int, entry=None, stream=None) -> np.ndarray:
+        """The (a, b) state after folding n device maps (serial, synchronous)."""
+        e = None if entry is None else np.asarray(entry, np.float32)
+        out = np.zeros(2, np.float32)
+        _check(_lib.load().sparsl_dev_scan_fold_device(self._h, _dptr(d_in), int(n),
+                                                       None if e is None else e.ctypes.data, out.ctypes.data,
+                                                       stream), "scan_fold")
+        return out
+
+    def scan_rejoin_device(self, d_in, d_out, n: int, entry, stream=None):
+        """Rewrite a run's output from its exact entry state until it rejoins
+        the stored trajectory; returns (exit state, rewritten maps)."""
+        e = np.asarray(entry, np.float32)
+        out = np.zeros(2, np.float32)
+        cnt = ctypes.c_uint64()
+        _check(_lib.load().sparsl_dev_scan_rejoin_device(self._h, _dptr(d_in), _dptr(d_out), int(n), e.ctypes.data,
+                                                         out.ctypes.data, ctypes.byref(cnt), stream), "scan_rejoin")
+        return out, cnt.value
+
+    def scan_table_device(self, d_in, n: int, stream=None) -> int:
+        """Transfer table (8 nibbles) of n device maps for the multiplier chain."""
+        t = ctypes.c_uint32()
+        _check(_lib.load().sparsl_dev_scan_table_device(self._h, _dptr(d_in), int(n), ctypes.byref(t), stream),
+               "scan_table")
+        return t.value
+
+    def scan_settle_device(self, d_in, n: int, stream=None):
+        """(multiplier, maps folded): the multiplier chain from a copy of the
+        first map until it settles in {0..7} * 2^-149 or the run ends."""
+        a = ctypes.c_float()
+        k = ctypes.c_uint64()
+        _check(_lib.load().sparsl_dev_scan_settle_device(self._h, _dptr(d_in), int(n), ctypes.byref(a),
+                                                         ctypes.byref(k), stream), "scan_settle")
+        return np.float32(a.value), int(k.value)
+
     def scan_stats(self):
         rep, seg = ctypes.c_uint64(), ctypes.c_uint64()
         _check(_lib.load().sparsl_dev_scan_stats(self._h, ctypes.byref(rep), ctypes.byref(seg)), "scan_stats")

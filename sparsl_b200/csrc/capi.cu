@@ -267,7 +267,8 @@ struct sparsl_dev {
   ScanScratch sc{};
   bool scan_dirty = false;
   DBuf lv, lth, lcur, lspk;
-  DBuf vscratch;  // device CSR validation results
+  DBuf vscratch;  // device CSR validation results, scan walk state
+  DBuf tscratch;  // scan transfer tables
 };
 
 namespace {
@@ -521,6 +522,7 @@ void sparsl_device_close(sparsl_dev* d) {
   dfree(d->lcur);
   dfree(d->lspk);
   dfree(d->vscratch);
+  dfree(d->tscratch);
   d->err.release();
   cudaEventDestroy(d->ev);
   cudaStreamDestroy(d->stream);
@@ -598,6 +600,11 @@ int sparsl_dev_assoc_scan(sparsl_dev* d, const float* in, uint64_t n, float* out
 }
 
 int sparsl_dev_assoc_scan_device(sparsl_dev* d, const float* d_in, uint64_t n, float* d_out, void* stream) {
+  return sparsl_dev_assoc_scan_from_device(d, d_in, n, d_out, nullptr, stream);
+}
+
+int sparsl_dev_assoc_scan_from_device(sparsl_dev* d, const float* d_in, uint64_t n, float* d_out, const float* entry,
+                                      void* stream) {
   ADMIT();
   if (!d) return fail(SPARSL_ERR_INVALID, "null device", "assoc_scan: null device");
   if (n == 0) return SPARSL_OK;
@@ -617,7 +624,7 @@ int sparsl_dev_assoc_scan_device(sparsl_dev* d, const float* d_in, uint64_t n, f
     CK("assoc_scan", cudaMemsetAsync(buf, 0, ntiles * 128, s));
     ScanScratch sc = d->sc;
     sc.timeline = buf;
-    CK("assoc_scan", launch_scan(d_in, d_out, n, sc, d->err.d, s));
+    CK("assoc_scan", launch_scan(d_in, d_out, n, sc, d->err.d, s, entry));
     std::vector<unsigned long long> h(ntiles * 16);
     CK("assoc_scan", cudaMemcpyAsync(h.data(), buf, ntiles * 128, cudaMemcpyDeviceToHost, s));
     CK("assoc_scan", cudaStreamSynchronize(s));
@@ -628,7 +635,69 @@ int sparsl_dev_assoc_scan_device(sparsl_dev* d, const float* d_in, uint64_t n, f
     }
     return SPARSL_OK;
   }
-  CK("assoc_scan", launch_scan(d_in, d_out, n, d->sc, d->err.d, s));
+  CK("assoc_scan", launch_scan(d_in, d_out, n, d->sc, d->err.d, s, entry));
+  return SPARSL_OK;
+}
+
+namespace {
+int dev_scan_walk(sparsl_dev* d, const float* d_in, float* d_out, uint64_t n, const float* entry, int repair,
+                  float* state, uint64_t* rewritten, void* stream, const char* what) {
+  ADMIT();
+  if (!d || !state) return fail(SPARSL_ERR_INVALID, "null argument", std::string(what) + ": null argument");
+  if (n == 0) return fail(SPARSL_ERR_LENGTH, "empty run", std::string(what) + ": a run needs at least one map");
+  std::lock_guard<std::mutex> lk(d->mu);
+  CK(what, cudaSetDevice(d->ordinal));
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : d->stream;
+  if (!d->vscratch.p && dalloc(d->vscratch, 32, false, d->stream) != cudaSuccess)
+    return fail(SPARSL_ERR_ALLOCATION, "walk scratch", "device allocation failed for scan walk scratch");
+  float* dstate = d->vscratch.as<float>();
+  unsigned long long* dstats = d->vscratch.as<unsigned long long>() + 1;
+  CK(what, launch_scan_walk(d_in, d_out, n, entry, repair, dstate, dstats, s));
+  unsigned long long h[2] = {0, 0};
+  CK(what, cudaMemcpyAsync(h, d->vscratch.p, 16, cudaMemcpyDeviceToHost, s));
+  CK(what, cudaStreamSynchronize(s));
+  std::memcpy(state, h, 8);
+  if (rewritten) *rewritten = h[1];
+  return SPARSL_OK;
+}
+}  // namespace
+
+int sparsl_dev_scan_fold_device(sparsl_dev* d, const float* d_in, uint64_t n, const float* entry, float* state,
+                                void* stream) {
+  return dev_scan_walk(d, d_in, nullptr, n, entry, 0, state, nullptr, stream, "scan_fold");
+}
+
+int sparsl_dev_scan_rejoin_device(sparsl_dev* d, const float* d_in, float* d_out, uint64_t n, const float* entry,
+                                  float* exit_state, uint64_t* rewritten, void* stream) {
+  if (!entry) return fail(SPARSL_ERR_INVALID, "null argument", "scan_rejoin: an entry state is required");
+  return dev_scan_walk(d, d_in, d_out, n, entry, 1, exit_state, rewritten, stream, "scan_rejoin");
+}
+
+int sparsl_dev_scan_settle_device(sparsl_dev* d, const float* d_in, uint64_t n, float* multiplier,
+                                  uint64_t* folded, void* stream) {
+  float st[2] = {0.f, 0.f};
+  TRY(dev_scan_walk(d, d_in, nullptr, n, nullptr, 2, st, folded, stream, "scan_settle"));
+  if (multiplier) *multiplier = st[0];
+  return SPARSL_OK;
+}
+
+int sparsl_dev_scan_table_device(sparsl_dev* d, const float* d_in, uint64_t n, uint32_t* table, void* stream) {
+  ADMIT();
+  if (!d || !table) return fail(SPARSL_ERR_INVALID, "null argument", "scan_table: null argument");
+  if (n == 0) {
+    *table = 0x76543210u;  // the identity table
+    return SPARSL_OK;
+  }
+  std::lock_guard<std::mutex> lk(d->mu);
+  CK("scan_table", cudaSetDevice(d->ordinal));
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : d->stream;
+  constexpr uint32_t kBlk = 1184;
+  if (!d->tscratch.p && dalloc(d->tscratch, (kBlk + 64) * 4, false, d->stream) != cudaSuccess)
+    return fail(SPARSL_ERR_ALLOCATION, "table scratch", "device allocation failed for scan table scratch");
+  uint32_t* out = d->tscratch.as<uint32_t>() + kBlk;
+  CK("scan_table", launch_scan_table(d_in, n, d->tscratch.as<uint32_t>(), kBlk, out, s));
+  CK("scan_table", cudaMemcpyAsync(table, out, 4, cudaMemcpyDeviceToHost, s));
+  CK("scan_table", cudaStreamSynchronize(s));
   return SPARSL_OK;
 }
 

@@ -127,7 +127,8 @@ __device__ void walk_multiplier(float A, int first, const float2* sm, const uint
 }
 
 __global__ void __launch_bounds__(kScanBlock, 5) scan_main(const float2* __restrict__ in, float2* __restrict__ out,
-                                                       uint64_t n, ScanScratch s, uint32_t* err) {
+                                                       uint64_t n, ScanScratch s, uint32_t* err, int has_entry,
+                                                       float2 entry) {
   extern __shared__ __align__(16) float2 sm[];  // kRows x kRowStride
   __shared__ float s_Eb[kScanThreads];  // in-tile exclusive guess of B (from identity)
   __shared__ uint32_t s_tab[kScanThreads];
@@ -165,6 +166,15 @@ __global__ void __launch_bounds__(kScanBlock, 5) scan_main(const float2* __restr
     for (int i = 0; i < kPer; ++i) {
       const int li = t + i * kScanBlock;
       sm[(li / kScanK) * kRowStride + (li % kScanK)] = v[i];
+    }
+    // A run that continues a longer sequence: its first map is the entry
+    // state combined with x[0], exactly as the fold combines it; the
+    // copy-first rule then emits it unchanged.  The thread that staged x[0]
+    // patches it.
+    if (has_entry && tile == 0 && t == kScanHalo % kScanBlock) {
+      float2* f = sm + (kScanHalo / kScanK) * kRowStride + (kScanHalo % kScanK);
+      const Aff e = comb(Aff{entry.x, entry.y}, Aff{f->x, f->y});
+      *f = make_float2(e.a, e.b);
     }
   }
   __syncthreads();
@@ -676,15 +686,17 @@ ScanScratch scan_scratch_carve(void* base, uint64_t n) {
 }
 
 cudaError_t launch_scan(const float* in, float* out, uint64_t n, const ScanScratch& s, uint32_t* err,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, const float* entry) {
   if (n == 0) return cudaSuccess;
   const uint64_t ntiles = (n + kScanTile - 1) / kScanTile;
   if (ntiles > 0x7fffffffull) return cudaErrorInvalidValue;
   const size_t smem = sizeof(float2) * kRows * kRowStride;
   cudaError_t e = cudaFuncSetAttribute(scan_main, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
+  const float2 ent = entry ? make_float2(entry[0], entry[1]) : make_float2(1.0f, 0.0f);
   scan_main<<<(unsigned)ntiles, kScanBlock, smem, stream>>>(reinterpret_cast<const float2*>(in),
-                                                              reinterpret_cast<float2*>(out), n, s, err);
+                                                              reinterpret_cast<float2*>(out), n, s, err,
+                                                              entry ? 1 : 0, ent);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (ntiles > 1) {
@@ -695,6 +707,188 @@ cudaError_t launch_scan(const float* in, float* out, uint64_t n, const ScanScrat
   }
   scan_repair<<<1, 256, 0, stream>>>(reinterpret_cast<const float2*>(in), reinterpret_cast<float2*>(out), n,
                                      s, err);
+  return cudaGetLastError();
+}
+
+// Serial walks over a run, one block: the block stages batches of maps (and,
+// when repairing, of stored outputs) in shared memory with coalesced loads,
+// and thread 0 walks each batch from there, so the serial chain never waits
+// on a global load.
+//  FOLD (mode 0): the state after folding in[0..n) (the first map combined
+//    with *entry when given, else copied), into state[0..1].
+//  REJOIN (mode 1): walks the exact fold from *entry, overwriting out[i]
+//    until the recomputed state equals the stored one bit for bit (from there
+//    on the stored run is the exact trajectory); stats[0] = rewritten maps,
+//    state = the run's final state.
+//  SETTLE (mode 2): the multiplier chain from a copy of in[0] until it is one
+//    of {0..7} * 2^-149 (or the run ends); state[0] = that multiplier,
+//    stats[0] = maps folded (the table of in[stats[0]..n) continues it).
+constexpr int kWalkThreads = 256;
+constexpr int kWalkBatch = 2048;
+
+__global__ void __launch_bounds__(kWalkThreads) scan_walk_kernel(const float2* __restrict__ in,
+                                                                 float2* __restrict__ out, uint64_t n,
+                                                                 int has_entry, float2 entry, int mode,
+                                                                 float* state, unsigned long long* stats) {
+  __shared__ float2 s_in[kWalkBatch];
+  __shared__ float2 s_out[kWalkBatch];
+  __shared__ int s_stop;
+  __shared__ uint32_t s_upto;  // entries of the batch thread 0 rewrote
+  if (blockIdx.x != 0 || n == 0) return;
+  Aff acc{1.f, 0.f};
+  float am = 1.f;
+  uint64_t rewritten = 0, folded = 0;
+  for (uint64_t base = 0; base < n; base += kWalkBatch) {
+    const uint32_t cnt = (uint32_t)(n - base < (uint64_t)kWalkBatch ? n - base : (uint64_t)kWalkBatch);
+    for (uint32_t j = threadIdx.x; j < cnt; j += kWalkThreads) {
+      s_in[j] = in[base + j];
+      if (mode == 1) s_out[j] = out[base + j];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int stop = 0;
+      uint32_t upto = 0;
+      for (uint32_t j = 0; j < cnt; ++j) {
+        const uint64_t i = base + j;
+        const float2 x = s_in[j];
+        if (mode == 2) {
+          if (i == 0) {
+            am = x.x;
+          } else {
+            am = fmul(x.x, am);
+          }
+          folded = i + 1;
+          if (fbits(am) <= 7u) {
+            stop = 1;
+            break;
+          }
+          continue;
+        }
+        if (i == 0)
+          acc = has_entry ? comb(Aff{entry.x, entry.y}, Aff{x.x, x.y}) : Aff{x.x, x.y};
+        else
+          acc = comb(acc, Aff{x.x, x.y});
+        if (mode == 1) {
+          const float2 o = s_out[j];
+          if (__float_as_uint(o.x) == __float_as_uint(acc.a) && __float_as_uint(o.y) == __float_as_uint(acc.b)) {
+            stop = 1;
+            break;
+          }
+          s_out[j] = make_float2(acc.a, acc.b);
+          upto = j + 1;
+          ++rewritten;
+        }
+      }
+      s_stop = stop;
+      s_upto = upto;
+    }
+    __syncthreads();
+    if (mode == 1)
+      for (uint32_t j = threadIdx.x; j < s_upto; j += kWalkThreads) out[base + j] = s_out[j];
+    const int stop = s_stop;
+    __syncthreads();
+    if (stop) break;
+  }
+  if (threadIdx.x != 0) return;
+  if (mode == 2) {
+    state[0] = am;
+    state[1] = 0.f;
+    if (stats) stats[0] = folded;
+    return;
+  }
+  if (mode == 1) {
+    __threadfence_block();
+    const float2 last = out[n - 1];
+    acc = Aff{last.x, last.y};
+  }
+  state[0] = acc.a;
+  state[1] = acc.b;
+  if (stats) stats[0] = rewritten;
+}
+
+// Transfer table of a whole run for the multiplier chain: nibble m is the
+// multiplier leaving in[0..n) when m * 2^-149 entered it (or 8 when that
+// value is not one of {0..7} * 2^-149).  Each thread folds the eight chains
+// over a contiguous stretch with the actual products; stretches compose in
+// order (tab_comb) within the block, then across blocks in a second pass.
+constexpr int kTabThreads = 256;
+
+__device__ uint32_t chains_table(const float2* __restrict__ in, uint64_t lo, uint64_t hi) {
+  float v[8];
+#pragma unroll
+  for (uint32_t m = 0; m < 8; ++m) v[m] = __uint_as_float(m);
+  for (uint64_t i = lo; i < hi; ++i) {
+    const float a = __ldg(&in[i].x);
+#pragma unroll
+    for (uint32_t m = 0; m < 8; ++m) v[m] = fmul(a, v[m]);
+  }
+  uint32_t tab = 0;
+#pragma unroll
+  for (uint32_t m = 0; m < 8; ++m) {
+    const uint32_t b = fbits(v[m]);
+    tab |= (b <= 7u ? b : 8u) << (4 * m);
+  }
+  return tab;
+}
+
+__device__ uint32_t block_compose(uint32_t* s_t, uint32_t mine) {
+  s_t[threadIdx.x] = mine;
+  __syncthreads();
+  for (int d = 1; d < kTabThreads; d <<= 1) {
+    uint32_t r = 0;
+    const bool act = (threadIdx.x % (2 * d)) == 0 && threadIdx.x + d < kTabThreads;
+    if (act) r = tab_comb(s_t[threadIdx.x], s_t[threadIdx.x + d]);
+    __syncthreads();
+    if (act) s_t[threadIdx.x] = r;
+    __syncthreads();
+  }
+  return s_t[0];
+}
+
+__global__ void __launch_bounds__(kTabThreads) scan_table_kernel(const float2* __restrict__ in, uint64_t n,
+                                                                 uint32_t* __restrict__ blk_tab) {
+  __shared__ uint32_t s_t[kTabThreads];
+  const uint64_t per_blk = (n + gridDim.x - 1) / gridDim.x;
+  const uint64_t b0 = (uint64_t)blockIdx.x * per_blk, b1 = b0 + per_blk < n ? b0 + per_blk : n;
+  const uint64_t per_thr = b1 > b0 ? (b1 - b0 + kTabThreads - 1) / kTabThreads : 0;
+  uint64_t lo = b0 + (uint64_t)threadIdx.x * per_thr, hi = lo + per_thr;
+  if (lo > b1) lo = b1;
+  if (hi > b1) hi = b1;
+  const uint32_t t = block_compose(s_t, chains_table(in, lo, hi));
+  if (threadIdx.x == 0) blk_tab[blockIdx.x] = t;
+}
+
+__global__ void __launch_bounds__(kTabThreads) scan_table_reduce_kernel(const uint32_t* __restrict__ blk_tab,
+                                                                        uint32_t nblk, uint32_t* __restrict__ out) {
+  __shared__ uint32_t s_t[kTabThreads];
+  uint32_t acc = kTabId;
+  for (uint32_t base = 0; base < nblk; base += kTabThreads) {
+    const uint32_t i = base + threadIdx.x;
+    const uint32_t t = block_compose(s_t, i < nblk ? blk_tab[i] : kTabId);
+    acc = tab_comb(acc, t);
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *out = acc;
+}
+
+cudaError_t launch_scan_table(const float* in, uint64_t n, uint32_t* blk_scratch, uint32_t nblk_max, uint32_t* out,
+                              cudaStream_t stream) {
+  const float2* x = reinterpret_cast<const float2*>(in);
+  const uint64_t want = (n + 4095) / 4096;
+  const uint32_t nblk = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(want, nblk_max));
+  scan_table_kernel<<<nblk, kTabThreads, 0, stream>>>(x, n, blk_scratch);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  scan_table_reduce_kernel<<<1, kTabThreads, 0, stream>>>(blk_scratch, nblk, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scan_walk(const float* in, float* out, uint64_t n, const float* entry, int repair, float* state,
+                             unsigned long long* stats, cudaStream_t stream) {
+  if (n == 0) return cudaSuccess;
+  const float2 ent = entry ? make_float2(entry[0], entry[1]) : make_float2(1.0f, 0.0f);
+  scan_walk_kernel<<<1, kWalkThreads, 0, stream>>>(reinterpret_cast<const float2*>(in), reinterpret_cast<float2*>(out), n,
+                                         entry ? 1 : 0, ent, repair, state, stats);
   return cudaGetLastError();
 }
 

@@ -34,7 +34,24 @@ ScanScratch scan_scratch_carve(void* base, uint64_t n);
 // out[i] = in[0] o in[1] o ... o in[i] as an exact sequential left fold
 // (src/scan.rs:298-313).  `in` and `out` hold n (a, b) pairs and must not
 // alias.  scratch must be zeroed once before first use.
+// `entry` (host pointer to an (a, b) pair, or null): the run continues a
+// longer sequence whose state before in[0] is *entry, so out[0] is
+// entry o in[0] rather than a copy of in[0].
 cudaError_t launch_scan(const float* in, float* out, uint64_t n, const ScanScratch& s,
-                        uint32_t* err, cudaStream_t stream);
+                        uint32_t* err, cudaStream_t stream, const float* entry = nullptr);
+
+// Serial single-thread walks for runs split across devices (see scan.cu):
+// fold in[0..n) into state[2] (device memory), or repair out[0..n) from an
+// exact entry state until it rejoins the stored trajectory.
+// repair: 0 = fold, 1 = rejoin, 2 = settle (the multiplier chain from a copy
+// of in[0] until it is one of {0..7} * 2^-149; stats[0] = maps folded).
+cudaError_t launch_scan_walk(const float* in, float* out, uint64_t n, const float* entry, int repair,
+                             float* state, unsigned long long* stats, cudaStream_t stream);
+
+// Transfer table of in[0..n) for the multiplier chain (nibble m: the
+// multiplier leaving the run when m * 2^-149 entered it; 8 = outside that
+// set), into *out (device).  blk_scratch holds nblk_max words.
+cudaError_t launch_scan_table(const float* in, uint64_t n, uint32_t* blk_scratch, uint32_t nblk_max, uint32_t* out,
+                              cudaStream_t stream);
 
 }  // namespace sparsl
