@@ -486,7 +486,12 @@ def gen_distinct_rows(rng, nrows, ncols, deg):
 
 
 def flush_l2(buf):
+    """Evict the operands from L2: write a buffer 8x the L2, then read it back,
+    so the L2 holds clean lines of that buffer.  (A write alone leaves the L2
+    full of dirty lines whose write-back to DRAM would then be charged to the
+    timed kernel.)  Neither step is timed."""
     buf.zero_()
+    buf.sum()
 
 
 def time_launches(stream, fn, k, flush=None):
@@ -729,7 +734,11 @@ def bench_scan_sharded(args, dev, dist):
     din = torch.from_numpy(xs).cuda()
     dout = torch.empty_like(din)
     torch.cuda.synchronize()
-    gather = dist_scan.process_group_all_gather(dist.pg, dist.world)
+    if args.scan_exchange == "nccl":
+        group = dist.pg.new_group(backend="nccl")
+        gather = dist_scan.nccl_all_gather(group, dist.world, torch.device("cuda", dist.local))
+    else:
+        gather = dist_scan.process_group_all_gather(dist.pg, dist.world)
     run = dist_scan.DeviceRun(dev, din, dout, SCAN_N)
     stream = lib().sparsl_dev_stream(dev.handle)
     st = None
@@ -758,7 +767,7 @@ def bench_scan_sharded(args, dev, dist):
     # fold of the concatenated sequence.
     got = dout.cpu().numpy()
     per = dist.gather({"last": got[-1].tobytes(), "rounds": st.rounds, "rewritten": st.rewritten,
-                       "entry_exact": st.entry_exact})
+                       "entry_exact": st.entry_exact, "phases": st.phases_ms})
     x2 = xs.copy()
     if dist.rank > 0:
         x2[0] = _comb_f32(np.frombuffer(per[dist.rank - 1]["last"], np.float32), xs[0])
@@ -772,6 +781,7 @@ def bench_scan_sharded(args, dev, dist):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded numpy per rank: a U[0.9,1], b N(0,1))",
             "config": {"workload": f"scan: {dist.world} x {SCAN_N:,} maps, one consecutive run per GPU",
+                       "exchange": args.scan_exchange,
                        "parallelism": "contiguous runs; one all-gather of halos (2,048 maps) and multiplier "
                                       "tables, entry guess, local exact scan, boundary-state all-gather "
                                       "(rejoin rounds only on a mismatch)",
@@ -779,7 +789,9 @@ def bench_scan_sharded(args, dev, dist):
             "algorithmic_bytes": algo, "clocks": ck,
             "bit_exact_vs_oracle": all(oks),
             "boundary": {"rounds": per[0]["rounds"], "rewritten": sum(p["rewritten"] for p in per),
-                         "entry_guess_exact": sum(1 for p in per if p["entry_exact"]), "ranks": dist.world}}
+                         "entry_guess_exact": sum(1 for p in per if p["entry_exact"]), "ranks": dist.world,
+                         "phases_ms_last_step": {f"rank{i}": {k: round(v, 3) for k, v in p["phases"].items()}
+                                                 for i, p in enumerate(per)}}}
 
 
 def _comb_f32(p, q):
@@ -1096,6 +1108,8 @@ def main():
     ap.add_argument("--workload", default="lif_net", choices=["lif_net", "spmv", "spmm", "scan", "lif"])
     ap.add_argument("--no-extras", action="store_true", help="N=1: skip the SpMV / scan / LIF-1GPU figures")
     ap.add_argument("--kernel-iters", type=int, default=20)
+    ap.add_argument("--scan-exchange", default="gloo", choices=["gloo", "nccl"],
+                    help="N>1 scan: the process group that carries the boundary exchanges")
     # Smaller instances of the same workloads (profiling captures, quick runs).
     ap.add_argument("--scan-n", type=int, default=None, help="scan length (default 2^26)")
     ap.add_argument("--lif-ticks", type=int, default=1000, help="timed ticks of the 1-GPU LIF network")

@@ -161,6 +161,14 @@ int sparsl_csc_from_csr_device(sparsl_dev *dev, const uint32_t *d_row_ptr, uint6
 void sparsl_op_destroy(sparsl_op *op);
 int sparsl_op_shape(sparsl_op *op, sparsl_shape *out);
 int sparsl_op_weight_precision(sparsl_op *op);    /* mod.rs:1582 */
+/* Which device layouts an operator holds besides its CSR (a diagnostic; no
+ * reference counterpart). */
+enum {
+  SPARSL_LAYOUT_ELL = 1,            /* uniform rows: TMA-streamed [nrows x L] */
+  SPARSL_LAYOUT_SLICED_REVERSE = 4, /* transpose: sliced-ELL reverse index */
+  SPARSL_LAYOUT_CSC = 8             /* transpose: plain reverse index (hub columns) */
+};
+int sparsl_op_layouts(sparsl_op *op);
 int sparsl_op_has_transpose(sparsl_op *op);       /* mod.rs:1594 */
 /* SparseOp::set_weights (mod.rs:1392-1409). */
 int sparsl_op_set_weights(sparsl_op *op, const float *weights, uint64_t n);

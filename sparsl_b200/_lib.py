@@ -75,6 +75,7 @@ SIGNATURES = {
     "sparsl_dev_scan_rejoin_device": (i32, [vp, vp, vp, u64, vp, vp, ctypes.POINTER(u64), vp]),
     "sparsl_dev_scan_table_device": (i32, [vp, vp, u64, ctypes.POINTER(ctypes.c_uint32), vp]),
     "sparsl_dev_scan_settle_device": (i32, [vp, vp, u64, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(u64), vp]),
+    "sparsl_op_layouts": (i32, [vp]),
     "sparsl_op_destroy": (None, [vp]),
     "sparsl_op_shape": (i32, [vp, ctypes.POINTER(Shape)]),
     "sparsl_op_weight_precision": (i32, [vp]),

@@ -698,6 +698,10 @@ class SparseOp:
     def weight_precision(self) -> WeightPrecision:
         return WeightPrecision(_lib.load().sparsl_op_weight_precision(self._h))
 
+    def layouts(self) -> int:
+        """SPARSL_LAYOUT_* bits: the device layouts this operator holds."""
+        return int(_lib.load().sparsl_op_layouts(self._h))
+
     def has_transpose(self) -> bool:
         return bool(_lib.load().sparsl_op_has_transpose(self._h))
 

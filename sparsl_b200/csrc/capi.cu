@@ -1151,6 +1151,11 @@ int sparsl_op_shape(sparsl_op* op, sparsl_shape* out) {
 }
 
 int sparsl_op_weight_precision(sparsl_op* op) { return op ? op->precision : -1; }
+int sparsl_op_layouts(sparsl_op* op) {
+  if (!op) return 0;
+  return (op->ell.ok ? SPARSL_LAYOUT_ELL : 0) | (op->sell_ok ? SPARSL_LAYOUT_SLICED_REVERSE : 0) |
+         (op->has_t && !op->sell_ok ? SPARSL_LAYOUT_CSC : 0);
+}
 int sparsl_op_has_transpose(sparsl_op* op) { return op && op->has_t ? 1 : 0; }
 
 int sparsl_op_set_weights(sparsl_op* op, const float* weights, uint64_t n) {

@@ -813,12 +813,13 @@ __global__ void __launch_bounds__(kWalkThreads) scan_walk_kernel(const float2* _
 // order (tab_comb) within the block, then across blocks in a second pass.
 constexpr int kTabThreads = 256;
 
-__device__ uint32_t chains_table(const float2* __restrict__ in, uint64_t lo, uint64_t hi) {
+// The eight chains over in[lo..hi) with the actual products.
+__device__ uint32_t chains_table_smem(const float2* s, int stride, int cnt) {
   float v[8];
 #pragma unroll
   for (uint32_t m = 0; m < 8; ++m) v[m] = __uint_as_float(m);
-  for (uint64_t i = lo; i < hi; ++i) {
-    const float a = __ldg(&in[i].x);
+  for (int j = 0; j < cnt; ++j) {
+    const float a = s[j * stride].x;
 #pragma unroll
     for (uint32_t m = 0; m < 8; ++m) v[m] = fmul(a, v[m]);
   }
@@ -842,20 +843,39 @@ __device__ uint32_t block_compose(uint32_t* s_t, uint32_t mine) {
     if (act) s_t[threadIdx.x] = r;
     __syncthreads();
   }
-  return s_t[0];
+  const uint32_t t = s_t[0];
+  __syncthreads();
+  return t;
 }
+
+// Each block owns a contiguous stretch of the run and walks it in batches of
+// kTabThreads x kTabK maps, staged with coalesced loads into a padded
+// shared-memory block; thread t folds maps t*kTabK .. t*kTabK + kTabK - 1
+// of the batch, and the batch tables compose in order.
+constexpr int kTabK = 16;
+constexpr int kTabStride = kTabK + 1;  // float2 row pitch: no bank conflicts across threads
 
 __global__ void __launch_bounds__(kTabThreads) scan_table_kernel(const float2* __restrict__ in, uint64_t n,
                                                                  uint32_t* __restrict__ blk_tab) {
   __shared__ uint32_t s_t[kTabThreads];
-  const uint64_t per_blk = (n + gridDim.x - 1) / gridDim.x;
-  const uint64_t b0 = (uint64_t)blockIdx.x * per_blk, b1 = b0 + per_blk < n ? b0 + per_blk : n;
-  const uint64_t per_thr = b1 > b0 ? (b1 - b0 + kTabThreads - 1) / kTabThreads : 0;
-  uint64_t lo = b0 + (uint64_t)threadIdx.x * per_thr, hi = lo + per_thr;
-  if (lo > b1) lo = b1;
-  if (hi > b1) hi = b1;
-  const uint32_t t = block_compose(s_t, chains_table(in, lo, hi));
-  if (threadIdx.x == 0) blk_tab[blockIdx.x] = t;
+  __shared__ float2 s_x[kTabThreads * kTabStride];
+  constexpr uint64_t kBatch = (uint64_t)kTabThreads * kTabK;
+  const uint64_t nbatch = (n + kBatch - 1) / kBatch;
+  const uint64_t per_blk = (nbatch + gridDim.x - 1) / gridDim.x;
+  const uint64_t q0 = (uint64_t)blockIdx.x * per_blk, q1 = q0 + per_blk < nbatch ? q0 + per_blk : nbatch;
+  uint32_t acc = kTabId;
+  for (uint64_t q = q0; q < q1; ++q) {
+    const uint64_t base = q * kBatch;
+    const uint32_t cnt = (uint32_t)(n - base < kBatch ? n - base : kBatch);
+    for (uint32_t j = threadIdx.x; j < kBatch; j += kTabThreads) {
+      const float2 x = j < cnt ? __ldg(in + base + j) : make_float2(1.0f, 0.0f);
+      s_x[(j / kTabK) * kTabStride + (j % kTabK)] = x;
+    }
+    __syncthreads();
+    const uint32_t t = chains_table_smem(s_x + threadIdx.x * kTabStride, 1, kTabK);
+    acc = tab_comb(acc, block_compose(s_t, t));
+  }
+  if (threadIdx.x == 0) blk_tab[blockIdx.x] = acc;
 }
 
 __global__ void __launch_bounds__(kTabThreads) scan_table_reduce_kernel(const uint32_t* __restrict__ blk_tab,

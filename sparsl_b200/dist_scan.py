@@ -27,8 +27,9 @@ engine and, in the tests, on the CPU oracle.
 """
 from __future__ import annotations
 
-from dataclasses import dataclass
-from typing import Callable, List, Optional
+import time
+from dataclasses import dataclass, field
+from typing import Callable, Dict, List, Optional
 
 import numpy as np
 
@@ -40,6 +41,7 @@ class ShardedScanStats:
     rounds: int            # boundary exchanges after the first
     rewritten: int         # maps this rank rewrote while rejoining
     entry_exact: bool      # this rank's first guess was already exact
+    phases_ms: Dict[str, float] = field(default_factory=dict)  # host wall clock per phase
 
 
 def _bits(v) -> np.ndarray:
@@ -65,6 +67,15 @@ def sharded_scan(engine, rank: int, world: int, all_gather: Callable[[np.ndarray
     every rank) in rank order."""
     if engine.n < 1:
         raise ValueError("every rank's run needs at least one map")
+    ph: Dict[str, float] = {}
+    t0 = time.perf_counter()
+
+    def mark(name):
+        nonlocal t0
+        t1 = time.perf_counter()
+        ph[name] = ph.get(name, 0.0) + (t1 - t0) * 1e3
+        t0 = t1
+
     # 1. What every rank tells the others, in one all-gather:
     #    - its last `halo` maps (padded in front with identity maps) and how
     #      many are real: the offset chain B is guessed from them;
@@ -87,7 +98,9 @@ def sharded_scan(engine, rank: int, world: int, all_gather: Callable[[np.ndarray
     meta = np.array([min(engine.n, halo), 0, 0], np.uint32)
     meta[1], meta[2] = table, a_exit0
     blob = np.concatenate([tail.ravel(), meta.view(np.float32)])
+    mark("local_tables")
     parts = all_gather(blob)
+    mark("exchange_halo")
     tails = [p[: 2 * halo].reshape(halo, 2) for p in parts]
     metas = [p[2 * halo:].view(np.uint32) for p in parts]
     entry: Optional[np.ndarray] = None
@@ -110,6 +123,7 @@ def sharded_scan(engine, rank: int, world: int, all_gather: Callable[[np.ndarray
             m = _nibble(int(metas[r][1]), m)
         if m <= 7:
             entry[0] = _u2f(m)
+    mark("entry_guess")
     # 2. the run from the guessed entry state
     engine.scan(entry)
     first_entry = None if entry is None else entry.copy()
@@ -119,7 +133,9 @@ def sharded_scan(engine, rank: int, world: int, all_gather: Callable[[np.ndarray
     #    the first rank that fails rewrites its run from that exit.
     while True:
         mine = np.concatenate([nan2 if entry is None else np.asarray(entry, np.float32), engine.exit_state()])
+        mark("scan" if rounds == 0 else "rejoin")
         states = all_gather(mine.astype(np.float32))
+        mark("exchange_states")
         bad = next((r for r in range(1, world)
                     if not np.array_equal(_bits(states[r][:2]), _bits(states[r - 1][2:]))), None)
         if bad is None:
@@ -131,7 +147,7 @@ def sharded_scan(engine, rank: int, world: int, all_gather: Callable[[np.ndarray
             entry = states[bad - 1][2:].copy()
             rewritten += engine.rejoin(entry)
     exact_first = rank == 0 or (first_entry is not None and np.array_equal(_bits(first_entry), _bits(entry)))
-    return ShardedScanStats(rounds=rounds, rewritten=rewritten, entry_exact=bool(exact_first))
+    return ShardedScanStats(rounds=rounds, rewritten=rewritten, entry_exact=bool(exact_first), phases_ms=ph)
 
 
 class _Offset:
@@ -214,5 +230,21 @@ def process_group_all_gather(pg, world: int) -> Callable[[np.ndarray], List[np.n
         parts = [torch.zeros_like(t) for _ in range(world)]
         pg.all_gather(parts, t)
         return [p.numpy() for p in parts]
+
+    return gather
+
+
+def nccl_all_gather(group, world: int, device) -> Callable[[np.ndarray], List[np.ndarray]]:
+    """``all_gather`` over a torch.distributed NCCL group: the host values go
+    through a small device buffer (one all-gather over NVLink, then one copy
+    back to the host)."""
+    import torch
+
+    def gather(a: np.ndarray) -> List[np.ndarray]:
+        t = torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(device)
+        out = torch.empty((world,) + tuple(t.shape), dtype=torch.float32, device=device)
+        torch.distributed.all_gather_into_tensor(out, t, group=group)
+        h = out.cpu().numpy()
+        return [h[i] for i in range(world)]
 
     return gather

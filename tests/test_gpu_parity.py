@@ -455,6 +455,8 @@ def test_spmv_t_sliced_and_hub_layouts(O, cuda_device, hub):
     yt0[::7] = -0.0
     for p in (S.WeightPrecision.F32, S.WeightPrecision.F16, S.WeightPrecision.Bf16):
         op = cuda_device.prepare_with_transpose_precision(_scsr(csr), ncols, w, p)
+        # SPARSL_LAYOUT_CSC (8) for the hub, SPARSL_LAYOUT_SLICED_REVERSE (4) otherwise
+        assert op.layouts() & (8 if hub else 4) and not op.layouts() & (4 if hub else 8)
         got = yt0.copy()
         op.spmv_t(xt, got)
         want = O.spmv_t(csc, O.quantise(int(p), w), xt, yt0.copy())
