@@ -716,8 +716,9 @@ def bench_scan_sharded(args, dev, dist):
     """The exact scan of a sequence split into one run of SCAN_N maps per rank
     (weak scaling: N x SCAN_N maps in all): halo and table all-gather, entry
     guess, local scan, boundary-state check and rejoin rounds
-    (sparsl_b200/dist_scan.py).  Each step is timed by CUDA events on the
-    device's stream around the whole procedure, host exchanges included;
+    (sparsl_b200/dist_scan.py; by default the device pipeline: NCCL gathers,
+    one host sync).  Each step is timed by CUDA events on the device's
+    stream around the whole procedure, host work included;
     the step time is the max over ranks.  Rank r's run is drawn from seed
     SCAN_SEED + r (rank 0's run is exactly the 1-GPU workload)."""
     import torch
@@ -734,7 +735,10 @@ def bench_scan_sharded(args, dev, dist):
     din = torch.from_numpy(xs).cuda()
     dout = torch.empty_like(din)
     torch.cuda.synchronize()
-    if args.scan_exchange == "nccl":
+    if args.scan_pipeline == "device":
+        group = dist.pg.new_group(backend="nccl")
+        gather_dev = dist_scan.nccl_all_gather_dev(group, dist.world)
+    elif args.scan_exchange == "nccl":
         group = dist.pg.new_group(backend="nccl")
         gather = dist_scan.nccl_all_gather(group, dist.world, torch.device("cuda", dist.local))
     else:
@@ -745,7 +749,10 @@ def bench_scan_sharded(args, dev, dist):
 
     def step():
         nonlocal st
-        st = dist_scan.sharded_scan(run, dist.rank, dist.world, gather)
+        if args.scan_pipeline == "device":
+            st = dist_scan.sharded_scan_device(dev, din, dout, SCAN_N, dist.rank, dist.world, gather_dev)
+        else:
+            st = dist_scan.sharded_scan(run, dist.rank, dist.world, gather)
 
     for _ in range(args.warmup):
         step()
@@ -781,7 +788,8 @@ def bench_scan_sharded(args, dev, dist):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded numpy per rank: a U[0.9,1], b N(0,1))",
             "config": {"workload": f"scan: {dist.world} x {SCAN_N:,} maps, one consecutive run per GPU",
-                       "exchange": args.scan_exchange,
+                       "pipeline": args.scan_pipeline,
+                       "exchange": "nccl" if args.scan_pipeline == "device" else args.scan_exchange,
                        "parallelism": "contiguous runs; one all-gather of halos (2,048 maps) and multiplier "
                                       "tables, entry guess, local exact scan, boundary-state all-gather "
                                       "(rejoin rounds only on a mismatch)",
@@ -1109,7 +1117,10 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="N=1: skip the SpMV / scan / LIF-1GPU figures")
     ap.add_argument("--kernel-iters", type=int, default=20)
     ap.add_argument("--scan-exchange", default="gloo", choices=["gloo", "nccl"],
-                    help="N>1 scan: the process group that carries the boundary exchanges")
+                    help="N>1 host-driven scan: the process group that carries the boundary exchanges")
+    ap.add_argument("--scan-pipeline", default="device", choices=["device", "host"],
+                    help="N>1 scan: every step enqueued on the device with NCCL gathers and one host sync "
+                         "(device), or the host-driven steps (host)")
     # Smaller instances of the same workloads (profiling captures, quick runs).
     ap.add_argument("--scan-n", type=int, default=None, help="scan length (default 2^26)")
     ap.add_argument("--lif-ticks", type=int, default=1000, help="timed ticks of the 1-GPU LIF network")

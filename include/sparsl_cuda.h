@@ -291,6 +291,26 @@ int sparsl_dev_scan_rejoin_device(sparsl_dev *dev, const float *d_in, float *d_o
  *    *folded the number of maps folded so far. */
 int sparsl_dev_scan_table_device(sparsl_dev *dev, const float *d_in, uint64_t n, uint32_t *table,
                                  void *stream);
+/*  The same steps with no host round trip, for a host that all-gathers
+ *  device buffers (NCCL); all three only enqueue work on `stream`:
+ *  - scan_publish: writes the run's blob of 2*halo + 4 floats: its last
+ *    `halo` maps (identity maps in front when the run is shorter), then the
+ *    words {maps in that tail, the run's multiplier table, and on the first
+ *    run (first != 0) its exit multiplier bits (8 = not settled), 0}.
+ *  - scan_entry: from every run's blob, gathered in run order
+ *    (world x (2*halo + 4) floats), writes run `rank`'s guessed entry state
+ *    (2 floats, device memory): the offset folded over the halo, the
+ *    multiplier exact when it has settled.
+ *  - assoc_scan_after: the scan of the run from an entry state in device
+ *    memory.
+ *  halo is 1..4096 maps; world <= 64.  publish uses per-device scratch, so
+ *  order these calls of one device on one stream. */
+int sparsl_dev_scan_publish_device(sparsl_dev *dev, const float *d_in, uint64_t n, int first,
+                                   uint32_t halo, float *d_blob, void *stream);
+int sparsl_dev_scan_entry_device(sparsl_dev *dev, const float *d_gathered, uint32_t world,
+                                 uint32_t rank, uint32_t halo, float *d_entry, void *stream);
+int sparsl_dev_assoc_scan_after_device(sparsl_dev *dev, const float *d_in, uint64_t n, float *d_out,
+                                       const float *d_entry, void *stream);
 int sparsl_dev_scan_settle_device(sparsl_dev *dev, const float *d_in, uint64_t n, float *multiplier,
                                   uint64_t *folded, void *stream);
 /* Enqueue recurrent ticks on the operator's stream without waiting. */

@@ -533,6 +533,23 @@ class Device:
                                                          ctypes.byref(k), stream), "scan_settle")
         return np.float32(a.value), int(k.value)
 
+    def scan_publish_device(self, d_in, n: int, first: bool, halo: int, d_blob, stream=None) -> None:
+        """Enqueue a run's published blob (halo, multiplier table, first run's
+        exit multiplier) into ``d_blob`` (2*halo + 4 floats)."""
+        _check(_lib.load().sparsl_dev_scan_publish_device(self._h, _dptr(d_in), int(n), int(bool(first)), int(halo),
+                                                          _dptr(d_blob), stream), "scan_publish")
+
+    def scan_entry_device(self, d_gathered, world: int, rank: int, halo: int, d_entry, stream=None) -> None:
+        """Enqueue run ``rank``'s guessed entry state (2 floats) from the
+        gathered blobs of every run."""
+        _check(_lib.load().sparsl_dev_scan_entry_device(self._h, _dptr(d_gathered), int(world), int(rank), int(halo),
+                                                        _dptr(d_entry), stream), "scan_entry")
+
+    def assoc_scan_after_device(self, d_in, n: int, d_out, d_entry, stream=None) -> None:
+        """Enqueue the scan of a run whose entry state is in device memory."""
+        _check(_lib.load().sparsl_dev_assoc_scan_after_device(self._h, _dptr(d_in), int(n), _dptr(d_out),
+                                                              _dptr(d_entry), stream), "assoc_scan")
+
     def scan_stats(self):
         rep, seg = ctypes.c_uint64(), ctypes.c_uint64()
         _check(_lib.load().sparsl_dev_scan_stats(self._h, ctypes.byref(rep), ctypes.byref(seg)), "scan_stats")

@@ -603,8 +603,9 @@ int sparsl_dev_assoc_scan_device(sparsl_dev* d, const float* d_in, uint64_t n, f
   return sparsl_dev_assoc_scan_from_device(d, d_in, n, d_out, nullptr, stream);
 }
 
-int sparsl_dev_assoc_scan_from_device(sparsl_dev* d, const float* d_in, uint64_t n, float* d_out, const float* entry,
-                                      void* stream) {
+namespace {
+int dev_scan(sparsl_dev* d, const float* d_in, uint64_t n, float* d_out, const float* entry, const float* entry_dev,
+             void* stream) {
   ADMIT();
   if (!d) return fail(SPARSL_ERR_INVALID, "null device", "assoc_scan: null device");
   if (n == 0) return SPARSL_OK;
@@ -624,7 +625,7 @@ int sparsl_dev_assoc_scan_from_device(sparsl_dev* d, const float* d_in, uint64_t
     CK("assoc_scan", cudaMemsetAsync(buf, 0, ntiles * 128, s));
     ScanScratch sc = d->sc;
     sc.timeline = buf;
-    CK("assoc_scan", launch_scan(d_in, d_out, n, sc, d->err.d, s, entry));
+    CK("assoc_scan", launch_scan(d_in, d_out, n, sc, d->err.d, s, entry, entry_dev));
     std::vector<unsigned long long> h(ntiles * 16);
     CK("assoc_scan", cudaMemcpyAsync(h.data(), buf, ntiles * 128, cudaMemcpyDeviceToHost, s));
     CK("assoc_scan", cudaStreamSynchronize(s));
@@ -635,7 +636,60 @@ int sparsl_dev_assoc_scan_from_device(sparsl_dev* d, const float* d_in, uint64_t
     }
     return SPARSL_OK;
   }
-  CK("assoc_scan", launch_scan(d_in, d_out, n, d->sc, d->err.d, s, entry));
+  CK("assoc_scan", launch_scan(d_in, d_out, n, d->sc, d->err.d, s, entry, entry_dev));
+  return SPARSL_OK;
+}
+}  // namespace
+
+int sparsl_dev_assoc_scan_from_device(sparsl_dev* d, const float* d_in, uint64_t n, float* d_out, const float* entry,
+                                      void* stream) {
+  return dev_scan(d, d_in, n, d_out, entry, nullptr, stream);
+}
+
+int sparsl_dev_assoc_scan_after_device(sparsl_dev* d, const float* d_in, uint64_t n, float* d_out,
+                                       const float* d_entry, void* stream) {
+  if (!d_entry) return fail(SPARSL_ERR_INVALID, "null argument", "assoc_scan_after: a device entry state is required");
+  return dev_scan(d, d_in, n, d_out, nullptr, d_entry, stream);
+}
+
+namespace {
+// Lazily allocated per-device scratch of the split-scan pieces.
+constexpr uint32_t kTabBlk = 1184;
+int dev_split_scratch(sparsl_dev* d) {
+  if (!d->tscratch.p && dalloc(d->tscratch, (kTabBlk + 64) * 4, false, d->stream) != cudaSuccess)
+    return fail(SPARSL_ERR_ALLOCATION, "table scratch", "device allocation failed for scan table scratch");
+  if (!d->vscratch.p && dalloc(d->vscratch, 32, false, d->stream) != cudaSuccess)
+    return fail(SPARSL_ERR_ALLOCATION, "walk scratch", "device allocation failed for scan walk scratch");
+  return SPARSL_OK;
+}
+}  // namespace
+
+int sparsl_dev_scan_publish_device(sparsl_dev* d, const float* d_in, uint64_t n, int first, uint32_t halo,
+                                   float* d_blob, void* stream) {
+  ADMIT();
+  if (!d || !d_in || !d_blob) return fail(SPARSL_ERR_INVALID, "null argument", "scan_publish: null argument");
+  if (n == 0) return fail(SPARSL_ERR_LENGTH, "empty run", "scan_publish: a run needs at least one map");
+  if (halo == 0 || halo > 4096) return fail(SPARSL_ERR_LENGTH, "halo", "scan_publish: halo must be 1..4096 maps");
+  std::lock_guard<std::mutex> lk(d->mu);
+  CK("scan_publish", cudaSetDevice(d->ordinal));
+  TRY(dev_split_scratch(d));
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : d->stream;
+  CK("scan_publish", launch_scan_publish(d_in, n, first ? 1 : 0, halo, d_blob, d->tscratch.as<uint32_t>(), kTabBlk,
+                                         d->vscratch.as<float>(), d->vscratch.as<unsigned long long>() + 1, s));
+  return SPARSL_OK;
+}
+
+int sparsl_dev_scan_entry_device(sparsl_dev* d, const float* d_gathered, uint32_t world, uint32_t rank,
+                                 uint32_t halo, float* d_entry, void* stream) {
+  ADMIT();
+  if (!d || !d_gathered || !d_entry) return fail(SPARSL_ERR_INVALID, "null argument", "scan_entry: null argument");
+  if (rank == 0 || rank >= world || world > 64)
+    return fail(SPARSL_ERR_INVALID, "rank", "scan_entry: needs 0 < rank < world <= 64");
+  if (halo == 0 || halo > 4096) return fail(SPARSL_ERR_LENGTH, "halo", "scan_entry: halo must be 1..4096 maps");
+  std::lock_guard<std::mutex> lk(d->mu);
+  CK("scan_entry", cudaSetDevice(d->ordinal));
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : d->stream;
+  CK("scan_entry", launch_scan_entry(d_gathered, world, rank, halo, d_entry, s));
   return SPARSL_OK;
 }
 
@@ -691,11 +745,9 @@ int sparsl_dev_scan_table_device(sparsl_dev* d, const float* d_in, uint64_t n, u
   std::lock_guard<std::mutex> lk(d->mu);
   CK("scan_table", cudaSetDevice(d->ordinal));
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : d->stream;
-  constexpr uint32_t kBlk = 1184;
-  if (!d->tscratch.p && dalloc(d->tscratch, (kBlk + 64) * 4, false, d->stream) != cudaSuccess)
-    return fail(SPARSL_ERR_ALLOCATION, "table scratch", "device allocation failed for scan table scratch");
-  uint32_t* out = d->tscratch.as<uint32_t>() + kBlk;
-  CK("scan_table", launch_scan_table(d_in, n, d->tscratch.as<uint32_t>(), kBlk, out, s));
+  TRY(dev_split_scratch(d));
+  uint32_t* out = d->tscratch.as<uint32_t>() + kTabBlk;
+  CK("scan_table", launch_scan_table(d_in, n, d->tscratch.as<uint32_t>(), kTabBlk, out, s));
   CK("scan_table", cudaMemcpyAsync(table, out, 4, cudaMemcpyDeviceToHost, s));
   CK("scan_table", cudaStreamSynchronize(s));
   return SPARSL_OK;

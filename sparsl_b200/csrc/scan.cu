@@ -128,7 +128,7 @@ __device__ void walk_multiplier(float A, int first, const float2* sm, const uint
 
 __global__ void __launch_bounds__(kScanBlock, 5) scan_main(const float2* __restrict__ in, float2* __restrict__ out,
                                                        uint64_t n, ScanScratch s, uint32_t* err, int has_entry,
-                                                       float2 entry) {
+                                                       float2 entry, const float2* entry_dev) {
   extern __shared__ __align__(16) float2 sm[];  // kRows x kRowStride
   __shared__ float s_Eb[kScanThreads];  // in-tile exclusive guess of B (from identity)
   __shared__ uint32_t s_tab[kScanThreads];
@@ -173,7 +173,8 @@ __global__ void __launch_bounds__(kScanBlock, 5) scan_main(const float2* __restr
     // patches it.
     if (has_entry && tile == 0 && t == kScanHalo % kScanBlock) {
       float2* f = sm + (kScanHalo / kScanK) * kRowStride + (kScanHalo % kScanK);
-      const Aff e = comb(Aff{entry.x, entry.y}, Aff{f->x, f->y});
+      const float2 en = entry_dev ? *entry_dev : entry;
+      const Aff e = comb(Aff{en.x, en.y}, Aff{f->x, f->y});
       *f = make_float2(e.a, e.b);
     }
   }
@@ -686,7 +687,7 @@ ScanScratch scan_scratch_carve(void* base, uint64_t n) {
 }
 
 cudaError_t launch_scan(const float* in, float* out, uint64_t n, const ScanScratch& s, uint32_t* err,
-                        cudaStream_t stream, const float* entry) {
+                        cudaStream_t stream, const float* entry, const float* entry_dev) {
   if (n == 0) return cudaSuccess;
   const uint64_t ntiles = (n + kScanTile - 1) / kScanTile;
   if (ntiles > 0x7fffffffull) return cudaErrorInvalidValue;
@@ -696,7 +697,8 @@ cudaError_t launch_scan(const float* in, float* out, uint64_t n, const ScanScrat
   const float2 ent = entry ? make_float2(entry[0], entry[1]) : make_float2(1.0f, 0.0f);
   scan_main<<<(unsigned)ntiles, kScanBlock, smem, stream>>>(reinterpret_cast<const float2*>(in),
                                                               reinterpret_cast<float2*>(out), n, s, err,
-                                                              entry ? 1 : 0, ent);
+                                                              (entry || entry_dev) ? 1 : 0, ent,
+                                                              reinterpret_cast<const float2*>(entry_dev));
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   if (ntiles > 1) {
@@ -856,9 +858,15 @@ constexpr int kTabK = 16;
 constexpr int kTabStride = kTabK + 1;  // float2 row pitch: no bank conflicts across threads
 
 __global__ void __launch_bounds__(kTabThreads) scan_table_kernel(const float2* __restrict__ in, uint64_t n,
+                                                                 const unsigned long long* start,
                                                                  uint32_t* __restrict__ blk_tab) {
   __shared__ uint32_t s_t[kTabThreads];
   __shared__ float2 s_x[kTabThreads * kTabStride];
+  if (start) {  // the run begins at a device-side offset (the same for every thread)
+    const uint64_t lo = *start < n ? *start : n;
+    in += lo;
+    n -= lo;
+  }
   constexpr uint64_t kBatch = (uint64_t)kTabThreads * kTabK;
   const uint64_t nbatch = (n + kBatch - 1) / kBatch;
   const uint64_t per_blk = (nbatch + gridDim.x - 1) / gridDim.x;
@@ -892,11 +900,11 @@ __global__ void __launch_bounds__(kTabThreads) scan_table_reduce_kernel(const ui
 }
 
 cudaError_t launch_scan_table(const float* in, uint64_t n, uint32_t* blk_scratch, uint32_t nblk_max, uint32_t* out,
-                              cudaStream_t stream) {
+                              cudaStream_t stream, const unsigned long long* start) {
   const float2* x = reinterpret_cast<const float2*>(in);
   const uint64_t want = (n + 4095) / 4096;
   const uint32_t nblk = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(want, nblk_max));
-  scan_table_kernel<<<nblk, kTabThreads, 0, stream>>>(x, n, blk_scratch);
+  scan_table_kernel<<<nblk, kTabThreads, 0, stream>>>(x, n, start, blk_scratch);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   scan_table_reduce_kernel<<<1, kTabThreads, 0, stream>>>(blk_scratch, nblk, out);
@@ -909,6 +917,111 @@ cudaError_t launch_scan_walk(const float* in, float* out, uint64_t n, const floa
   const float2 ent = entry ? make_float2(entry[0], entry[1]) : make_float2(1.0f, 0.0f);
   scan_walk_kernel<<<1, kWalkThreads, 0, stream>>>(reinterpret_cast<const float2*>(in), reinterpret_cast<float2*>(out), n,
                                          entry ? 1 : 0, ent, repair, state, stats);
+  return cudaGetLastError();
+}
+
+// ---- a run's part of a split scan, entirely on the device ----------------
+
+// blob[0 .. 2*halo): the run's last min(n, halo) maps, identity maps in front.
+__global__ void scan_tail_kernel(const float2* __restrict__ in, uint64_t n, uint32_t halo, float2* __restrict__ blob) {
+  for (uint32_t j = blockIdx.x * blockDim.x + threadIdx.x; j < halo; j += gridDim.x * blockDim.x) {
+    const int64_t src = (int64_t)n - (int64_t)halo + (int64_t)j;
+    blob[j] = src >= 0 ? in[src] : make_float2(1.0f, 0.0f);
+  }
+}
+
+// meta = {maps in the tail, the run's multiplier table (runs after the
+// first), the first run's exit multiplier bits (8 = not in {0..7} * 2^-149), 0}.
+__global__ void scan_publish_meta_kernel(const float* __restrict__ settle, const unsigned long long* __restrict__ settle_k,
+                                         const uint32_t* __restrict__ table, uint64_t n, int first, uint32_t len,
+                                         uint32_t* __restrict__ meta) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  meta[0] = len;
+  if (first) {
+    const uint32_t b = fbits(settle[0]);
+    uint32_t ax = 8u;
+    if (b <= 7u) ax = *settle_k < n ? tab_at(*table, b) : b;
+    meta[1] = 0xffffffffu;
+    meta[2] = ax;
+  } else {
+    meta[1] = *table;
+    meta[2] = 8u;
+  }
+  meta[3] = 0u;
+}
+
+constexpr int kEntryMaxHalo = 4096;
+
+// A run's guessed entry state from every run's published blob (stride
+// 2*halo + 4 floats): the offset from a fold of the maps just before the run
+// (nearest last, at most `halo`) starting from a copy of the first of them;
+// the multiplier exactly, when the first run's exit multiplier and the tables
+// of the runs in between keep it in {0..7} * 2^-149.
+__global__ void __launch_bounds__(256) scan_entry_kernel(const float* __restrict__ gathered, uint32_t world,
+                                                         uint32_t rank, uint32_t halo, float* __restrict__ entry) {
+  __shared__ float2 s_h[kEntryMaxHalo];
+  __shared__ uint32_t s_take[64], s_from[64], s_nr, s_total;
+  const uint64_t stride = 2ull * halo + 4;
+  if (threadIdx.x == 0) {
+    uint32_t need = halo, k = 0, total = 0;
+    for (int r = (int)rank - 1; r >= 0 && need > 0 && k < 64; --r, ++k) {
+      const uint32_t len = __float_as_uint(gathered[(uint64_t)r * stride + 2ull * halo]);
+      const uint32_t take = len < need ? len : need;
+      s_take[k] = take;
+      s_from[k] = (uint32_t)r;
+      need -= take;
+      total += take;
+    }
+    s_nr = k;
+    s_total = total;
+  }
+  __syncthreads();
+  // Oldest first: the last entry of the list is the earliest run.
+  uint32_t dst = 0;
+  for (int k = (int)s_nr - 1; k >= 0; --k) {
+    const float2* tail = reinterpret_cast<const float2*>(gathered + (uint64_t)s_from[k] * stride);
+    const uint32_t take = s_take[k];
+    for (uint32_t j = threadIdx.x; j < take; j += blockDim.x) s_h[dst + j] = tail[halo - take + j];
+    dst += take;
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  Aff acc{1.0f, 0.0f};
+  if (s_total) {
+    acc = Aff{s_h[0].x, s_h[0].y};
+    for (uint32_t j = 1; j < s_total; ++j) acc = comb(acc, Aff{s_h[j].x, s_h[j].y});
+  }
+  uint32_t m = __float_as_uint(gathered[2ull * halo + 2]);  // run 0's exit multiplier
+  for (uint32_t r = 1; r < rank && m <= 7u; ++r) m = tab_at(__float_as_uint(gathered[r * stride + 2ull * halo + 1]), m);
+  entry[0] = m <= 7u ? __uint_as_float(m) : acc.a;
+  entry[1] = acc.b;
+}
+
+cudaError_t launch_scan_publish(const float* in, uint64_t n, int first, uint32_t halo, float* blob,
+                                uint32_t* tab_scratch, uint32_t nblk_max, float* walk_state,
+                                unsigned long long* walk_stats, cudaStream_t stream) {
+  if (n == 0 || halo == 0) return cudaErrorInvalidValue;
+  const float2* x = reinterpret_cast<const float2*>(in);
+  scan_tail_kernel<<<(halo + 255) / 256, 256, 0, stream>>>(x, n, halo, reinterpret_cast<float2*>(blob));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  uint32_t* table = tab_scratch + nblk_max;
+  if (first) {
+    if ((e = launch_scan_walk(in, nullptr, n, nullptr, 2, walk_state, walk_stats, stream)) != cudaSuccess) return e;
+    if ((e = launch_scan_table(in, n, tab_scratch, nblk_max, table, stream, walk_stats)) != cudaSuccess) return e;
+  } else {
+    if ((e = launch_scan_table(in, n, tab_scratch, nblk_max, table, stream)) != cudaSuccess) return e;
+  }
+  const uint32_t len = (uint32_t)(n < halo ? n : halo);
+  scan_publish_meta_kernel<<<1, 32, 0, stream>>>(walk_state, walk_stats, table, n, first, len,
+                                                 reinterpret_cast<uint32_t*>(blob + 2ull * halo));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scan_entry(const float* gathered, uint32_t world, uint32_t rank, uint32_t halo, float* entry,
+                              cudaStream_t stream) {
+  if (halo == 0 || halo > (uint32_t)kEntryMaxHalo || rank == 0 || rank >= world) return cudaErrorInvalidValue;
+  scan_entry_kernel<<<1, 256, 0, stream>>>(gathered, world, rank, halo, entry);
   return cudaGetLastError();
 }
 

@@ -38,7 +38,8 @@ ScanScratch scan_scratch_carve(void* base, uint64_t n);
 // longer sequence whose state before in[0] is *entry, so out[0] is
 // entry o in[0] rather than a copy of in[0].
 cudaError_t launch_scan(const float* in, float* out, uint64_t n, const ScanScratch& s,
-                        uint32_t* err, cudaStream_t stream, const float* entry = nullptr);
+                        uint32_t* err, cudaStream_t stream, const float* entry = nullptr,
+                        const float* entry_dev = nullptr);
 
 // Serial single-thread walks for runs split across devices (see scan.cu):
 // fold in[0..n) into state[2] (device memory), or repair out[0..n) from an
@@ -52,6 +53,18 @@ cudaError_t launch_scan_walk(const float* in, float* out, uint64_t n, const floa
 // multiplier leaving the run when m * 2^-149 entered it; 8 = outside that
 // set), into *out (device).  blk_scratch holds nblk_max words.
 cudaError_t launch_scan_table(const float* in, uint64_t n, uint32_t* blk_scratch, uint32_t nblk_max, uint32_t* out,
+                              cudaStream_t stream, const unsigned long long* start = nullptr);
+
+// A run's part of a split scan with no host round trip (see scan.cu):
+// publish writes blob = [last `halo` maps, identity-padded | len, table,
+// first run's exit multiplier, 0] (2*halo + 4 floats); entry reads every
+// run's blob (gathered, in run order) and writes the run's guessed entry
+// state (2 floats).  Scratch: tab_scratch (nblk_max + 1 words), walk_state
+// (2 floats), walk_stats (1 word).
+cudaError_t launch_scan_publish(const float* in, uint64_t n, int first, uint32_t halo, float* blob,
+                                uint32_t* tab_scratch, uint32_t nblk_max, float* walk_state,
+                                unsigned long long* walk_stats, cudaStream_t stream);
+cudaError_t launch_scan_entry(const float* gathered, uint32_t world, uint32_t rank, uint32_t halo, float* entry,
                               cudaStream_t stream);
 
 }  // namespace sparsl

@@ -248,3 +248,82 @@ def nccl_all_gather(group, world: int, device) -> Callable[[np.ndarray], List[np
         return [h[i] for i in range(world)]
 
     return gather
+
+
+def sharded_scan_device(device, d_in, d_out, n: int, rank: int, world: int, all_gather_dev,
+                        halo: int = DEFAULT_HALO) -> ShardedScanStats:
+    """The same algorithm as ``sharded_scan`` with every step enqueued on the
+    device's own stream and one host synchronisation per call.
+
+    ``d_in`` / ``d_out`` are (n, 2) float32 CUDA tensors of this rank's run;
+    ``all_gather_dev(t)`` returns a (world, *t.shape) CUDA tensor of every
+    rank's ``t`` in rank order, enqueued on the current stream (an NCCL
+    all-gather).  The halo and tables travel in one gather, the boundary
+    states in a second; only those states come back to the host, and only a
+    failed boundary check (rare: the multiplier arrives exactly and the offset
+    contracts) falls back to host-driven rejoin rounds.
+    """
+    import torch
+
+    if n < 1:
+        raise ValueError("every rank's run needs at least one map")
+    t0 = time.perf_counter()
+    dev_t = torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.ExternalStream(device.stream_handle(), device=dev_t)
+    with torch.cuda.stream(stream):
+        blob = torch.empty(2 * halo + 4, dtype=torch.float32, device=dev_t)
+        device.scan_publish_device(d_in, n, rank == 0, halo, blob)
+        gathered = all_gather_dev(blob)
+        st = torch.empty(4, dtype=torch.float32, device=dev_t)
+        if rank > 0:
+            entry_d = torch.empty(2, dtype=torch.float32, device=dev_t)
+            device.scan_entry_device(gathered, world, rank, halo, entry_d)
+            device.assoc_scan_after_device(d_in, n, d_out, entry_d)
+            st[:2].copy_(entry_d)
+        else:
+            device.assoc_scan_from_device(d_in, n, d_out, None)
+            st[:2].fill_(float("nan"))
+        st[2:].copy_(d_out[n - 1])
+        states = all_gather_dev(st).cpu().numpy()
+    ph = {"device_pipeline": (time.perf_counter() - t0) * 1e3}
+    entry = None if rank == 0 else states[rank][:2].copy()
+    first_entry = None if entry is None else entry.copy()
+    exit_state = states[rank][2:].copy()
+    rewritten, rounds = 0, 0
+
+    def host_gather(a: np.ndarray) -> List[np.ndarray]:
+        with torch.cuda.stream(stream):
+            g = all_gather_dev(torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev_t)).cpu().numpy()
+        return [g[i] for i in range(world)]
+
+    while True:
+        bad = next((r for r in range(1, world)
+                    if not np.array_equal(_bits(states[r][:2]), _bits(states[r - 1][2:]))), None)
+        if bad is None:
+            break
+        rounds += 1
+        if rounds >= world:
+            raise RuntimeError("sharded scan: boundary states did not settle")
+        if rank == bad:
+            entry = states[bad - 1][2:].copy()
+            ex, k = device.scan_rejoin_device(d_in, d_out, n, entry)
+            exit_state = np.asarray(ex, np.float32)
+            rewritten += int(k)
+        nan2 = np.array([np.nan, np.nan], np.float32)
+        states = host_gather(np.concatenate([nan2 if entry is None else np.asarray(entry, np.float32), exit_state]))
+    if rounds:
+        ph["rejoin_rounds"] = (time.perf_counter() - t0) * 1e3 - ph["device_pipeline"]
+    exact_first = rank == 0 or np.array_equal(_bits(first_entry), _bits(entry))
+    return ShardedScanStats(rounds=rounds, rewritten=rewritten, entry_exact=bool(exact_first), phases_ms=ph)
+
+
+def nccl_all_gather_dev(group, world: int):
+    """``all_gather_dev`` for ``sharded_scan_device`` over an NCCL group."""
+    import torch
+
+    def gather(t):
+        out = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+        torch.distributed.all_gather_into_tensor(out, t.contiguous(), group=group)
+        return out
+
+    return gather

@@ -134,3 +134,62 @@ def test_sharded_driver_on_one_gpu(O, cuda_device, world, kind, n, plant, halo):
         assert stats[plant].rewritten > 0
     elif kind == "contracting":
         assert all(s.entry_exact for s in stats) and stats[0].rounds == 0
+
+
+class _DevGather:
+    """all_gather_dev for threads sharing one GPU: every rank's tensor is
+    stacked on the caller's current stream (all are on the device's stream,
+    in enqueue order)."""
+
+    def __init__(self, world):
+        self.bar = threading.Barrier(world, timeout=120)
+        self.slots = [None] * world
+
+    def for_rank(self, r):
+        def gather(t):
+            self.slots[r] = t
+            self.bar.wait()
+            out = torch.stack(self.slots)
+            self.bar.wait()
+            return out
+
+        return gather
+
+
+@pytest.mark.parametrize("world,kind,n,halo", [
+    (4, "contracting", (1 << 22) + 12_345, 2048),
+    (3, "contracting", 3_000, 2048),        # short runs: the halo spans several runs, the whole prefix
+    (3, "flat", 5_000, 256),                # no contraction: guesses off, host rejoin rounds
+])
+def test_device_pipeline_on_one_gpu(O, cuda_device, world, kind, n, halo):
+    x = _data(kind, n)
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.empty_like(dx)
+    torch.cuda.synchronize()
+    g = _DevGather(world)
+    stats, errs = [None] * world, []
+
+    def rank_main(r):
+        try:
+            lo, hi = r * n // world, (r + 1) * n // world
+            stats[r] = dist_scan.sharded_scan_device(cuda_device, dx[lo:hi], dy[lo:hi], hi - lo, r, world,
+                                                     g.for_rank(r), halo=halo)
+        except Exception as e:  # noqa: BLE001
+            errs.append(e)
+            g.bar.abort()
+
+    th = [threading.Thread(target=rank_main, args=(r,)) for r in range(world)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join(timeout=300)
+    assert not errs, errs
+    cuda_device.wait()
+    torch.cuda.synchronize()
+    want = O.scan_sequential(x)
+    assert np.array_equal(dy.cpu().numpy().view(np.uint32), want.view(np.uint32))
+    assert len({s.rounds for s in stats}) == 1
+    if kind == "contracting":
+        assert all(s.entry_exact for s in stats) and stats[0].rounds == 0
+    else:
+        assert stats[0].rounds >= 1
