@@ -850,40 +850,74 @@ __device__ uint32_t block_compose(uint32_t* s_t, uint32_t mine) {
   return t;
 }
 
-// Each block owns a contiguous stretch of the run and walks it in batches of
-// kTabThreads x kTabK maps, staged with coalesced loads into a padded
-// shared-memory block; thread t folds maps t*kTabK .. t*kTabK + kTabK - 1
-// of the batch, and the batch tables compose in order.
+// Each warp owns a contiguous stretch of the run (blocks own consecutive
+// stretches, warps consecutive parts of them) and walks it in batches of
+// 32 x kTabK maps: the lanes load the next batch into registers (coalesced)
+// while they fold the current one from the warp's padded shared-memory slice
+// (lane l folds maps l*kTabK .. l*kTabK + kTabK - 1), and the 32 lane tables
+// compose in order with shuffles.  No block barrier inside the loop; the
+// warps' tables compose in warp order at the end, the blocks' in a second
+// pass.
 constexpr int kTabK = 16;
-constexpr int kTabStride = kTabK + 1;  // float2 row pitch: no bank conflicts across threads
+constexpr int kTabStride = kTabK + 1;  // float2 row pitch: no bank conflicts across lanes
+constexpr int kTabWarps = kTabThreads / 32;
+constexpr uint32_t kTabBatch = 32u * kTabK;
+
+__device__ __forceinline__ uint32_t warp_compose(uint32_t t, uint32_t lane) {
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const uint32_t o = __shfl_down_sync(0xffffffffu, t, d);
+    if ((lane & (2 * d - 1)) == 0) t = tab_comb(t, o);  // lane covers [lane, lane + 2d) in order
+  }
+  return __shfl_sync(0xffffffffu, t, 0);
+}
 
 __global__ void __launch_bounds__(kTabThreads) scan_table_kernel(const float2* __restrict__ in, uint64_t n,
                                                                  const unsigned long long* start,
                                                                  uint32_t* __restrict__ blk_tab) {
-  __shared__ uint32_t s_t[kTabThreads];
-  __shared__ float2 s_x[kTabThreads * kTabStride];
+  __shared__ float2 s_x[kTabWarps][32 * kTabStride];
+  __shared__ uint32_t s_w[kTabWarps];
   if (start) {  // the run begins at a device-side offset (the same for every thread)
     const uint64_t lo = *start < n ? *start : n;
     in += lo;
     n -= lo;
   }
-  constexpr uint64_t kBatch = (uint64_t)kTabThreads * kTabK;
-  const uint64_t nbatch = (n + kBatch - 1) / kBatch;
-  const uint64_t per_blk = (nbatch + gridDim.x - 1) / gridDim.x;
-  const uint64_t q0 = (uint64_t)blockIdx.x * per_blk, q1 = q0 + per_blk < nbatch ? q0 + per_blk : nbatch;
-  uint32_t acc = kTabId;
-  for (uint64_t q = q0; q < q1; ++q) {
-    const uint64_t base = q * kBatch;
-    const uint32_t cnt = (uint32_t)(n - base < kBatch ? n - base : kBatch);
-    for (uint32_t j = threadIdx.x; j < kBatch; j += kTabThreads) {
-      const float2 x = j < cnt ? __ldg(in + base + j) : make_float2(1.0f, 0.0f);
-      s_x[(j / kTabK) * kTabStride + (j % kTabK)] = x;
+  const uint32_t lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const uint64_t nb = (n + kTabBatch - 1) / kTabBatch;  // batches in the run
+  const uint64_t per_blk = (nb + gridDim.x - 1) / gridDim.x;
+  const uint64_t per_w = (per_blk + kTabWarps - 1) / kTabWarps;
+  const uint64_t b0 = min((uint64_t)blockIdx.x * per_blk + wid * per_w, nb);
+  const uint64_t b1 = min(min(b0 + per_w, (uint64_t)(blockIdx.x + 1) * per_blk), nb);
+  float2* sx = s_x[wid];
+  float2 nxt[kTabK];
+  auto load = [&](uint64_t q) {
+    const uint64_t base = q * kTabBatch;
+#pragma unroll
+    for (int j = 0; j < kTabK; ++j) {
+      const uint64_t i = base + (uint64_t)j * 32 + lane;
+      nxt[j] = i < n ? __ldg(in + i) : make_float2(1.0f, 0.0f);  // identity maps past the end
     }
-    __syncthreads();
-    const uint32_t t = chains_table_smem(s_x + threadIdx.x * kTabStride, 1, kTabK);
-    acc = tab_comb(acc, block_compose(s_t, t));
+  };
+  uint32_t acc = kTabId;
+  if (b0 < b1) load(b0);
+  for (uint64_t q = b0; q < b1; ++q) {
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < kTabK; ++j) {
+      const uint32_t e = (uint32_t)j * 32 + lane;  // map e of the batch
+      sx[(e / kTabK) * kTabStride + (e % kTabK)] = nxt[j];
+    }
+    __syncwarp();
+    if (q + 1 < b1) load(q + 1);
+    acc = tab_comb(acc, warp_compose(chains_table_smem(sx + lane * kTabStride, 1, kTabK), lane));
   }
-  if (threadIdx.x == 0) blk_tab[blockIdx.x] = acc;
+  if (lane == 0) s_w[wid] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t t = kTabId;
+    for (int w = 0; w < kTabWarps; ++w) t = tab_comb(t, s_w[w]);
+    blk_tab[blockIdx.x] = t;
+  }
 }
 
 __global__ void __launch_bounds__(kTabThreads) scan_table_reduce_kernel(const uint32_t* __restrict__ blk_tab,
@@ -902,8 +936,18 @@ __global__ void __launch_bounds__(kTabThreads) scan_table_reduce_kernel(const ui
 cudaError_t launch_scan_table(const float* in, uint64_t n, uint32_t* blk_scratch, uint32_t nblk_max, uint32_t* out,
                               cudaStream_t stream, const unsigned long long* start) {
   const float2* x = reinterpret_cast<const float2*>(in);
-  const uint64_t want = (n + 4095) / 4096;
-  const uint32_t nblk = (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(want, nblk_max));
+  // One wave of resident blocks, each with >= 8 batches.
+  static int resident = 0;
+  if (!resident) {
+    int dev = 0, sms = 0, per_sm = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_table_kernel, kTabThreads, 0) != cudaSuccess)
+      return cudaGetLastError();
+    resident = std::max(1, sms * per_sm);
+  }
+  const uint64_t want = (n + 8ull * kTabBatch - 1) / (8ull * kTabBatch);
+  const uint32_t nblk =
+      (uint32_t)std::max<uint64_t>(1, std::min<uint64_t>(std::min<uint64_t>(want, nblk_max), (uint64_t)resident));
   scan_table_kernel<<<nblk, kTabThreads, 0, stream>>>(x, n, start, blk_scratch);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
@@ -911,10 +955,48 @@ cudaError_t launch_scan_table(const float* in, uint64_t n, uint32_t* blk_scratch
   return cudaGetLastError();
 }
 
+// SETTLE on one warp: the multiplier chain from a copy of in[0] up to its
+// first value in {0..7} * 2^-149.  The warp loads 32 multipliers at a time
+// (the next 32 while it walks the current ones); every lane runs the same
+// serial chain from shuffled values, so the walk is one multiply per map
+// with the domain test off the dependency chain.
+__global__ void __launch_bounds__(32) scan_settle_kernel(const float2* __restrict__ in, uint64_t n, float* state,
+                                                         unsigned long long* stats) {
+  const uint32_t lane = threadIdx.x;
+  float am = 0.f, hit_a = 0.f;
+  uint64_t hit = n;  // maps folded when the chain settled (n: it never did)
+  float nxt = lane < n ? __ldg(&in[lane].x) : 1.0f;
+  for (uint64_t base = 0; base < n && hit == n; base += 32) {
+    const float cur = nxt;
+    if (base + 32 + lane < n) nxt = __ldg(&in[base + 32 + lane].x);
+    const uint32_t cnt = (uint32_t)(n - base < 32 ? n - base : 32);
+#pragma unroll
+    for (uint32_t j = 0; j < 32; ++j) {
+      const float a = __shfl_sync(0xffffffffu, cur, j);
+      if (j < cnt && hit == n) {
+        am = (base + j == 0) ? a : fmul(a, am);
+        if (fbits(am) <= 7u) {
+          hit = base + j + 1;
+          hit_a = am;
+        }
+      }
+    }
+  }
+  if (lane == 0) {
+    state[0] = hit < n ? hit_a : am;
+    state[1] = 0.f;
+    if (stats) stats[0] = hit;
+  }
+}
+
 cudaError_t launch_scan_walk(const float* in, float* out, uint64_t n, const float* entry, int repair, float* state,
                              unsigned long long* stats, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
   const float2 ent = entry ? make_float2(entry[0], entry[1]) : make_float2(1.0f, 0.0f);
+  if (repair == 2) {
+    scan_settle_kernel<<<1, 32, 0, stream>>>(reinterpret_cast<const float2*>(in), n, state, stats);
+    return cudaGetLastError();
+  }
   scan_walk_kernel<<<1, kWalkThreads, 0, stream>>>(reinterpret_cast<const float2*>(in), reinterpret_cast<float2*>(out), n,
                                          entry ? 1 : 0, ent, repair, state, stats);
   return cudaGetLastError();
