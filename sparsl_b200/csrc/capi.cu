@@ -388,6 +388,16 @@ RowLaunch fwd_launch(sparsl_op* op) {
 cudaError_t launch_fwd(sparsl_op* op, const RowLaunch& p, cudaStream_t s) {
   if (!op->ell.ok) return launch_rows(p, s);
   if (!p.idx_list) return launch_ell(op->ell, p, s);
+  if (p.out_bits && p.epilogue == EPI_LIF) {
+    // A recurrent tick: the streaming kernel only writes the packed spikes,
+    // and one small kernel turns them into the ascending index list.
+    RowLaunch q = p;
+    q.idx_list = nullptr;
+    q.idx_count = nullptr;
+    cudaError_t e = launch_ell(op->ell, q, s);
+    if (e != cudaSuccess) return e;
+    return launch_compact_bits(p.out_bits, ((uint64_t)p.nlines + 31) / 32, p.idx_list, p.idx_count, p.idx_base, s);
+  }
   // Compacting launches tag their look-back flags with a fresh epoch; the
   // flags are cleared only when the 30-bit tag wraps.
   RowLaunch q = p;

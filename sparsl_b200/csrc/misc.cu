@@ -142,6 +142,68 @@ __global__ void popcount_kernel(const uint32_t* __restrict__ words, uint64_t nwo
   if ((threadIdx.x & 31) == 0 && c) atomicAdd(slot, c);
 }
 
+// Ascending index list of the set bits of `words` (bit b of word w is line
+// 32w + b): one block walks the words in order, 8 per thread per round, with
+// a block-wide exclusive scan of the per-thread counts; *count receives the
+// total.  Run after a tick kernel that wrote the packed spikes, it replaces a
+// look-back inside the tick: the tick streams without waiting on other tiles.
+constexpr int kCompactThreads = 1024;
+constexpr int kCompactWords = 8;
+
+__global__ void __launch_bounds__(kCompactThreads) compact_bits_kernel(const uint32_t* __restrict__ words,
+                                                                      uint64_t nwords, uint32_t* __restrict__ idx,
+                                                                      uint32_t* count, uint32_t idx_base) {
+  __shared__ uint32_t s_warp[kCompactThreads / 32];
+  __shared__ uint32_t s_carry;
+  const uint32_t lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (threadIdx.x == 0) s_carry = 0;
+  __syncthreads();
+  constexpr uint64_t kRound = (uint64_t)kCompactThreads * kCompactWords;
+  for (uint64_t r0 = 0; r0 < nwords; r0 += kRound) {
+    const uint64_t w0 = r0 + (uint64_t)threadIdx.x * kCompactWords;
+    uint32_t v[kCompactWords];
+    uint32_t c = 0;
+#pragma unroll
+    for (int k = 0; k < kCompactWords; ++k) {
+      v[k] = w0 + k < nwords ? __ldg(words + w0 + k) : 0u;
+      c += __popc(v[k]);
+    }
+    uint32_t incl = c;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const uint32_t o = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= (uint32_t)d) incl += o;
+    }
+    if (lane == 31) s_warp[wid] = incl;
+    __syncthreads();
+    if (wid == 0) {
+      uint32_t t = s_warp[lane];
+      uint32_t ti = t;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const uint32_t o = __shfl_up_sync(0xffffffffu, ti, d);
+        if (lane >= (uint32_t)d) ti += o;
+      }
+      s_warp[lane] = ti - t;  // exclusive prefix of the warp totals
+    }
+    __syncthreads();
+    uint32_t pos = s_carry + s_warp[wid] + incl - c;
+#pragma unroll
+    for (int k = 0; k < kCompactWords; ++k) {
+      uint32_t b = v[k];
+      while (b) {
+        const uint32_t bit = __ffs(b) - 1;
+        idx[pos++] = idx_base + (uint32_t)((w0 + k) * 32 + bit);
+        b &= b - 1;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == kCompactThreads - 1) s_carry = pos;  // the last thread ends at the round's total
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *count = s_carry;
+}
+
 __global__ void canary_check_kernel(CanarySet set, uint32_t* err) {
   for (int d = blockIdx.x; d < set.count; d += gridDim.x) {
     const uint32_t* p = set.ptr[d];
@@ -216,6 +278,12 @@ cudaError_t launch_lif_integrate(float* v, float* theta, const float* cur, uint8
 cudaError_t launch_pack(const uint8_t* spk, uint64_t n, uint32_t* out, uint64_t out_words, cudaStream_t s) {
   if (out_words == 0) return cudaSuccess;
   pack_kernel<<<grid_for(out_words, 256), 256, 0, s>>>(spk, n, out, out_words);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_compact_bits(const uint32_t* words, uint64_t nwords, uint32_t* idx, uint32_t* count,
+                                uint32_t idx_base, cudaStream_t s) {
+  compact_bits_kernel<<<1, kCompactThreads, 0, s>>>(words, nwords, idx, count, idx_base);
   return cudaGetLastError();
 }
 

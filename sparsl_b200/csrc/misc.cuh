@@ -46,6 +46,10 @@ cudaError_t launch_spmm(const SpmmLaunch& p, int sm_count, cudaStream_t s);
 cudaError_t launch_lif_integrate(float* v, float* theta, const float* cur, uint8_t* spk, uint64_t n,
                                  float decay, float v_reset, float dtheta, cudaStream_t s);
 cudaError_t launch_pack(const uint8_t* spk, uint64_t n, uint32_t* out, uint64_t out_words, cudaStream_t s);
+// idx[0..) = idx_base + the ascending positions of the set bits of words
+// (bit b of word w is position 32w + b); *count = their number.
+cudaError_t launch_compact_bits(const uint32_t* words, uint64_t nwords, uint32_t* idx, uint32_t* count,
+                                uint32_t idx_base, cudaStream_t s);
 // Writes popcount(words) into *slot (zeroed first).
 cudaError_t launch_popcount(const uint32_t* words, uint64_t nwords, uint32_t* slot, cudaStream_t s);
 cudaError_t launch_canary_check(const CanarySet& set, uint32_t* err, cudaStream_t s);
