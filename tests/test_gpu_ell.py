@@ -179,3 +179,30 @@ def test_f16_weights_every_binary16_pattern(O, cuda_device, generic):
     op.spmv(x, got)
     want = O.spmv(csr, O.quantise(int(S.WeightPrecision.F16), w), x, np.zeros(nrows, np.float32))
     assert_bits_equal(got, want, f"all binary16 patterns generic={generic}")
+
+
+def test_recurrent_index_list_over_several_compaction_rounds(O, cuda_device):
+    """The ascending spike index list of a tick on the TMA path comes from a
+    separate one-block compaction over the packed words: 300,007 cells are
+    9,376 words (two rounds of 8,192) with a ragged last word."""
+    n, L = 300_007, 16
+    r = np.random.default_rng(300)
+    col = np.sort(r.integers(0, n, size=(n, L), dtype=np.uint32), axis=1).reshape(-1)
+    rp = (np.arange(n + 1, dtype=np.uint64) * L).astype(np.uint32)
+    w = (r.standard_normal(n * L) * 0.4).astype(np.float32)
+    csr = O.Csr(rp, col, n)
+    v0 = r.random(n).astype(np.float32)
+    t0 = np.full(n, 0.8, np.float32)
+    pk0 = O.pack_spikes((r.random(n) < 0.05).astype(np.uint8))
+    op = cuda_device.prepare(S.Csr(rp, col, n), n, w)
+    assert op.layouts() & 1, "uniform rows take the TMA path"
+    op.write_x_spikes(pk0)
+    op.write_lif_state(v0, t0)
+    vw, tw, sw, xw = v0.copy(), t0.copy(), np.zeros(n, np.uint8), pk0.copy()
+    steps = 4
+    op.fused_spmv_spikes_lif_recurrent_steps(S.LifParams.new(0.95, 0.0, 0.0), steps)
+    trace = O.recurrent_steps(csr, w, xw, vw, tw, sw, 0.95, 0.0, 0.0, steps, par=True)
+    assert np.array_equal(op.spike_trace(), trace)
+    idx = op.spike_indices()
+    assert np.array_equal(idx, np.flatnonzero(sw).astype(np.uint32))
+    assert sum(trace) > 1000 and (idx.size == 0 or idx[-1] < n)
