@@ -627,25 +627,6 @@ int dev_scan(sparsl_dev* d, const float* d_in, uint64_t n, float* d_out, const f
     TRY(dev_scan_prepare(d, n));
     CK("assoc_scan", cudaStreamSynchronize(d->stream));
   }
-  const char* tl = std::getenv("SPARSL_SCAN_TIMELINE");  // profiling aid: per-tile phase stamps
-  if (tl) {
-    const uint64_t ntiles = (n + kScanTile - 1) / kScanTile;
-    unsigned long long* buf = nullptr;
-    CK("assoc_scan", cudaMalloc(&buf, ntiles * 128));
-    CK("assoc_scan", cudaMemsetAsync(buf, 0, ntiles * 128, s));
-    ScanScratch sc = d->sc;
-    sc.timeline = buf;
-    CK("assoc_scan", launch_scan(d_in, d_out, n, sc, d->err.d, s, entry, entry_dev));
-    std::vector<unsigned long long> h(ntiles * 16);
-    CK("assoc_scan", cudaMemcpyAsync(h.data(), buf, ntiles * 128, cudaMemcpyDeviceToHost, s));
-    CK("assoc_scan", cudaStreamSynchronize(s));
-    cudaFree(buf);
-    if (FILE* f = std::fopen(tl, "wb")) {
-      std::fwrite(h.data(), 8, h.size(), f);
-      std::fclose(f);
-    }
-    return SPARSL_OK;
-  }
   CK("assoc_scan", launch_scan(d_in, d_out, n, d->sc, d->err.d, s, entry, entry_dev));
   return SPARSL_OK;
 }
