@@ -625,7 +625,7 @@ def bench_spmv(args, dev, want_cpu):
     return {"metric": "SpMV effective HBM GB/s", "value": algo / (ms * 1e-3) / 1e9, "unit": "GB/s",
             "ms_per_step": ms, "kernel_ms_samples": len(ts), "algorithmic_bytes": algo,
             "config": "100,000 x 100,000, 64 distinct sorted cols/row, w U[-1,1], x U[0,1], f32; L2 flushed "
-                      "(1 GiB write) before every launch",
+                      "(1 GiB written, then read back) before every launch",
             "e2e": {"value": algo / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 2 * SPMV_N * 4,
                     "d2h_bytes_per_step": SPMV_N * 4, "path": "sparsl_op_spmv, pinned host x/y"},
             "bit_exact_vs_oracle": exact, "cpu_baseline": cpu,
@@ -708,7 +708,7 @@ def bench_rowshard(args, dev, dist, kind):
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, row block per rank)",
             "config": {"workload": f"{kind}: {dist.world} row blocks of {shape}; x replicated",
                        "parallelism": "row blocks, x replicated, no exchange",
-                       "l2": "L2 flushed (1 GiB write) before every launch"},
+                       "l2": "L2 flushed (1 GiB written, then read back) before every launch"},
             "algorithmic_bytes_per_gpu": algo, "clocks": ck, "bit_exact_vs_oracle": all(oks)}
 
 
@@ -970,7 +970,7 @@ def bench_spmm(args, dev, want_cpu):
             "ms_per_step": f32["ms_per_step"], "algorithmic_bytes": f32["algorithmic_bytes"],
             "config": f"{n:,} x {n:,}, row lengths Zipf({SPMM_ALPHA}) restricted to [1,{SPMM_KMAX}] "
                       f"(realised nnz {nnz:,}, mean {nnz / n:.1f}), distinct sorted uniform cols, w U[-1,1], "
-                      f"X {n:,} x {nv} row-major U[-1,1]; L2 flushed (1 GiB write) before every launch",
+                      f"X {n:,} x {nv} row-major U[-1,1]; L2 flushed (1 GiB written, then read back) before every launch",
             "setup_s": round(setup_s, 1), "e2e": f32.get("e2e"),
             "bit_exact_vs_oracle_row_sample": f32["bit_exact_vs_oracle_row_sample"], "f16": out["f16"],
             "cpu_baseline": cpu}

@@ -158,8 +158,9 @@ int wait_bounded(cudaStream_t s, cudaEvent_t ev, uint32_t* err_d, uint32_t* err_
                   std::string(operation) + ": did not complete within " + std::to_string(g_timeout_ms.load()) +
                       " ms; backend quarantined");
     }
-    // ~100 us of spinning, then short sleeps (metal.rs:3108-3152).
-    if (++polls > 200) std::this_thread::sleep_for(std::chrono::microseconds(20));
+    // About a millisecond of spinning, so calls that finish within it return
+    // as soon as they complete; then short sleeps (metal.rs:3108-3152).
+    if (++polls > 2000) std::this_thread::sleep_for(std::chrono::microseconds(20));
   }
   const uint32_t bits = *err_h;
   if (bits) {
