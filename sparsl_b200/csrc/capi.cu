@@ -321,6 +321,11 @@ struct sparsl_op {
   int cur = 0;
   // compaction + trace
   DBuf idx_list, tile_flags, ticket, trace;
+  // Recurrent ticks on the TMA path compact the spikes on a side stream,
+  // concurrently with the next tick; done[b] marks the compaction that last
+  // read spike buffer b (created on first use).
+  cudaStream_t side = nullptr;
+  cudaEvent_t tick_ev = nullptr, done_ev[2] = {nullptr, nullptr};
   // SpMM work units (rows by descending length unless all rows are equal)
   DBuf spmm_order, spmm_units, spmm_ctr;
   uint32_t spmm_nunits = 0, spmm_rows_per_unit = 1;
@@ -1179,6 +1184,10 @@ void sparsl_op_destroy(sparsl_op* op) {
                   &op->spmm_order, &op->spmm_units, &op->spmm_ctr};
   for (DBuf* b : bufs) dfree(*b);
   op->err.release();
+  if (op->side) cudaStreamSynchronize(op->side);
+  for (cudaEvent_t e : {op->tick_ev, op->done_ev[0], op->done_ev[1]})
+    if (e) cudaEventDestroy(e);
+  if (op->side) cudaStreamDestroy(op->side);
   if (op->ev) cudaEventDestroy(op->ev);
   if (op->stream) cudaStreamDestroy(op->stream);
   delete op;
@@ -1524,8 +1533,47 @@ int sparsl_op_pack_resident_spikes(sparsl_op* op) {
   return wait_op(op, "pack_resident_spikes_to_x_spikes");
 }
 
+// Uniform rows: each tick is the streaming kernel on the operator's stream,
+// then the compaction of its packed spikes on the side stream, overlapping
+// the next tick.  Tick t + 1 overwrites the buffer tick t - 1 wrote, so it
+// first waits for the compaction that read it.
+static int enqueue_recurrent_ell(sparsl_op* op, float decay, float v_reset, float dtheta, uint64_t steps) {
+  const char* name = "fused_spmv_spikes_lif_recurrent_steps";
+  if (!op->side) {
+    CK(name, cudaStreamCreateWithFlags(&op->side, cudaStreamNonBlocking));
+    CK(name, cudaEventCreateWithFlags(&op->tick_ev, cudaEventDisableTiming));
+    CK(name, cudaEventCreateWithFlags(&op->done_ev[0], cudaEventDisableTiming));
+    CK(name, cudaEventCreateWithFlags(&op->done_ev[1], cudaEventDisableTiming));
+    CK(name, cudaEventRecord(op->done_ev[0], op->side));
+    CK(name, cudaEventRecord(op->done_ev[1], op->side));
+  }
+  for (uint64_t t = 0; t < steps; ++t) {
+    const int out = op->cur ^ 1;
+    RowLaunch p = fwd_launch(op);
+    set_bits_mode(p, op->rxs[op->cur].as<uint32_t>(), op->words());
+    lif_resident_launch(op, p, decay, v_reset, dtheta);
+    p.out_bits = op->rxs[out].as<uint32_t>();
+    p.tile_flags = op->tile_flags.as<unsigned long long>();
+    p.tile_ticket = op->ticket.as<uint32_t>();
+    CK(name, cudaStreamWaitEvent(op->stream, op->done_ev[out], 0));
+    CK(name, launch_ell(op->ell, p, op->stream));
+    CK(name, cudaEventRecord(op->tick_ev, op->stream));
+    CK(name, cudaStreamWaitEvent(op->side, op->tick_ev, 0));
+    CK(name, launch_compact_bits(p.out_bits, op->words(), op->idx_list.as<uint32_t>(), op->trace.as<uint32_t>() + t,
+                                 0, op->side));
+    CK(name, cudaEventRecord(op->done_ev[out], op->side));
+    op->cur = out;
+  }
+  // Everything after this call (waits, reads of the list and the trace)
+  // follows the last compaction.
+  CK(name, cudaStreamWaitEvent(op->stream, op->done_ev[op->cur], 0));
+  op->last_steps = steps;
+  return SPARSL_OK;
+}
+
 static int enqueue_recurrent(sparsl_op* op, float decay, float v_reset, float dtheta, uint64_t steps) {
   TRY(ensure_trace(op, steps));
+  if (op->ell.ok) return enqueue_recurrent_ell(op, decay, v_reset, dtheta, steps);
   for (uint64_t t = 0; t < steps; ++t) {
     RowLaunch p = fwd_launch(op);
     set_bits_mode(p, op->rxs[op->cur].as<uint32_t>(), op->words());
