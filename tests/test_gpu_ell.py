@@ -206,3 +206,25 @@ def test_recurrent_index_list_over_several_compaction_rounds(O, cuda_device):
     idx = op.spike_indices()
     assert np.array_equal(idx, np.flatnonzero(sw).astype(np.uint32))
     assert sum(trace) > 1000 and (idx.size == 0 or idx[-1] < n)
+
+
+@pytest.mark.parametrize("precision", [S.WeightPrecision.F32, S.WeightPrecision.F16, S.WeightPrecision.Bf16])
+def test_uniform_rows_dense_fused_lif_bit_exact(O, cuda_device, precision):
+    """The dense-x fused LIF (fused_spmv_lif, mod.rs:1609-1636) on the TMA path:
+    one CTA per SM with x cached in L1, the LIF epilogue on every row."""
+    nrows, ncols, L = 20_003, 60_000, 64
+    csr, w = _uniform(O, nrows, ncols, L, 2024)
+    wq = O.quantise(int(precision), w)
+    op = _prepare(cuda_device, csr, w, precision, generic=False)
+    assert op.layouts() & 1
+    r = np.random.default_rng(9)
+    x = r.uniform(-1, 1, ncols).astype(np.float32)
+    v0 = r.uniform(-1, 1, nrows).astype(np.float32)
+    t0 = np.abs(r.uniform(-1, 1, nrows)).astype(np.float32)
+    v, t, sp = v0.copy(), t0.copy(), np.zeros(nrows, np.bool_)
+    op.fused_spmv_lif(x, v, t, sp, S.LifParams.new(0.9, 0.0, 0.1))
+    vw, tw, sw = v0.copy(), t0.copy(), np.zeros(nrows, np.uint8)
+    O.fused_lif(csr, wq, x, vw, tw, sw, 0.9, 0.0, 0.1, par=True)
+    assert_bits_equal(v, vw, "v")
+    assert_bits_equal(t, tw, "theta")
+    assert np.array_equal(sp.astype(np.uint8), sw) and 0 < sw.sum() < nrows
