@@ -6,18 +6,20 @@ namespace sparsl {
 namespace {
 
 // Y += A X for batch-minor X[ncols][n_vec] / Y[nrows][n_vec].  One warp owns
-// one row at a time; lane l folds vectors l and l + 32 of each 64-vector
-// block, so every (row, vector) output is its own left fold in edge order, as
-// row_dot_batched computes it (src/backend/mod.rs:2331-2360).  Each step reads
-// one X row slice with a coalesced 128-byte access per 32 vectors; kSpmmDepth
-// steps' gathers are issued before their dependent adds.  Warps are
-// persistent and take work units from a counter, long rows first.
+// one row at a time and folds a 64-vector block per sweep of the row: lane l
+// folds vectors 2l and 2l + 1 with one 8-byte load (V2: n_vec even, X 8-byte
+// aligned), else vectors l and l + 32.  Every (row, vector) output is its own
+// left fold in edge order, as row_dot_batched computes it
+// (src/backend/mod.rs:2331-2360).  Each step reads one X row slice with a
+// coalesced 256-byte access per 64 vectors; kSpmmDepth steps' gathers are
+// issued before their dependent adds.  Warps are persistent and take work
+// units from a counter, long rows first.
 #ifndef SPARSL_SPMM_DEPTH
 #define SPARSL_SPMM_DEPTH 4
 #endif
 constexpr int kSpmmDepth = SPARSL_SPMM_DEPTH;  // gathers in flight per lane and vector
 
-template <int WK>
+template <int WK, bool V2>
 __global__ void __launch_bounds__(256) spmm_kernel(const SpmmLaunch p) {
   const int lane = threadIdx.x & 31;
   const uint32_t nwarps = (gridDim.x * blockDim.x) >> 5;
@@ -40,8 +42,8 @@ __global__ void __launch_bounds__(256) spmm_kernel(const SpmmLaunch p) {
       const uint32_t r = p.order ? __ldg(p.order + pos) : pos;
       const uint32_t s = __ldg(p.ptr + r), e = __ldg(p.ptr + r + 1);
       for (uint32_t vb = 0; vb < nv; vb += 64) {
-        const uint32_t v0 = vb + lane, v1 = vb + 32 + lane;
-        const bool ok0 = v0 < nv, ok1 = v1 < nv;
+        const uint32_t v0 = V2 ? vb + 2 * lane : vb + lane, v1 = V2 ? v0 + 1 : vb + 32 + lane;
+        const bool ok0 = v0 < nv, ok1 = V2 ? ok0 : v1 < nv;
         float a0 = 0.0f, a1 = 0.0f;
         for (uint32_t e0 = s; e0 < e; e0 += 32) {
           const uint32_t ee = e0 + lane;
@@ -60,8 +62,14 @@ __global__ void __launch_bounds__(256) spmm_kernel(const SpmmLaunch p) {
               const uint32_t cj = __shfl_sync(0xffffffffu, c, j + k);
               wj[k] = __shfl_sync(0xffffffffu, wv, j + k);
               const float* xr = x + (uint64_t)cj * nv;
-              xa[k] = ok0 ? __ldg(xr + v0) : 0.0f;
-              xb[k] = ok1 ? __ldg(xr + v1) : 0.0f;
+              if (V2) {
+                const float2 t = ok0 ? __ldg(reinterpret_cast<const float2*>(xr + v0)) : make_float2(0.f, 0.f);
+                xa[k] = t.x;
+                xb[k] = t.y;
+              } else {
+                xa[k] = ok0 ? __ldg(xr + v0) : 0.0f;
+                xb[k] = ok1 ? __ldg(xr + v1) : 0.0f;
+              }
             }
 #pragma unroll
             for (int k = 0; k < kSpmmDepth; ++k) {
@@ -73,8 +81,16 @@ __global__ void __launch_bounds__(256) spmm_kernel(const SpmmLaunch p) {
             const uint32_t cj = __shfl_sync(0xffffffffu, c, j);
             const float wj = __shfl_sync(0xffffffffu, wv, j);
             const float* xr = x + (uint64_t)cj * nv;
-            if (ok0) a0 = fadd(a0, fmul(wj, __ldg(xr + v0)));
-            if (ok1) a1 = fadd(a1, fmul(wj, __ldg(xr + v1)));
+            if (V2) {
+              if (ok0) {
+                const float2 t = __ldg(reinterpret_cast<const float2*>(xr + v0));
+                a0 = fadd(a0, fmul(wj, t.x));
+                a1 = fadd(a1, fmul(wj, t.y));
+              }
+            } else {
+              if (ok0) a0 = fadd(a0, fmul(wj, __ldg(xr + v0)));
+              if (ok1) a1 = fadd(a1, fmul(wj, __ldg(xr + v1)));
+            }
           }
         }
         // An empty row still adds its 0.0 fold: -0.0 + 0.0 is +0.0.
@@ -234,26 +250,32 @@ inline unsigned grid_for(uint64_t n, unsigned block, unsigned cap = 148 * 16) {
 
 }  // namespace
 
-cudaError_t launch_spmm(const SpmmLaunch& p, int sm_count, cudaStream_t s) {
-  if (p.nrows == 0 || p.nunits == 0) return cudaSuccess;
+template <bool V2>
+static cudaError_t launch_spmm_t(const SpmmLaunch& p, int sm_count, cudaStream_t s) {
   const unsigned block = 256;
   int per_sm = 0;
   cudaError_t e;
   switch (p.wkind) {
-    case W_F16: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, spmm_kernel<W_F16>, block, 0); break;
-    case W_BF16: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, spmm_kernel<W_BF16>, block, 0); break;
-    default: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, spmm_kernel<W_F32>, block, 0); break;
+    case W_F16: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, spmm_kernel<W_F16, V2>, block, 0); break;
+    case W_BF16: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, spmm_kernel<W_BF16, V2>, block, 0); break;
+    default: e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, spmm_kernel<W_F32, V2>, block, 0); break;
   }
   if (e != cudaSuccess) return e;
   const uint64_t want = ((uint64_t)p.nunits * 32 + block - 1) / block;
   const uint64_t cap = (uint64_t)sm_count * (per_sm > 0 ? per_sm : 1);
   const unsigned blocks = (unsigned)(want < cap ? want : cap);
   switch (p.wkind) {
-    case W_F16: spmm_kernel<W_F16><<<blocks, block, 0, s>>>(p); break;
-    case W_BF16: spmm_kernel<W_BF16><<<blocks, block, 0, s>>>(p); break;
-    default: spmm_kernel<W_F32><<<blocks, block, 0, s>>>(p); break;
+    case W_F16: spmm_kernel<W_F16, V2><<<blocks, block, 0, s>>>(p); break;
+    case W_BF16: spmm_kernel<W_BF16, V2><<<blocks, block, 0, s>>>(p); break;
+    default: spmm_kernel<W_F32, V2><<<blocks, block, 0, s>>>(p); break;
   }
   return cudaGetLastError();
+}
+
+cudaError_t launch_spmm(const SpmmLaunch& p, int sm_count, cudaStream_t s) {
+  if (p.nrows == 0 || p.nunits == 0) return cudaSuccess;
+  const bool v2 = (p.n_vec % 2 == 0) && ((uintptr_t)p.x % 8 == 0);
+  return v2 ? launch_spmm_t<true>(p, sm_count, s) : launch_spmm_t<false>(p, sm_count, s);
 }
 
 cudaError_t launch_gather_weights(const void* w, const uint32_t* idx, uint64_t n, int wbytes, void* out,
