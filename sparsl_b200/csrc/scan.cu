@@ -227,10 +227,16 @@ __global__ void __launch_bounds__(kScanBlock, 5) scan_main(const float2* __restr
         if (lane >= d) h = comb(o, h);
       }
       const Aff htot{__shfl_sync(0xffffffffu, h.a, 31), __shfl_sync(0xffffffffu, h.b, 31)};
-      // lane 0: the prefix through halo row 15; lanes 1-7: through row t + 23
-      const float hb = __shfl_sync(0xffffffffu, h.b, lane == 0 ? 15 : (lane + 23) & 31);
-      const Aff exw{__shfl_sync(0xffffffffu, ex.a, (lane + 24) & 31), __shfl_sync(0xffffffffu, ex.b, (lane + 24) & 31)};
-      w0_guess = lane < 8 ? hb : comb(htot, exw).b;  // exw is lane t - 8's in-tile prefix
+      // Lane t's warm-up starts at row t + 32 - W (W = kScanWarmSub); lane 0
+      // starts at halo row 16.  Lanes 1 .. W-1 start in the halo: the prefix
+      // through halo row t + 31 - W.  The others start in the tile: the halo
+      // total, then lane t - W's in-tile exclusive prefix.
+      constexpr int W = kScanWarmSub;
+      static_assert(W >= 1 && W < 32, "warp 0 warm-up guesses");
+      const float hb = __shfl_sync(0xffffffffu, h.b, lane == 0 ? 15 : (lane + 31 - W) & 31);
+      const Aff exw{__shfl_sync(0xffffffffu, ex.a, (lane + 32 - W) & 31),
+                    __shfl_sync(0xffffffffu, ex.b, (lane + 32 - W) & 31)};
+      w0_guess = lane < W ? hb : comb(htot, exw).b;
     }
   }
   // Warp 0's warm-up needs nothing from the block scan: it only signals the
