@@ -7,11 +7,11 @@ namespace {
 
 // Y += A X for batch-minor X[ncols][n_vec] / Y[nrows][n_vec].  One warp owns
 // one row at a time and folds a 64-vector block per sweep of the row: lane l
-// folds vectors 2l and 2l + 1 with one 8-byte load (V2: n_vec even, X 8-byte
+// folds vectors 2l and 2l + 1 with one 8-byte load (V2: n_vec even, X and Y 8-byte
 // aligned), else vectors l and l + 32.  Every (row, vector) output is its own
 // left fold in edge order, as row_dot_batched computes it
 // (src/backend/mod.rs:2331-2360).  Each step reads one X row slice with a
-// coalesced 256-byte access per 64 vectors; kSpmmDepth steps' gathers are
+// coalesced 256-byte access per 64 vectors (Y rows alike); kSpmmDepth steps' gathers are
 // issued before their dependent adds.  Warps are persistent and take work
 // units from a counter, long rows first.
 #ifndef SPARSL_SPMM_DEPTH
@@ -38,65 +38,92 @@ __global__ void __launch_bounds__(256) spmm_kernel(const SpmmLaunch p) {
       pb = u * p.rows_per_unit;
       pe = min(p.nrows, pb + p.rows_per_unit);
     }
-    for (uint32_t pos = pb; pos < pe; ++pos) {
-      const uint32_t r = p.order ? __ldg(p.order + pos) : pos;
-      const uint32_t s = __ldg(p.ptr + r), e = __ldg(p.ptr + r + 1);
-      for (uint32_t vb = 0; vb < nv; vb += 64) {
-        const uint32_t v0 = V2 ? vb + 2 * lane : vb + lane, v1 = V2 ? v0 + 1 : vb + 32 + lane;
-        const bool ok0 = v0 < nv, ok1 = V2 ? ok0 : v1 < nv;
-        float a0 = 0.0f, a1 = 0.0f;
-        for (uint32_t e0 = s; e0 < e; e0 += 32) {
-          const uint32_t ee = e0 + lane;
-          uint32_t c = 0;
-          float wv = 0.0f;
-          if (ee < e) {
-            c = __ldg(p.idx + ee);
-            wv = load_weight<WK>(p.w, ee);
+    for (uint32_t cb = pb; cb < pe; cb += 32) {
+      // Lane l fetches the index and extent of the unit's row cb + l, so a
+      // run of short rows does not wait on two dependent loads per row.
+      uint32_t lr = 0, ls = 0, le = 0;
+      if (cb + lane < pe) {
+        lr = p.order ? __ldg(p.order + cb + lane) : cb + lane;
+        ls = __ldg(p.ptr + lr);
+        le = __ldg(p.ptr + lr + 1);
+      }
+      const uint32_t cn = min(32u, pe - cb);
+      for (uint32_t q = 0; q < cn; ++q) {
+        const uint32_t r = __shfl_sync(0xffffffffu, lr, q);
+        const uint32_t s = __shfl_sync(0xffffffffu, ls, q), e = __shfl_sync(0xffffffffu, le, q);
+        float* yr = p.y + (uint64_t)r * nv;
+        for (uint32_t vb = 0; vb < nv; vb += 64) {
+          const uint32_t v0 = V2 ? vb + 2 * lane : vb + lane, v1 = V2 ? v0 + 1 : vb + 32 + lane;
+          const bool ok0 = v0 < nv, ok1 = V2 ? ok0 : v1 < nv;
+          // Y is read before the fold, so its latency overlaps the gathers.
+          float y0 = 0.0f, y1 = 0.0f;
+          if (V2) {
+            if (ok0) {
+              const float2 t = *reinterpret_cast<const float2*>(yr + v0);
+              y0 = t.x;
+              y1 = t.y;
+            }
+          } else {
+            if (ok0) y0 = yr[v0];
+            if (ok1) y1 = yr[v1];
           }
-          const uint32_t cnt = min(32u, e - e0);
-          uint32_t j = 0;
-          for (; j + kSpmmDepth <= cnt; j += kSpmmDepth) {
-            float xa[kSpmmDepth], xb[kSpmmDepth], wj[kSpmmDepth];
+          float a0 = 0.0f, a1 = 0.0f;
+          for (uint32_t e0 = s; e0 < e; e0 += 32) {
+            const uint32_t ee = e0 + lane;
+            uint32_t c = 0;
+            float wv = 0.0f;
+            if (ee < e) {
+              c = __ldg(p.idx + ee);
+              wv = load_weight<WK>(p.w, ee);
+            }
+            const uint32_t cnt = min(32u, e - e0);
+            uint32_t j = 0;
+            for (; j + kSpmmDepth <= cnt; j += kSpmmDepth) {
+              float xa[kSpmmDepth], xb[kSpmmDepth], wj[kSpmmDepth];
 #pragma unroll
-            for (int k = 0; k < kSpmmDepth; ++k) {
-              const uint32_t cj = __shfl_sync(0xffffffffu, c, j + k);
-              wj[k] = __shfl_sync(0xffffffffu, wv, j + k);
+              for (int k = 0; k < kSpmmDepth; ++k) {
+                const uint32_t cj = __shfl_sync(0xffffffffu, c, j + k);
+                wj[k] = __shfl_sync(0xffffffffu, wv, j + k);
+                const float* xr = x + (uint64_t)cj * nv;
+                if (V2) {
+                  const float2 t = ok0 ? __ldg(reinterpret_cast<const float2*>(xr + v0)) : make_float2(0.f, 0.f);
+                  xa[k] = t.x;
+                  xb[k] = t.y;
+                } else {
+                  xa[k] = ok0 ? __ldg(xr + v0) : 0.0f;
+                  xb[k] = ok1 ? __ldg(xr + v1) : 0.0f;
+                }
+              }
+#pragma unroll
+              for (int k = 0; k < kSpmmDepth; ++k) {
+                a0 = fadd(a0, fmul(wj[k], xa[k]));
+                a1 = fadd(a1, fmul(wj[k], xb[k]));
+              }
+            }
+            for (; j < cnt; ++j) {
+              const uint32_t cj = __shfl_sync(0xffffffffu, c, j);
+              const float wj = __shfl_sync(0xffffffffu, wv, j);
               const float* xr = x + (uint64_t)cj * nv;
               if (V2) {
-                const float2 t = ok0 ? __ldg(reinterpret_cast<const float2*>(xr + v0)) : make_float2(0.f, 0.f);
-                xa[k] = t.x;
-                xb[k] = t.y;
+                if (ok0) {
+                  const float2 t = __ldg(reinterpret_cast<const float2*>(xr + v0));
+                  a0 = fadd(a0, fmul(wj, t.x));
+                  a1 = fadd(a1, fmul(wj, t.y));
+                }
               } else {
-                xa[k] = ok0 ? __ldg(xr + v0) : 0.0f;
-                xb[k] = ok1 ? __ldg(xr + v1) : 0.0f;
+                if (ok0) a0 = fadd(a0, fmul(wj, __ldg(xr + v0)));
+                if (ok1) a1 = fadd(a1, fmul(wj, __ldg(xr + v1)));
               }
-            }
-#pragma unroll
-            for (int k = 0; k < kSpmmDepth; ++k) {
-              a0 = fadd(a0, fmul(wj[k], xa[k]));
-              a1 = fadd(a1, fmul(wj[k], xb[k]));
             }
           }
-          for (; j < cnt; ++j) {
-            const uint32_t cj = __shfl_sync(0xffffffffu, c, j);
-            const float wj = __shfl_sync(0xffffffffu, wv, j);
-            const float* xr = x + (uint64_t)cj * nv;
-            if (V2) {
-              if (ok0) {
-                const float2 t = __ldg(reinterpret_cast<const float2*>(xr + v0));
-                a0 = fadd(a0, fmul(wj, t.x));
-                a1 = fadd(a1, fmul(wj, t.y));
-              }
-            } else {
-              if (ok0) a0 = fadd(a0, fmul(wj, __ldg(xr + v0)));
-              if (ok1) a1 = fadd(a1, fmul(wj, __ldg(xr + v1)));
-            }
+          // An empty row still adds its 0.0 fold: -0.0 + 0.0 is +0.0.
+          if (V2) {
+            if (ok0) *reinterpret_cast<float2*>(yr + v0) = make_float2(fadd(y0, a0), fadd(y1, a1));
+          } else {
+            if (ok0) yr[v0] = fadd(y0, a0);
+            if (ok1) yr[v1] = fadd(y1, a1);
           }
         }
-        // An empty row still adds its 0.0 fold: -0.0 + 0.0 is +0.0.
-        float* yr = p.y + (uint64_t)r * nv;
-        if (ok0) yr[v0] = fadd(yr[v0], a0);
-        if (ok1) yr[v1] = fadd(yr[v1], a1);
       }
     }
   }
@@ -274,7 +301,7 @@ static cudaError_t launch_spmm_t(const SpmmLaunch& p, int sm_count, cudaStream_t
 
 cudaError_t launch_spmm(const SpmmLaunch& p, int sm_count, cudaStream_t s) {
   if (p.nrows == 0 || p.nunits == 0) return cudaSuccess;
-  const bool v2 = (p.n_vec % 2 == 0) && ((uintptr_t)p.x % 8 == 0);
+  const bool v2 = (p.n_vec % 2 == 0) && ((uintptr_t)p.x % 8 == 0) && ((uintptr_t)p.y % 8 == 0);
   return v2 ? launch_spmm_t<true>(p, sm_count, s) : launch_spmm_t<false>(p, sm_count, s);
 }
 
