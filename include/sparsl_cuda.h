@@ -105,7 +105,10 @@ int sparsl_device_name(sparsl_dev *dev, char *buf, size_t cap);
 int sparsl_device_reset(void);
 int sparsl_quarantined(void);
 /* Device::assoc_scan (mod.rs:1183-1197): in/out are n (a, b) pairs.
- * Bit-identical to assoc_scan_sequential (scan.rs:298-313). */
+ * Bit-identical to assoc_scan_sequential (scan.rs:298-313).  From 2^23 maps
+ * the copies run in 2^22-map chunks on two copy streams of the device,
+ * overlapping each other and the scan (page-locked host memory lets them
+ * run concurrently); the call returns when all of `out` is written. */
 int sparsl_dev_assoc_scan(sparsl_dev *dev, const float *in, uint64_t n, float *out);
 /* Device::lif_integrate (mod.rs:1202-1229). */
 int sparsl_dev_lif_integrate(sparsl_dev *dev, float *v, float *theta, const float *currents,

@@ -270,6 +270,9 @@ struct sparsl_dev {
   DBuf lv, lth, lcur, lspk;
   DBuf vscratch;  // device CSR validation results, scan walk state
   DBuf tscratch;  // scan transfer tables
+  // Copy streams of the chunked host-buffer scan (created on first use).
+  cudaStream_t up = nullptr, down = nullptr;
+  cudaEvent_t up_ev = nullptr, scan_ev = nullptr, down_ev = nullptr;
 };
 
 namespace {
@@ -540,6 +543,13 @@ void sparsl_device_close(sparsl_dev* d) {
   dfree(d->vscratch);
   dfree(d->tscratch);
   d->err.release();
+  for (cudaStream_t st : {d->up, d->down})
+    if (st) {
+      cudaStreamSynchronize(st);
+      cudaStreamDestroy(st);
+    }
+  for (cudaEvent_t e : {d->up_ev, d->scan_ev, d->down_ev})
+    if (e) cudaEventDestroy(e);
   cudaEventDestroy(d->ev);
   cudaStreamDestroy(d->stream);
   delete d;
@@ -595,9 +605,39 @@ int sparsl_dev_assoc_scan(sparsl_dev* d, const float* in, uint64_t n, float* out
       ensure(d->scan_out, bytes, true, d->stream) != cudaSuccess)
     return fail(SPARSL_ERR_ALLOCATION, "scan buffers", "device allocation failed for scan buffers");
   TRY(dev_scan_prepare(d, n));
-  CK("assoc_scan", cudaMemcpyAsync(d->scan_in.p, in, bytes, cudaMemcpyHostToDevice, d->stream));
-  CK("assoc_scan", launch_scan(d->scan_in.as<float>(), d->scan_out.as<float>(), n, d->sc, d->err.d, d->stream));
-  CK("assoc_scan", cudaMemcpyAsync(out, d->scan_out.p, bytes, cudaMemcpyDeviceToHost, d->stream));
+  if (n < 2 * kScanPipeChunk) {
+    CK("assoc_scan", cudaMemcpyAsync(d->scan_in.p, in, bytes, cudaMemcpyHostToDevice, d->stream));
+    CK("assoc_scan", launch_scan(d->scan_in.as<float>(), d->scan_out.as<float>(), n, d->sc, d->err.d, d->stream));
+    CK("assoc_scan", cudaMemcpyAsync(out, d->scan_out.p, bytes, cudaMemcpyDeviceToHost, d->stream));
+  } else {
+    // Chunked: chunk k's upload, chunk k-1's scan and chunk k-2's download
+    // overlap (copy engines in both directions, the SMs).  Chunk k continues
+    // from the last state chunk k-1 wrote (device memory, same stream), so
+    // the result is the same single left fold.
+    if (!d->up) {
+      CK("assoc_scan", cudaStreamCreateWithFlags(&d->up, cudaStreamNonBlocking));
+      CK("assoc_scan", cudaStreamCreateWithFlags(&d->down, cudaStreamNonBlocking));
+      for (cudaEvent_t* e : {&d->up_ev, &d->scan_ev, &d->down_ev})
+        CK("assoc_scan", cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+    }
+    CK("assoc_scan", cudaEventRecord(d->scan_ev, d->stream));  // after the scratch reset
+    CK("assoc_scan", cudaStreamWaitEvent(d->up, d->scan_ev, 0));
+    float* din = d->scan_in.as<float>();
+    float* dout = d->scan_out.as<float>();
+    for (uint64_t s0 = 0; s0 < n; s0 += kScanPipeChunk) {
+      const uint64_t m = std::min<uint64_t>(kScanPipeChunk, n - s0);
+      CK("assoc_scan", cudaMemcpyAsync(din + 2 * s0, in + 2 * s0, m * 8, cudaMemcpyHostToDevice, d->up));
+      CK("assoc_scan", cudaEventRecord(d->up_ev, d->up));
+      CK("assoc_scan", cudaStreamWaitEvent(d->stream, d->up_ev, 0));
+      CK("assoc_scan", launch_scan(din + 2 * s0, dout + 2 * s0, m, d->sc, d->err.d, d->stream, nullptr,
+                                   s0 ? dout + 2 * (s0 - 1) : nullptr));
+      CK("assoc_scan", cudaEventRecord(d->scan_ev, d->stream));
+      CK("assoc_scan", cudaStreamWaitEvent(d->down, d->scan_ev, 0));
+      CK("assoc_scan", cudaMemcpyAsync(out + 2 * s0, dout + 2 * s0, m * 8, cudaMemcpyDeviceToHost, d->down));
+    }
+    CK("assoc_scan", cudaEventRecord(d->down_ev, d->down));
+    CK("assoc_scan", cudaStreamWaitEvent(d->stream, d->down_ev, 0));
+  }
   CanarySet set;
   set.ptr[set.count++] = d->scan_out.canary();
   CK("assoc_scan", launch_canary_check(set, d->err.d, d->stream));

@@ -13,6 +13,8 @@ constexpr int kScanTile = kScanThreads * kScanK;
 constexpr int kScanWarmSub = 8;    // warm-up of an in-tile guess, in sub-chunks
 constexpr int kScanHaloSub = 32;   // warm-up of a tile's first warp, reaching into the previous tile
 constexpr int kScanHalo = kScanHaloSub * kScanK;
+// Maps per chunk of the pipelined host-buffer scan (32 MiB each way).
+constexpr uint64_t kScanPipeChunk = 1ull << 22;
 
 // Scratch the scan needs, sized by scan_scratch_bytes(n).  All of it is
 // left in its zero state (or self-resetting) after each call.

@@ -6,6 +6,7 @@ stronger rule the oracle makes checkable: identical bits (NaN payloads aside).
 """
 import numpy as np
 import pytest
+import torch
 
 from conftest import SHAPES, assert_bits_equal
 
@@ -243,6 +244,28 @@ def test_scan_bit_exact_decay_workload(O, cuda_device, n):
     assert_bits_equal(got, O.scan_sequential(xs))
     rep, seg = cuda_device.scan_stats()
     assert rep < n // 4, f"scan replayed {rep} of {n} elements serially"
+
+
+@pytest.mark.parametrize("n", [2 << 22, 3 << 22 | 4097])
+def test_scan_host_buffers_chunked_pipeline(O, cuda_device, n):
+    """Host buffers of at least two 2^22-map chunks are uploaded, scanned and
+    downloaded chunk by chunk, each chunk continuing from the last state the
+    previous one wrote: the result is still the one sequential fold, equal to
+    the single-pass device entry point, and only the very first map is copied
+    (a first map of (inf, -0.0) survives bit for bit)."""
+    r = np.random.default_rng(n)
+    xs = np.stack([r.uniform(0.9, 1.0, n), r.standard_normal(n)], 1).astype(np.float32)
+    xs[0] = (np.inf, -0.0)
+    xs[(1 << 22) - 1] = (1.0, 0.0)  # identity on a chunk's last map
+    xs[1 << 22] = (0.5, 7.0)  # and a plain map on the next chunk's first
+    got = cuda_device.assoc_scan(xs)
+    assert_bits_equal(got, O.scan_sequential(xs), f"n={n}")
+    d_in = torch.from_numpy(xs).cuda()
+    d_out = torch.empty_like(d_in)
+    cuda_device.assoc_scan_from_device(d_in, n, d_out)
+    cuda_device.wait()
+    assert_bits_equal(got, d_out.cpu().numpy(), "chunked host path vs one device pass")
+    assert_bits_equal(cuda_device.assoc_scan(xs), got, "repeat is byte-identical")
 
 
 def test_scan_known_answers(O, cuda_device):
