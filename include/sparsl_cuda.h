@@ -182,7 +182,9 @@ int sparsl_op_spmv_spikes(sparsl_op *op, const uint32_t *spikes, uint64_t words,
                           uint64_t y_len);
 /* SparseOp::spmv_t (mod.rs:1486-1505): y += A^T x. */
 int sparsl_op_spmv_t(sparsl_op *op, const float *x, uint64_t x_len, float *y, uint64_t y_len);
-/* SparseOp::spmm (mod.rs:1528-1571): batch-minor X[ncols][n_vec], Y[nrows][n_vec]. */
+/* SparseOp::spmm (mod.rs:1528-1571): batch-minor X[ncols][n_vec], Y[nrows][n_vec].
+ * For operators of 65,536 rows or more, Y moves in eight row ranges on two
+ * copy streams, each range folded as soon as its rows are in. */
 int sparsl_op_spmm(sparsl_op *op, const float *x, uint64_t x_len, uint64_t n_vec, float *y,
                    uint64_t y_len);
 /* SparseOp::fused_spmv_lif (mod.rs:1609-1636). */

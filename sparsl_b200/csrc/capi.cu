@@ -332,6 +332,15 @@ struct sparsl_op {
   // SpMM work units (rows by descending length unless all rows are equal)
   DBuf spmm_order, spmm_units, spmm_ctr;
   uint32_t spmm_nunits = 0, spmm_rows_per_unit = 1;
+  // Row ranges of the host-buffer SpMM pipeline (empty: one launch): range k
+  // is rows [range_row[k], range_row[k+1]) and units [range_unit[k],
+  // range_unit[k+1]) of spmm_runits / spmm_rorder (of the plain units when
+  // rows are equal).  Copy streams and events are created on first use.
+  DBuf spmm_rorder, spmm_runits;
+  std::vector<uint32_t> spmm_range_unit;
+  std::vector<uint64_t> spmm_range_row;
+  cudaStream_t up = nullptr, down = nullptr;
+  cudaEvent_t up_ev = nullptr, fold_ev = nullptr, down_ev = nullptr;
   uint64_t trace_cap = 0, last_steps = 0;
   // staging for host-slice calls (kept apart from resident state, as the
   // reference CPU arm's slice API never touches its resident scratch)
@@ -1162,46 +1171,81 @@ int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int 
   }
   // SpMM work units.  Equal rows: fixed runs of rows.  Otherwise rows by
   // descending length (ties by index), cut into units of >= kSpmmUnitNnz
-  // entries or a single row, at most kSpmmUnitRows rows each.
-  std::vector<uint32_t> sp_order, sp_units;
+  // entries or a single row, at most kSpmmUnitRows rows each.  Operators of
+  // kSpmmRangeMinRows rows or more also get units per range of consecutive
+  // rows (the host-buffer pipeline launches one range at a time); for equal
+  // rows those are runs of the same units.
+  std::vector<uint32_t> sp_order, sp_units, rg_order, rg_units;
   PALLOC(op->spmm_ctr, 16, false, "spmm counters");
   cudaMemsetAsync(op->spmm_ctr.p, 0, op->spmm_ctr.bytes, op->stream);
   if (nrows) {
     const uint32_t maxlen = (uint32_t)sh.max_row_nnz;
     uint32_t minlen = maxlen;
     for (uint64_t r = 0; r < nrows && minlen; ++r) minlen = std::min(minlen, row_ptr[r + 1] - row_ptr[r]);
+    const bool ranged = nrows >= kSpmmRangeMinRows;
     if (minlen == maxlen) {
       const uint32_t R = std::max(1u, std::min(kSpmmUnitRows, kSpmmUnitNnz / std::max(maxlen, 1u)));
       op->spmm_rows_per_unit = R;
       op->spmm_nunits = (uint32_t)((nrows + R - 1) / R);
-    } else {
-      sp_order.resize(nrows);
-      auto len = [&](uint64_t r) { return row_ptr[r + 1] - row_ptr[r]; };
-      if ((uint64_t)maxlen <= 4 * nrows + 4096) {
-        // Counting sort by length (descending, stable).
-        std::vector<uint32_t> start((size_t)maxlen + 2, 0);
-        for (uint64_t r = 0; r < nrows; ++r) ++start[maxlen - len(r) + 1];
-        for (size_t k = 1; k < start.size(); ++k) start[k] += start[k - 1];
-        for (uint64_t r = 0; r < nrows; ++r) sp_order[start[maxlen - len(r)]++] = (uint32_t)r;
-      } else {
-        for (uint64_t r = 0; r < nrows; ++r) sp_order[r] = (uint32_t)r;
-        std::stable_sort(sp_order.begin(), sp_order.end(), [&](uint32_t a, uint32_t b) { return len(a) > len(b); });
-      }
-      sp_units.push_back(0);
-      uint64_t acc = 0, rows_in = 0;
-      for (uint64_t i = 0; i < nrows; ++i) {
-        acc += row_ptr[sp_order[i] + 1] - row_ptr[sp_order[i]];
-        ++rows_in;
-        if (acc >= kSpmmUnitNnz || rows_in >= kSpmmUnitRows || i + 1 == nrows) {
-          sp_units.push_back((uint32_t)(i + 1));
-          acc = rows_in = 0;
+      if (ranged) {
+        const uint64_t per = ((op->spmm_nunits + kSpmmRanges - 1) / kSpmmRanges);
+        for (uint64_t k = 0; k <= kSpmmRanges; ++k) {
+          const uint64_t u = std::min<uint64_t>(k * per, op->spmm_nunits);
+          op->spmm_range_unit.push_back((uint32_t)u);
+          op->spmm_range_row.push_back(std::min<uint64_t>(u * R, nrows));
         }
       }
+    } else {
+      auto len = [&](uint64_t r) { return row_ptr[r + 1] - row_ptr[r]; };
+      // Rows [r0, r1) by descending length, appended to `order`, and their
+      // units appended to `units` (positions in `order`).
+      auto build = [&](uint64_t r0, uint64_t r1, std::vector<uint32_t>& order, std::vector<uint32_t>& units) {
+        const size_t base = order.size();
+        order.resize(base + (r1 - r0));
+        uint32_t* o = order.data() + base;
+        if ((uint64_t)maxlen <= 4 * (r1 - r0) + 4096) {
+          // Counting sort by length (descending, stable).
+          std::vector<uint32_t> start((size_t)maxlen + 2, 0);
+          for (uint64_t r = r0; r < r1; ++r) ++start[maxlen - len(r) + 1];
+          for (size_t k = 1; k < start.size(); ++k) start[k] += start[k - 1];
+          for (uint64_t r = r0; r < r1; ++r) o[start[maxlen - len(r)]++] = (uint32_t)r;
+        } else {
+          for (uint64_t r = r0; r < r1; ++r) o[r - r0] = (uint32_t)r;
+          std::stable_sort(o, o + (r1 - r0), [&](uint32_t a, uint32_t b) { return len(a) > len(b); });
+        }
+        if (units.empty()) units.push_back(0);
+        uint64_t acc = 0, rows_in = 0;
+        for (uint64_t i = base; i < order.size(); ++i) {
+          acc += len(order[i]);
+          ++rows_in;
+          if (acc >= kSpmmUnitNnz || rows_in >= kSpmmUnitRows || i + 1 == order.size()) {
+            units.push_back((uint32_t)(i + 1));
+            acc = rows_in = 0;
+          }
+        }
+      };
+      build(0, nrows, sp_order, sp_units);
       op->spmm_nunits = (uint32_t)(sp_units.size() - 1);
       PALLOC(op->spmm_order, nrows * 4, false, "spmm row order");
       PALLOC(op->spmm_units, sp_units.size() * 4, false, "spmm units");
       cudaMemcpyAsync(op->spmm_order.p, sp_order.data(), nrows * 4, cudaMemcpyHostToDevice, op->stream);
       cudaMemcpyAsync(op->spmm_units.p, sp_units.data(), sp_units.size() * 4, cudaMemcpyHostToDevice, op->stream);
+      if (ranged) {
+        const uint64_t per = (nrows + kSpmmRanges - 1) / kSpmmRanges;
+        op->spmm_range_unit.push_back(0);
+        op->spmm_range_row.push_back(0);
+        for (uint64_t k = 0; k < kSpmmRanges; ++k) {
+          const uint64_t r0 = std::min(k * per, nrows), r1 = std::min((k + 1) * per, nrows);
+          if (r1 > r0) build(r0, r1, rg_order, rg_units);
+          op->spmm_range_unit.push_back(rg_units.empty() ? 0 : (uint32_t)(rg_units.size() - 1));
+          op->spmm_range_row.push_back(r1);
+        }
+        PALLOC(op->spmm_rorder, nrows * 4, false, "spmm ranged row order");
+        PALLOC(op->spmm_runits, rg_units.size() * 4, false, "spmm ranged units");
+        cudaMemcpyAsync(op->spmm_rorder.p, rg_order.data(), nrows * 4, cudaMemcpyHostToDevice, op->stream);
+        cudaMemcpyAsync(op->spmm_runits.p, rg_units.data(), rg_units.size() * 4, cudaMemcpyHostToDevice,
+                        op->stream);
+      }
     }
   }
   rc = wait_op(op, "prepare");  // host vectors above must outlive the copies
@@ -1221,13 +1265,20 @@ void sparsl_op_destroy(sparsl_op* op) {
                   &op->rx,      &op->rxs[0],  &op->rxs[1],  &op->ry,      &op->rv,      &op->rth,
                   &op->rspk,    &op->idx_list, &op->tile_flags, &op->ticket, &op->trace, &op->sx,
                   &op->sbits,   &op->sy,      &op->sv,      &op->sth,     &op->sspk,
-                  &op->spmm_order, &op->spmm_units, &op->spmm_ctr};
+                  &op->spmm_order, &op->spmm_units, &op->spmm_ctr, &op->spmm_rorder, &op->spmm_runits};
   for (DBuf* b : bufs) dfree(*b);
   op->err.release();
   if (op->side) cudaStreamSynchronize(op->side);
   for (cudaEvent_t e : {op->tick_ev, op->done_ev[0], op->done_ev[1]})
     if (e) cudaEventDestroy(e);
   if (op->side) cudaStreamDestroy(op->side);
+  for (cudaStream_t st : {op->up, op->down})
+    if (st) {
+      cudaStreamSynchronize(st);
+      cudaStreamDestroy(st);
+    }
+  for (cudaEvent_t e : {op->up_ev, op->fold_ev, op->down_ev})
+    if (e) cudaEventDestroy(e);
   if (op->ev) cudaEventDestroy(op->ev);
   if (op->stream) cudaStreamDestroy(op->stream);
   delete op;
@@ -1407,11 +1458,47 @@ int sparsl_op_spmm(sparsl_op* op, const float* x, uint64_t x_len, uint64_t n_vec
   CK("spmm", cudaSetDevice(op->dev->ordinal));
   ALLOC(op->sx, need_x * 4 + 16, false, "X staging");
   ALLOC(op->sy, need_y * 4 + 16, true, "Y staging");
-  if (need_x) CK("spmm", cudaMemcpyAsync(op->sx.p, x, need_x * 4, cudaMemcpyHostToDevice, op->stream));
-  CK("spmm", cudaMemcpyAsync(op->sy.p, y, need_y * 4, cudaMemcpyHostToDevice, op->stream));
-  CK("spmm", launch_spmm(spmm_launch(op, op->sx.as<float>(), op->sy.as<float>(), (uint32_t)n_vec),
-                         op->dev->sm_count, op->stream));
-  CK("spmm", cudaMemcpyAsync(y, op->sy.p, need_y * 4, cudaMemcpyDeviceToHost, op->stream));
+  SpmmLaunch p = spmm_launch(op, op->sx.as<float>(), op->sy.as<float>(), (uint32_t)n_vec);
+  if (op->spmm_range_unit.empty()) {
+    if (need_x) CK("spmm", cudaMemcpyAsync(op->sx.p, x, need_x * 4, cudaMemcpyHostToDevice, op->stream));
+    CK("spmm", cudaMemcpyAsync(op->sy.p, y, need_y * 4, cudaMemcpyHostToDevice, op->stream));
+    CK("spmm", launch_spmm(p, op->dev->sm_count, op->stream));
+    CK("spmm", cudaMemcpyAsync(y, op->sy.p, need_y * 4, cudaMemcpyDeviceToHost, op->stream));
+    return finish(op, "spmm");
+  }
+  // Pipelined by row range: X, then each range's Y rows, go up on one copy
+  // stream; range k is folded once its rows are in, and its rows go down on
+  // another copy stream while later ranges go up.  Each range is one launch
+  // over its own units, so every output is still its own left fold.
+  if (!op->up) {
+    CK("spmm", cudaStreamCreateWithFlags(&op->up, cudaStreamNonBlocking));
+    CK("spmm", cudaStreamCreateWithFlags(&op->down, cudaStreamNonBlocking));
+    for (cudaEvent_t* e : {&op->up_ev, &op->fold_ev, &op->down_ev})
+      CK("spmm", cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+  }
+  if (op->spmm_rorder.p) {
+    p.order = op->spmm_rorder.as<uint32_t>();
+    p.unit_start = op->spmm_runits.as<uint32_t>();
+  }
+  CK("spmm", cudaEventRecord(op->fold_ev, op->stream));  // staging is free once earlier work is done
+  CK("spmm", cudaStreamWaitEvent(op->up, op->fold_ev, 0));
+  if (need_x) CK("spmm", cudaMemcpyAsync(op->sx.p, x, need_x * 4, cudaMemcpyHostToDevice, op->up));
+  for (size_t k = 0; k + 1 < op->spmm_range_unit.size(); ++k) {
+    const uint64_t r0 = op->spmm_range_row[k], r1 = op->spmm_range_row[k + 1];
+    if (r1 == r0) continue;
+    const uint64_t off = r0 * n_vec, cnt = (r1 - r0) * n_vec;
+    CK("spmm", cudaMemcpyAsync(op->sy.as<float>() + off, y + off, cnt * 4, cudaMemcpyHostToDevice, op->up));
+    CK("spmm", cudaEventRecord(op->up_ev, op->up));
+    CK("spmm", cudaStreamWaitEvent(op->stream, op->up_ev, 0));
+    p.unit_base = op->spmm_range_unit[k];
+    p.nunits = op->spmm_range_unit[k + 1] - op->spmm_range_unit[k];
+    CK("spmm", launch_spmm(p, op->dev->sm_count, op->stream));
+    CK("spmm", cudaEventRecord(op->fold_ev, op->stream));
+    CK("spmm", cudaStreamWaitEvent(op->down, op->fold_ev, 0));
+    CK("spmm", cudaMemcpyAsync(y + off, op->sy.as<float>() + off, cnt * 4, cudaMemcpyDeviceToHost, op->down));
+  }
+  CK("spmm", cudaEventRecord(op->down_ev, op->down));
+  CK("spmm", cudaStreamWaitEvent(op->stream, op->down_ev, 0));
   return finish(op, "spmm");
 }
 

@@ -30,6 +30,7 @@ __global__ void __launch_bounds__(256) spmm_kernel(const SpmmLaunch p) {
     if (lane == 0) u = atomicAdd(p.ctr, 1u);
     u = __shfl_sync(0xffffffffu, u, 0);
     if (u >= p.nunits) break;
+    u += p.unit_base;
     uint32_t pb, pe;
     if (p.order) {
       pb = __ldg(p.unit_start + u);

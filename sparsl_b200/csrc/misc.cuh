@@ -36,11 +36,17 @@ struct SpmmLaunch {
   const uint32_t* unit_start = nullptr;  // nunits + 1 entries when order is set
   uint32_t nunits = 0, rows_per_unit = 1;
   uint32_t* ctr = nullptr;
+  uint32_t unit_base = 0;  // the launch takes units [unit_base, unit_base + nunits)
 };
 
 // Work units over rows sorted by descending length: each unit holds at least
 // kSpmmUnitNnz entries or is a single row, and at most kSpmmUnitRows rows.
 constexpr uint32_t kSpmmUnitNnz = 512, kSpmmUnitRows = 256;
+// Row ranges of the host-buffer SpMM pipeline: operators of at least
+// kSpmmRangeMinRows rows also get work units per range of consecutive rows,
+// so range k's Y rows can be copied in, folded and copied out while the
+// next range's rows are copied in.
+constexpr uint32_t kSpmmRanges = 8, kSpmmRangeMinRows = 1u << 16;
 
 cudaError_t launch_spmm(const SpmmLaunch& p, int sm_count, cudaStream_t s);
 cudaError_t launch_lif_integrate(float* v, float* theta, const float* cur, uint8_t* spk, uint64_t n,

@@ -11,6 +11,7 @@ import torch
 from conftest import SHAPES, assert_bits_equal
 
 import sparsl_b200 as S
+from sparsl_b200 import _lib
 
 pytestmark = pytest.mark.gpu
 
@@ -484,3 +485,39 @@ def test_spmv_t_sliced_and_hub_layouts(O, cuda_device, hub):
         op.spmv_t(xt, got)
         want = O.spmv_t(csc, O.quantise(int(p), w), xt, yt0.copy())
         assert_bits_equal(got, want, f"spmv_t hub={hub} {p}")
+
+
+@pytest.mark.parametrize("kind", ["power_law", "uniform"])
+@pytest.mark.parametrize("n_vec", [3, 64])
+def test_spmm_row_range_pipeline_bit_exact(O, cuda_device, kind, n_vec):
+    """Operators of 65,536 rows or more run the host-buffer SpMM one row
+    range at a time, with each range's Y rows copied in and out around its own
+    launch.  The result is the oracle's bit for bit, and equals the device
+    entry point, which runs all rows in one launch."""
+    r = np.random.default_rng(n_vec * 7 + len(kind))
+    nrows, ncols = 70_001, 5000
+    if kind == "power_law":
+        lens = np.minimum(r.zipf(1.5, nrows), 1000)
+        lens[::97] = 0
+    else:
+        lens = np.full(nrows, 5)
+    rp = np.zeros(nrows + 1, np.uint64)
+    np.cumsum(lens, out=rp[1:])
+    col = np.concatenate([np.sort(r.choice(ncols, k, replace=False)) for k in lens]).astype(np.uint32)
+    csr = O.Csr(rp.astype(np.uint32), col, ncols)
+    w = r.uniform(-1, 1, col.size).astype(np.float32)
+    X = r.uniform(-1, 1, ncols * n_vec).astype(np.float32)
+    Y0 = r.uniform(-1, 1, nrows * n_vec).astype(np.float32)
+    Y0[::5] = -0.0
+    op = cuda_device.prepare(_scsr(csr), ncols, w)
+    want = O.spmm(csr, w, X, n_vec, Y0.copy())
+    got = Y0.copy()
+    op.spmm(X, n_vec, got)
+    assert_bits_equal(got, want, f"spmm ranges {kind} n_vec={n_vec}")
+    dx = torch.from_numpy(X).cuda()
+    dy = torch.from_numpy(Y0).cuda()
+    assert _lib.load().sparsl_op_spmm_device(op.handle, dx.data_ptr(), n_vec, dy.data_ptr(), None) == 0
+    torch.cuda.synchronize()
+    assert_bits_equal(dy.cpu().numpy(), want, "device entry point, one launch")
+    op.spmm(X, n_vec, got)  # again: the unit counters rewound after every range
+    assert_bits_equal(got, O.spmm(csr, w, X, n_vec, want.copy()), "second call")
