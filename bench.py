@@ -1036,7 +1036,7 @@ def bench_lif(args, dev, want_cpu):
         for _ in range(e2e_steps):
             check(L.sparsl_op_fused_spikes_lif(op.handle, hs.ptr, n // 32, hv.ptr, ht.ptr, ho.ptr, n, 0.95, 0.0, 0.0),
                   "e2e tick")
-            hs.a[:] = np.packbits(ho.a.reshape(-1, 32)[:, ::-1], axis=1).view(">u4").reshape(-1)
+            hs.a[:] = S.pack_spikes(ho.a)  # the host-side pack_spikes_into of the reference API
 
     e2e_ms = events_ms(st, torch.cuda.current_device(), e2e)
     for h in (hs, hv, ht, ho):

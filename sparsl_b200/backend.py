@@ -337,20 +337,23 @@ def packed_len(n: int) -> int:
 
 
 def pack_spikes(spikes) -> np.ndarray:
-    """LSB-first packing, tail bits zero (src/spikes.rs:207-235)."""
-    s = np.asarray(spikes, dtype=bool)
+    """LSB-first packing, tail bits zero (src/spikes.rs:207-235): spike i is
+    bit i % 32 of word i // 32.  Little-endian bit order within each byte,
+    read as little-endian words, is exactly that layout."""
+    s = np.asarray(spikes, dtype=bool).reshape(-1)
     n = s.size
-    padded = np.zeros(packed_len(n) * 32, dtype=np.uint32)
-    padded[:n] = s
-    return (padded.reshape(-1, 32) << np.arange(32, dtype=np.uint32)).sum(axis=1, dtype=np.uint64).astype(np.uint32)
+    pad = packed_len(n) * 32 - n
+    if pad:
+        s = np.concatenate([s, np.zeros(pad, dtype=bool)])
+    return np.packbits(s, bitorder="little").view("<u4").astype(np.uint32, copy=False)
 
 
 def unpack_spikes(words, n: int) -> np.ndarray:
     w = np.asarray(words, dtype=np.uint32)
     if w.size < packed_len(n):
         raise ValueError(f"sparsl: {w.size} words cannot hold {n} spikes")
-    bits = (w[: packed_len(n)][:, None] >> np.arange(32, dtype=np.uint32)) & 1
-    return bits.reshape(-1)[:n].astype(bool)
+    b = np.ascontiguousarray(w[: packed_len(n)]).astype("<u4", copy=False).view(np.uint8)
+    return np.unpackbits(b, bitorder="little")[:n].astype(bool)
 
 
 def spikes_to_f32(words, n: int) -> np.ndarray:
