@@ -114,10 +114,17 @@ def test_tolerances_match_oracle(O):
 
 def test_spike_helpers_match_oracle(O):
     r = np.random.default_rng(3)
-    for n in (0, 1, 31, 32, 33, 63, 64, 65, 1000):
+    for n in (0, 1, 31, 32, 33, 63, 64, 65, 1000, 262_145):
         s = r.random(n) < 0.37
         assert np.array_equal(S.pack_spikes(s), O.pack_spikes(s.astype(np.uint8)))
         assert np.array_equal(S.unpack_spikes(S.pack_spikes(s), n), s)
+        # any nonzero byte is a spike; bits past n in the last word are ignored
+        b = s.astype(np.uint8) * r.integers(1, 256, n, dtype=np.uint8)
+        assert np.array_equal(S.pack_spikes(b), O.pack_spikes(s.astype(np.uint8)))
+        w = S.pack_spikes(s)
+        if n % 32:
+            w[-1] |= np.uint32(0xFFFFFFFF) << np.uint32(n % 32)
+        assert np.array_equal(S.unpack_spikes(w, n), s)
 
 
 @pytest.mark.skipif(_lib.load().sparsl_device_count() > 0, reason="a GPU is visible")
