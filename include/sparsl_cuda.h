@@ -150,6 +150,24 @@ int sparsl_op_prepare_device(sparsl_dev *dev, const uint32_t *d_row_ptr, uint64_
                              uint64_t ncols, const float *d_weights, uint64_t weights_len,
                              int precision, int with_transpose, sparsl_shape *shape,
                              sparsl_op **out);
+/* Extension, no counterpart in the reference (its operators always own
+ * their arrays): sparsl_op_prepare_device in f32 precision, where the
+ * operator uses the caller's row_ptr, col and weights in place instead of
+ * copying them, for operators too large to hold twice (a 4.3e9-synapse
+ * network's CSR is 34 GB).  Same gate, same products, bit for bit.
+ * Requirements, each refused with SPARSL_ERR_INVALID:
+ *  - each array starts on a 256-byte boundary;
+ *  - each array is followed by 256 bytes of the same cudaMalloc allocation
+ *    (not managed memory).
+ * The caller keeps the arrays alive until sparsl_op_destroy, which never
+ * frees them, and keeps row_ptr and col unchanged.  Forward products read
+ * the weights in place.  sparsl_op_set_weights writes into d_weights.  The
+ * reverse index keeps its own weight copy, refreshed by set_weights. */
+int sparsl_op_prepare_device_borrowed(sparsl_dev *dev, const uint32_t *d_row_ptr,
+                                      uint64_t row_ptr_len, const uint32_t *d_col,
+                                      uint64_t col_len, uint64_t csr_ncols, uint64_t ncols,
+                                      float *d_weights, uint64_t weights_len, int with_transpose,
+                                      sparsl_shape *shape, sparsl_op **out);
 /* Csc::from_csr_slices (sparse.rs:361-427) on the GPU, for a CSR in device
  * memory of `dev`: writes d_col_ptr[ncols + 1], and per slot d_row[col_len]
  * and d_edge_idx[col_len] -- each column's edges in CSR order, the same

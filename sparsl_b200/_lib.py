@@ -60,6 +60,8 @@ SIGNATURES = {
                                 ctypes.POINTER(vp)]),
     "sparsl_op_prepare_device": (i32, [vp, vp, u64, vp, u64, u64, u64, vp, u64, i32, i32,
                                        ctypes.POINTER(Shape), ctypes.POINTER(vp)]),
+    "sparsl_op_prepare_device_borrowed": (i32, [vp, vp, u64, vp, u64, u64, u64, vp, u64, i32,
+                                                ctypes.POINTER(Shape), ctypes.POINTER(vp)]),
     "sparsl_csc_from_csr_device": (i32, [vp, vp, u64, vp, u64, u64, vp, vp, vp, ctypes.POINTER(Shape)]),
     "sparsl_op_bind_x": (i32, [vp, vp]),
     "sparsl_op_bind_y": (i32, [vp, vp]),

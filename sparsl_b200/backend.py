@@ -468,6 +468,17 @@ class Device:
         return SparseOp._prepare_device(self, row_ptr, col, ncols if csr_ncols is None else csr_ncols, ncols,
                                         weights, transpose, precision)
 
+    def prepare_device_borrowed(self, row_ptr, col, ncols: int, weights, transpose: bool = False,
+                                csr_ncols: Optional[int] = None) -> "SparseOp":
+        """``prepare_device`` in f32 where the operator uses the caller's
+        arrays in place instead of copying them (extension: for operators too
+        large to hold twice).  Each tensor must start on a 256-byte boundary
+        and be followed by 256 bytes of its allocation; the operator keeps
+        references to the tensors, and ``set_weights`` writes into
+        ``weights``.  Keep ``row_ptr`` and ``col`` unchanged."""
+        return SparseOp._prepare_device(self, row_ptr, col, ncols if csr_ncols is None else csr_ncols, ncols,
+                                        weights, transpose, WeightPrecision.F32, borrow=True)
+
     # ---- device-level ops ----
     def assoc_scan(self, xs) -> np.ndarray:
         """Inclusive scan of (a, b) maps, bit-identical to assoc_scan_sequential.
@@ -658,7 +669,7 @@ class SparseOp:
 
     @classmethod
     def _prepare_device(cls, device: Device, row_ptr, col, csr_ncols: int, ncols: int, weights, transpose: bool,
-                        precision: WeightPrecision) -> "SparseOp":
+                        precision: WeightPrecision, borrow: bool = False) -> "SparseOp":
         """``prepare`` from arrays already on the GPU (sparsl_op_prepare_device).
 
         ``row_ptr`` and ``col`` are 32-bit integer tensors and ``weights`` a
@@ -676,6 +687,13 @@ class SparseOp:
             torch.cuda.synchronize(weights.device)
         sh = Shape()
         h = ctypes.c_void_p()
+        if borrow:
+            rc = _lib.load().sparsl_op_prepare_device_borrowed(
+                device.handle, row_ptr.data_ptr(), row_ptr.numel(), col.data_ptr(), col.numel(), int(csr_ncols),
+                int(ncols), weights.data_ptr(), weights.numel(), int(transpose), ctypes.byref(sh), ctypes.byref(h))
+            op = cls._finish(device, rc, sh, h, precision)
+            op._borrowed = (row_ptr, col, weights)  # alive as long as the operator
+            return op
         rc = _lib.load().sparsl_op_prepare_device(device.handle, row_ptr.data_ptr(), row_ptr.numel(), col.data_ptr(),
                                                   col.numel(), int(csr_ncols), int(ncols), weights.data_ptr(),
                                                   weights.numel(), int(precision), int(transpose), ctypes.byref(sh),

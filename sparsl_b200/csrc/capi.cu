@@ -85,6 +85,7 @@ struct DBuf {
   void* p = nullptr;
   size_t bytes = 0;  // payload capacity
   bool guarded = false;
+  bool borrowed = false;  // the caller's memory: never freed here
   template <class T>
   T* as() const {
     return static_cast<T*>(p);
@@ -108,9 +109,10 @@ cudaError_t dalloc(DBuf& b, size_t bytes, bool guard, cudaStream_t s) {
 }
 
 void dfree(DBuf& b) {
-  if (b.p) cudaFree(b.p);
+  if (b.p && !b.borrowed) cudaFree(b.p);
   b.p = nullptr;
   b.bytes = 0;
+  b.borrowed = false;
 }
 
 // Grow-only buffer.
@@ -856,6 +858,7 @@ struct PrepSrc {
   const uint32_t* col;
   const float* weights;
   bool device;
+  bool borrow = false;  // device f32 sources the operator uses in place
 };
 
 void to_shape(const PlanResult& r, sparsl_shape* out) {
@@ -994,6 +997,50 @@ int sparsl_op_prepare_device(sparsl_dev* d, const uint32_t* d_row_ptr, uint64_t 
   return prepare_body(d, PrepSrc{rp.data(), d_row_ptr, d_col, d_weights, true}, sh, precision, with_transpose, out);
 }
 
+namespace {
+// A borrowed array must meet what the operator's own arrays guarantee every
+// kernel: a kAlign-aligned start and kAlign bytes of the same allocation
+// after its end (vector loads and staged tiles may read into that slack).
+// Managed memory is refused: its allocation extent cannot be checked.
+int check_borrowable(const void* p, uint64_t bytes, int ordinal, const char* what) {
+  cudaPointerAttributes at{};
+  if (p && cudaPointerGetAttributes(&at, p) == cudaSuccess && at.type == cudaMemoryTypeManaged)
+    return fail(SPARSL_ERR_INVALID, "not device memory", std::string(what) + ": managed memory cannot be borrowed");
+  cudaGetLastError();
+  int rc = check_device_span(p, bytes + kAlign, ordinal, what);
+  if (rc != SPARSL_OK && std::string(sparsl_last_reason()) == "device array too short")
+    return fail(SPARSL_ERR_INVALID, "device array too short",
+                std::string(what) + ": a borrowed array must be followed by 256 bytes of its allocation");
+  if (rc != SPARSL_OK) return rc;
+  if (reinterpret_cast<uintptr_t>(p) % kAlign)
+    return fail(SPARSL_ERR_INVALID, "misaligned device array",
+                std::string(what) + ": a borrowed array must start on a 256-byte boundary");
+  return SPARSL_OK;
+}
+}  // namespace
+
+int sparsl_op_prepare_device_borrowed(sparsl_dev* d, const uint32_t* d_row_ptr, uint64_t row_ptr_len,
+                                      const uint32_t* d_col, uint64_t col_len, uint64_t csr_ncols, uint64_t ncols,
+                                      float* d_weights, uint64_t weights_len, int with_transpose,
+                                      sparsl_shape* shape, sparsl_op** out) {
+  ADMIT();
+  if (!out || !d) return fail(SPARSL_ERR_INVALID, "null argument", "sparsl_op_prepare_device_borrowed: null argument");
+  *out = nullptr;
+  CK("prepare_device", cudaSetDevice(d->ordinal));
+  TRY(check_borrowable(d_row_ptr, row_ptr_len * 4, d->ordinal, "row_ptr"));
+  TRY(check_borrowable(d_col, col_len * 4, d->ordinal, "col"));
+  TRY(check_borrowable(d_weights, weights_len * 4, d->ordinal, "weights"));
+  std::vector<uint32_t> rp;
+  sparsl_shape sh{};
+  TRY(gate_device(d, d_row_ptr, row_ptr_len, d_col, col_len, csr_ncols, ncols, rp, &sh));
+  if (shape) *shape = sh;
+  if (sh.code != PLAN_OK) return fail(SPARSL_ERR_INVALID, "invalid CSR", "CSR failed validation");
+  TRY(check_prepare_args(sh, weights_len, 0, shape));
+  PrepSrc src{rp.data(), d_row_ptr, d_col, d_weights, true};
+  src.borrow = true;
+  return prepare_body(d, src, sh, 0, with_transpose, out);
+}
+
 int sparsl_csc_from_csr_device(sparsl_dev* d, const uint32_t* d_row_ptr, uint64_t row_ptr_len, const uint32_t* d_col,
                                uint64_t col_len, uint64_t ncols, uint32_t* d_col_ptr, uint32_t* d_row,
                                uint32_t* d_edge_idx, sparsl_shape* shape) {
@@ -1050,9 +1097,21 @@ int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int 
     if (dalloc((buf), (bytes) + 16, (guard), op->stream) != cudaSuccess)                   \
       return bail(fail(SPARSL_ERR_ALLOCATION, what, std::string("device allocation failed for ") + what)); \
   } while (0)
-  PALLOC(op->row_ptr, (nrows + 1) * 4, false, "row_ptr");
-  PALLOC(op->col, nnz * 4, false, "col");
-  PALLOC(op->w, nnz * wbytes, false, "values");
+  const bool borrow = src.borrow && nnz > 0;
+  auto lend = [](DBuf& b, const void* p, size_t bytes) {
+    b.p = const_cast<void*>(p);
+    b.bytes = bytes;
+    b.borrowed = true;
+  };
+  if (borrow) {
+    lend(op->row_ptr, src.d_row_ptr, (nrows + 1) * 4);
+    lend(op->col, src.col, nnz * 4);
+    lend(op->w, src.weights, nnz * 4);
+  } else {
+    PALLOC(op->row_ptr, (nrows + 1) * 4, false, "row_ptr");
+    PALLOC(op->col, nnz * 4, false, "col");
+    PALLOC(op->w, nnz * wbytes, false, "values");
+  }
   PALLOC(op->rx, nc * 4, false, "x");
   PALLOC(op->rxs[0], words * 4, true, "x_spikes");
   PALLOC(op->rxs[1], words * 4, true, "x_spikes");
@@ -1065,15 +1124,15 @@ int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int 
          "tile flags");
   PALLOC(op->ticket, 64, false, "tile ticket");
   const cudaMemcpyKind in_kind = src.device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
-  if (cudaMemcpyAsync(op->row_ptr.p, src.d_row_ptr ? src.d_row_ptr : row_ptr, (nrows + 1) * 4, in_kind,
-                      op->stream) != cudaSuccess)
+  if (!borrow && cudaMemcpyAsync(op->row_ptr.p, src.d_row_ptr ? src.d_row_ptr : row_ptr, (nrows + 1) * 4, in_kind,
+                                 op->stream) != cudaSuccess)
     return bail(fail_cuda("prepare", cudaGetLastError()));
-  if (nnz) {
+  if (nnz && !borrow) {
     if (cudaMemcpyAsync(op->col.p, src.col, nnz * 4, in_kind, op->stream) != cudaSuccess)
       return bail(fail_cuda("prepare", cudaGetLastError()));
   }
   std::vector<uint16_t> narrow;
-  if (nnz) {
+  if (nnz && !borrow) {
     if (precision == 0) {
       if (cudaMemcpyAsync(op->w.p, src.weights, nnz * 4, in_kind, op->stream) != cudaSuccess)
         return bail(fail_cuda("prepare", cudaGetLastError()));
