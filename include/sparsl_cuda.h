@@ -101,7 +101,9 @@ void sparsl_device_close(sparsl_dev *dev);
 /* Device::device_name (mod.rs:948-954). */
 int sparsl_device_name(sparsl_dev *dev, char *buf, size_t cap);
 /* Device::reset_metal analogue (mod.rs:825-843): clears the process-wide
- * quarantine only when no call is admitted. */
+ * quarantine only when no call is admitted and every dispatch that timed out
+ * has since completed on the GPU (metal.rs:440-445); SPARSL_ERR_BACKEND
+ * otherwise. */
 int sparsl_device_reset(void);
 int sparsl_quarantined(void);
 /* Device::assoc_scan (mod.rs:1183-1197): in/out are n (a, b) pairs.
@@ -190,6 +192,23 @@ enum {
   SPARSL_LAYOUT_CSC = 8             /* transpose: plain reverse index (hub columns) */
 };
 int sparsl_op_layouts(sparsl_op *op);
+/* Test and diagnostic hook, no reference counterpart: forget the operator's
+ * uniform-row (TMA) layout so every later forward product runs on the
+ * generic row-fold engine.  The engine choice at prepare stays a function of
+ * the operator's shape alone; this only lets a caller compare both engines
+ * on one operator.  Results are identical either way. */
+int sparsl_op_drop_uniform_layout(sparsl_op *op);
+/* Failure-detection test hooks, no reference counterpart.
+ * sparsl_dev_test_expired_wait runs one look-back whose predecessor never
+ * publishes: the device's bounded wait runs out (about 0.1 s), records the
+ * look-back-timeout bit in the device error word and returns, and the call
+ * reports SPARSL_ERR_EXECUTION.  The device stays usable.
+ * sparsl_op_test_mark_canary overwrites one word of the operator's y canary
+ * tail from the host (inside the allocation) and runs the canary check: the
+ * call reports SPARSL_ERR_EXECUTION, and so does every later call on that
+ * operator, whose tail stays marked. */
+int sparsl_dev_test_expired_wait(sparsl_dev *dev);
+int sparsl_op_test_mark_canary(sparsl_op *op);
 int sparsl_op_has_transpose(sparsl_op *op);       /* mod.rs:1594 */
 /* SparseOp::set_weights (mod.rs:1392-1409). */
 int sparsl_op_set_weights(sparsl_op *op, const float *weights, uint64_t n);
@@ -352,13 +371,22 @@ int sparsl_dev_scan_stats(sparsl_dev *dev, uint64_t *repaired, uint64_t *segment
  * library buffers it holds.  Scratch lives in a static device array of about
  * 256 KiB that every GPU loading the library keeps until exit, so n is capped
  * at 4,194,304 maps (larger n returns SPARSL_ERR_LENGTH).  d_in / d_out are
- * caller-owned device buffers of n (a, b) pairs on device `ordinal`; the work
+ * caller-owned device buffers of n (a, b) pairs on device `ordinal`, each
+ * inside one allocation (checked; SPARSL_ERR_INVALID otherwise); the work
  * runs on `stream` (cudaStream_t, NULL = legacy default stream) and the call
- * waits for it with a bounded poll (timeout_ms, 0 = 60 s).  It calls no
- * cudaMalloc, cudaFree or allocating routine.  The first call on a device
- * looks up the array's device address; make that call before any stream
- * capture.  All calls share the one array: calls that overlap on a GPU race,
- * so serialize them.  Results are bit-identical to sparsl_dev_assoc_scan. */
+ * waits for it with a bounded poll (timeout_ms, 0 = the process-wide
+ * sparsl_set_timeout_ms value).  It calls no cudaMalloc, cudaFree or
+ * allocating routine.  The first call on a device looks up the array's device
+ * address.  The call polls the stream and reads the device error word back,
+ * so it cannot be captured into a CUDA graph: on a capturing stream it
+ * returns SPARSL_ERR_INVALID.  All calls share the one array: calls that
+ * overlap on a GPU race, so serialize them.  Like every entry point it is
+ * refused while the backend is quarantined.  A timeout quarantines the
+ * backend: the scan may then still be running on the shared array, and a
+ * later call's clearing of the array would race with it, so let the stream
+ * drain before sparsl_device_reset.  A device fault or a set device error
+ * word (expired bounded wait, repair limit) also quarantines and returns
+ * SPARSL_ERR_EXECUTION.  Results are bit-identical to sparsl_dev_assoc_scan. */
 int sparsl_dev_assoc_scan_noalloc(int ordinal, const float *d_in, uint64_t n, float *d_out,
                                   void *stream, uint64_t timeout_ms);
 

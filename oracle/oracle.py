@@ -104,6 +104,15 @@ def lib():
     L.or_tolerance_for_scan.restype = c_f
     L.or_tolerance_for_scan.argtypes = [ctypes.c_uint64, c_f]
     L.or_golden_fingerprint.restype = ctypes.c_uint64
+    L.or_wl_log.restype = ctypes.c_double
+    L.or_wl_log.argtypes = [ctypes.c_double]
+    L.or_wl_cos2pi.restype = ctypes.c_double
+    L.or_wl_cos2pi.argtypes = [ctypes.c_double]
+    L.or_wl_fixed_fanin.argtypes = [ctypes.c_uint64, ctypes.c_uint64, sz, ctypes.c_uint64, ctypes.c_uint32, c_f,
+                                    u32p, f32p]
+    L.or_wl_lif_state.argtypes = [ctypes.c_uint64, ctypes.c_uint64, sz, c_f, c_f, c_f, c_f, f32p, f32p, u8p]
+    L.or_net_ticks.argtypes = [sz, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, sz, u32p,
+                               f32p, f32p, u8p, c_f, c_f, c_f, sz, ctypes.c_void_p]
     _lib = L
     return L
 
@@ -391,3 +400,49 @@ def set_threads(n: int) -> None:
 
 def num_threads() -> int:
     return lib().or_num_threads()
+
+
+# --------------------------------------------------------------------------
+# Benchmark workloads (no reference counterpart): the definition the GPU
+# generator follows, drawn on the host.
+# --------------------------------------------------------------------------
+def wl_log(x: float) -> float:
+    return lib().or_wl_log(float(x))
+
+
+def wl_cos2pi(u: float) -> float:
+    return lib().or_wl_cos2pi(float(u))
+
+
+def wl_fixed_fanin(seed: int, row0: int, nrows: int, ncols: int, fan_in: int, sigma: float, col=None, w=None):
+    """Rows [row0, row0 + nrows) of the fixed fan-in network: (col u32, w f32),
+    nrows * fan_in each (row-major); drawn on all host threads."""
+    n = nrows * fan_in
+    col = np.empty(max(n, 1), np.uint32) if col is None else col
+    w = np.empty(max(n, 1), np.float32) if w is None else w
+    lib().or_wl_fixed_fanin(seed & (2 ** 64 - 1), row0, nrows, ncols, fan_in, sigma, col, w)
+    return col[:n], w[:n]
+
+
+def wl_lif_state(seed: int, cell0: int, n: int, v_lo: float, v_hi: float, theta0: float, density: float):
+    """(v, theta, spikes u8) of cells [cell0, cell0 + n)."""
+    v = np.empty(max(n, 1), np.float32)
+    th = np.empty(max(n, 1), np.float32)
+    sp = np.empty(max(n, 1), np.uint8)
+    lib().or_wl_lif_state(seed & (2 ** 64 - 1), cell0, n, v_lo, v_hi, theta0, density, v, th, sp)
+    return v[:n], th[:n], sp[:n]
+
+
+def net_ticks(blocks, n_total: int, x_spikes, v, theta, spikes, decay, v_reset, dtheta, steps: int):
+    """Recurrent ticks of a network split into row blocks [(row_ptr, col, w), ...]
+    (CpuParallel arm); returns the per-tick spike counts.  Updates x_spikes,
+    v, theta, spikes in place."""
+    nb = len(blocks)
+    rps = (ctypes.c_void_p * nb)(*[b[0].ctypes.data for b in blocks])
+    cols = (ctypes.c_void_p * nb)(*[b[1].ctypes.data for b in blocks])
+    ws = (ctypes.c_void_p * nb)(*[b[2].ctypes.data for b in blocks])
+    rows = (ctypes.c_size_t * nb)(*[b[0].size - 1 for b in blocks])
+    trace = np.zeros(max(steps, 1), np.uint32)
+    lib().or_net_ticks(nb, rps, cols, ws, rows, n_total, x_spikes, v, theta, spikes, decay, v_reset, dtheta,
+                       steps, trace.ctypes.data)
+    return trace[:steps]

@@ -819,3 +819,273 @@ uint64_t or_golden_fingerprint(void) {
     }
     return hash;
 }
+
+/* ------------------------------------------------------------------------ */
+/* Benchmark workloads (no reference counterpart)                            */
+/* ------------------------------------------------------------------------ */
+/*
+ * The definition of the seeded synthetic networks the benchmark runs, so the
+ * host can draw exactly the arrays the GPU generator (libsparsl_cuda's
+ * sparsl_workload_* entry points) draws.  Streams are the reference's Rng
+ * (ChaCha12 keyed by seed_from_u64, src/rng.rs:21-71), one per row:
+ *   row r's columns: gen_index(ncols) x fan_in from seed ^ (r * 0x9E3779B97F4A7C15),
+ *                    sorted ascending (duplicates kept);
+ *   row r's weights: stream (seed ^ 0x5EED5EED5EED5EED) ^ (r * 0x9E3779B97F4A7C15),
+ *                    two next_f64 draws (u1, u2) per synapse,
+ *                    w = (float)(sigma * sqrt(-2 ln(1 - u1)) * cos(2 pi u2))  (Box-Muller).
+ * ln and cos are evaluated by fixed sequences of IEEE double operations (no
+ * libm), so the host and the GPU agree bit for bit:
+ *   ln x  = e ln2 + 2 s (1 + s^2/3 + ... + s^24/25),  x = m 2^e, m in (1/sqrt2, sqrt2],
+ *           s = (m - 1)/(m + 1)  (the atanh series);
+ *   cos 2 pi u by quadrant: 4u = q + r exactly, then the Taylor series of
+ *           sin / cos at t = r pi/2 or (1 - r) pi/2, t in [0, pi/4], through t^17 / t^18.
+ * Series coefficients are 1/(2k+1) and (-1)^k / n! computed as IEEE quotients.
+ */
+
+#define WL_GOLDEN 0x9E3779B97F4A7C15ull
+#define WL_WEIGHT_SALT 0x5EED5EED5EED5EEDull
+
+typedef struct {
+    double inv_odd[13];  /* 1/(2k+1), k = 0..12 */
+    double sin_c[9];     /* (-1)^k / (2k+1)!, k = 0..8 */
+    double cos_c[10];    /* (-1)^k / (2k)!, k = 0..9 */
+} wl_coeffs;
+
+static void wl_coeffs_init(wl_coeffs *c) {
+    double fact[19];
+    fact[0] = 1.0;
+    for (int n = 1; n <= 18; n++) fact[n] = fact[n - 1] * (double)n; /* exact below 2^53 */
+    for (int k = 0; k <= 12; k++) c->inv_odd[k] = 1.0 / (double)(2 * k + 1);
+    for (int k = 0; k <= 8; k++) c->sin_c[k] = (k & 1 ? -1.0 : 1.0) / fact[2 * k + 1];
+    for (int k = 0; k <= 9; k++) c->cos_c[k] = (k & 1 ? -1.0 : 1.0) / fact[2 * k];
+}
+
+/* ln x for normal x in (0, 1]. */
+static double wl_log(const wl_coeffs *c, double x) {
+    uint64_t b;
+    memcpy(&b, &x, 8);
+    int e = (int)((b >> 52) & 0x7ff) - 1023;
+    b = (b & 0x000fffffffffffffull) | 0x3ff0000000000000ull;
+    double m;
+    memcpy(&m, &b, 8);
+    if (m > 1.4142135623730951) {
+        m = m * 0.5;
+        e += 1;
+    }
+    double s = (m - 1.0) / (m + 1.0);
+    double s2 = s * s;
+    double p = c->inv_odd[12];
+    for (int k = 11; k >= 1; k--) p = c->inv_odd[k] + s2 * p;
+    double poly = 1.0 + s2 * p;
+    return (double)e * 0.6931471805599453 + 2.0 * s * poly;
+}
+
+static double wl_sin_t(const wl_coeffs *c, double t) {
+    double t2 = t * t;
+    double p = c->sin_c[8];
+    for (int k = 7; k >= 0; k--) p = c->sin_c[k] + t2 * p;
+    return t * p;
+}
+
+static double wl_cos_t(const wl_coeffs *c, double t) {
+    double t2 = t * t;
+    double p = c->cos_c[9];
+    for (int k = 8; k >= 0; k--) p = c->cos_c[k] + t2 * p;
+    return p;
+}
+
+/* cos(2 pi u) for u in [0, 1).  With 4u = q + r (q = 0..3, r in [0, 1)):
+ * cos(2 pi u) = +cos(pi r/2), -sin(pi r/2), -cos(pi r/2), +sin(pi r/2) for
+ * q = 0..3, and cos(pi r/2) = sin(pi (1-r)/2), so the series only ever see
+ * t in [0, pi/4]. */
+static double wl_cos2pi(const wl_coeffs *c, double u) {
+    const double half_pi = 1.5707963267948966;
+    double t4 = 4.0 * u;
+    int q = (int)t4;
+    double r = t4 - (double)q;
+    double v;
+    if ((q & 1) == 0) { /* cos(pi r / 2) */
+        v = r <= 0.5 ? wl_cos_t(c, r * half_pi) : wl_sin_t(c, (1.0 - r) * half_pi);
+        return q == 0 ? v : -v;
+    }
+    /* sin(pi r / 2): negated for q = 1 */
+    v = r <= 0.5 ? wl_sin_t(c, r * half_pi) : wl_cos_t(c, (1.0 - r) * half_pi);
+    return q == 1 ? -v : v;
+}
+
+double or_wl_log(double x) {
+    wl_coeffs c;
+    wl_coeffs_init(&c);
+    return wl_log(&c, x);
+}
+
+double or_wl_cos2pi(double u) {
+    wl_coeffs c;
+    wl_coeffs_init(&c);
+    return wl_cos2pi(&c, u);
+}
+
+/* Key of a stream (seed_from_u64's PCG32 expansion). */
+static void wl_key(uint64_t seed, uint32_t key[8]) {
+    or_rng r;
+    or_rng_init(&r, seed);
+    memcpy(key, r.key, sizeof r.key);
+}
+
+/* Eight consecutive ChaCha12 blocks from `counter`, computed lane-parallel
+ * (the same rounds as chacha12_block, laid out so the compiler vectorises
+ * across the eight blocks). */
+#define WL_LANES 8
+#define WL_QR(a, b, c, d)                                                   \
+    for (int l = 0; l < WL_LANES; l++) {                                    \
+        x[a][l] += x[b][l]; x[d][l] = rotl32(x[d][l] ^ x[a][l], 16);      \
+        x[c][l] += x[d][l]; x[b][l] = rotl32(x[b][l] ^ x[c][l], 12);      \
+        x[a][l] += x[b][l]; x[d][l] = rotl32(x[d][l] ^ x[a][l], 8);       \
+        x[c][l] += x[d][l]; x[b][l] = rotl32(x[b][l] ^ x[c][l], 7);       \
+    }
+static void chacha12_x8(const uint32_t key[8], uint64_t counter, uint32_t out[WL_LANES][16]) {
+    uint32_t x[16][WL_LANES], s[16][WL_LANES];
+    for (int l = 0; l < WL_LANES; l++) {
+        s[0][l] = 0x61707865u; s[1][l] = 0x3320646eu; s[2][l] = 0x79622d32u; s[3][l] = 0x6b206574u;
+        for (int i = 0; i < 8; i++) s[4 + i][l] = key[i];
+        uint64_t c = counter + (uint64_t)l;
+        s[12][l] = (uint32_t)c;
+        s[13][l] = (uint32_t)(c >> 32);
+        s[14][l] = 0;
+        s[15][l] = 0;
+    }
+    memcpy(x, s, sizeof x);
+    for (int r = 0; r < 6; r++) {
+        WL_QR(0, 4, 8, 12) WL_QR(1, 5, 9, 13) WL_QR(2, 6, 10, 14) WL_QR(3, 7, 11, 15)
+        WL_QR(0, 5, 10, 15) WL_QR(1, 6, 11, 12) WL_QR(2, 7, 8, 13) WL_QR(3, 4, 9, 14)
+    }
+    for (int i = 0; i < 16; i++)
+        for (int l = 0; l < WL_LANES; l++) out[l][i] = x[i][l] + s[i][l];
+}
+
+/* u64 draws [0, n) of a fresh stream: next_u64 k is words (2k, 2k+1) of
+ * block k / 8, exactly what BlockRng hands out from a fresh state. */
+static void wl_u64_stream(const uint32_t key[8], uint64_t *out, size_t n) {
+    uint32_t blk[WL_LANES][16];
+    for (size_t b0 = 0; b0 * 8 < n; b0 += WL_LANES) {
+        chacha12_x8(key, (uint64_t)b0, blk);
+        for (size_t l = 0; l < WL_LANES; l++) {
+            const size_t b = b0 + l;
+            for (size_t k = 0; k < 8 && b * 8 + k < n; k++)
+                out[b * 8 + k] = ((uint64_t)blk[l][2 * k + 1] << 32) | blk[l][2 * k];
+        }
+    }
+}
+
+typedef struct {
+    uint64_t seed, row0, ncols;
+    uint32_t fan_in;
+    double sigma;
+    uint32_t *col;
+    float *w;
+    size_t nrows, rows_per_item;
+    wl_coeffs coeffs;
+} wl_fanin_job;
+
+/* Stable LSD radix sort of n keys below 2^bits, 11 bits per pass. */
+static void wl_radix_sort(uint32_t *a, uint32_t *tmp, size_t n, int bits) {
+    uint32_t cnt[2048];
+    uint32_t *src = a, *dst = tmp;
+    int passes = 0;
+    for (int shift = 0; shift < bits; shift += 11, passes++) {
+        memset(cnt, 0, sizeof cnt);
+        for (size_t i = 0; i < n; i++) cnt[(src[i] >> shift) & 2047u]++;
+        uint32_t sum = 0;
+        for (int d = 0; d < 2048; d++) {
+            uint32_t c = cnt[d];
+            cnt[d] = sum;
+            sum += c;
+        }
+        for (size_t i = 0; i < n; i++) dst[cnt[(src[i] >> shift) & 2047u]++] = src[i];
+        uint32_t *t = src;
+        src = dst;
+        dst = t;
+    }
+    if (passes & 1) memcpy(a, src, n * sizeof(uint32_t));
+}
+
+static void wl_fanin_item(void *ctx, size_t item) {
+    wl_fanin_job *j = (wl_fanin_job *)ctx;
+    size_t r0 = item * j->rows_per_item, r1 = r0 + j->rows_per_item;
+    if (r1 > j->nrows) r1 = j->nrows;
+    uint64_t *u = (uint64_t *)malloc(sizeof(uint64_t) * 2 * j->fan_in + 64);
+    uint32_t *tmp = (uint32_t *)malloc(sizeof(uint32_t) * j->fan_in + 64);
+    int bits = 0;
+    while (bits < 64 && ((j->ncols - 1) >> bits)) bits++;
+    uint32_t key[8];
+    for (size_t lr = r0; lr < r1; lr++) {
+        const uint64_t r = j->row0 + lr;
+        uint32_t *out = j->col + lr * j->fan_in;
+        wl_key(j->seed ^ (r * WL_GOLDEN), key);
+        wl_u64_stream(key, u, j->fan_in);
+        for (uint32_t i = 0; i < j->fan_in; i++) out[i] = (uint32_t)(u[i] % j->ncols);
+        wl_radix_sort(out, tmp, j->fan_in, bits);
+        wl_key((j->seed ^ WL_WEIGHT_SALT) ^ (r * WL_GOLDEN), key);
+        wl_u64_stream(key, u, 2 * (size_t)j->fan_in);
+        float *wo = j->w + lr * j->fan_in;
+        for (uint32_t i = 0; i < j->fan_in; i++) {
+            double u1 = (double)(u[2 * i] >> 11) * (1.0 / 9007199254740992.0);
+            double u2 = (double)(u[2 * i + 1] >> 11) * (1.0 / 9007199254740992.0);
+            double z = sqrt(-2.0 * wl_log(&j->coeffs, 1.0 - u1)) * wl_cos2pi(&j->coeffs, u2);
+            wo[i] = (float)(j->sigma * z);
+        }
+    }
+    free(u);
+    free(tmp);
+}
+
+void or_wl_fixed_fanin(uint64_t seed, uint64_t row0, size_t nrows, uint64_t ncols, uint32_t fan_in, float sigma,
+                       uint32_t *col, float *w) {
+    if (nrows == 0 || fan_in == 0 || ncols == 0) return;
+    wl_fanin_job j = {.seed = seed, .row0 = row0, .ncols = ncols, .fan_in = fan_in, .sigma = (double)sigma,
+                      .col = col, .w = w, .nrows = nrows, .rows_per_item = 64};
+    wl_coeffs_init(&j.coeffs);
+    par_for((nrows + j.rows_per_item - 1) / j.rows_per_item, wl_fanin_item, &j);
+}
+
+/* Per-cell initial state: cell c's stream seed ^ (c * 0x9E37...) gives
+ * next_f32 f0, f1: v = v_lo + (v_hi - v_lo) f0, theta = theta0, spike = f1 < density. */
+void or_wl_lif_state(uint64_t seed, uint64_t cell0, size_t n, float v_lo, float v_hi, float theta0, float density,
+                     float *v, float *theta, uint8_t *spikes) {
+    for (size_t i = 0; i < n; i++) {
+        or_rng r;
+        or_rng_init(&r, seed ^ ((cell0 + i) * WL_GOLDEN));
+        float f0 = or_rng_next_f32(&r);
+        float f1 = or_rng_next_f32(&r);
+        v[i] = v_lo + (v_hi - v_lo) * f0;
+        if (theta) theta[i] = theta0;
+        if (spikes) spikes[i] = f1 < density;
+    }
+}
+
+/* Recurrent ticks of a network whose rows are split into row blocks that
+ * all read the same input spike words (the 4.3e9-synapse network needs two
+ * blocks: CSR offsets are u32).  Each tick runs every block's fused
+ * spike-SpMV + LIF (or_fused_spikes_lif, CpuParallel arm), then packs all
+ * cells' spikes into x_spikes and records their count: or_recurrent_steps
+ * with the rows partitioned, which changes no row's fold. */
+void or_net_ticks(size_t nblocks, const uint32_t *const *row_ptr, const uint32_t *const *col,
+                  const float *const *w, const size_t *block_rows, size_t n_total, uint32_t *x_spikes,
+                  float *v, float *theta, uint8_t *spikes, float decay, float v_reset, float dtheta,
+                  size_t steps, uint32_t *trace) {
+    size_t words = or_packed_len(n_total);
+    for (size_t t = 0; t < steps; t++) {
+        size_t off = 0;
+        for (size_t b = 0; b < nblocks; b++) {
+            or_fused_spikes_lif(1, row_ptr[b], col[b], w[b], block_rows[b], x_spikes, v + off, theta + off,
+                                spikes + off, decay, v_reset, dtheta);
+            off += block_rows[b];
+        }
+        or_pack_spikes_into(spikes, n_total, x_spikes, words);
+        if (trace) {
+            uint32_t cnt = 0;
+            for (size_t i = 0; i < n_total; i++) cnt += spikes[i] != 0;
+            trace[t] = cnt;
+        }
+    }
+}

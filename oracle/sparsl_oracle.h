@@ -122,6 +122,18 @@ float or_tolerance_for_spmv_narrow(int precision, uint64_t max_row_nnz, float ma
                                    float max_abs_result);
 float or_tolerance_for_scan(uint64_t prefix_len, float magnitude_envelope);
 
+/* ---- benchmark workloads (no reference counterpart; see sparsl_oracle.c) ---- */
+double or_wl_log(double x);
+double or_wl_cos2pi(double u);
+void or_wl_fixed_fanin(uint64_t seed, uint64_t row0, size_t nrows, uint64_t ncols, uint32_t fan_in,
+                       float sigma, uint32_t *col, float *w);
+void or_wl_lif_state(uint64_t seed, uint64_t cell0, size_t n, float v_lo, float v_hi, float theta0,
+                     float density, float *v, float *theta, uint8_t *spikes);
+void or_net_ticks(size_t nblocks, const uint32_t *const *row_ptr, const uint32_t *const *col,
+                  const float *const *w, const size_t *block_rows, size_t n_total, uint32_t *x_spikes,
+                  float *v, float *theta, uint8_t *spikes, float decay, float v_reset, float dtheta,
+                  size_t steps, uint32_t *trace);
+
 /* ---- tests/golden.rs:30-77 ---- */
 uint64_t or_golden_fingerprint(void);
 

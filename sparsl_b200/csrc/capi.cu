@@ -43,6 +43,26 @@ thread_local const char* t_reason = "";
 std::atomic<uint64_t> g_timeout_ms{60000};
 std::atomic<bool> g_quarantine{false};
 std::atomic<int> g_admitted{0};
+// Dispatches that timed out, as events recorded behind their work: the
+// quarantine may be cleared only once every one of them has completed
+// (metal.rs:440-445, TIMED_OUT_COMMANDS).
+std::mutex g_timed_out_mu;
+std::vector<cudaEvent_t> g_timed_out;
+
+void retain_timed_out(cudaStream_t s) {
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  if (cudaEventRecord(e, s) != cudaSuccess) {
+    cudaGetLastError();
+    cudaEventDestroy(e);
+    return;
+  }
+  std::lock_guard<std::mutex> lk(g_timed_out_mu);
+  g_timed_out.push_back(e);
+}
 
 int fail(int code, const char* reason, const std::string& detail) {
   t_reason = reason;
@@ -156,6 +176,7 @@ int wait_bounded(cudaStream_t s, cudaEvent_t ev, uint32_t* err_d, uint32_t* err_
     }
     if (std::chrono::steady_clock::now() - t0 > limit) {
       g_quarantine.store(true);
+      retain_timed_out(s);
       return fail(SPARSL_ERR_EXECUTION, operation,
                   std::string(operation) + ": did not complete within " + std::to_string(g_timeout_ms.load()) +
                       " ms; backend quarantined");
@@ -250,8 +271,17 @@ ncclResult_t nccl_settle(ncclComm_t comm, ncclResult_t r) {
 }  // namespace
 
 namespace sparsl {
-// Lets other translation units report through sparsl_last_error.
+// Lets other translation units report through sparsl_last_error and share
+// the process-wide admission and quarantine state.
 int record_error(int code, const char* message) { return fail(code, message, message); }
+int record_error_detail(int code, const char* reason, const std::string& detail) { return fail(code, reason, detail); }
+bool admission_enter() {
+  g_admitted.fetch_add(1);
+  return !g_quarantine.load();
+}
+void admission_leave() { g_admitted.fetch_sub(1); }
+void quarantine_backend() { g_quarantine.store(true); }
+uint64_t timeout_ms_setting() { return g_timeout_ms.load(); }
 }  // namespace sparsl
 
 // ==========================================================================
@@ -272,6 +302,7 @@ struct sparsl_dev {
   DBuf lv, lth, lcur, lspk;
   DBuf vscratch;  // device CSR validation results, scan walk state
   DBuf tscratch;  // scan transfer tables
+  DBuf cscratch;  // reverse-index sort scratch (sparsl_csc_from_csr_device)
   // Copy streams of the chunked host-buffer scan (created on first use).
   cudaStream_t up = nullptr, down = nullptr;
   cudaEvent_t up_ev = nullptr, scan_ev = nullptr, down_ev = nullptr;
@@ -553,6 +584,7 @@ void sparsl_device_close(sparsl_dev* d) {
   dfree(d->lspk);
   dfree(d->vscratch);
   dfree(d->tscratch);
+  dfree(d->cscratch);
   d->err.release();
   for (cudaStream_t st : {d->up, d->down})
     if (st) {
@@ -573,10 +605,23 @@ int sparsl_device_name(sparsl_dev* d, char* buf, size_t cap) {
 }
 
 int sparsl_device_reset(void) {
-  // Refuse while any call is admitted (mod.rs:825-843).
+  // Refuse while any call is admitted (mod.rs:825-843) or while a dispatch
+  // that timed out is still running on the GPU (metal.rs:440-445).
   if (g_admitted.load() > 0)
     return fail(SPARSL_ERR_BACKEND, "reset refused: admissions outstanding",
                 "reset refused: a call is still admitted");
+  {
+    std::lock_guard<std::mutex> lk(g_timed_out_mu);
+    for (cudaEvent_t e : g_timed_out) {
+      const cudaError_t q = cudaEventQuery(e);
+      if (q == cudaErrorNotReady)
+        return fail(SPARSL_ERR_BACKEND, "reset refused: a timed-out dispatch is still running",
+                    "reset refused: a dispatch that timed out has not completed on the GPU yet");
+      if (q != cudaSuccess) cudaGetLastError();
+    }
+    for (cudaEvent_t e : g_timed_out) cudaEventDestroy(e);
+    g_timed_out.clear();
+  }
   g_quarantine.store(false);
   return SPARSL_OK;
 }
@@ -653,16 +698,7 @@ int sparsl_dev_assoc_scan(sparsl_dev* d, const float* in, uint64_t n, float* out
   set.ptr[set.count++] = d->scan_out.canary();
   CK("assoc_scan", launch_canary_check(set, d->err.d, d->stream));
   int rc = wait_bounded(d->stream, d->ev, d->err.d, d->err.h, "assoc_scan");
-  if (rc != SPARSL_OK) {
-    d->scan_dirty = true;
-    if (std::getenv("SPARSL_SCAN_DEBUG")) {
-      uint32_t st[16] = {0};
-      cudaMemcpy(st, d->sc.repair_stats, sizeof st, cudaMemcpyDeviceToHost);
-      std::fprintf(stderr, "scan debug:");
-      for (uint32_t v : st) std::fprintf(stderr, " %u", v);
-      std::fprintf(stderr, "\n");
-    }
-  }
+  if (rc != SPARSL_OK) d->scan_dirty = true;
   return rc;
 }
 
@@ -840,6 +876,17 @@ int sparsl_dev_lif_integrate(sparsl_dev* d, float* v, float* theta, const float*
 }
 
 void* sparsl_dev_stream(sparsl_dev* d) { return d ? d->stream : nullptr; }
+int sparsl_dev_test_expired_wait(sparsl_dev* d) {
+  ADMIT();
+  if (!d) return fail(SPARSL_ERR_INVALID, "null device", "test_expired_wait: null device");
+  std::lock_guard<std::mutex> lk(d->mu);
+  CK("test_expired_wait", cudaSetDevice(d->ordinal));
+  if (ensure(d->vscratch, 32, false, d->stream) != cudaSuccess)
+    return fail(SPARSL_ERR_ALLOCATION, "validation scratch", "device allocation failed for validation scratch");
+  CK("test_expired_wait", launch_expired_wait(d->vscratch.p, d->err.d, d->stream));
+  return wait_bounded(d->stream, d->ev, d->err.d, d->err.h, "test_expired_wait");
+}
+
 int sparsl_dev_wait(sparsl_dev* d) {
   if (!d) return fail(SPARSL_ERR_INVALID, "null device", "null device");
   cudaSetDevice(d->ordinal);
@@ -929,6 +976,20 @@ int check_device_span(const void* p, uint64_t bytes, int ordinal, const char* wh
   }
   return SPARSL_OK;
 }
+
+}  // namespace
+}  // extern "C"
+
+// C++ linkage: shared with the allocation-free entry point (noalloc.cu).
+namespace sparsl {
+int check_device_array(const void* p, uint64_t bytes, int ordinal, const char* what) {
+  return check_device_span(p, bytes, ordinal, what);
+}
+std::string describe_device_error(uint32_t bits) { return describe_dev_err(bits); }
+}  // namespace sparsl
+
+extern "C" {
+namespace {
 
 int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int precision, int with_transpose,
                  sparsl_op** out);
@@ -1059,11 +1120,12 @@ int sparsl_csc_from_csr_device(sparsl_dev* d, const uint32_t* d_row_ptr, uint64_
   TRY(check_device_span(d_row, col_len * 4, d->ordinal, "row"));
   TRY(check_device_span(d_edge_idx, col_len * 4, d->ordinal, "edge_idx"));
   std::lock_guard<std::mutex> lk(d->mu);
-  TmpBufs tmp;
-  if (dalloc(tmp.scratch, csc_scratch_bytes(sh.nnz), false, d->stream) != cudaSuccess)
+  // The sort's scratch is kept on the device and grows only, so repeated
+  // builds of similar size allocate nothing.
+  if (ensure(d->cscratch, csc_scratch_bytes(sh.nnz), false, d->stream) != cudaSuccess)
     return fail(SPARSL_ERR_ALLOCATION, "reverse index", "device allocation failed for the reverse index");
   CK("csc_from_csr", csc_build(d_row_ptr, sh.nrows, d_col, sh.nnz, ncols, d_col_ptr, d_row, d_edge_idx, nullptr,
-                               tmp.scratch.p, d->err.d, d->stream));
+                               d->cscratch.p, d->err.d, d->stream));
   return wait_bounded(d->stream, d->ev, d->err.d, d->err.h, "csc_from_csr");
 }
 
@@ -1222,7 +1284,7 @@ int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int 
   cudaMemsetAsync(op->tile_flags.p, 0, op->tile_flags.bytes, op->stream);
   cudaMemsetAsync(op->ticket.p, 0, op->ticket.bytes, op->stream);
   // Uniform row length (fixed fan-in / fixed degree): enable the TMA path.
-  if (nrows && nnz && nnz % nrows == 0 && !std::getenv("SPARSL_NO_ELL")) {
+  if (nrows && nnz && nnz % nrows == 0) {
     const uint64_t L = nnz / nrows;
     bool uniform = L <= 0xffffffffull;
     for (uint64_t r = 0; uniform && r <= nrows; ++r) uniform = (uint64_t)row_ptr[r] == r * L;
@@ -1360,6 +1422,29 @@ int sparsl_op_layouts(sparsl_op* op) {
          (op->has_t && !op->sell_ok ? SPARSL_LAYOUT_CSC : 0);
 }
 int sparsl_op_has_transpose(sparsl_op* op) { return op && op->has_t ? 1 : 0; }
+
+int sparsl_op_test_mark_canary(sparsl_op* op) {
+  ADMIT();
+  if (!op) return fail(SPARSL_ERR_INVALID, "null argument", "test_mark_canary: null operator");
+  std::lock_guard<std::mutex> lk(op->mu);
+  CK("test_mark_canary", cudaSetDevice(op->dev->ordinal));
+  // The host writes one word of y's canary tail (inside the allocation), as
+  // an out-of-bounds kernel write within the tail would.
+  static const uint32_t kMark = 0;
+  CK("test_mark_canary", cudaMemcpyAsync(const_cast<uint32_t*>(op->ry.canary()), &kMark, sizeof kMark,
+                                         cudaMemcpyHostToDevice, op->stream));
+  return finish(op, "test_mark_canary");
+}
+
+int sparsl_op_drop_uniform_layout(sparsl_op* op) {
+  if (!op) return fail(SPARSL_ERR_INVALID, "null argument", "sparsl_op_drop_uniform_layout: null operator");
+  std::lock_guard<std::mutex> lk(op->mu);
+  // The tensor maps are host-side descriptors over the operator's own col /
+  // weight arrays; clearing the flag is all it takes to route every later
+  // forward launch through the generic row fold.
+  op->ell.ok = false;
+  return SPARSL_OK;
+}
 
 int sparsl_op_set_weights(sparsl_op* op, const float* weights, uint64_t n) {
   ADMIT();

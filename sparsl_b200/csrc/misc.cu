@@ -256,6 +256,14 @@ __global__ void canary_check_kernel(CanarySet set, uint32_t* err) {
   }
 }
 
+// Tile 1 of a two-tile look-back whose tile 0 never publishes (its flag
+// stays zero): the library's bounded wait runs out, records
+// DEVERR_LOOKBACK_TIMEOUT and returns.  Only the failure-detection tests
+// launch it.
+__global__ void expired_wait_kernel(unsigned long long* flags, uint32_t* err, uint32_t* out) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) out[0] = lookback_count(flags, 1, 1, err);
+}
+
 __global__ void fill_kernel(uint32_t* p, uint64_t n, uint32_t v) {
   for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
        i += (uint64_t)gridDim.x * blockDim.x)
@@ -347,6 +355,14 @@ cudaError_t launch_popcount(const uint32_t* words, uint64_t nwords, uint32_t* sl
 cudaError_t launch_canary_check(const CanarySet& set, uint32_t* err, cudaStream_t s) {
   if (set.count == 0) return cudaSuccess;
   canary_check_kernel<<<set.count, 64, 0, s>>>(set, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_expired_wait(void* scratch32, uint32_t* err, cudaStream_t s) {
+  cudaError_t e = cudaMemsetAsync(scratch32, 0, 32, s);
+  if (e != cudaSuccess) return e;
+  unsigned long long* flags = static_cast<unsigned long long*>(scratch32);
+  expired_wait_kernel<<<1, 32, 0, s>>>(flags, err, reinterpret_cast<uint32_t*>(flags + 2));
   return cudaGetLastError();
 }
 

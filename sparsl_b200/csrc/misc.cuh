@@ -60,6 +60,10 @@ cudaError_t launch_compact_bits(const uint32_t* words, uint64_t nwords, uint32_t
 cudaError_t launch_popcount(const uint32_t* words, uint64_t nwords, uint32_t* slot, cudaStream_t s);
 cudaError_t launch_canary_check(const CanarySet& set, uint32_t* err, cudaStream_t s);
 cudaError_t launch_fill(uint32_t* p, uint64_t n, uint32_t v, cudaStream_t s);
+// A look-back over a predecessor that never publishes, in 32 zeroed bytes of
+// `scratch32`: the bounded wait expires and sets DEVERR_LOOKBACK_TIMEOUT in
+// *err (failure-detection tests).
+cudaError_t launch_expired_wait(void* scratch32, uint32_t* err, cudaStream_t s);
 // out[k] = w[idx[k]] for k < n, elements of `wbytes` (4 or 2) bytes.
 cudaError_t launch_gather_weights(const void* w, const uint32_t* idx, uint64_t n, int wbytes, void* out,
                                   cudaStream_t s);

@@ -1,7 +1,5 @@
 """The TMA-pipelined row fold (operators whose rows all have the same length)
 against the oracle and against the generic row-fold kernel, bit for bit."""
-import os
-
 import numpy as np
 import pytest
 
@@ -21,12 +19,11 @@ def _uniform(O, nrows, ncols, L, seed):
 
 
 def _prepare(dev, csr, w, precision, generic):
+    op = dev.prepare_with(S.Csr(csr.row_ptr, csr.col, csr.ncols), csr.ncols, w, precision)
     if generic:
-        os.environ["SPARSL_NO_ELL"] = "1"
-    try:
-        return dev.prepare_with(S.Csr(csr.row_ptr, csr.col, csr.ncols), csr.ncols, w, precision)
-    finally:
-        os.environ.pop("SPARSL_NO_ELL", None)
+        op.drop_uniform_layout()
+        assert not op.layouts() & 1
+    return op
 
 
 @pytest.mark.parametrize("nrows,ncols,L", [(1, 64, 8), (31, 100, 32), (33, 1000, 40), (129, 4096, 64),

@@ -137,12 +137,17 @@ def test_event_handoff(O, cuda_device):
     src = torch.from_numpy(x).cuda()
     torch.cuda.synchronize()
     # A peer (torch) produces x on its own stream, after a bounded busy
-    # kernel of about 10 ms, then records an event.
+    # kernel of about 50 ms, then records an event.  Everything the peer
+    # needs is allocated first: an allocation inside the block could make
+    # the host wait for the busy kernel before the wait below is tried.
     peer = torch.cuda.Stream()
     done = torch.cuda.Event()
+    dx = torch.empty_like(src)
+    done.record(peer)  # creates the event before the busy kernel
+    torch.cuda.synchronize()
     with torch.cuda.stream(peer):
-        torch.cuda._sleep(20_000_000)
-        dx = src.clone()
+        torch.cuda._sleep(100_000_000)
+        dx.copy_(src)
         done.record(peer)
     with pytest.raises(S.OpError) as ei:
         op.wait_cuda_event(done, 0)  # not complete yet: the bounded wait runs out
