@@ -13,7 +13,12 @@ row-block sharded over the ranks, so the total work is fixed as N grows
 
 Inputs are generated on the GPU from seeded ChaCha12 streams (one per row),
 resident in HBM before timing; each rank's synapse arrays (34.4 GB / N) far
-exceed the 126 MB L2, so no flush is needed between ticks.
+exceed the 126 MB L2, so no flush is needed between ticks.  Before timing,
+every rank copies its blocks to host memory and the first ticks (by default
+every warm-up and timed tick, up to --check-ticks) are compared bit for bit
+with the oracle's CpuParallel tick over the same arrays: the global spike
+trace, each rank's final membrane state and the final spike words.  At N=1
+that CPU run over the whole network is also the reported CPU baseline.
 
 Other workloads (``--workload``): ``spmv`` (100k x 100k, 64 distinct sorted
 columns per row), ``scan`` (2^26 affine maps, a ~ U[0.9, 1], b ~ N(0, 1)),
@@ -21,7 +26,9 @@ columns per row), ``scan`` (2^26 affine maps, a ~ U[0.9, 1], b ~ N(0, 1)),
 ``spmm`` (1M x 1M Zipf(1.5) rows clipped to [1, 4096], 64 vectors).
 
 ``--impl reference`` times the CPU restatement of the reference crate's
-CpuParallel arm (the oracle) on this host's cores on a bounded sample.
+CpuParallel arm (the oracle) on this host's cores: full ticks of the whole
+config network, drawn on the host from the workload definition (the same
+arrays the GPU arm draws).
 """
 from __future__ import annotations
 
@@ -53,6 +60,13 @@ NET_THETA0 = 1.0
 NET_DENSITY = 0.01
 NET_SEED = 0x5EED_0005
 BLOCK_NNZ_MAX = 1 << 31
+# Tick-kernel DRAM traffic per algorithmic byte, from an ncu capture of
+# ell_stream_kernel (f32 weights, spike bitmask through the shared-memory
+# summary, LIF epilogue) at 1,048,576 x 1,024: dram__bytes_read.sum +
+# dram__bytes_write.sum over the launch's algorithmic bytes.
+NET_TRAFFIC_RATIO = 4_315_442_000 / 4_312_006_660
+NET_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the same kernel and spike mode at "
+                      "1,048,576 x 512, per algorithmic byte, scaled to this launch")
 
 
 def peaks():
@@ -262,13 +276,16 @@ def net_blocks(local_rows, fan_in):
     return out
 
 
-def build_lif_net(S, dev, dist, n_total, fan_in, keep_sample_rows=0):
+def build_lif_net(S, dev, dist, n_total, fan_in, keep_host=False):
+    """This rank's row blocks, drawn and prepared on the GPU.  With keep_host
+    each block's CSR is also copied to host memory (the arrays the GPU
+    operators were prepared from) for the CPU check."""
     world, rank = dist.world, dist.rank
     local = n_total // world
     row0 = rank * local
     import torch
 
-    ops, sample = [], None
+    ops, host = [], []
     t0 = time.time()
     for (off, nrows) in net_blocks(local, fan_in):
         # The synapses are drawn on the GPU and the operator is prepared from
@@ -282,10 +299,9 @@ def build_lif_net(S, dev, dist, n_total, fan_in, keep_sample_rows=0):
                                                 dw.ptr, None), "workload")
         torch.cuda.synchronize()
         ops.append(dev.prepare_device(drp.span(nrows + 1), dcol.span(nnz), n_total, dw.span(nnz)))
-        if keep_sample_rows and sample is None:
-            k = min(keep_sample_rows, nrows)
-            sample = (drp.to_host(np.uint32, k + 1), dcol.to_host(np.uint32, k * fan_in),
-                      dw.to_host(np.float32, k * fan_in))
+        if keep_host:
+            host.append((drp.to_host(np.uint32, nrows + 1), dcol.to_host(np.uint32, nnz),
+                         dw.to_host(np.float32, nnz), row0 + off))
         for a in (drp, dcol, dw):
             a.free()
     # initial state for every cell (the spike vector is global)
@@ -300,7 +316,7 @@ def build_lif_net(S, dev, dist, n_total, fan_in, keep_sample_rows=0):
     for a in (dv, dth, dpk):
         a.free()
     setup_s = time.time() - t0
-    return ops, (row0, local), (v, th, pk), sample, setup_s
+    return ops, (row0, local), (v, th, pk), host, setup_s
 
 
 def make_net(S, dev, dist, ops, row0, n_total):
@@ -326,46 +342,107 @@ def net_bytes_per_tick_per_gpu(n_total, fan_in, world):
     return local * fan_in * 8 + (local + 1) * 4 + local * 8 + local * 4 + 2 * (n_total // 8) // world
 
 
-def cpu_sample_rate(sample, n_total, pk, v, th, seconds=10.0):
-    """Synapses/s of the oracle's CpuParallel fused tick on a sample row block."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
+def _popcount(words):
+    return int(np.unpackbits(np.ascontiguousarray(words).view(np.uint8)).sum())
 
-    rp, col, w = sample
-    csr = O.Csr(rp, col, n_total)
-    k = csr.nrows
-    vv, tt, sp = v[:k].copy(), th[:k].copy(), np.zeros(k, np.uint8)
-    O.fused_spikes_lif(csr, w, pk, vv, tt, sp, NET_DECAY, NET_VRESET, NET_DTHETA, par=True)  # warm
+
+def cpu_net_ticks(O, dist, host, n_total, v, th, pk, ticks):
+    """The oracle's CpuParallel fused tick (cpu_fused_spikes_*, mod.rs:2572-2614,
+    as recurrent_steps, mod.rs:1889-1932) over this rank's row blocks, `ticks`
+    ticks from (v, th, pk).  Ranks exchange their packed spike words after each
+    tick over the host process group (gloo), so every rank folds against the
+    global spike vector; rows never depend on the split.  Returns the global
+    per-tick spike counts, the final local (v, theta), the final global spike
+    words and the seconds the ticks took (exchange included)."""
+    import torch
+
+    local = v.size
+    sp = np.zeros(local, np.uint8)
+    csrs = [(O.Csr(rp, col, n_total), w) for (rp, col, w, _) in host]
+    trace = []
     t0 = time.perf_counter()
-    ticks = 0
-    while True:
-        O.fused_spikes_lif(csr, w, pk, vv, tt, sp, NET_DECAY, NET_VRESET, NET_DTHETA, par=True)
-        ticks += 1
-        if time.perf_counter() - t0 > seconds:
-            break
-    dt = time.perf_counter() - t0
-    return ticks * csr.nnz / dt, O.num_threads(), f"{ticks} fused ticks over a {k}-row x {NET_FANIN} block " \
-        f"({csr.nnz} synapses) of the same network, {dt:.1f} s"
+    for _ in range(ticks):
+        off = 0
+        for csr, w in csrs:
+            k = csr.nrows
+            O.fused_spikes_lif(csr, w, pk, v[off:off + k], th[off:off + k], sp[off:off + k], NET_DECAY, NET_VRESET,
+                               NET_DTHETA, par=True)
+            off += k
+        words = O.pack_spikes(sp)
+        if dist.world > 1:
+            mine = torch.from_numpy(words.view(np.int32).copy())
+            parts = [torch.empty_like(mine) for _ in range(dist.world)]
+            dist.pg.all_gather(parts, mine)
+            pk = np.concatenate([t_.numpy().view(np.uint32) for t_ in parts])
+        else:
+            pk = words
+        trace.append(_popcount(pk))
+    return np.array(trace, np.uint32), v, th, pk, time.perf_counter() - t0
 
 
 def bench_lif_net(args, dist):
     import torch
     import sparsl_b200 as S
 
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
     torch.cuda.set_device(dist.local)
     dev = S.Device.try_new(S.Backend.Cuda, dist.local)
     n_total, fan_in = NET_N, NET_FANIN
-    want_cpu = dist.world == 1 and dist.rank == 0 and not args.no_cpu
-    ops, (row0, local), (v, th, pk), sample, setup_s = build_lif_net(S, dev, dist, n_total, fan_in,
-                                                                     keep_sample_rows=4096 if want_cpu else 0)
+    check_ticks = 0 if args.no_check else min(args.check_ticks, args.warmup + args.steps)
+    ops, (row0, local), (v, th, pk), host, setup_s = build_lif_net(S, dev, dist, n_total, fan_in,
+                                                                   keep_host=check_ticks > 0)
     net = make_net(S, dev, dist, ops, row0, n_total)
     L = lib()
     stream = L.sparsl_net_stream(net)
-    check(L.sparsl_net_write_state(net, pk.ctypes.data, pk.size, v[row0:row0 + local].ctypes.data,
-                                   th[row0:row0 + local].ctypes.data, local), "write_state")
     p = (NET_DECAY, NET_VRESET, NET_DTHETA)
+    v_l, th_l = v[row0:row0 + local].copy(), th[row0:row0 + local].copy()
+
+    # Bit-exact check against the CPU: the first check_ticks ticks from the
+    # initial state on the GPU, and the same ticks of the oracle over the same
+    # arrays (the ones the operators were prepared from) on the host.  The
+    # check covers every tick the timed run below executes (warm-up ticks
+    # included) unless --check-ticks caps it.
+    chk = None
+    if check_ticks:
+        O.set_threads(max(1, (os.cpu_count() or 1) // dist.world))
+        # The device generator against its host definition, on the first and
+        # last 64 rows of every block of this rank.
+        gen_ok = True
+        for (rp, col, w, r0) in host:
+            k = rp.size - 1
+            for a in (0, max(0, k - 64)):
+                m = min(64, k - a)
+                hc, hw = O.wl_fixed_fanin(NET_SEED, r0 + a, m, n_total, fan_in, NET_SIGMA)
+                gen_ok &= bool(np.array_equal(col[a * fan_in:(a + m) * fan_in], hc)
+                               and np.array_equal(w[a * fan_in:(a + m) * fan_in].view(np.uint32), hw.view(np.uint32)))
+        hv, hth, hs = O.wl_lif_state(NET_SEED ^ 0x57A7E, 0, n_total, 0.0, 1.0, NET_THETA0, NET_DENSITY)
+        gen_ok &= bool(np.array_equal(hv.view(np.uint32), v.view(np.uint32)) and np.array_equal(O.pack_spikes(hs), pk))
+        check(L.sparsl_net_write_state(net, pk.ctypes.data, pk.size, v_l.ctypes.data, th_l.ctypes.data, local),
+              "write_state")
+        check(L.sparsl_net_steps(net, *p, check_ticks), "check ticks")
+        gtrace = np.zeros(check_ticks, np.uint32)
+        nn = ctypes.c_uint64()
+        check(L.sparsl_net_trace(net, gtrace.ctypes.data, gtrace.size, ctypes.byref(nn)), "trace")
+        gpk, gv, gth = np.zeros_like(pk), np.zeros(local, np.float32), np.zeros(local, np.float32)
+        check(L.sparsl_net_read_state(net, gpk.ctypes.data, gpk.size, gv.ctypes.data, gth.ctypes.data, local),
+              "read_state")
+        ctrace, cv, cth, cpk, cpu_s = cpu_net_ticks(O, dist, host, n_total, v_l.copy(), th_l.copy(), pk.copy(),
+                                                    check_ticks)
+        ok = bool(np.array_equal(gtrace, ctrace) and np.array_equal(gv.view(np.uint32), cv.view(np.uint32))
+                  and np.array_equal(gth.view(np.uint32), cth.view(np.uint32)) and np.array_equal(gpk, cpk))
+        oks = dist.gather((ok, gen_ok))
+        chk = {"ticks": check_ticks, "cpu_s": dist.max(cpu_s), "trace": gtrace,
+               "bit_exact_vs_cpu": all(o for o, _ in oks), "generator_matches_host": all(g for _, g in oks)}
+        del host
+    check(L.sparsl_net_write_state(net, pk.ctypes.data, pk.size, v_l.ctypes.data, th_l.ctypes.data, local),
+          "write_state")
     # warm-up (untimed)
     check(L.sparsl_net_steps(net, *p, args.warmup), "warmup")
+    wtrace = np.zeros(args.warmup, np.uint32)
+    nn = ctypes.c_uint64()
+    check(L.sparsl_net_trace(net, wtrace.ctypes.data, wtrace.size, ctypes.byref(nn)), "warm-up trace")
     dist.barrier()
     clocks = Clocks(dist.local)
     if dist.rank == 0:
@@ -381,11 +458,14 @@ def bench_lif_net(args, dist):
     kt = ctypes.c_uint64()
     check(L.sparsl_net_kernel_ms(net, ctypes.byref(kms), ctypes.byref(kt)), "kernel ms")
     kernel_ms_tick = kms.value / max(kt.value, 1)
+    tick_ms = np.zeros(args.steps, np.float32)
+    check(L.sparsl_net_tick_ms(net, tick_ms.ctypes.data, tick_ms.size, ctypes.byref(kt)), "tick ms")
     trace = np.zeros(args.steps, np.uint32)
     n = ctypes.c_uint64()
     check(L.sparsl_net_trace(net, trace.ctypes.data, trace.size, ctypes.byref(n)), "trace")
     traces = dist.gather(trace.tolist())
     consistent = all(t == traces[0] for t in traces)
+    full_trace = np.concatenate([wtrace, trace])
 
     # End to end through the C ABI with pinned host buffers: every step writes
     # the spike vector and this rank's membrane state from the host, runs one
@@ -396,8 +476,8 @@ def bench_lif_net(args, dist):
     hv = Pinned(np.float32, local)
     ht = Pinned(np.float32, local)
     hp.a[:] = pk
-    hv.a[:] = v[row0:row0 + local]
-    ht.a[:] = th[row0:row0 + local]
+    hv.a[:] = v_l
+    ht.a[:] = th_l
     dist.barrier()
 
     def e2e():
@@ -411,27 +491,27 @@ def bench_lif_net(args, dist):
     d2h = h2d
 
     cpu = None
-    if want_cpu and sample is not None:
-        rate, cores, desc = cpu_sample_rate(sample, n_total, pk, v, th, seconds=args.cpu_seconds)
-        cpu = {"value": rate / (n_total * fan_in), "unit": "ticks/s", "cores": cores, "kind": "port",
-               "sample": desc + "; C restatement of the reference's CpuParallel arm, full-network ticks/s = "
-                                "sample synapses/s / 4.29e9 synapses"}
+    if chk and dist.world == 1:
+        cpu = {"value": chk["ticks"] / chk["cpu_s"], "unit": "ticks/s", "cores": O.num_threads(), "kind": "port",
+               "sample": f"{chk['ticks']} full ticks of the same {n_total * fan_in:.3g}-synapse network (the "
+                         "parity check below), C restatement of the reference's CpuParallel fused tick"}
     kernels_per_tick = len(ops) + 1  # fused tick kernel per block + global spike count
     pk_, how = peaks()
     peak = float(pk_.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
     algo = net_bytes_per_tick_per_gpu(n_total, fan_in, dist.world)
     achieved = algo / (kernel_ms_tick * 1e-3) / 1e9
-    # DRAM traffic of the tick kernel from one ncu capture of the same kernel and
-    # spike mode (1,048,576 x 512, profiles/ell_stream_kernel_lif_net.md):
-    # dram read + write = 4,315,442,000 B against 4,312,006,660 algorithmic B.
-    # Traffic grows with the synapses, so it is scaled by the algorithmic bytes.
-    traffic = algo * (4_315_442_000 / 4_312_006_660)
+    # DRAM traffic of the tick kernel: dram__bytes_read.sum + dram__bytes_write.sum
+    # of one ncu capture of this kernel in this spike mode at 1,048,576 x 1,024
+    # (8.6 GB of synapses), per launch, scaled to this launch by its algorithmic
+    # bytes (traffic grows with the synapses streamed).
+    traffic = algo * NET_TRAFFIC_RATIO
     value = args.steps / (ms_max * 1e-3)
+    ts = np.sort(tick_ms)
     line = {
         "metric": "LIF net ticks/sec", "value": value, "unit": "ticks/s", "n_gpus": dist.world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded ChaCha12 per row, generated on the GPU)",
+        "data": "synthetic (seeded ChaCha12 per row, drawn on the GPU; identical to the host definition)",
         "config": {"workload": f"lif_net: {n_total:,} neurons x fan-in {fan_in} ({n_total * fan_in:.3g} synapses), "
                                "f32 weights N(0,0.03^2), decay 0.95, theta 1.0, reset 0, Bernoulli(0.01) initial spikes",
                    "parallelism": f"row-block shards x{dist.world}, NCCL all-gather of packed spikes per tick",
@@ -443,17 +523,29 @@ def bench_lif_net(args, dist):
                 "path": "sparsl_net_write_state + sparsl_net_steps(1) + sparsl_net_read_state, pinned host"},
         "gpu_launches": kernels_per_tick * args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "traffic_source": "ncu dram__bytes_read+write of the same kernel at "
-                                                           "1,048,576 x 512, scaled by algorithmic bytes",
+                     "traffic": traffic, "traffic_source": NET_TRAFFIC_SOURCE,
                      "kernel": "ell_stream_kernel<f32, spike bitmask via shared-memory summary, LIF> "
                                "(TMA-streamed fused spike SpMV + LIF + ballot pack)",
                      "algorithmic_bytes_per_tick_per_gpu": algo, "kernel_ms_per_tick": kernel_ms_tick,
+                     "kernel_ms_per_tick_min_median_max": [float(ts[0]), float(ts[len(ts) // 2]), float(ts[-1])],
+                     "kernel_ms_first_ticks": [round(float(x), 4) for x in tick_ms[:4]],
                      "peak_source": how},
         "cpu_baseline": cpu,
         "check": {"spike_trace_sum": int(trace.sum()), "trace_identical_on_all_ranks": consistent,
                   "trace_sha1": __import__("hashlib").sha1(trace.tobytes()).hexdigest()[:16],
-                  "trace_head": trace[:8].tolist()},
+                  "trace_head": trace[:8].tolist(),
+                  f"trace_sha1_first_{full_trace.size}_ticks": __import__("hashlib").sha1(
+                      full_trace.tobytes()).hexdigest()[:16]},
     }
+    if chk:
+        k = chk["ticks"]
+        line["check"].update({
+            "cpu_check_ticks": k, "bit_exact_vs_cpu": chk["bit_exact_vs_cpu"],
+            "cpu_check_scope": "global spike trace, every rank's final v and theta, final global spike words, "
+                               "after the first ticks from the initial state (warm-up and timed ticks)",
+            "timed_trace_equals_checked_ticks": bool(np.array_equal(full_trace[:k], chk["trace"][:full_trace.size])),
+            "device_generator_matches_host_definition": chk["generator_matches_host"],
+            "cpu_check_s": round(chk["cpu_s"], 1)})
     for h in (hp, hv, ht):
         h.free()
     L.sparsl_net_destroy(net)
@@ -671,21 +763,17 @@ def bench_rowshard(args, dev, dist, kind):
         run = lambda: check(L.sparsl_op_spmm_device(op.handle, dx.data_ptr(), nv, dy.data_ptr(), s.cuda_stream),
                             "spmm")
         algo = nnz * 8 + (n + 1) * 4 + n * nv * 4 + 2 * n * nv * 4
-    # parity: one product from y = 0 against the oracle (SpMM on a row sample)
+    # parity: one product from y = 0 against the oracle over the whole output
+    O.set_threads(max(1, (os.cpu_count() or 1) // dist.world))
     run()
     s.synchronize()
     got = dy.cpu().numpy()
     if kind == "spmv":
         want = O.spmv(O.Csr(rp, col, n), w, x, np.zeros(n, np.float32), par=True)
-        exact = bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))
     else:
-        sample = np.sort(np.random.default_rng(seed ^ 1).choice(n, 2000, replace=False))
-        sub_rp = np.zeros(sample.size + 1, np.uint64)
-        np.cumsum(rp[sample + 1].astype(np.uint64) - rp[sample], out=sub_rp[1:])
-        sel = np.concatenate([np.arange(rp[i], rp[i + 1]) for i in sample])
-        want = O.spmm(O.Csr(sub_rp.astype(np.uint32), col[sel], n), w[sel], x, nv,
-                      np.zeros(sample.size * nv, np.float32), par=True).reshape(sample.size, nv)
-        exact = bool(np.array_equal(got.reshape(n, nv)[sample].view(np.uint32), want.view(np.uint32)))
+        want = O.spmm(O.Csr(rp, col, n), w, x, nv, np.zeros(n * nv, np.float32), par=True)
+    exact = bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))
+    del got, want
     for _ in range(args.warmup):
         run()
     dist.barrier()
@@ -913,32 +1001,33 @@ def bench_spmm(args, dev, want_cpu):
     dx = torch.from_numpy(x).cuda()
     dy = torch.zeros((n, nv), dtype=torch.float32, device="cuda")
     flush = torch.empty(64 << 22, dtype=torch.float32, device="cuda")  # 1 GiB > L2
-    sample = np.sort(np.random.default_rng(SPMM_SEED ^ 1).choice(n, 2000, replace=False))
-    sub_rp = np.zeros(sample.size + 1, np.uint64)
-    np.cumsum(rp[sample + 1].astype(np.uint64) - rp[sample], out=sub_rp[1:])
-    sel = np.concatenate([np.arange(rp[i], rp[i + 1]) for i in sample])
-    sub = O.Csr(sub_rp.astype(np.uint32), col[sel], n)
+    csr = O.Csr(rp, col, n)
     out = {}
+    cpu_s = None
     for prec, tag in ((S.WeightPrecision.F32, "f32"), (S.WeightPrecision.F16, "f16")):
         op = dev.prepare_with(S.Csr(rp, col, n), n, w, prec)
         wb = 4 if tag == "f32" else 2
         run = lambda: check(L.sparsl_op_spmm_device(op.handle, dx.data_ptr(), nv, dy.data_ptr(), s.cuda_stream),
                             "spmm")
-        # parity on a row sample: one product from Y = 0 against the oracle
+        # parity over the whole Y: one product from Y = 0 against the oracle
         dy.zero_()
         run()
         s.synchronize()
-        got = dy.cpu().numpy()[sample]
-        want = O.spmm(sub, O.quantise(int(prec), w)[sel], x.reshape(-1), nv, np.zeros(sample.size * nv, np.float32),
-                      par=True).reshape(sample.size, nv)
+        got = dy.cpu().numpy()
+        t1 = time.perf_counter()
+        want = O.spmm(csr, O.quantise(int(prec), w), x.reshape(-1), nv, np.zeros(n * nv, np.float32),
+                      par=True).reshape(n, nv)
+        if tag == "f32":
+            cpu_s = time.perf_counter() - t1
         exact = bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))
+        del got, want
         for _ in range(args.warmup):
             run()
         ts = time_launches(s, run, max(3, args.kernel_iters // 2), flush=lambda: flush_l2(flush))
         ms = statistics.median(ts)
         algo = nnz * (4 + wb) + (n + 1) * 4 + n * nv * 4 + 2 * n * nv * 4
         out[tag] = {"value": algo / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms, "algorithmic_bytes": algo,
-                    "bit_exact_vs_oracle_row_sample": exact}
+                    "bit_exact_vs_oracle": exact}
         if tag == "f32":
             hx, hy = Pinned(np.float32, n * nv), Pinned(np.float32, n * nv)
             hx.a[:] = x.reshape(-1)
@@ -955,16 +1044,9 @@ def bench_spmm(args, dev, want_cpu):
         del op
     cpu = None
     if want_cpu:
-        wsub = w[sel]
-        yy = np.zeros(sample.size * nv, np.float32)
-        t1, k = time.perf_counter(), 0
-        while time.perf_counter() - t1 < args.cpu_seconds / 2:
-            O.spmm(sub, wsub, x.reshape(-1), nv, yy, par=True)
-            k += 1
-        dt = (time.perf_counter() - t1) / k * (nnz / sel.size)  # full-matrix seconds
-        cpu = {"value": out["f32"]["algorithmic_bytes"] / dt / 1e9, "unit": "GB/s", "cores": O.num_threads(),
-               "kind": "port", "sample": f"{k} SpMMs of a {sample.size}-row sample ({sel.size} nnz), "
-                                         "CpuParallel restatement, scaled to the full matrix by nnz"}
+        cpu = {"value": out["f32"]["algorithmic_bytes"] / cpu_s / 1e9, "unit": "GB/s", "cores": O.num_threads(),
+               "kind": "port", "sample": f"one full f32 SpMM of the same matrix ({cpu_s:.2f} s, the parity check), "
+                                         "CpuParallel restatement"}
     f32 = out["f32"]
     return {"metric": "SpMM effective HBM GB/s", "value": f32["value"], "unit": "GB/s",
             "ms_per_step": f32["ms_per_step"], "algorithmic_bytes": f32["algorithmic_bytes"],
@@ -972,7 +1054,7 @@ def bench_spmm(args, dev, want_cpu):
                       f"(realised nnz {nnz:,}, mean {nnz / n:.1f}), distinct sorted uniform cols, w U[-1,1], "
                       f"X {n:,} x {nv} row-major U[-1,1]; L2 flushed (1 GiB written, then read back) before every launch",
             "setup_s": round(setup_s, 1), "e2e": f32.get("e2e"),
-            "bit_exact_vs_oracle_row_sample": f32["bit_exact_vs_oracle_row_sample"], "f16": out["f16"],
+            "bit_exact_vs_oracle": f32["bit_exact_vs_oracle"], "f16": out["f16"],
             "cpu_baseline": cpu}
 
 
@@ -998,21 +1080,9 @@ def bench_lif(args, dev, want_cpu):
     for a in (dv, dth, dpk):
         a.free()
     op = dev.prepare(S.Csr(rp, col, n), n, w)
-    params = S.LifParams.new(0.95, 0.0, 0.0)
     L = lib()
-    # bit-exact check of the first ticks against the oracle's CpuParallel arm
-    check_ticks = 5
-    op.write_x_spikes(pk0)
-    op.write_lif_state(v0, th0)
-    op.fused_spmv_spikes_lif_recurrent_steps(params, check_ticks)
-    csr = O.Csr(rp, col, n)
-    vw, tw, sw, xw = v0.copy(), th0.copy(), np.zeros(n, np.uint8), pk0.copy()
-    trace_w = O.recurrent_steps(csr, w, xw, vw, tw, sw, 0.95, 0.0, 0.0, check_ticks, par=True)
-    vg, tg, sg = np.zeros(n, np.float32), np.zeros(n, np.float32), np.zeros(n, np.bool_)
-    op.sync_lif_state(vg, tg, sg)
-    exact = bool(np.array_equal(op.spike_trace(), trace_w) and np.array_equal(vg.view(np.uint32), vw.view(np.uint32))
-                 and np.array_equal(op.sync_x_spikes(), xw))
-    # timed run: the 1000-tick network from its initial state
+    # warm-up from the initial state, then the timed run of `ticks` ticks from
+    # the initial state again; the timed ticks are the ones checked below
     op.write_x_spikes(pk0)
     op.write_lif_state(v0, th0)
     check(L.sparsl_op_recurrent_steps(op.handle, 0.95, 0.0, 0.0, args.warmup), "warm")
@@ -1024,6 +1094,20 @@ def bench_lif(args, dev, want_cpu):
                    lambda: check(L.sparsl_op_recurrent_steps_async(op.handle, 0.95, 0.0, 0.0, ticks), "ticks"))
     check(L.sparsl_op_wait(op.handle), "wait")
     trace = op.spike_trace()
+    vg, tg, sg = np.zeros(n, np.float32), np.zeros(n, np.float32), np.zeros(n, np.bool_)
+    op.sync_lif_state(vg, tg, sg)
+    xg = op.sync_x_spikes()
+    # Bit-exact against the oracle's CpuParallel recurrent ticks over the same
+    # arrays: every tick's spike count, the final membrane, threshold, spikes
+    # and packed spike words.  The CPU run is also the CPU baseline.
+    csr = O.Csr(rp, col, n)
+    vw, tw, sw, xw = v0.copy(), th0.copy(), np.zeros(n, np.uint8), pk0.copy()
+    t0 = time.perf_counter()
+    trace_w = O.recurrent_steps(csr, w, xw, vw, tw, sw, 0.95, 0.0, 0.0, ticks, par=True)
+    cpu_s = time.perf_counter() - t0
+    exact = bool(np.array_equal(trace, trace_w) and np.array_equal(vg.view(np.uint32), vw.view(np.uint32))
+                 and np.array_equal(tg.view(np.uint32), tw.view(np.uint32))
+                 and np.array_equal(sg.astype(np.uint8), sw) and np.array_equal(xg, xw))
     algo = nnz * 8 + (n + 1) * 4 + 2 * n * 4 + n * 4 + 2 * n // 8
     # end to end: one tick per slice-API call with pinned host buffers
     hs, hv, ht, ho = Pinned(np.uint32, n // 32), Pinned(np.float32, n), Pinned(np.float32, n), Pinned(np.uint8, n)
@@ -1043,14 +1127,9 @@ def bench_lif(args, dev, want_cpu):
         h.free()
     cpu = None
     if want_cpu:
-        vv, tt, ss, xx = v0.copy(), th0.copy(), np.zeros(n, np.uint8), pk0.copy()
-        t0, k = time.perf_counter(), 0
-        while time.perf_counter() - t0 < args.cpu_seconds / 2:
-            O.recurrent_steps(csr, w, xx, vv, tt, ss, 0.95, 0.0, 0.0, 1, par=True)
-            k += 1
-        dt = time.perf_counter() - t0
-        cpu = {"value": k / dt, "unit": "ticks/s", "cores": O.num_threads(), "kind": "port",
-               "sample": f"{k} full ticks of the same network, CpuParallel restatement"}
+        cpu = {"value": ticks / cpu_s, "unit": "ticks/s", "cores": O.num_threads(), "kind": "port",
+               "sample": f"{ticks} full ticks of the same network ({cpu_s:.1f} s, the parity check), "
+                         "CpuParallel restatement"}
     per_tick = ms / ticks
     return {"metric": "LIF net ticks/sec (1 GPU)", "value": 1e3 / per_tick, "unit": "ticks/s",
             "ms_per_step": per_tick, "ticks": ticks, "algorithmic_bytes_per_tick": algo,
@@ -1060,49 +1139,63 @@ def bench_lif(args, dev, want_cpu):
             "e2e": {"value": e2e_steps / (e2e_ms * 1e-3), "unit": "ticks/s",
                     "h2d_bytes_per_step": n // 8 + 8 * n, "d2h_bytes_per_step": 9 * n,
                     "path": "sparsl_op_fused_spikes_lif per tick + host repack, pinned host"},
-            "bit_exact_vs_oracle_first_ticks": exact, "cpu_baseline": cpu}
+            "bit_exact_vs_oracle": exact, "checked_ticks": ticks, "cpu_baseline": cpu}
 
 
 # --------------------------------------------------------------------------
 # reference arm: the oracle's CpuParallel restatement on the host cores
 # --------------------------------------------------------------------------
 def bench_reference(args, dist):
+    """The reference arm: the oracle's CpuParallel restatement of the tick
+    (cpu_fused_spikes_*, mod.rs:2572-2614, driven as recurrent_steps,
+    mod.rs:1889-1932) on this host's cores, over the whole 4.29e9-synapse
+    network drawn on the host from the workload's definition (the arrays the
+    GPU arm draws, bit for bit).  Every step is one full tick; nothing is
+    sampled or extrapolated.  Rank 0 alone runs it."""
     if dist.rank != 0:
         return None
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
 
     n_total, fan_in = NET_N, NET_FANIN
-    k = 8192  # sample rows
-    r = np.random.default_rng(NET_SEED)
-    col = np.sort(r.integers(0, n_total, size=(k, fan_in), dtype=np.uint32), axis=1).reshape(-1)
-    w = (r.standard_normal(k * fan_in) * NET_SIGMA).astype(np.float32)
-    rp = (np.arange(k + 1, dtype=np.uint64) * fan_in).astype(np.uint32)
-    pk = O.pack_spikes((r.random(n_total) < NET_DENSITY).astype(np.uint8))
-    v = r.random(k).astype(np.float32)
-    th = np.full(k, NET_THETA0, np.float32)
-    sp = np.zeros(k, np.uint8)
-    csr = O.Csr(rp, col, n_total)
-    for _ in range(max(args.warmup, 1)):
-        O.fused_spikes_lif(csr, w, pk, v, th, sp, NET_DECAY, NET_VRESET, NET_DTHETA, par=True)
+    O.set_threads(os.cpu_count() or 1)
     t0 = time.perf_counter()
+    blocks = []
+    for (off, nrows) in net_blocks(n_total, fan_in):
+        rp = (np.arange(nrows + 1, dtype=np.uint64) * fan_in).astype(np.uint32)
+        col, w = O.wl_fixed_fanin(NET_SEED, off, nrows, n_total, fan_in, NET_SIGMA)
+        blocks.append((rp, col, w))
+    v, th, s0 = O.wl_lif_state(NET_SEED ^ 0x57A7E, 0, n_total, 0.0, 1.0, NET_THETA0, NET_DENSITY)
+    pk = O.pack_spikes(s0)
+    setup_s = time.perf_counter() - t0
+    sp = np.zeros(n_total, np.uint8)
+    p = (NET_DECAY, NET_VRESET, NET_DTHETA)
+    trace = [O.net_ticks(blocks, n_total, pk, v, th, sp, *p, args.warmup)]
+    ts = []
     for _ in range(args.steps):
-        O.fused_spikes_lif(csr, w, pk, v, th, sp, NET_DECAY, NET_VRESET, NET_DTHETA, par=True)
-    dt = time.perf_counter() - t0
-    rate = args.steps * csr.nnz / dt
-    value = rate / (n_total * fan_in)
-    desc = (f"{args.steps} fused ticks over a {k}-row x {fan_in} sample block ({csr.nnz} synapses) of the "
-            f"network, {dt:.2f} s; full-network ticks/s = sample synapses/s / 4.29e9")
+        t1 = time.perf_counter()
+        trace.append(O.net_ticks(blocks, n_total, pk, v, th, sp, *p, 1))
+        ts.append(time.perf_counter() - t1)
+    full = np.concatenate(trace).astype(np.uint32)
+    dt = sum(ts)
+    value = args.steps / dt
+    desc = (f"{args.steps} full ticks of the {n_total:,} x {fan_in} network ({n_total * fan_in:.3g} synapses) after "
+            f"{args.warmup} warm-up ticks, {dt:.1f} s; network drawn on the host in {setup_s:.0f} s")
     return {
         "impl": "reference", "metric": "LIF net ticks/sec", "value": value, "unit": "ticks/s",
         "n_gpus": dist.world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / value,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (numpy PCG64 sample of the same distribution)",
-        "config": {"workload": "lif_net: 4,194,304 neurons x fan-in 1024 (4.29e9 synapses)",
-                   "arm": "C restatement of sparsl's CpuParallel arm (Rust toolchain absent here)"},
+        "data": "synthetic (seeded ChaCha12 per row, drawn on the host from the workload definition)",
+        "config": {"workload": f"lif_net: {n_total:,} neurons x fan-in {fan_in} ({n_total * fan_in:.3g} synapses), "
+                               "f32 weights N(0,0.03^2), decay 0.95, theta 1.0, reset 0, Bernoulli(0.01) initial spikes",
+                   "arm": "C restatement of sparsl's CpuParallel arm (Rust toolchain absent here)",
+                   "setup_s": round(setup_s, 1)},
         "cpu_baseline": {"value": value, "unit": "ticks/s", "cores": O.num_threads(), "kind": "port",
                          "sample": desc},
         "e2e": {"value": value, "unit": "ticks/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "check": {"spike_trace_sum": int(full[args.warmup:].sum()), "trace_head": full[args.warmup:][:8].tolist(),
+                  f"trace_sha1_first_{full.size}_ticks": __import__("hashlib").sha1(full.tobytes()).hexdigest()[:16],
+                  "tick_s_min_median_max": [min(ts), sorted(ts)[len(ts) // 2], max(ts)]},
     }
 
 
@@ -1127,6 +1220,9 @@ def main():
     ap.add_argument("--net-n", type=int, default=None, help="neurons of the LIF network (default 4,194,304)")
     ap.add_argument("--net-fanin", type=int, default=None, help="fan-in of the LIF network (default 1024)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--check-ticks", type=int, default=32,
+                    help="LIF network: ticks compared bit for bit with the CPU (capped at warm-up + steps)")
+    ap.add_argument("--no-check", action="store_true", help="LIF network: skip the CPU comparison")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
     global SCAN_N, NET_N, NET_FANIN

@@ -427,6 +427,9 @@ int sparsl_net_trace(sparsl_net *net, uint32_t *out, uint64_t cap, uint64_t *n_o
 int sparsl_net_set_timing(sparsl_net *net, uint64_t max_ticks);
 /* Sum of those kernel durations over the ticks of the last steps call. */
 int sparsl_net_kernel_ms(sparsl_net *net, double *total_ms, uint64_t *ticks);
+/* The same durations per tick (ms): out[t] for the first min(cap, n) timed
+ * ticks of the last steps call; *n_out = the number timed. */
+int sparsl_net_tick_ms(sparsl_net *net, float *out, uint64_t cap, uint64_t *n_out);
 
 #ifdef __cplusplus
 }

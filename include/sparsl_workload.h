@@ -23,8 +23,11 @@ extern "C" {
 /* Fixed fan-in connectivity for rows [row0, row0 + nrows): row r receives
  * `fan_in` presynaptic indices gen_index(ncols) from its stream, sorted
  * ascending (duplicates kept, as multi-edges), written to col[(r-row0)*fan_in..];
- * weights N(0, sigma^2) by Box-Muller in f64 from two next_f64 draws of the
- * row's weight stream (seed ^ 0x5EED...) rounded to f32.  fan_in <= 4096. */
+ * weights N(0, sigma^2) by Box-Muller in f64 from two next_f64 draws (u1, u2)
+ * of the row's weight stream (seed ^ 0x5EED5EED5EED5EED) ^ (r * 0x9E37...),
+ * w = (float)(sigma * sqrt(-2 ln(1 - u1)) * cos(2 pi u2)), where ln and cos are
+ * fixed series of IEEE double operations (no libm), so a host restatement
+ * draws the same arrays bit for bit.  fan_in <= 4096. */
 int sparsl_workload_fixed_fanin(uint64_t seed, uint64_t row0, uint64_t nrows, uint64_t ncols,
                                 uint32_t fan_in, float sigma, uint32_t *col, float *weights,
                                 void *stream);

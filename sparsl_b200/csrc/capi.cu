@@ -2438,6 +2438,16 @@ int sparsl_net_kernel_ms(sparsl_net* net, double* total_ms, uint64_t* ticks) {
   return SPARSL_OK;
 }
 
+int sparsl_net_tick_ms(sparsl_net* net, float* out, uint64_t cap, uint64_t* n_out) {
+  if (!net) return fail(SPARSL_ERR_INVALID, "null net", "null net");
+  CK("net_tick_ms", cudaSetDevice(net->dev->ordinal));
+  CK("net_tick_ms", cudaStreamSynchronize(net->stream));
+  if (n_out) *n_out = net->timed_ticks;
+  const uint64_t n = std::min<uint64_t>(cap, net->timed_ticks);
+  for (uint64_t t = 0; t < n; ++t) CK("net_tick_ms", cudaEventElapsedTime(&out[t], net->ev_a[t], net->ev_b[t]));
+  return SPARSL_OK;
+}
+
 int sparsl_net_trace(sparsl_net* net, uint32_t* out, uint64_t cap, uint64_t* n_out) {
   ADMIT();
   CK("net_trace", cudaSetDevice(net->dev->ordinal));

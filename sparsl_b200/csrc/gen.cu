@@ -65,13 +65,91 @@ __device__ void chacha12(const Key& key, uint64_t counter, uint32_t out[16]) {
   for (int i = 0; i < 16; ++i) out[i] = x[i] + s[i];
 }
 
+// Box-Muller without libm: ln and cos come from fixed sequences of IEEE
+// double operations, so the host definition of this workload draws the same
+// weights bit for bit (this file is built with -fmad=false, so no step is
+// contracted into an FMA).
+//   ln x = e ln2 + 2 s (1 + s^2/3 + ... + s^24/25), x = m 2^e with
+//          m in (1/sqrt2, sqrt2], s = (m - 1)/(m + 1)  (atanh series);
+//   cos(2 pi u): 4u = q + r exactly, then sin / cos Taylor series through
+//          t^17 / t^18 at t = r pi/2 or (1 - r) pi/2 in [0, pi/4].
+// The series coefficients are IEEE quotients 1/(2k+1) and (-1)^k/n!, computed
+// on the host and passed in by value.
+struct GenCoeffs {
+  double inv_odd[13];
+  double sin_c[9];
+  double cos_c[10];
+};
+
+GenCoeffs make_coeffs() {
+  GenCoeffs c;
+  double fact[19];
+  fact[0] = 1.0;
+  for (int n = 1; n <= 18; ++n) fact[n] = fact[n - 1] * (double)n;  // exact below 2^53
+  for (int k = 0; k <= 12; ++k) c.inv_odd[k] = 1.0 / (double)(2 * k + 1);
+  for (int k = 0; k <= 8; ++k) c.sin_c[k] = (k & 1 ? -1.0 : 1.0) / fact[2 * k + 1];
+  for (int k = 0; k <= 9; ++k) c.cos_c[k] = (k & 1 ? -1.0 : 1.0) / fact[2 * k];
+  return c;
+}
+
+// ln x for normal x in (0, 1].
+__device__ double gen_log(const GenCoeffs& c, double x) {
+  unsigned long long b = (unsigned long long)__double_as_longlong(x);
+  int e = (int)((b >> 52) & 0x7ff) - 1023;
+  b = (b & 0x000fffffffffffffull) | 0x3ff0000000000000ull;
+  double m = __longlong_as_double((long long)b);
+  if (m > 1.4142135623730951) {
+    m = m * 0.5;
+    e += 1;
+  }
+  const double s = (m - 1.0) / (m + 1.0);
+  const double s2 = s * s;
+  double p = c.inv_odd[12];
+#pragma unroll
+  for (int k = 11; k >= 1; --k) p = c.inv_odd[k] + s2 * p;
+  const double poly = 1.0 + s2 * p;
+  return (double)e * 0.6931471805599453 + 2.0 * s * poly;
+}
+
+__device__ double gen_sin_t(const GenCoeffs& c, double t) {
+  const double t2 = t * t;
+  double p = c.sin_c[8];
+#pragma unroll
+  for (int k = 7; k >= 0; --k) p = c.sin_c[k] + t2 * p;
+  return t * p;
+}
+
+__device__ double gen_cos_t(const GenCoeffs& c, double t) {
+  const double t2 = t * t;
+  double p = c.cos_c[9];
+#pragma unroll
+  for (int k = 8; k >= 0; --k) p = c.cos_c[k] + t2 * p;
+  return p;
+}
+
+// cos(2 pi u) for u in [0, 1): +cos, -sin, -cos, +sin of pi r/2 for q = 0..3.
+__device__ double gen_cos2pi(const GenCoeffs& c, double u) {
+  const double half_pi = 1.5707963267948966;
+  const double t4 = 4.0 * u;
+  const int q = (int)t4;
+  const double r = t4 - (double)q;
+  double v;
+  if ((q & 1) == 0) {
+    v = r <= 0.5 ? gen_cos_t(c, r * half_pi) : gen_sin_t(c, (1.0 - r) * half_pi);
+    return q == 0 ? v : -v;
+  }
+  v = r <= 0.5 ? gen_sin_t(c, r * half_pi) : gen_cos_t(c, (1.0 - r) * half_pi);
+  return q == 1 ? -v : v;
+}
+
 constexpr int kGenWarps = 4;
 constexpr uint32_t kMaxFanIn = 4096;
 
 // One warp per row: draw, bitonic-sort, write; then the weights.
 __global__ void __launch_bounds__(kGenWarps * 32) fixed_fanin_kernel(uint64_t seed, uint64_t row0, uint64_t nrows,
                                                                     uint64_t ncols, uint32_t fan_in, uint32_t pow2,
-                                                                    float sigma, uint32_t* __restrict__ col,
+                                                                    float sigma, GenCoeffs coeffs,
+                                                                    uint32_t* __restrict__ col,
                                                                     float* __restrict__ weights) {
   extern __shared__ uint32_t sm[];
   const int lane = threadIdx.x & 31;
@@ -129,7 +207,7 @@ __global__ void __launch_bounds__(kGenWarps * 32) fixed_fanin_kernel(uint64_t se
           const uint64_t d1 = ((uint64_t)w[4 * k + 3] << 32) | w[4 * k + 2];
           const double u1 = (double)(d0 >> 11) * (1.0 / 9007199254740992.0);
           const double u2 = (double)(d1 >> 11) * (1.0 / 9007199254740992.0);
-          const double z = sqrt(-2.0 * log(1.0 - u1)) * cos(6.283185307179586 * u2);
+          const double z = sqrt(-2.0 * gen_log(coeffs, 1.0 - u1)) * gen_cos2pi(coeffs, u2);
           wo[i] = (float)((double)sigma * z);
         }
       }
@@ -183,8 +261,8 @@ extern "C" int sparsl_workload_fixed_fanin(uint64_t seed, uint64_t row0, uint64_
   cudaFuncSetAttribute(fixed_fanin_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const uint64_t blocks = (nrows + kGenWarps - 1) / kGenWarps;
   fixed_fanin_kernel<<<(unsigned)(blocks > 148ull * 64 ? 148ull * 64 : blocks), kGenWarps * 32, smem,
-                       static_cast<cudaStream_t>(stream)>>>(seed, row0, nrows, ncols, fan_in, pow2, sigma, col,
-                                                            weights);
+                       static_cast<cudaStream_t>(stream)>>>(seed, row0, nrows, ncols, fan_in, pow2, sigma,
+                                                            make_coeffs(), col, weights);
   return cudaGetLastError() == cudaSuccess ? 0 : 2;
 }
 

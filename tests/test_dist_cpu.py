@@ -112,3 +112,65 @@ def test_row_blocks_respect_the_u32_offset_limit(local, fan):
         assert off + n == nxt[0]
         assert n * fan <= 1 << 31
         assert off % 32 == 0
+
+
+# bench.py's CPU check of the sharded network: each rank draws its rows from
+# the workload definition, splits them into row blocks, and runs
+# bench.cpu_net_ticks (oracle ticks + gloo all-gather of the packed words).
+WL_N, WL_FAN, WL_SEED, WL_TICKS = 4096, 96, 0xC0FFEE, 6
+
+
+def _wl_rank_main(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import bench
+    import oracle as O
+
+    dist = bench.Dist()
+    try:
+        local = WL_N // world
+        row0 = rank * local
+        host = []
+        for off, k in ((0, local // 2), (local // 2, local - local // 2)):
+            col, w = O.wl_fixed_fanin(WL_SEED, row0 + off, k, WL_N, WL_FAN, 0.4)
+            rp = (np.arange(k + 1, dtype=np.uint64) * WL_FAN).astype(np.uint32)
+            host.append((rp, col, w, row0 + off))
+        v, th, s0 = O.wl_lif_state(WL_SEED ^ 1, 0, WL_N, 0.0, 1.0, 1.0, 0.05)
+        trace, vv, tt, pk, _ = bench.cpu_net_ticks(O, dist, host, WL_N, v[row0:row0 + local].copy(),
+                                                   th[row0:row0 + local].copy(), O.pack_spikes(s0), WL_TICKS)
+        q.put((rank, trace.tolist(), vv.tobytes(), tt.tobytes(), pk.tobytes()))
+    finally:
+        dist.close()
+
+
+def test_bench_cpu_check_over_two_ranks_matches_one_process():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_wl_rank_main, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=240) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    # One process: the whole network as one CSR, the reference's recurrent ticks.
+    col, w = O.wl_fixed_fanin(WL_SEED, 0, WL_N, WL_N, WL_FAN, 0.4)
+    rp = (np.arange(WL_N + 1, dtype=np.uint64) * WL_FAN).astype(np.uint32)
+    v, th, s0 = O.wl_lif_state(WL_SEED ^ 1, 0, WL_N, 0.0, 1.0, 1.0, 0.05)
+    xs = O.pack_spikes(s0)
+    want = O.recurrent_steps(O.Csr(rp, col, WL_N), w, xs, v, th, np.zeros(WL_N, np.uint8), 0.95, 0.0, 0.0, WL_TICKS,
+                             par=True)
+    assert want.sum() > 0, "the test network should spike"
+    local = WL_N // world
+    for rank, trace, vb, tb, pb in res:
+        assert trace == want.tolist()
+        assert np.frombuffer(vb, np.uint32).tolist() == v[rank * local:(rank + 1) * local].view(np.uint32).tolist()
+        assert np.frombuffer(tb, np.uint32).tolist() == th[rank * local:(rank + 1) * local].view(np.uint32).tolist()
+        assert np.frombuffer(pb, np.uint32).tolist() == xs.tolist()

@@ -64,9 +64,11 @@ def test_net_ticks_match_oracle_recurrent_steps(O, cuda_device, n, deg, splits):
 
 def test_workload_generator_matches_its_definition(O, cuda_device):
     """Row r's columns are gen_index(ncols) draws of ChaCha12 seeded with
-    seed ^ (r * 0x9E3779B97F4A7C15), sorted -- checked with the oracle's Rng."""
+    seed ^ (r * 0x9E3779B97F4A7C15), sorted -- checked with the oracle's Rng;
+    the whole (col, w) block and the LIF state equal the host definition
+    (oracle wl_*) bit for bit."""
     L = _lib.load()
-    seed, row0, nrows, ncols, fan_in = 0x1234, 77, 5, 1_000_003, 300
+    seed, row0, nrows, ncols, fan_in = 0x1234, 77, 300, 1_000_003, 300
     dcol = L.sparsl_device_alloc(cuda_device.handle, nrows * fan_in * 4)
     dw = L.sparsl_device_alloc(cuda_device.handle, nrows * fan_in * 4)
     try:
@@ -78,9 +80,54 @@ def test_workload_generator_matches_its_definition(O, cuda_device):
     finally:
         L.sparsl_device_free(dcol)
         L.sparsl_device_free(dw)
-    for i in range(nrows):
+    for i in range(5):
         r = row0 + i
         rng = O.Rng(seed ^ ((r * 0x9E3779B97F4A7C15) & (2 ** 64 - 1)))
         want = np.sort(np.array([rng.gen_index(ncols) for _ in range(fan_in)], np.uint32))
         assert np.array_equal(col[i * fan_in:(i + 1) * fan_in], want)
-    assert abs(float(w.std()) - 0.05) < 0.01 and abs(float(w.mean())) < 0.01
+    hcol, hw = O.wl_fixed_fanin(seed, row0, nrows, ncols, fan_in, 0.05)
+    assert np.array_equal(col, hcol)
+    assert_bits_equal(w, hw, "weights vs the host definition")
+    assert abs(float(w.std()) - 0.05) < 0.002 and abs(float(w.mean())) < 0.002
+
+
+@pytest.mark.parametrize("fan_in,ncols", [(1024, 4_194_304), (512, 262_144), (1, 7), (33, 1 << 31)])
+def test_workload_generator_bit_identical_to_host(O, cuda_device, fan_in, ncols):
+    L = _lib.load()
+    seed, row0, nrows = 0x5EED0005, 2_097_152 - 40, 96
+    n = nrows * fan_in
+    dcol = L.sparsl_device_alloc(cuda_device.handle, n * 4)
+    dw = L.sparsl_device_alloc(cuda_device.handle, n * 4)
+    try:
+        _check(L.sparsl_workload_fixed_fanin(seed, row0, nrows, ncols, fan_in, 0.03, dcol, dw, None))
+        col = np.zeros(n, np.uint32)
+        w = np.zeros(n, np.float32)
+        _check(L.sparsl_memcpy(col.ctypes.data, dcol, col.nbytes))
+        _check(L.sparsl_memcpy(w.ctypes.data, dw, w.nbytes))
+    finally:
+        L.sparsl_device_free(dcol)
+        L.sparsl_device_free(dw)
+    hcol, hw = O.wl_fixed_fanin(seed, row0, nrows, ncols, fan_in, 0.03)
+    assert np.array_equal(col, hcol)
+    assert_bits_equal(w, hw, "weights")
+
+
+def test_lif_state_generator_bit_identical_to_host(O, cuda_device):
+    L = _lib.load()
+    seed, cell0, n = 0x5EED0005 ^ 0x57A7E, 64, 100_000
+    dv = L.sparsl_device_alloc(cuda_device.handle, n * 4)
+    dt = L.sparsl_device_alloc(cuda_device.handle, n * 4)
+    dp = L.sparsl_device_alloc(cuda_device.handle, (n + 31) // 32 * 4)
+    try:
+        _check(L.sparsl_workload_lif_state(seed, cell0, n, 0.0, 1.0, 1.0, 0.01, dv, dt, dp, None))
+        v, t = np.zeros(n, np.float32), np.zeros(n, np.float32)
+        pk = np.zeros((n + 31) // 32, np.uint32)
+        for h, d in ((v, dv), (t, dt), (pk, dp)):
+            _check(L.sparsl_memcpy(h.ctypes.data, d, h.nbytes))
+    finally:
+        for d in (dv, dt, dp):
+            L.sparsl_device_free(d)
+    hv, ht, hs = O.wl_lif_state(seed, cell0, n, 0.0, 1.0, 1.0, 0.01)
+    assert_bits_equal(v, hv, "v")
+    assert_bits_equal(t, ht, "theta")
+    assert np.array_equal(pk, O.pack_spikes(hs))

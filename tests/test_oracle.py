@@ -200,3 +200,47 @@ def test_oracle_fused_matches_unfused_order(O, shape):
     assert_bits_equal(v2, v1)
     assert_bits_equal(t2, t1)
     assert np.array_equal(s1, s2)
+
+
+def test_workload_definition_series_and_streams(O):
+    """The benchmark workload's host definition: the ln / cos series agree
+    with libm to a few ulp, row streams are the reference Rng's, and the
+    multi-block network tick equals recurrent_steps on one CSR."""
+    import math
+
+    r = np.random.default_rng(3)
+    for u in r.random(2000):
+        x = 1.0 - u
+        assert abs(O.wl_log(x) - math.log(x)) <= 4e-16 * max(1.0, abs(math.log(x)))
+        assert abs(O.wl_cos2pi(u) - math.cos(2 * math.pi * u)) <= 2e-15
+    assert O.wl_log(1.0) == 0.0 and O.wl_cos2pi(0.0) == 1.0
+    seed, row0, nrows, ncols, fan = 0x77, 5, 4, 1 << 31, 100
+    col, w = O.wl_fixed_fanin(seed, row0, nrows, ncols, fan, 0.03)
+    for i in range(nrows):
+        rr = row0 + i
+        rng = O.Rng(seed ^ ((rr * 0x9E3779B97F4A7C15) & (2 ** 64 - 1)))
+        want = np.sort(np.array([rng.gen_index(ncols) for _ in range(fan)], np.uint32))
+        assert np.array_equal(col[i * fan:(i + 1) * fan], want)
+        wr = O.Rng((seed ^ 0x5EED5EED5EED5EED) ^ ((rr * 0x9E3779B97F4A7C15) & (2 ** 64 - 1)))
+        for k in range(fan):
+            u1, u2 = wr.next_f64(), wr.next_f64()
+            z = math.sqrt(-2.0 * O.wl_log(1.0 - u1)) * O.wl_cos2pi(u2)
+            assert np.float32(np.float64(np.float32(0.03)) * z) == w[i * fan + k]
+    v, th, sp = O.wl_lif_state(9, 32, 64, 0.0, 1.0, 1.0, 0.5)
+    for i in range(64):
+        rng = O.Rng(9 ^ (((32 + i) * 0x9E3779B97F4A7C15) & (2 ** 64 - 1)))
+        f0, f1 = rng.next_f32(), rng.next_f32()
+        assert v[i] == np.float32(f0) and sp[i] == (f1 < np.float32(0.5))
+    # multi-block ticks == one CSR's recurrent steps
+    n, fan = 2048, 40
+    col, w = O.wl_fixed_fanin(11, 0, n, n, fan, 0.5)
+    rp = (np.arange(n + 1, dtype=np.uint64) * fan).astype(np.uint32)
+    v0, t0, s0 = O.wl_lif_state(12, 0, n, 0.0, 1.0, 1.0, 0.05)
+    xs, v, t = O.pack_spikes(s0), v0.copy(), t0.copy()
+    want = O.recurrent_steps(O.Csr(rp, col, n), w, xs, v, t, np.zeros(n, np.uint8), 0.9, 0.0, 0.0, 7)
+    blocks = [((rp[:1025] - rp[0]).astype(np.uint32), col[:1024 * fan], w[:1024 * fan]),
+              ((rp[1024:] - rp[1024]).astype(np.uint32), col[1024 * fan:], w[1024 * fan:])]
+    xs2, v2, t2 = O.pack_spikes(s0), v0.copy(), t0.copy()
+    got = O.net_ticks(blocks, n, xs2, v2, t2, np.zeros(n, np.uint8), 0.9, 0.0, 0.0, 7)
+    assert got.tolist() == want.tolist() and want.sum() > 0
+    assert np.array_equal(v2.view(np.uint32), v.view(np.uint32)) and np.array_equal(xs2, xs)
