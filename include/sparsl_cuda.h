@@ -188,16 +188,18 @@ int sparsl_op_weight_precision(sparsl_op *op);    /* mod.rs:1582 */
  * reference counterpart). */
 enum {
   SPARSL_LAYOUT_ELL = 1,            /* uniform rows: TMA-streamed [nrows x L] */
+  SPARSL_LAYOUT_ROW_ORDER = 2,      /* skewed rows: row folds in descending-length order */
   SPARSL_LAYOUT_SLICED_REVERSE = 4, /* transpose: sliced-ELL reverse index */
   SPARSL_LAYOUT_CSC = 8             /* transpose: plain reverse index (hub columns) */
 };
 int sparsl_op_layouts(sparsl_op *op);
 /* Test and diagnostic hook, no reference counterpart: forget the operator's
- * uniform-row (TMA) layout so every later forward product runs on the
- * generic row-fold engine.  The engine choice at prepare stays a function of
- * the operator's shape alone; this only lets a caller compare both engines
- * on one operator.  Results are identical either way. */
-int sparsl_op_drop_uniform_layout(sparsl_op *op);
+ * uniform-row (TMA) layout and its descending-length row order, so every
+ * later forward product runs on the generic row-fold engine in natural row
+ * order.  The engine choice at prepare stays a function of the operator's
+ * shape alone; this only lets a caller compare the engines on one operator.
+ * Results are identical either way. */
+int sparsl_op_force_plain_row_fold(sparsl_op *op);
 /* Failure-detection test hooks, no reference counterpart.
  * sparsl_dev_test_expired_wait runs one look-back whose predecessor never
  * publishes: the device's bounded wait runs out (about 0.1 s), records the

@@ -78,7 +78,7 @@ SIGNATURES = {
     "sparsl_dev_scan_table_device": (i32, [vp, vp, u64, ctypes.POINTER(ctypes.c_uint32), vp]),
     "sparsl_dev_scan_settle_device": (i32, [vp, vp, u64, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(u64), vp]),
     "sparsl_op_layouts": (i32, [vp]),
-    "sparsl_op_drop_uniform_layout": (i32, [vp]),
+    "sparsl_op_force_plain_row_fold": (i32, [vp]),
     "sparsl_dev_test_expired_wait": (i32, [vp]),
     "sparsl_op_test_mark_canary": (i32, [vp]),
     "sparsl_dev_scan_publish_device": (i32, [vp, vp, u64, i32, ctypes.c_uint32, vp, vp]),

@@ -740,10 +740,10 @@ class SparseOp:
         """SPARSL_LAYOUT_* bits: the device layouts this operator holds."""
         return int(_lib.load().sparsl_op_layouts(self._h))
 
-    def drop_uniform_layout(self) -> None:
+    def force_plain_row_fold(self) -> None:
         """Route later forward products through the generic row-fold engine
         (a test hook that compares both engines on one operator)."""
-        _check(_lib.load().sparsl_op_drop_uniform_layout(self._h), "drop_uniform_layout")
+        _check(_lib.load().sparsl_op_force_plain_row_fold(self._h), "force_plain_row_fold")
 
     def has_transpose(self) -> bool:
         return bool(_lib.load().sparsl_op_has_transpose(self._h))

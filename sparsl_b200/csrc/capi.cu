@@ -364,6 +364,8 @@ struct sparsl_op {
   cudaEvent_t tick_ev = nullptr, done_ev[2] = {nullptr, nullptr};
   // SpMM work units (rows by descending length unless all rows are equal)
   DBuf spmm_order, spmm_units, spmm_ctr;
+  // Skewed row lengths: forward row folds also walk rows in spmm_order.
+  bool row_ordered = false;
   uint32_t spmm_nunits = 0, spmm_rows_per_unit = 1;
   // Row ranges of the host-buffer SpMM pipeline (empty: one launch): range k
   // is rows [range_row[k], range_row[k+1]) and units [range_unit[k],
@@ -437,6 +439,21 @@ RowLaunch fwd_launch(sparsl_op* op) {
 // Forward launches take the TMA-pipelined kernel when the operator's rows all
 // have the same length, the generic row-fold kernel otherwise.
 cudaError_t launch_fwd(sparsl_op* op, const RowLaunch& p, cudaStream_t s) {
+  if (!op->ell.ok && op->row_ordered && !p.eidx) {
+    // Skewed rows: warps fold rows in descending-length order; the packed
+    // spike words (and from them the index list) come from the spike bytes.
+    RowLaunch q = p;
+    q.order = op->spmm_order.as<uint32_t>();
+    q.out_bits = nullptr;
+    q.idx_list = nullptr;
+    q.idx_count = nullptr;
+    cudaError_t e = launch_rows(q, s);
+    if (e != cudaSuccess || !p.out_bits) return e;
+    const uint64_t words = ((uint64_t)p.nlines + 31) / 32;
+    e = launch_pack(p.spikes, p.nlines, p.out_bits, words, s);
+    if (e != cudaSuccess || !p.idx_list) return e;
+    return launch_compact_bits(p.out_bits, words, p.idx_list, p.idx_count, p.idx_base, s);
+  }
   if (!op->ell.ok) return launch_rows(p, s);
   if (!p.idx_list) return launch_ell(op->ell, p, s);
   if (p.out_bits && p.epilogue == EPI_LIF) {
@@ -1347,6 +1364,10 @@ int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int 
       };
       build(0, nrows, sp_order, sp_units);
       op->spmm_nunits = (uint32_t)(sp_units.size() - 1);
+      // Row folds take the descending-length order when a natural-order warp
+      // would often idle behind one long row: the longest row exceeds both
+      // one staging chunk and four times the mean (a function of the shape).
+      op->row_ordered = maxlen > 32 && (uint64_t)maxlen * nrows > 4 * (uint64_t)nnz;
       PALLOC(op->spmm_order, nrows * 4, false, "spmm row order");
       PALLOC(op->spmm_units, sp_units.size() * 4, false, "spmm units");
       cudaMemcpyAsync(op->spmm_order.p, sp_order.data(), nrows * 4, cudaMemcpyHostToDevice, op->stream);
@@ -1418,7 +1439,8 @@ int sparsl_op_shape(sparsl_op* op, sparsl_shape* out) {
 int sparsl_op_weight_precision(sparsl_op* op) { return op ? op->precision : -1; }
 int sparsl_op_layouts(sparsl_op* op) {
   if (!op) return 0;
-  return (op->ell.ok ? SPARSL_LAYOUT_ELL : 0) | (op->sell_ok ? SPARSL_LAYOUT_SLICED_REVERSE : 0) |
+  return (op->ell.ok ? SPARSL_LAYOUT_ELL : 0) | (op->row_ordered ? SPARSL_LAYOUT_ROW_ORDER : 0) |
+         (op->sell_ok ? SPARSL_LAYOUT_SLICED_REVERSE : 0) |
          (op->has_t && !op->sell_ok ? SPARSL_LAYOUT_CSC : 0);
 }
 int sparsl_op_has_transpose(sparsl_op* op) { return op && op->has_t ? 1 : 0; }
@@ -1436,13 +1458,14 @@ int sparsl_op_test_mark_canary(sparsl_op* op) {
   return finish(op, "test_mark_canary");
 }
 
-int sparsl_op_drop_uniform_layout(sparsl_op* op) {
-  if (!op) return fail(SPARSL_ERR_INVALID, "null argument", "sparsl_op_drop_uniform_layout: null operator");
+int sparsl_op_force_plain_row_fold(sparsl_op* op) {
+  if (!op) return fail(SPARSL_ERR_INVALID, "null argument", "sparsl_op_force_plain_row_fold: null operator");
   std::lock_guard<std::mutex> lk(op->mu);
   // The tensor maps are host-side descriptors over the operator's own col /
-  // weight arrays; clearing the flag is all it takes to route every later
-  // forward launch through the generic row fold.
+  // weight arrays; clearing the flags is all it takes to route every later
+  // forward launch through the generic row fold in natural row order.
   op->ell.ok = false;
+  op->row_ordered = false;
   return SPARSL_OK;
 }
 

@@ -6,7 +6,10 @@
 //   y[r] = y[r] + (((0 + w0*x0) + w1*x1) + ...)     (src/backend/mod.rs:2259-2267)
 // so one lane owns one line and a line is never split across lanes.
 //
-// Layout: a warp owns 32 consecutive lines.  Their CSR segments are staged
+// Layout: a warp owns 32 lines -- 32 consecutive lines, or, for operators
+// with skewed row lengths, 32 consecutive entries of the rows-by-descending-
+// length order, so a warp's lanes fold rows of similar length and the
+// longest rows start first.  Their CSR segments are staged
 // chunk by chunk (kChunk entries per line) into a padded shared-memory tile by
 // coalesced loads -- one 128-byte load per line per array -- and each lane
 // then folds its own line out of shared memory.  The padding (stride kChunk+1)
@@ -27,7 +30,7 @@ struct WarpStage {
   uint32_t len[32];
 };
 
-template <int WK, int XM, bool CSC, int EPI, bool COMPACT>
+template <int WK, int XM, bool CSC, int EPI, bool COMPACT, bool ORDERED = false>
 __global__ void __launch_bounds__(kRowWarps * 32) row_fold_kernel(const RowLaunch p) {
   extern __shared__ __align__(16) unsigned char smem[];
   __shared__ uint32_t s_tile, s_base, s_last;
@@ -60,8 +63,11 @@ __global__ void __launch_bounds__(kRowWarps * 32) row_fold_kernel(const RowLaunc
   }
 
   const uint32_t line0 = tile * kRowLines + wid * 32;
-  const uint32_t line = line0 + lane;
+  uint32_t line = line0 + lane;
   const bool valid = line < p.nlines;
+  if constexpr (ORDERED) {
+    if (valid) line = __ldg(p.order + line);
+  }
   uint32_t start = 0, len = 0;
   if (valid) {
     start = __ldg(p.ptr + line);
@@ -128,8 +134,9 @@ __global__ void __launch_bounds__(kRowWarps * 32) row_fold_kernel(const RowLaunc
     }
     // Lane i of the ballot is line 32w+i: exactly the LSB-first packing of
     // src/spikes.rs:237-262, with tail bits of a partial word left zero.
+    // (Ordered launches leave packing to a pass over the spike bytes.)
     const uint32_t ballot = __ballot_sync(0xffffffffu, spike);
-    if (p.out_bits && lane == 0 && line0 < p.nlines) p.out_bits[line0 >> 5] = ballot;
+    if (!ORDERED && p.out_bits && lane == 0 && line0 < p.nlines) p.out_bits[line0 >> 5] = ballot;
 
     if constexpr (COMPACT) {
       const uint32_t ntiles = row_tiles(p.nlines);
@@ -166,9 +173,9 @@ __global__ void __launch_bounds__(kRowWarps * 32) row_fold_kernel(const RowLaunc
   }
 }
 
-template <int WK, int XM, bool CSC, int EPI, bool COMPACT>
+template <int WK, int XM, bool CSC, int EPI, bool COMPACT, bool ORDERED = false>
 cudaError_t launch_t(const RowLaunch& p, cudaStream_t stream) {
-  auto kern = row_fold_kernel<WK, XM, CSC, EPI, COMPACT>;
+  auto kern = row_fold_kernel<WK, XM, CSC, EPI, COMPACT, ORDERED>;
   const size_t bits_bytes = (XM == X_BITS_SMEM) ? (((size_t)p.xbits_words * 4 + 15) & ~(size_t)15) : 0;
   const size_t smem = bits_bytes + sizeof(WarpStage) * kRowWarps;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -182,6 +189,20 @@ template <int WK>
 cudaError_t dispatch_x(const RowLaunch& p, cudaStream_t s) {
   const bool csc = p.eidx != nullptr;
   const bool compact = p.idx_list != nullptr;
+  if (p.order && !csc && !compact) {
+    if (p.epilogue == EPI_ACCUM) {
+      switch (p.xmode) {
+        case X_DENSE: return launch_t<WK, X_DENSE, false, EPI_ACCUM, false, true>(p, s);
+        case X_BITS_SMEM: return launch_t<WK, X_BITS_SMEM, false, EPI_ACCUM, false, true>(p, s);
+        default: return launch_t<WK, X_BITS_GLOBAL, false, EPI_ACCUM, false, true>(p, s);
+      }
+    }
+    switch (p.xmode) {
+      case X_DENSE: return launch_t<WK, X_DENSE, false, EPI_LIF, false, true>(p, s);
+      case X_BITS_SMEM: return launch_t<WK, X_BITS_SMEM, false, EPI_LIF, false, true>(p, s);
+      default: return launch_t<WK, X_BITS_GLOBAL, false, EPI_LIF, false, true>(p, s);
+    }
+  }
   if (p.epilogue == EPI_ACCUM) {
     if (csc) return launch_t<WK, X_DENSE, true, EPI_ACCUM, false>(p, s);
     switch (p.xmode) {

@@ -33,6 +33,11 @@ struct RowLaunch {
   const uint32_t* xbits = nullptr; // spike operand
   uint32_t xbits_words = 0;
   uint32_t nlines = 0;
+  // Optional line order (CSR rows by descending length, ties by index): warp
+  // slot k folds line order[k], so the 32 lines of a warp have similar
+  // lengths and no lane idles behind a long neighbour.  Packed spike words,
+  // compaction and the transpose are not produced by ordered launches.
+  const uint32_t* order = nullptr;
   int xmode = X_DENSE;
   int epilogue = EPI_ACCUM;
   float* y = nullptr;              // EPI_ACCUM output

@@ -21,7 +21,7 @@ def _uniform(O, nrows, ncols, L, seed):
 def _prepare(dev, csr, w, precision, generic):
     op = dev.prepare_with(S.Csr(csr.row_ptr, csr.col, csr.ncols), csr.ncols, w, precision)
     if generic:
-        op.drop_uniform_layout()
+        op.force_plain_row_fold()
         assert not op.layouts() & 1
     return op
 

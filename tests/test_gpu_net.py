@@ -26,10 +26,22 @@ def _make_net(dev, ops, row0, n):
     return h
 
 
-@pytest.mark.parametrize("n,deg,splits", [(4096, 64, [2048, 2048]), (6016, 200, [1024, 32, 4960])])
+def _skewed_csr(O, n, seed):
+    r = np.random.default_rng(seed)
+    lens = np.minimum(r.zipf(1.5, n), 1200)
+    lens[n // 2] = 1200
+    rp = np.zeros(n + 1, np.uint64)
+    np.cumsum(lens, out=rp[1:])
+    col = np.concatenate([np.sort(r.choice(n, k, replace=False)) for k in lens]).astype(np.uint32)
+    return O.Csr(rp.astype(np.uint32), col, n)
+
+
+@pytest.mark.parametrize("n,deg,splits", [(4096, 64, [2048, 2048]), (6016, 200, [1024, 32, 4960]),
+                                          (8192, 0, [4096, 4096])])
 def test_net_ticks_match_oracle_recurrent_steps(O, cuda_device, n, deg, splits):
     rng = O.Rng(0xE7 + n)
-    csr = O.random_csr(n, n, deg, rng)
+    # deg 0: power-law rows, whose blocks fold in descending-length order
+    csr = O.random_csr(n, n, deg, rng) if deg else _skewed_csr(O, n, n)
     w = O.random_vec(csr.nnz, 0.5, rng)
     v0 = O.random_vec(n, 1.0, rng)
     t0 = np.full(n, 0.45, np.float32)

@@ -521,3 +521,87 @@ def test_spmm_row_range_pipeline_bit_exact(O, cuda_device, kind, n_vec):
     assert_bits_equal(dy.cpu().numpy(), want, "device entry point, one launch")
     op.spmm(X, n_vec, got)  # again: the unit counters rewound after every range
     assert_bits_equal(got, O.spmm(csr, w, X, n_vec, want.copy()), "second call")
+
+
+def _skewed(O, nrows, ncols, seed, cap=3000):
+    """Zipf(1.5) row lengths clipped to [0, cap], a few empty rows and one hub
+    row of `cap` entries: the shape that takes the descending-length order."""
+    r = np.random.default_rng(seed)
+    lens = np.minimum(r.zipf(1.5, nrows), cap)
+    lens[::53] = 0
+    lens[nrows // 3] = cap
+    rp = np.zeros(nrows + 1, np.uint64)
+    np.cumsum(lens, out=rp[1:])
+    col = np.concatenate([np.sort(r.choice(ncols, k, replace=False)) for k in lens]).astype(np.uint32)
+    return O.Csr(rp.astype(np.uint32), col, ncols), r
+
+
+@pytest.mark.parametrize("precision", [S.WeightPrecision.F32, S.WeightPrecision.F16, S.WeightPrecision.Bf16])
+@pytest.mark.parametrize("nrows,ncols", [(5000, 6000), (40000, 700_000)])
+def test_skewed_rows_take_the_length_order_bit_exact(O, cuda_device, precision, nrows, ncols):
+    """Power-law rows fold in descending-length order (warps of similar
+    rows); every product still equals the reference's per-row left fold, and
+    the natural-order engine on the same operator."""
+    csr, r = _skewed(O, nrows, ncols, nrows + int(precision))
+    w = r.uniform(-1, 1, csr.nnz).astype(np.float32)
+    wq = O.quantise(int(precision), w)
+    op = cuda_device.prepare_with(_scsr(csr), ncols, w, precision)
+    assert op.layouts() & 2, "skewed rows should take the descending-length order"
+    plain = cuda_device.prepare_with(_scsr(csr), ncols, w, precision)
+    plain.force_plain_row_fold()
+    assert not plain.layouts() & 2
+    x = r.uniform(-1, 1, ncols).astype(np.float32)
+    y0 = r.uniform(-1, 1, nrows).astype(np.float32)
+    y0[::7] = -0.0
+    got, ref = y0.copy(), y0.copy()
+    op.spmv(x, got)
+    plain.spmv(x, ref)
+    want = O.spmv(csr, wq, x, y0.copy())
+    assert_bits_equal(got, want, "spmv")
+    assert_bits_equal(ref, want, "spmv, natural order")
+    pk = O.pack_spikes((r.random(ncols) < 0.2).astype(np.uint8))
+    got = y0.copy()
+    op.spmv_spikes(pk, got)
+    assert_bits_equal(got, O.spmv_spikes(csr, wq, pk, y0.copy()), "spmv_spikes")
+    v0 = r.uniform(-1, 1, nrows).astype(np.float32)
+    t0 = np.abs(r.uniform(0, 1, nrows)).astype(np.float32)
+    v, t, sp = v0.copy(), t0.copy(), np.zeros(nrows, np.bool_)
+    op.fused_spmv_lif(x, v, t, sp, PARAMS)
+    vw, tw, sw = v0.copy(), t0.copy(), np.zeros(nrows, np.uint8)
+    O.fused_lif(csr, wq, x, vw, tw, sw, 0.9, 0.0, 0.1)
+    assert_bits_equal(v, vw, "fused v")
+    assert_bits_equal(t, tw, "fused theta")
+    assert np.array_equal(sp.astype(np.uint8), sw)
+    v, t, sp = v0.copy(), t0.copy(), np.zeros(nrows, np.bool_)
+    op.fused_spmv_spikes_lif(pk, v, t, sp, PARAMS)
+    vw, tw, sw = v0.copy(), t0.copy(), np.zeros(nrows, np.uint8)
+    O.fused_spikes_lif(csr, wq, pk, vw, tw, sw, 0.9, 0.0, 0.1)
+    assert_bits_equal(v, vw, "fused spikes v")
+    assert np.array_equal(sp.astype(np.uint8), sw)
+
+
+@pytest.mark.parametrize("n", [3000, 70_001])
+def test_skewed_recurrent_ticks_pack_and_compact_bit_exact(O, cuda_device, n):
+    """Recurrent ticks on a square skewed operator: the ordered fold, then the
+    packing and the index list from the spike bytes."""
+    csr, r = _skewed(O, n, n, n, cap=1500)
+    w = (r.standard_normal(csr.nnz) * 0.3).astype(np.float32)
+    v0 = r.uniform(0, 1, n).astype(np.float32)
+    t0 = np.full(n, 0.5, np.float32)
+    xs0 = O.pack_spikes((r.random(n) < 0.1).astype(np.uint8))
+    op = cuda_device.prepare(_scsr(csr), n, w)
+    assert op.layouts() & 2
+    op.write_x_spikes(xs0)
+    op.write_lif_state(v0, t0)
+    steps = 12
+    op.fused_spmv_spikes_lif_recurrent_steps(S.LifParams.new(0.95, 0.0, 0.0), steps)
+    vw, tw, sw, xw = v0.copy(), t0.copy(), np.zeros(n, np.uint8), xs0.copy()
+    trace_w = O.recurrent_steps(csr, w, xw, vw, tw, sw, 0.95, 0.0, 0.0, steps)
+    assert trace_w.sum() > 0
+    assert np.array_equal(op.spike_trace(), trace_w)
+    v, t, sp = np.zeros(n, np.float32), np.zeros(n, np.float32), np.zeros(n, np.bool_)
+    op.sync_lif_state(v, t, sp)
+    assert_bits_equal(v, vw)
+    assert_bits_equal(t, tw)
+    assert np.array_equal(op.sync_x_spikes(), xw)
+    assert np.array_equal(op.spike_indices(), np.flatnonzero(sw).astype(np.uint32))
