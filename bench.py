@@ -78,6 +78,24 @@ def peaks():
     return PEAKS_FALLBACK, "fallback"
 
 
+# DRAM traffic per algorithmic byte of each workload's dominant kernel, from
+# ncu captures (dram__bytes_read.sum + dram__bytes_write.sum of one launch
+# over the launch's algorithmic bytes), keyed by workload.
+TRAFFIC_RATIO = {}
+
+
+def roofline(algo_bytes, ms, kernel, key=None):
+    """The roofline block of a workload line: algorithmic bytes per launch over
+    the launch's event-timed duration, against the measured HBM copy peak."""
+    pk_, how = peaks()
+    peak = float(pk_.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
+    achieved = algo_bytes / (ms * 1e-3) / 1e9
+    ratio = TRAFFIC_RATIO.get(key)
+    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "traffic": algo_bytes * ratio[0] if ratio else None,
+            "traffic_source": ratio[1] if ratio else None, "kernel": kernel, "peak_source": how}
+
+
 # --------------------------------------------------------------------------
 # process plumbing
 # --------------------------------------------------------------------------
@@ -675,12 +693,14 @@ def bench_spmv(args, dev, want_cpu):
             want_fn(ref)
         ok_ = bool(np.array_equal(dyy.cpu().numpy().view(np.uint32), ref.view(np.uint32)))
         return {"value": algo_ / (ms_ * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms_, "algorithmic_bytes": algo_,
-                "bit_exact_vs_oracle": ok_}
+                "bit_exact_vs_oracle": ok_}, ms_
 
     op16 = dev.prepare_with(S.Csr(rp, col, SPMV_N), SPMV_N, w, S.WeightPrecision.F16)
     w16 = O.quantise(int(S.WeightPrecision.F16), w)
     algo16 = col.size * 6 + (SPMV_N + 1) * 4 + SPMV_N * 4 + 2 * SPMV_N * 4
-    f16 = measure(op16, L.sparsl_op_spmv_device, dx, SPMV_N, algo16, lambda ref: O.spmv(csr, w16, x, ref, par=True))
+    f16, ms16 = measure(op16, L.sparsl_op_spmv_device, dx, SPMV_N, algo16,
+                        lambda ref: O.spmv(csr, w16, x, ref, par=True))
+    f16["roofline"] = roofline(algo16, ms16, "ell_stream_kernel<f16 weights, dense x>", "spmv_f16")
     del op16
     opt = dev.prepare_with_transpose(S.Csr(rp, col, SPMV_N), SPMV_N, w)
     xt = r.uniform(0.0, 1.0, SPMV_N).astype(np.float32)
@@ -689,8 +709,10 @@ def bench_spmv(args, dev, want_cpu):
     # CSC walk: row index + weight (kept in reverse-index order) per entry, x
     # gathered by row; col_ptr, x and y once.
     algot = col.size * 8 + (SPMV_N + 1) * 4 + SPMV_N * 4 + 2 * SPMV_N * 4
-    tr = measure(opt, L.sparsl_op_spmv_t_device, dxt, SPMV_N, algot,
-                 lambda ref: O.spmv_t(csc, w, xt, ref, par=True))
+    tr, mst = measure(opt, L.sparsl_op_spmv_t_device, dxt, SPMV_N, algot,
+                      lambda ref: O.spmv_t(csc, w, xt, ref, par=True))
+    tr["roofline"] = roofline(algot, mst, "sell_fold_kernel (transpose over the sliced-ELL reverse index)",
+                              "spmv_t")
     del opt
     # The reverse index itself, built on the GPU from device arrays (gate
     # included; wall clock of the blocking C-ABI call) against the oracle's
@@ -721,6 +743,7 @@ def bench_spmv(args, dev, want_cpu):
             "e2e": {"value": algo / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 2 * SPMV_N * 4,
                     "d2h_bytes_per_step": SPMV_N * 4, "path": "sparsl_op_spmv, pinned host x/y"},
             "bit_exact_vs_oracle": exact, "cpu_baseline": cpu,
+            "roofline": roofline(algo, ms, "ell_stream_kernel<f32, dense x>", "spmv"),
             "f16_weights": f16, "transpose": tr, "reverse_index": rev}
 
 
@@ -947,6 +970,7 @@ def bench_scan(args, dev, want_cpu):
             "repair": {"elements_replayed": rep, "segments": seg},
             "e2e": {"value": algo / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 8 * SCAN_N,
                     "d2h_bytes_per_step": 8 * SCAN_N, "path": "sparsl_dev_assoc_scan, pinned host"},
+            "roofline": roofline(algo, ms, "scan_main + scan_check (+ scan_repair)", "scan"),
             "bit_exact_vs_oracle": exact, "cpu_baseline": cpu}
 
 
@@ -1027,7 +1051,8 @@ def bench_spmm(args, dev, want_cpu):
         ms = statistics.median(ts)
         algo = nnz * (4 + wb) + (n + 1) * 4 + n * nv * 4 + 2 * n * nv * 4
         out[tag] = {"value": algo / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms, "algorithmic_bytes": algo,
-                    "bit_exact_vs_oracle": exact}
+                    "bit_exact_vs_oracle": exact,
+                    "roofline": roofline(algo, ms, f"SpMM kernels ({tag} weights; compulsory bytes)", "spmm_" + tag)}
         if tag == "f32":
             hx, hy = Pinned(np.float32, n * nv), Pinned(np.float32, n * nv)
             hx.a[:] = x.reshape(-1)
@@ -1041,6 +1066,8 @@ def bench_spmm(args, dev, want_cpu):
             out[tag]["e2e"] = {"value": algo / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
                                "h2d_bytes_per_step": 2 * n * nv * 4, "d2h_bytes_per_step": n * nv * 4,
                                "path": "sparsl_op_spmm, pinned host X/Y"}
+        if tag == "f32":
+            ragged, rtick = bench_ragged(args, op, csr, w, s, flush)
         del op
     cpu = None
     if want_cpu:
@@ -1054,8 +1081,81 @@ def bench_spmm(args, dev, want_cpu):
                       f"(realised nnz {nnz:,}, mean {nnz / n:.1f}), distinct sorted uniform cols, w U[-1,1], "
                       f"X {n:,} x {nv} row-major U[-1,1]; L2 flushed (1 GiB written, then read back) before every launch",
             "setup_s": round(setup_s, 1), "e2e": f32.get("e2e"),
-            "bit_exact_vs_oracle": f32["bit_exact_vs_oracle"], "f16": out["f16"],
-            "cpu_baseline": cpu}
+            "bit_exact_vs_oracle": f32["bit_exact_vs_oracle"], "roofline": f32["roofline"], "f16": out["f16"],
+            "cpu_baseline": cpu, "ragged_spmv": ragged, "ragged_lif_tick": rtick}
+
+
+def bench_ragged(args, op, csr, w, s, flush):
+    """SpMV and the recurrent fused spike-LIF tick over the config-4 power-law
+    matrix (n_vec = 1): the row fold in descending-length order.  Bit-exact
+    against the oracle; the tick's CPU arm is timed on the same ticks."""
+    import torch
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    L = lib()
+    n, nnz = csr.nrows, csr.nnz
+    r = np.random.default_rng(SPMM_SEED ^ 0x5A)
+    x = r.uniform(0.0, 1.0, n).astype(np.float32)
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.zeros(n, dtype=torch.float32, device="cuda")
+    run = lambda: check(L.sparsl_op_spmv_device(op.handle, dx.data_ptr(), dy.data_ptr(), s.cuda_stream), "spmv")
+    for _ in range(args.warmup):
+        run()
+    dy.zero_()
+    ts = time_launches(s, run, args.kernel_iters, flush=lambda: flush_l2(flush))
+    ms = statistics.median(ts)
+    want = np.zeros(n, np.float32)
+    for _ in range(args.kernel_iters):
+        O.spmv(csr, w, x, want, par=True)
+    exact = bool(np.array_equal(dy.cpu().numpy().view(np.uint32), want.view(np.uint32)))
+    algo = nnz * 8 + (n + 1) * 4 + n * 4 + 2 * n * 4
+    spmv = {"metric": "ragged SpMV effective HBM GB/s", "value": algo / (ms * 1e-3) / 1e9, "unit": "GB/s",
+            "ms_per_step": ms, "algorithmic_bytes": algo, "bit_exact_vs_oracle": exact,
+            "config": f"the SpMM matrix ({n:,} rows, {nnz:,} nnz, Zipf(1.5) lengths) times a dense x U[0,1]; "
+                      "L2 flushed before every launch",
+            "roofline": roofline(algo, ms, "row_fold_kernel<f32, dense x, descending-length order>", "ragged_spmv")}
+    # Recurrent ticks (fused spike SpMV + LIF + packing + index list), timed
+    # from the initial state; the timed ticks are checked against the CPU.
+    ticks = 20
+    v0 = r.uniform(0.0, 1.0, n).astype(np.float32)
+    th0 = np.full(n, 1.0, np.float32)
+    pk0 = O.pack_spikes((r.random(n) < 0.02).astype(np.uint8))
+    wt = (w * np.float32(0.05)).astype(np.float32)  # a network that neither dies out nor saturates
+    # (the caller destroys the operator right after, so its weights stay scaled)
+    check(L.sparsl_op_set_weights(op.handle, wt.ctypes.data, wt.size), "set_weights")
+    opx = lambda a: a.ctypes.data
+    for _ in range(2):
+        check(L.sparsl_op_write_x_spikes(op.handle, opx(pk0), pk0.size), "write spikes")
+        check(L.sparsl_op_write_lif_state(op.handle, opx(v0), opx(th0), n), "write state")
+        st = L.sparsl_op_stream(op.handle)
+        tms = events_ms(st, torch.cuda.current_device(),
+                        lambda: check(L.sparsl_op_recurrent_steps_async(op.handle, 0.95, 0.0, 0.0, ticks), "ticks"))
+        check(L.sparsl_op_wait(op.handle), "wait")
+    trace = np.zeros(ticks, np.uint32)
+    cnt = ctypes.c_uint64()
+    check(L.sparsl_op_spike_trace(op.handle, trace.ctypes.data, ticks, ctypes.byref(cnt)), "trace")
+    vg, tg, sg = np.zeros(n, np.float32), np.zeros(n, np.float32), np.zeros(n, np.uint8)
+    check(L.sparsl_op_sync_lif_state(op.handle, opx(vg), opx(tg), opx(sg), n), "sync state")
+    vw, tw, sw, xw = v0.copy(), th0.copy(), np.zeros(n, np.uint8), pk0.copy()
+    t0 = time.perf_counter()
+    trace_w = O.recurrent_steps(csr, wt, xw, vw, tw, sw, 0.95, 0.0, 0.0, ticks, par=True)
+    cpu_s = time.perf_counter() - t0
+    ok = bool(np.array_equal(trace, trace_w) and np.array_equal(vg.view(np.uint32), vw.view(np.uint32))
+              and np.array_equal(sg, sw))
+    per = tms / ticks
+    talgo = nnz * 8 + (n + 1) * 4 + 2 * n * 4 + n * 4 + 2 * n // 8
+    tick = {"metric": "ragged LIF ticks/sec", "value": 1e3 / per, "unit": "ticks/s", "ms_per_step": per,
+            "ticks": ticks, "algorithmic_bytes_per_tick": talgo, "spike_trace": trace.tolist(),
+            "bit_exact_vs_oracle": ok,
+            "config": f"the SpMM matrix as a recurrent network (weights x 0.05), decay 0.95, theta 1, reset 0, "
+                      "Bernoulli(0.02) initial spikes",
+            "roofline": roofline(talgo, per, "row_fold_kernel<f32, spike bitmask, LIF, descending-length order> + "
+                                             "pack_kernel + compact_bits_kernel", "ragged_tick"),
+            "cpu_baseline": {"value": ticks / cpu_s, "unit": "ticks/s", "cores": O.num_threads(), "kind": "port",
+                             "sample": f"the same {ticks} ticks (the parity check), CpuParallel restatement"}}
+    return spmv, tick
 
 
 def bench_lif(args, dev, want_cpu):
@@ -1139,6 +1239,8 @@ def bench_lif(args, dev, want_cpu):
             "e2e": {"value": e2e_steps / (e2e_ms * 1e-3), "unit": "ticks/s",
                     "h2d_bytes_per_step": n // 8 + 8 * n, "d2h_bytes_per_step": 9 * n,
                     "path": "sparsl_op_fused_spikes_lif per tick + host repack, pinned host"},
+            "roofline": roofline(algo, per_tick, "ell_stream_kernel<f32, spike bitmask in shared memory, LIF> + "
+                                                 "compact_bits_kernel (side stream)", "lif"),
             "bit_exact_vs_oracle": exact, "checked_ticks": ticks, "cpu_baseline": cpu}
 
 

@@ -364,8 +364,11 @@ struct sparsl_op {
   cudaEvent_t tick_ev = nullptr, done_ev[2] = {nullptr, nullptr};
   // SpMM work units (rows by descending length unless all rows are equal)
   DBuf spmm_order, spmm_units, spmm_ctr;
-  // Skewed row lengths: forward row folds also walk rows in spmm_order.
+  // Skewed row lengths: forward row folds walk rows in row_order (rows of
+  // 32 or more entries by descending length, then the rest in index order).
   bool row_ordered = false;
+  DBuf row_order;
+
   uint32_t spmm_nunits = 0, spmm_rows_per_unit = 1;
   // Row ranges of the host-buffer SpMM pipeline (empty: one launch): range k
   // is rows [range_row[k], range_row[k+1]) and units [range_unit[k],
@@ -443,7 +446,7 @@ cudaError_t launch_fwd(sparsl_op* op, const RowLaunch& p, cudaStream_t s) {
     // Skewed rows: warps fold rows in descending-length order; the packed
     // spike words (and from them the index list) come from the spike bytes.
     RowLaunch q = p;
-    q.order = op->spmm_order.as<uint32_t>();
+    q.order = op->row_order.as<uint32_t>();
     q.out_bits = nullptr;
     q.idx_list = nullptr;
     q.idx_count = nullptr;
@@ -1368,6 +1371,19 @@ int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int 
       // would often idle behind one long row: the longest row exceeds both
       // one staging chunk and four times the mean (a function of the shape).
       op->row_ordered = maxlen > 32 && (uint64_t)maxlen * nrows > 4 * (uint64_t)nnz;
+      if (op->row_ordered) {
+        // Rows of a staging chunk or more (32 entries), longest first, then
+        // the shorter rows in their natural order, so runs of consecutive
+        // short rows keep coalesced loads and stores.
+        std::vector<uint32_t> ro;
+        ro.reserve(nrows);
+        for (uint64_t i = 0; i < nrows && len(sp_order[i]) >= 32; ++i) ro.push_back(sp_order[i]);
+        for (uint64_t r = 0; r < nrows; ++r)
+          if (len(r) < 32) ro.push_back((uint32_t)r);
+        PALLOC(op->row_order, nrows * 4, false, "row order");
+        cudaMemcpyAsync(op->row_order.p, ro.data(), nrows * 4, cudaMemcpyHostToDevice, op->stream);
+        cudaStreamSynchronize(op->stream);
+      }
       PALLOC(op->spmm_order, nrows * 4, false, "spmm row order");
       PALLOC(op->spmm_units, sp_units.size() * 4, false, "spmm units");
       cudaMemcpyAsync(op->spmm_order.p, sp_order.data(), nrows * 4, cudaMemcpyHostToDevice, op->stream);
@@ -1407,7 +1423,8 @@ void sparsl_op_destroy(sparsl_op* op) {
                   &op->rx,      &op->rxs[0],  &op->rxs[1],  &op->ry,      &op->rv,      &op->rth,
                   &op->rspk,    &op->idx_list, &op->tile_flags, &op->ticket, &op->trace, &op->sx,
                   &op->sbits,   &op->sy,      &op->sv,      &op->sth,     &op->sspk,
-                  &op->spmm_order, &op->spmm_units, &op->spmm_ctr, &op->spmm_rorder, &op->spmm_runits};
+                  &op->spmm_order, &op->spmm_units, &op->spmm_ctr, &op->spmm_rorder, &op->spmm_runits,
+                  &op->row_order};
   for (DBuf* b : bufs) dfree(*b);
   op->err.release();
   if (op->side) cudaStreamSynchronize(op->side);

@@ -26,9 +26,23 @@ constexpr int kStride = kChunk + 1;
 struct WarpStage {
   uint32_t idx[32][kStride];
   float w[32][kStride];
-  uint32_t start[32];
-  uint32_t len[32];
 };
+
+// f32 CSR launches stage chunks asynchronously into two buffers per warp.
+#ifndef SPARSL_ROWS_ASYNC
+#define SPARSL_ROWS_ASYNC 1
+#endif
+template <int WK, bool CSC>
+constexpr bool kAsyncStage = SPARSL_ROWS_ASYNC && WK == W_F32 && !CSC;
+
+// 4-byte asynchronous global -> shared copy; a false `ok` zero-fills the
+// destination and reads nothing.
+template <typename T>
+__device__ __forceinline__ void cp_async4(T* dst, const T* src, bool ok) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  const uint32_t n = ok ? 4u : 0u;
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(d), "l"(src), "r"(n) : "memory");
+}
 
 template <int WK, int XM, bool CSC, int EPI, bool COMPACT, bool ORDERED = false>
 __global__ void __launch_bounds__(kRowWarps * 32) row_fold_kernel(const RowLaunch p) {
@@ -39,6 +53,7 @@ __global__ void __launch_bounds__(kRowWarps * 32) row_fold_kernel(const RowLaunc
   const int wid = threadIdx.x >> 5;
   uint32_t* s_bits = reinterpret_cast<uint32_t*>(smem);
   const size_t bits_bytes = (XM == X_BITS_SMEM) ? (((size_t)p.xbits_words * 4 + 15) & ~(size_t)15) : 0;
+  // Stage buffers: [buffer][warp]; two buffers for asynchronous staging.
   WarpStage* st = reinterpret_cast<WarpStage*>(smem + bits_bytes) + wid;
 
   uint32_t tile;
@@ -73,43 +88,96 @@ __global__ void __launch_bounds__(kRowWarps * 32) row_fold_kernel(const RowLaunc
     start = __ldg(p.ptr + line);
     len = __ldg(p.ptr + line + 1) - start;
   }
-  st->start[lane] = start;
-  st->len[lane] = len;
   const uint32_t maxlen = __reduce_max_sync(0xffffffffu, len);
-  __syncwarp();
 
+  // The lane's operand value for entry column c (spikes are multiplied as
+  // 0.0 / 1.0, never branched on).
+  auto operand = [&](uint32_t c) -> float {
+    if constexpr (XM == X_DENSE) {
+      return __ldg(p.x + c);
+    } else if constexpr (XM == X_BITS_SMEM) {
+      return (float)((s_bits[c >> 5] >> (c & 31)) & 1u);
+    } else {
+      return (float)((__ldg(p.xbits + (c >> 5)) >> (c & 31)) & 1u);
+    }
+  };
+  // Fold the lane's own entries of one staged chunk: every operand gather
+  // first, then the dependent add chain in entry order.
   float sum = 0.0f;
-  for (uint32_t k = 0; k < maxlen; k += kChunk) {
-    const uint32_t off = k + lane;
+  auto fold = [&](const WarpStage* sg, uint32_t k) {
+    const uint32_t cnt = len > k ? min((uint32_t)kChunk, len - k) : 0u;
+    float xv[kChunk];
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) xv[j] = (uint32_t)j < cnt ? operand(sg->idx[lane][j]) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j)
+      if ((uint32_t)j < cnt) sum = fadd(sum, fmul(sg->w[lane][j], xv[j]));
+  };
+
+  if constexpr (kAsyncStage<WK, CSC>) {
+    // f32 CSR: chunks are staged by asynchronous 4-byte copies into two
+    // buffers, so chunk k + 1 is in flight while chunk k is folded.  Lane l
+    // copies entry k + l of each of the warp's 32 lines (coalesced per line);
+    // entries past a line's end are zero-filled and never folded.
+    auto stage = [&](WarpStage* sg, uint32_t k) {
+      const uint32_t off = k + lane;
 #pragma unroll 8
-    for (int rr = 0; rr < 32; ++rr) {
-      if (off < st->len[rr]) {
-        const uint32_t e = st->start[rr] + off;
-        st->idx[rr][lane] = __ldg(p.idx + e);
-        if constexpr (CSC) {
-          st->w[rr][lane] = load_weight<WK>(p.w, __ldg(p.eidx + e));
-        } else {
-          st->w[rr][lane] = load_weight<WK>(p.w, e);
+      for (int rr = 0; rr < 32; ++rr) {
+        const uint32_t s_rr = __shfl_sync(0xffffffffu, start, rr);
+        const uint32_t l_rr = __shfl_sync(0xffffffffu, len, rr);
+        const bool ok = off < l_rr;
+        const uint64_t e = ok ? (uint64_t)s_rr + off : 0;
+        cp_async4(&sg->idx[rr][lane], p.idx + e, ok);
+        cp_async4(&sg->w[rr][lane], reinterpret_cast<const float*>(p.w) + e, ok);
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    if (maxlen) stage(st, 0);
+    int buf = 0;
+    for (uint32_t k = 0; k < maxlen; k += kChunk, buf ^= 1) {
+      if (k + kChunk < maxlen) {
+        stage(st + kRowWarps * (buf ^ 1), k + kChunk);
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+      } else {
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+      }
+      __syncwarp();
+      fold(st + kRowWarps * buf, k);
+      __syncwarp();
+    }
+  } else {
+    for (uint32_t k = 0; k < maxlen; k += kChunk) {
+      const uint32_t off = k + lane;
+      // Stage the chunk: lane l loads entry k + l of each of the warp's 32
+      // lines (one coalesced access per line and array), all loads issued
+      // into registers before any is stored so their latencies overlap.
+      uint32_t ci[32];
+      float cw[32];
+#pragma unroll
+      for (int rr = 0; rr < 32; ++rr) {
+        const uint32_t s_rr = __shfl_sync(0xffffffffu, start, rr);
+        const uint32_t l_rr = __shfl_sync(0xffffffffu, len, rr);
+        ci[rr] = 0u;
+        cw[rr] = 0.0f;
+        if (off < l_rr) {
+          const uint32_t e = s_rr + off;
+          ci[rr] = __ldg(p.idx + e);
+          if constexpr (CSC) {
+            cw[rr] = load_weight<WK>(p.w, __ldg(p.eidx + e));
+          } else {
+            cw[rr] = load_weight<WK>(p.w, e);
+          }
         }
       }
-    }
-    __syncwarp();
-    const uint32_t cnt = len > k ? min((uint32_t)kChunk, len - k) : 0u;
-#pragma unroll 4
-    for (uint32_t j = 0; j < cnt; ++j) {
-      const uint32_t c = st->idx[lane][j];
-      const float wv = st->w[lane][j];
-      float xv;
-      if constexpr (XM == X_DENSE) {
-        xv = __ldg(p.x + c);
-      } else if constexpr (XM == X_BITS_SMEM) {
-        xv = (float)((s_bits[c >> 5] >> (c & 31)) & 1u);  // multiply, never branch
-      } else {
-        xv = (float)((__ldg(p.xbits + (c >> 5)) >> (c & 31)) & 1u);
+#pragma unroll
+      for (int rr = 0; rr < 32; ++rr) {
+        st->idx[rr][lane] = ci[rr];
+        st->w[rr][lane] = cw[rr];
       }
-      sum = fadd(sum, fmul(wv, xv));
+      __syncwarp();
+      fold(st, k);
+      __syncwarp();
     }
-    __syncwarp();
   }
 
   if constexpr (EPI == EPI_ACCUM) {
@@ -177,7 +245,7 @@ template <int WK, int XM, bool CSC, int EPI, bool COMPACT, bool ORDERED = false>
 cudaError_t launch_t(const RowLaunch& p, cudaStream_t stream) {
   auto kern = row_fold_kernel<WK, XM, CSC, EPI, COMPACT, ORDERED>;
   const size_t bits_bytes = (XM == X_BITS_SMEM) ? (((size_t)p.xbits_words * 4 + 15) & ~(size_t)15) : 0;
-  const size_t smem = bits_bytes + sizeof(WarpStage) * kRowWarps;
+  const size_t smem = bits_bytes + sizeof(WarpStage) * kRowWarps * (kAsyncStage<WK, CSC> ? 2 : 1);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const uint32_t tiles = row_tiles(p.nlines);
