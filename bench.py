@@ -5,8 +5,11 @@ Headline workload (``--workload lif_net``, the default): the recurrent LIF
 network tick -- 4,194,304 neurons, fixed fan-in 1,024 (4.29e9 synapses, f32
 weights N(0, 0.03^2)), decay 0.95, threshold 1.0, reset 0, Bernoulli(0.01)
 initial spikes.  One step is one tick of the whole network: the fused
-spike-SpMV + LIF kernel over every row block, the in-place NCCL all-gather of
-the packed spike words across ranks, and the global spike count.  Neurons are
+spike-SpMV + LIF kernel over every row block, the exchange of the packed spike
+words across ranks (by default the tick kernel stores them into every peer
+GPU's copy over NVLink and one small kernel per tick trades flags and spike
+counts; --net-exchange nccl uses an in-place NCCL all-gather instead), and the
+global spike count.  Neurons are
 row-block sharded over the ranks, so the total work is fixed as N grows
 (strong scaling).  Rows are split into operators of at most 2^31 synapses
 (u32 offsets), so one GPU holds two blocks.
@@ -413,6 +416,7 @@ def bench_lif_net(args, dist):
                                                                    keep_host=check_ticks > 0)
     net = make_net(S, dev, dist, ops, row0, n_total)
     L = lib()
+    check(L.sparsl_net_set_exchange(net, 1 if args.net_exchange == "nccl" else 0), "exchange mode")
     stream = L.sparsl_net_stream(net)
     p = (NET_DECAY, NET_VRESET, NET_DTHETA)
     v_l, th_l = v[row0:row0 + local].copy(), th[row0:row0 + local].copy()
@@ -513,7 +517,9 @@ def bench_lif_net(args, dist):
         cpu = {"value": chk["ticks"] / chk["cpu_s"], "unit": "ticks/s", "cores": O.num_threads(), "kind": "port",
                "sample": f"{chk['ticks']} full ticks of the same {n_total * fan_in:.3g}-synapse network (the "
                          "parity check below), C restatement of the reference's CpuParallel fused tick"}
-    kernels_per_tick = len(ops) + 1  # fused tick kernel per block + global spike count
+    # fused tick kernel per block + the exchange step (N>1, peer) or the
+    # global spike count (N=1, or after the NCCL all-gather)
+    kernels_per_tick = len(ops) + 1
     pk_, how = peaks()
     peak = float(pk_.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"]))
     algo = net_bytes_per_tick_per_gpu(n_total, fan_in, dist.world)
@@ -532,7 +538,11 @@ def bench_lif_net(args, dist):
         "data": "synthetic (seeded ChaCha12 per row, drawn on the GPU; identical to the host definition)",
         "config": {"workload": f"lif_net: {n_total:,} neurons x fan-in {fan_in} ({n_total * fan_in:.3g} synapses), "
                                "f32 weights N(0,0.03^2), decay 0.95, theta 1.0, reset 0, Bernoulli(0.01) initial spikes",
-                   "parallelism": f"row-block shards x{dist.world}, NCCL all-gather of packed spikes per tick",
+                   "parallelism": f"row-block shards x{dist.world}" + (
+                       "" if dist.world == 1 else
+                       (", packed spike words stored by the tick kernel into every peer GPU's copy over NVLink, "
+                        "one flag/count kernel per tick" if args.net_exchange == "peer" else
+                        ", in-place NCCL all-gather of the packed spike words per tick")),
                    "blocks_per_gpu": len(ops), "l2": "inputs per GPU >> 126 MB L2 (no flush needed)",
                    "setup_s": round(setup_s, 1)},
         "clocks": ck,
@@ -1158,6 +1168,28 @@ def bench_ragged(args, op, csr, w, s, flush):
     return spmv, tick
 
 
+def bench_ragged_only(args, dev, want_cpu):
+    """The config-4 power-law matrix as a plain SpMV and as a recurrent
+    network (n_vec = 1), without the SpMM legs."""
+    import torch
+    import sparsl_b200 as S
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    n = SPMM_N
+    rp, col, r = gen_zipf_csr(n, n, SPMM_KMAX, SPMM_ALPHA, SPMM_SEED)
+    w = r.uniform(-1.0, 1.0, col.size).astype(np.float32)
+    s = torch.cuda.Stream()
+    torch.cuda.set_stream(s)
+    flush = torch.empty(64 << 22, dtype=torch.float32, device="cuda")  # 1 GiB > L2
+    op = dev.prepare(S.Csr(rp, col, n), n, w)
+    spmv, tick = bench_ragged(args, op, O.Csr(rp, col, n), w, s, flush)
+    del op
+    spmv["ragged_lif_tick"] = tick
+    return spmv
+
+
 def bench_lif(args, dev, want_cpu):
     import torch
     import sparsl_b200 as S
@@ -1308,7 +1340,7 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="sparsl", choices=["sparsl", "reference"])
-    ap.add_argument("--workload", default="lif_net", choices=["lif_net", "spmv", "spmm", "scan", "lif"])
+    ap.add_argument("--workload", default="lif_net", choices=["lif_net", "spmv", "spmm", "scan", "lif", "ragged"])
     ap.add_argument("--no-extras", action="store_true", help="N=1: skip the SpMV / scan / LIF-1GPU figures")
     ap.add_argument("--kernel-iters", type=int, default=20)
     ap.add_argument("--scan-exchange", default="gloo", choices=["gloo", "nccl"],
@@ -1325,6 +1357,8 @@ def main():
     ap.add_argument("--check-ticks", type=int, default=32,
                     help="LIF network: ticks compared bit for bit with the CPU (capped at warm-up + steps)")
     ap.add_argument("--no-check", action="store_true", help="LIF network: skip the CPU comparison")
+    ap.add_argument("--net-exchange", default="peer", choices=["peer", "nccl"],
+                    help="LIF network, N>1: spike-vector exchange through peer memory or an NCCL all-gather")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
     global SCAN_N, NET_N, NET_FANIN
@@ -1352,7 +1386,8 @@ def main():
             elif args.workload in ("spmv", "spmm") and dist.world > 1:
                 line = bench_rowshard(args, dev, dist, args.workload)
             else:
-                fn = {"spmv": bench_spmv, "spmm": bench_spmm, "scan": bench_scan, "lif": bench_lif}[args.workload]
+                fn = {"spmv": bench_spmv, "spmm": bench_spmm, "scan": bench_scan, "lif": bench_lif,
+                      "ragged": bench_ragged_only}[args.workload]
                 line = fn(args, dev, dist.rank == 0 and not args.no_cpu) if dist.rank == 0 else None
         else:
             line = bench_lif_net(args, dist)

@@ -429,6 +429,16 @@ int sparsl_net_trace(sparsl_net *net, uint32_t *out, uint64_t cap, uint64_t *n_o
 int sparsl_net_set_timing(sparsl_net *net, uint64_t max_ticks);
 /* Sum of those kernel durations over the ticks of the last steps call. */
 int sparsl_net_kernel_ms(sparsl_net *net, double *total_ms, uint64_t *ticks);
+/* How the ranks exchange the spike vector after each tick (nranks > 1):
+ * SPARSL_NET_EXCHANGE_PEER (default): the tick kernels store their packed
+ * words straight into every peer GPU's copy over NVLink (cudaIpc mappings
+ * made at create), and one small kernel per tick publishes a flag and the
+ * spike count to each peer and waits, bounded, for theirs.
+ * SPARSL_NET_EXCHANGE_NCCL: an in-place ncclAllGather of the packed words,
+ * then a popcount (the plain-collective baseline).  Every rank must choose
+ * the same mode; the trace and state are identical either way. */
+enum { SPARSL_NET_EXCHANGE_PEER = 0, SPARSL_NET_EXCHANGE_NCCL = 1 };
+int sparsl_net_set_exchange(sparsl_net *net, int mode);
 /* The same durations per tick (ms): out[t] for the first min(cap, n) timed
  * ticks of the last steps call; *n_out = the number timed. */
 int sparsl_net_tick_ms(sparsl_net *net, float *out, uint64_t cap, uint64_t *n_out);

@@ -139,6 +139,7 @@ SIGNATURES = {
     "sparsl_net_set_timing": (i32, [vp, u64]),
     "sparsl_net_kernel_ms": (i32, [vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(u64)]),
     "sparsl_net_tick_ms": (i32, [vp, vp, u64, ctypes.POINTER(u64)]),
+    "sparsl_net_set_exchange": (i32, [vp, i32]),
     # include/sparsl_workload.h
     "sparsl_workload_fixed_fanin": (i32, [u64, u64, u64, u64, ctypes.c_uint32, f32, vp, vp, vp]),
     "sparsl_workload_uniform_row_ptr": (i32, [u64, ctypes.c_uint32, vp, vp]),

@@ -29,6 +29,7 @@
 #include "ell.cuh"
 #include "host.hpp"
 #include "misc.cuh"
+#include "net.cuh"
 #include "rows.cuh"
 #include "scan.cuh"
 #include "sell.cuh"
@@ -150,6 +151,7 @@ std::string describe_dev_err(uint32_t bits) {
   if (bits & DEVERR_LOOKBACK_TIMEOUT) d += "a bounded look-back wait expired; ";
   if (bits & DEVERR_CANARY) d += "a canary tail was overwritten (out-of-bounds device write); ";
   if (bits & DEVERR_REPAIR_LIMIT) d += "scan repair exceeded its bound; ";
+  if (bits & DEVERR_PEER_TIMEOUT) d += "a peer GPU did not publish its tick in time; ";
   return d.empty() ? std::string("device error word set") : d;
 }
 
@@ -2209,11 +2211,108 @@ struct sparsl_net {
   uint64_t trace_cap = 0, last_steps = 0;
   ncclComm_t comm = nullptr;
   // Optional per-tick timing of the fused tick kernels (events bracket the
-  // block kernels of each tick, excluding the all-gather and the count).
+  // block kernels of each tick, excluding the exchange).
   bool timing = false;
   std::vector<cudaEvent_t> ev_a, ev_b;
   uint64_t timed_ticks = 0;
+  // Exchange of the spike vector between ranks: SPARSL_NET_EXCHANGE_PEER
+  // (peer stores over NVLink and one small flag kernel per tick) or
+  // SPARSL_NET_EXCHANGE_NCCL (an in-place ncclAllGather, then a count).
+  int exchange = SPARSL_NET_EXCHANGE_PEER;
+  DBuf box;         // this rank's NetMailbox, written by the peers
+  DBuf tick_count;  // this rank's spike count of the current tick
+  // Peers' memory mapped into this process (cudaIpcOpenMemHandle), to close.
+  std::vector<void*> opened;
+  // Device pointer tables: [parity][block][rank] peer words at each block's
+  // offset, [parity][rank] peer words at this rank's slice, [rank] mailboxes.
+  DBuf peer_out, peer_slice, peer_box;
+  uint32_t tick = 0;  // ticks run so far (the same on every rank)
 };
+
+namespace {
+// Maps every peer's spike vectors and mailbox into this process: each rank
+// exports cudaIpc handles of its two spike-vector copies and its mailbox,
+// one ncclAllGather hands them to every rank, and each rank opens the
+// others'.  All of it happens once, at create; the tick path uses only the
+// resulting device pointers.
+int net_map_peers(sparsl_net* net) {
+  const uint32_t R = (uint32_t)net->nranks, me = (uint32_t)net->rank;
+  if (R > kNetMaxRanks) return fail(SPARSL_ERR_INVALID, "nranks", "at most 32 ranks per network");
+  cudaStream_t s = net->stream;
+  if (dalloc(net->box, sizeof(NetMailbox), false, s) != cudaSuccess ||
+      dalloc(net->tick_count, 16, false, s) != cudaSuccess)
+    return fail(SPARSL_ERR_ALLOCATION, "exchange area", "device allocation failed for the exchange area");
+  CK("net_create", cudaMemsetAsync(net->box.p, 0, sizeof(NetMailbox), s));
+  CK("net_create", cudaMemsetAsync(net->tick_count.p, 0, 16, s));
+  constexpr size_t kH = sizeof(cudaIpcMemHandle_t);
+  std::vector<unsigned char> mine(3 * kH), all(3 * kH * R);
+  void* bases[3] = {net->xs[0].p, net->xs[1].p, net->box.p};
+  for (int i = 0; i < 3; ++i) {
+    cudaIpcMemHandle_t h;
+    CK("net_create", cudaIpcGetMemHandle(&h, bases[i]));
+    std::memcpy(mine.data() + i * kH, &h, kH);
+  }
+  DBuf xfer;
+  if (dalloc(xfer, all.size(), false, s) != cudaSuccess)
+    return fail(SPARSL_ERR_ALLOCATION, "exchange setup", "device allocation failed for the handle exchange");
+  unsigned char* d = xfer.as<unsigned char>();
+  int rc = SPARSL_OK;
+  do {
+    if (cudaMemcpyAsync(d + me * mine.size(), mine.data(), mine.size(), cudaMemcpyHostToDevice, s) != cudaSuccess) {
+      rc = fail_cuda("net_create", cudaGetLastError());
+      break;
+    }
+    ncclResult_t r = nccl_settle(net->comm, g_nccl.AllGather(d + me * mine.size(), d, mine.size(), ncclUint8,
+                                                            net->comm, s));
+    if (r != ncclSuccess) {
+      rc = fail(SPARSL_ERR_EXECUTION, "ncclAllGather failed", "handle exchange: ncclAllGather failed");
+      break;
+    }
+    if (cudaMemcpyAsync(all.data(), d, all.size(), cudaMemcpyDeviceToHost, s) != cudaSuccess) {
+      rc = fail_cuda("net_create", cudaGetLastError());
+      break;
+    }
+    rc = wait_bounded(s, net->ev, net->err.d, net->err.h, "net_create");
+  } while (false);
+  dfree(xfer);
+  if (rc != SPARSL_OK) return rc;
+  std::vector<uint32_t*> px[2] = {std::vector<uint32_t*>(R, nullptr), std::vector<uint32_t*>(R, nullptr)};
+  std::vector<NetMailbox*> pbox(R, nullptr);
+  for (uint32_t r = 0; r < R; ++r) {
+    if (r == me) continue;
+    void* ptrs[3] = {};
+    for (int i = 0; i < 3; ++i) {
+      cudaIpcMemHandle_t h;
+      std::memcpy(&h, all.data() + (r * 3 + i) * kH, kH);
+      const cudaError_t e = cudaIpcOpenMemHandle(&ptrs[i], h, cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess)
+        return fail(SPARSL_ERR_BACKEND, "peer memory unavailable",
+                    std::string("net_create: cannot map rank ") + std::to_string(r) +
+                        "'s memory (cudaIpcOpenMemHandle: " + cudaGetErrorString(e) + ")");
+      net->opened.push_back(ptrs[i]);
+    }
+    px[0][r] = static_cast<uint32_t*>(ptrs[0]);
+    px[1][r] = static_cast<uint32_t*>(ptrs[1]);
+    pbox[r] = static_cast<NetMailbox*>(ptrs[2]);
+  }
+  const size_t nb = net->blocks.size();
+  std::vector<uint32_t*> out(2 * nb * R, nullptr), slice(2 * R, nullptr);
+  for (int q = 0; q < 2; ++q)
+    for (uint32_t r = 0; r < R; ++r) {
+      if (!px[q][r]) continue;
+      slice[q * R + r] = px[q][r] + net->row_offset / 32;
+      for (size_t b = 0; b < nb; ++b) out[(q * nb + b) * R + r] = px[q][r] + (net->row_offset + net->block_off[b]) / 32;
+    }
+  if (dalloc(net->peer_out, out.size() * sizeof(void*), false, s) != cudaSuccess ||
+      dalloc(net->peer_slice, slice.size() * sizeof(void*), false, s) != cudaSuccess ||
+      dalloc(net->peer_box, R * sizeof(void*), false, s) != cudaSuccess)
+    return fail(SPARSL_ERR_ALLOCATION, "exchange tables", "device allocation failed for the peer tables");
+  CK("net_create", cudaMemcpyAsync(net->peer_out.p, out.data(), out.size() * sizeof(void*), cudaMemcpyHostToDevice, s));
+  CK("net_create", cudaMemcpyAsync(net->peer_slice.p, slice.data(), slice.size() * sizeof(void*), cudaMemcpyHostToDevice, s));
+  CK("net_create", cudaMemcpyAsync(net->peer_box.p, pbox.data(), R * sizeof(void*), cudaMemcpyHostToDevice, s));
+  return wait_bounded(s, net->ev, net->err.d, net->err.h, "net_create");
+}
+}  // namespace
 
 extern "C" {
 
@@ -2300,6 +2399,10 @@ int sparsl_net_create(sparsl_dev* d, sparsl_op* const* blocks, uint32_t n_blocks
   }
   int rc = wait_bounded(net->stream, net->ev, net->err.d, net->err.h, "net_create");
   if (rc != SPARSL_OK) return bail(rc);
+  if (nranks > 1) {
+    rc = net_map_peers(net);
+    if (rc != SPARSL_OK) return bail(rc);
+  }
   *out = net;
   return SPARSL_OK;
 }
@@ -2318,6 +2421,8 @@ void sparsl_net_destroy(sparsl_net* net) {
   }
   for (cudaEvent_t e : net->ev_a) cudaEventDestroy(e);
   for (cudaEvent_t e : net->ev_b) cudaEventDestroy(e);
+  for (void* p : net->opened) cudaIpcCloseMemHandle(p);
+  for (DBuf* b : {&net->box, &net->tick_count, &net->peer_out, &net->peer_slice, &net->peer_box}) dfree(*b);
   dfree(net->xs[0]);
   dfree(net->xs[1]);
   dfree(net->trace);
@@ -2368,7 +2473,11 @@ static int net_enqueue(sparsl_net* net, float decay, float v_reset, float dtheta
       CK("net_steps", cudaEventRecord(net->ev_fork, net->stream));
       CK("net_steps", cudaStreamWaitEvent(net->side, net->ev_fork, 0));
     }
-    for (size_t b = 0; b < net->blocks.size(); ++b) {
+    const bool peer = net->nranks > 1 && net->exchange == SPARSL_NET_EXCHANGE_PEER;
+    const int q = net->cur ^ 1;  // parity of the destination copy
+    const size_t nb = net->blocks.size();
+    bool all_pushed = true;
+    for (size_t b = 0; b < nb; ++b) {
       sparsl_op* op = net->blocks[b];
       if (!op->nrows) continue;
       RowLaunch p = fwd_launch(op);
@@ -2376,6 +2485,14 @@ static int net_enqueue(sparsl_net* net, float decay, float v_reset, float dtheta
       lif_resident_launch(op, p, decay, v_reset, dtheta);
       p.out_bits = dst + (net->row_offset + net->block_off[b]) / 32;
       p.err = net->err.d;
+      // The TMA tick stores its words into the peers' copies itself.
+      if (peer && op->ell.ok) {
+        p.peer_out = net->peer_out.as<uint32_t*>() + (q * nb + b) * net->nranks;
+        p.npeers = (uint32_t)net->nranks;
+        p.tick_count = net->tick_count.as<uint32_t>();
+      } else {
+        all_pushed = false;
+      }
       CK("net_steps", launch_fwd(op, p, (b & 1) ? net->side : net->stream));
     }
     if (fork) {
@@ -2383,6 +2500,27 @@ static int net_enqueue(sparsl_net* net, float decay, float v_reset, float dtheta
       CK("net_steps", cudaStreamWaitEvent(net->stream, net->ev_join, 0));
     }
     if (tm) CK("net_steps", cudaEventRecord(net->ev_b[t], net->stream));
+    if (peer) {
+      NetExchange x;
+      x.self = (uint32_t)net->rank;
+      x.nranks = (uint32_t)net->nranks;
+      x.local_words = dst + net->row_offset / 32;
+      x.nwords = (uint32_t)(net->local_rows / 32);
+      x.peer_words = net->peer_slice.as<uint32_t*>() + q * net->nranks;
+      x.push = !all_pushed;
+      x.count = all_pushed ? net->tick_count.as<uint32_t>() : nullptr;
+      x.peer_box = net->peer_box.as<NetMailbox*>();
+      x.my_box = net->box.as<NetMailbox>();
+      x.tick = net->tick++;
+      // Half the host's deadline (at most 30 s): an expired wait is reported
+      // through the error word before the host would give up on the stream.
+      x.wait_ns = std::min<uint64_t>(g_timeout_ms.load() / 2, 30000) * 1000000ull;
+      x.trace_slot = net->trace.as<uint32_t>() + t;
+      x.err = net->err.d;
+      CK("net_steps", launch_net_exchange(x, net->stream));
+      net->cur ^= 1;
+      continue;
+    }
     if (net->nranks > 1) {
       ncclResult_t r = nccl_settle(
           net->comm, g_nccl.AllGather(dst + (uint64_t)net->rank * slice, dst, slice, ncclUint32, net->comm, net->stream));
@@ -2475,6 +2613,16 @@ int sparsl_net_kernel_ms(sparsl_net* net, double* total_ms, uint64_t* ticks) {
   }
   if (total_ms) *total_ms = sum;
   if (ticks) *ticks = net->timed_ticks;
+  return SPARSL_OK;
+}
+
+int sparsl_net_set_exchange(sparsl_net* net, int mode) {
+  if (!net) return fail(SPARSL_ERR_INVALID, "null net", "null net");
+  if (mode != SPARSL_NET_EXCHANGE_PEER && mode != SPARSL_NET_EXCHANGE_NCCL)
+    return fail(SPARSL_ERR_INVALID, "exchange mode", "unknown exchange mode");
+  CK("net_set_exchange", cudaSetDevice(net->dev->ordinal));
+  CK("net_set_exchange", cudaStreamSynchronize(net->stream));
+  net->exchange = mode;
   return SPARSL_OK;
 }
 

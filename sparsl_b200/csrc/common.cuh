@@ -21,6 +21,7 @@ enum DevErr : uint32_t {
   DEVERR_LOOKBACK_TIMEOUT = 1u << 0,  // a bounded look-back spin gave up
   DEVERR_CANARY = 1u << 1,            // a canary tail was overwritten
   DEVERR_REPAIR_LIMIT = 1u << 2,      // scan repair hit its iteration cap
+  DEVERR_PEER_TIMEOUT = 1u << 3,      // a peer GPU's tick did not arrive in time
 };
 
 // Iteration cap for every device-side spin.  At ~100 ns per poll this bounds a

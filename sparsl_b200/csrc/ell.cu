@@ -413,7 +413,18 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1)
         p.spikes[line] = spike ? 1 : 0;
       }
       const uint32_t ballot = __ballot_sync(0xffffffffu, spike);
-      if (p.out_bits && lane == 0) p.out_bits[tile] = ballot;
+      if (p.out_bits && lane == 0) {
+        p.out_bits[tile] = ballot;
+        // The word goes straight to every peer GPU over NVLink while the
+        // tick streams on; no separate collective moves the spike vector.
+        if (p.peer_out) {
+          for (uint32_t r = 0; r < p.npeers; ++r) {
+            uint32_t* q = p.peer_out[r];
+            if (q) q[tile] = ballot;
+          }
+        }
+        if (p.tick_count && ballot) atomicAdd(p.tick_count, (uint32_t)__popc(ballot));
+      }
       if constexpr (COMPACT) {
         const uint32_t agg = __popc(ballot);
         const uint32_t excl = lookback_warp(p.tile_flags, tile, agg, p.epoch, p.err, lane);
@@ -432,6 +443,9 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1)
       c_phase ^= (c_slot == 0);
     }
   }
+  // Peer stores become visible system-wide before the warp is done, so the
+  // exchange that follows the tick can publish them with one flag per peer.
+  if (p.peer_out && lane == 0) __threadfence_system();
   // The last warp out rewinds the ticket counters for the next launch; the
   // epoch-tagged flags need no clearing.
   if (lane == 0) {

@@ -102,13 +102,16 @@ __global__ void __launch_bounds__(kRowWarps * 32) row_fold_kernel(const RowLaunc
     }
   };
   // Fold the lane's own entries of one staged chunk: every operand gather
-  // first, then the dependent add chain in entry order.
+  // first, then the dependent add chain in entry order.  Entries past the
+  // line's end were staged as column 0 (in bounds: a line with entries
+  // implies ncols >= 1), so all gathers are issued unconditionally; only
+  // their adds are skipped.
   float sum = 0.0f;
   auto fold = [&](const WarpStage* sg, uint32_t k) {
     const uint32_t cnt = len > k ? min((uint32_t)kChunk, len - k) : 0u;
     float xv[kChunk];
 #pragma unroll
-    for (int j = 0; j < kChunk; ++j) xv[j] = (uint32_t)j < cnt ? operand(sg->idx[lane][j]) : 0.0f;
+    for (int j = 0; j < kChunk; ++j) xv[j] = operand(sg->idx[lane][j]);
 #pragma unroll
     for (int j = 0; j < kChunk; ++j)
       if ((uint32_t)j < cnt) sum = fadd(sum, fmul(sg->w[lane][j], xv[j]));

@@ -46,6 +46,14 @@ struct RowLaunch {
   float* theta = nullptr;
   uint8_t* spikes = nullptr;
   uint32_t* out_bits = nullptr;    // optional packed spike words (word = line / 32)
+  // Network ticks across GPUs (TMA path): each packed word is also stored
+  // into every peer's copy of the spike vector (peer_out[r] is peer r's
+  // words at the same offset as out_bits, null for this rank), the spikes
+  // are counted into *tick_count, and every warp that stored to a peer
+  // fences those stores system-wide before it exits.
+  uint32_t* const* peer_out = nullptr;
+  uint32_t npeers = 0;
+  uint32_t* tick_count = nullptr;
   float decay = 0.f, v_reset = 0.f, dtheta = 0.f;
   // Optional spike compaction (requires EPI_LIF): ascending index list.
   uint32_t* idx_list = nullptr;

@@ -20,10 +20,11 @@
 //  * Offset chain B (b' = x.a * b + x.b) -- speculated, with no look-back.
 //    The recurrence contracts: B's dependence on its value n elements earlier
 //    is a product of n multipliers.  So each thread replays the elements
-//    before its sub-chunk (128; 256 for a tile's thread 0) from a
-//    tree-composed guess that assumes B = 0 at the start of the tile, or of a
-//    512-element halo reaching into the previous tile; that assumption is
-//    contracted over >= 256 elements and the replay removes the tree's
+//    before its sub-chunk (kScanWarmSub sub-chunks, 192 elements; half the
+//    halo for a tile's thread 0) from a tree-composed guess that assumes
+//    B = 0 at the start of the tile, or of a 32-sub-chunk halo reaching into
+//    the previous tile; that assumption is contracted over at least the
+//    replay plus a warp's sub-chunks, and the replay removes the tree's
 //    rounding.  For contracting data this lands on the sequential trajectory
 //    bit for bit; the look-back warp works meanwhile.
 //  * Verify: each thread's assumed incoming state is compared bitwise with the
@@ -126,7 +127,12 @@ __device__ void walk_multiplier(float A, int first, const float2* sm, const uint
   }
 }
 
-__global__ void __launch_bounds__(kScanBlock, 5) scan_main(const float2* __restrict__ in, float2* __restrict__ out,
+// Two tiles per SM: a tile (32 sub-chunk rows of halo + 256 of tile, 32
+// maps each, padded) takes 76 KB of shared memory.
+#ifndef SPARSL_SCAN_MIN_BLOCKS
+#define SPARSL_SCAN_MIN_BLOCKS 2
+#endif
+__global__ void __launch_bounds__(kScanBlock, SPARSL_SCAN_MIN_BLOCKS) scan_main(const float2* __restrict__ in, float2* __restrict__ out,
                                                        uint64_t n, ScanScratch s, uint32_t* err, int has_entry,
                                                        float2 entry, const float2* entry_dev) {
   extern __shared__ __align__(16) float2 sm[];  // kRows x kRowStride
@@ -214,7 +220,7 @@ __global__ void __launch_bounds__(kScanBlock, 5) scan_main(const float2* __restr
       Aff ex{__shfl_up_sync(0xffffffffu, inc.a, 1), __shfl_up_sync(0xffffffffu, inc.b, 1)};
       if (lane == 0) ex = Aff{1.f, 0.f};
       s_Eb[t] = ex.b;
-      // Warp 0's warm-up guesses reach into the 512-element halo: lane t
+      // Warp 0's warm-up guesses reach into the 32-sub-chunk halo: lane t
       // composes halo sub-chunk t, a warp scan chains them (from B = 0 at the
       // halo start), and the halo total continues into the in-tile prefix.
       const float2* hrow = sm + t * kRowStride;
@@ -386,11 +392,12 @@ __global__ void __launch_bounds__(kScanBlock, 5) scan_main(const float2* __restr
   } else if (!copy_first) {
     // Each thread replays the elements before its sub-chunk from a tree
     // guess that assumes B = 0 at the start of the tile (warps 1-7) or of the
-    // halo (warp 0); by contraction over >= 256 elements that no longer
-    // shows, and the replay removes the tree's rounding.  Replays are 128
-    // elements, except thread 0's, which only the cross-tile check (and a
-    // serial repair) would catch: it replays 256.  In tile 0 the first
-    // element is copied, so warp 0 starts there exactly.
+    // halo (warp 0); by contraction over the replay and the sub-chunks
+    // before it that no longer shows, and the replay removes the tree's
+    // rounding.  Replays are kScanWarmSub sub-chunks, except thread 0's,
+    // which only the cross-tile check (and a serial repair) would catch: it
+    // replays half the halo.  In tile 0 the first element is copied, so warp
+    // 0 starts there exactly.
     int r0;
     float b;
     if (wid == 0 && tile == 0) {
