@@ -321,7 +321,10 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1)
       // end (and rows past the last line) were zero-filled by the TMA box
       // (column 0, weight 0), so their gathers stay in bounds; only their
       // adds are skipped.
-      constexpr bool kGatherAll = XM != X_DENSE;
+#ifndef SPARSL_ELL_DENSE_GATHER_ALL
+#define SPARSL_ELL_DENSE_GATHER_ALL 0
+#endif
+      constexpr bool kGatherAll = XM != X_DENSE || SPARSL_ELL_DENSE_GATHER_ALL;
       float prod[kChunk];
 #pragma unroll
       for (uint32_t g = 0; g < kChunk / 8; ++g) {  // 8 entries per group

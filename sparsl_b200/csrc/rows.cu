@@ -34,6 +34,11 @@ struct WarpStage {
 #endif
 template <int WK, bool CSC>
 constexpr bool kAsyncStage = SPARSL_ROWS_ASYNC && WK == W_F32 && !CSC;
+#ifndef SPARSL_ROWS_STAGES
+#define SPARSL_ROWS_STAGES 2
+#endif
+constexpr int kRowStages = SPARSL_ROWS_STAGES;  // stage buffers per warp on the asynchronous path
+static_assert(kRowStages >= 2 && kRowStages <= 4, "2 to 4 stage buffers");
 
 // 4-byte asynchronous global -> shared copy; a false `ok` zero-fills the
 // destination and reads nothing.
@@ -135,19 +140,34 @@ __global__ void __launch_bounds__(kRowWarps * 32) row_fold_kernel(const RowLaunc
       }
       asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    if (maxlen) stage(st, 0);
-    int buf = 0;
-    for (uint32_t k = 0; k < maxlen; k += kChunk, buf ^= 1) {
-      if (k + kChunk < maxlen) {
-        stage(st + kRowWarps * (buf ^ 1), k + kChunk);
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
+    // kRowStages buffers: chunks k + 1 .. k + kRowStages - 1 are in flight
+    // while chunk k folds.  Every iteration commits one group (empty past the
+    // end), so "all but the newest kRowStages - 1 groups complete" is always
+    // chunk k.
+#pragma unroll
+    for (int i = 0; i < kRowStages - 1; ++i) {
+      if ((uint32_t)i * kChunk < maxlen) {
+        stage(st + kRowWarps * i, (uint32_t)i * kChunk);
       } else {
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        asm volatile("cp.async.commit_group;" ::: "memory");
       }
+    }
+    int buf = 0;
+    for (uint32_t k = 0; k < maxlen; k += kChunk) {
+      const uint32_t ahead = k + (kRowStages - 1) * kChunk;
+      const int abuf = (buf + kRowStages - 1) % kRowStages;
+      if (ahead < maxlen) {
+        stage(st + kRowWarps * abuf, ahead);
+      } else {
+        asm volatile("cp.async.commit_group;" ::: "memory");
+      }
+      asm volatile("cp.async.wait_group %0;" ::"n"(kRowStages - 1) : "memory");
       __syncwarp();
       fold(st + kRowWarps * buf, k);
       __syncwarp();
+      buf = (buf + 1 == kRowStages) ? 0 : buf + 1;
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
   } else {
     for (uint32_t k = 0; k < maxlen; k += kChunk) {
       const uint32_t off = k + lane;
@@ -248,7 +268,7 @@ template <int WK, int XM, bool CSC, int EPI, bool COMPACT, bool ORDERED = false>
 cudaError_t launch_t(const RowLaunch& p, cudaStream_t stream) {
   auto kern = row_fold_kernel<WK, XM, CSC, EPI, COMPACT, ORDERED>;
   const size_t bits_bytes = (XM == X_BITS_SMEM) ? (((size_t)p.xbits_words * 4 + 15) & ~(size_t)15) : 0;
-  const size_t smem = bits_bytes + sizeof(WarpStage) * kRowWarps * (kAsyncStage<WK, CSC> ? 2 : 1);
+  const size_t smem = bits_bytes + sizeof(WarpStage) * kRowWarps * (kAsyncStage<WK, CSC> ? kRowStages : 1);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const uint32_t tiles = row_tiles(p.nlines);
