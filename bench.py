@@ -1190,6 +1190,49 @@ def bench_ragged_only(args, dev, want_cpu):
     return spmv
 
 
+def bench_lif_integrate(args, dev, n=1 << 26):
+    """Device::lif_integrate over dense currents (mod.rs:1202-1229) on 2^26
+    cells in device memory: v, theta, currents read, v, theta, spike bytes
+    written (21 B per cell; 1.4 GB > L2, no flush needed)."""
+    import torch
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    L = lib()
+    r = np.random.default_rng(0x11F)
+    v0 = r.uniform(0.0, 1.0, n).astype(np.float32)
+    t0 = np.full(n, 1.0, np.float32)
+    cur = (r.standard_normal(n) * 0.1).astype(np.float32)
+    s = torch.cuda.Stream()
+    dv, dt, dc = (torch.from_numpy(a.copy()).cuda() for a in (v0, t0, cur))
+    ds = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    run = lambda: check(L.sparsl_dev_lif_integrate_device(dev.handle, dv.data_ptr(), dt.data_ptr(), dc.data_ptr(),
+                                                          ds.data_ptr(), n, 0.95, 0.0, 0.0, s.cuda_stream), "lif")
+    for _ in range(args.warmup):
+        run()
+    # parity: one more step from a fresh state against the oracle
+    dv.copy_(torch.from_numpy(v0))
+    dt.copy_(torch.from_numpy(t0))
+    torch.cuda.synchronize()
+    run()
+    s.synchronize()
+    vw, tw, sw = v0.copy(), t0.copy(), np.zeros(n, np.uint8)
+    O.lif_integrate(vw, tw, cur, sw, np.float32(0.95), np.float32(0.0), np.float32(0.0), par=True)
+    ok = bool(np.array_equal(dv.cpu().numpy().view(np.uint32), vw.view(np.uint32))
+              and np.array_equal(dt.cpu().numpy().view(np.uint32), tw.view(np.uint32))
+              and np.array_equal(ds.cpu().numpy(), sw))
+    ts = time_launches(s, run, args.kernel_iters)
+    ms = statistics.median(ts)
+    algo = 21 * n
+    del dv, dt, dc, ds
+    return {"metric": "lif_integrate effective HBM GB/s", "value": algo / (ms * 1e-3) / 1e9, "unit": "GB/s",
+            "ms_per_step": ms, "algorithmic_bytes": algo, "bit_exact_vs_oracle": ok,
+            "config": f"{n:,} cells, v U[0,1], theta 1, currents N(0,0.1^2), decay 0.95; 1.4 GB > L2",
+            "roofline": roofline(algo, ms, "lif_integrate_kernel", "lif_integrate")}
+
+
 def bench_lif(args, dev, want_cpu):
     import torch
     import sparsl_b200 as S
@@ -1263,6 +1306,7 @@ def bench_lif(args, dev, want_cpu):
                "sample": f"{ticks} full ticks of the same network ({cpu_s:.1f} s, the parity check), "
                          "CpuParallel restatement"}
     per_tick = ms / ticks
+    standalone = bench_lif_integrate(args, dev)
     return {"metric": "LIF net ticks/sec (1 GPU)", "value": 1e3 / per_tick, "unit": "ticks/s",
             "ms_per_step": per_tick, "ticks": ticks, "algorithmic_bytes_per_tick": algo,
             "effective_GBs": algo / (per_tick * 1e-3) / 1e9,
@@ -1273,7 +1317,8 @@ def bench_lif(args, dev, want_cpu):
                     "path": "sparsl_op_fused_spikes_lif per tick + host repack, pinned host"},
             "roofline": roofline(algo, per_tick, "ell_stream_kernel<f32, spike bitmask in shared memory, LIF> + "
                                                  "compact_bits_kernel (side stream)", "lif"),
-            "bit_exact_vs_oracle": exact, "checked_ticks": ticks, "cpu_baseline": cpu}
+            "bit_exact_vs_oracle": exact, "checked_ticks": ticks, "cpu_baseline": cpu,
+            "lif_integrate": standalone}
 
 
 # --------------------------------------------------------------------------

@@ -116,6 +116,12 @@ int sparsl_dev_assoc_scan(sparsl_dev *dev, const float *in, uint64_t n, float *o
 int sparsl_dev_lif_integrate(sparsl_dev *dev, float *v, float *theta, const float *currents,
                              uint8_t *spikes, uint64_t n, float decay, float v_reset,
                              float delta_theta);
+/* The same over device arrays (each inside one allocation of this GPU),
+ * enqueued on `stream` (cudaStream_t, NULL = the device's own) without
+ * waiting: v, theta updated in place, spikes written as 0/1 bytes. */
+int sparsl_dev_lif_integrate_device(sparsl_dev *dev, float *d_v, float *d_theta, const float *d_currents,
+                                    uint8_t *d_spikes, uint64_t n, float decay, float v_reset,
+                                    float delta_theta, void *stream);
 
 /* ---- CSR gate: validate_csr (mod.rs:2116-2182) ---------------------------- */
 int sparsl_validate_csr(const uint32_t *row_ptr, uint64_t row_ptr_len, const uint32_t *col,

@@ -52,6 +52,7 @@ SIGNATURES = {
     "sparsl_quarantined": (i32, []),
     "sparsl_dev_assoc_scan": (i32, [vp, vp, u64, vp]),
     "sparsl_dev_lif_integrate": (i32, [vp, vp, vp, vp, vp, u64, f32, f32, f32]),
+    "sparsl_dev_lif_integrate_device": (i32, [vp, vp, vp, vp, vp, u64, f32, f32, f32, vp]),
     "sparsl_validate_csr": (i32, [vp, u64, vp, u64, u64, u64, ctypes.POINTER(Shape)]),
     "sparsl_f32_to_f16_bits": (None, [vp, vp, u64]),
     "sparsl_f32_to_bf16_bits": (None, [vp, vp, u64]),

@@ -277,6 +277,7 @@ namespace sparsl {
 // the process-wide admission and quarantine state.
 int record_error(int code, const char* message) { return fail(code, message, message); }
 int record_error_detail(int code, const char* reason, const std::string& detail) { return fail(code, reason, detail); }
+int check_device_array(const void* p, uint64_t bytes, int ordinal, const char* what);  // defined below
 bool admission_enter() {
   g_admitted.fetch_add(1);
   return !g_quarantine.load();
@@ -895,6 +896,21 @@ int sparsl_dev_lif_integrate(sparsl_dev* d, float* v, float* theta, const float*
   set.ptr[set.count++] = d->lspk.canary();
   CK("lif_integrate", launch_canary_check(set, d->err.d, d->stream));
   return wait_bounded(d->stream, d->ev, d->err.d, d->err.h, "lif_integrate");
+}
+
+int sparsl_dev_lif_integrate_device(sparsl_dev* d, float* d_v, float* d_theta, const float* d_cur, uint8_t* d_spk,
+                                    uint64_t n, float decay, float v_reset, float dtheta, void* stream) {
+  ADMIT();
+  if (!d) return fail(SPARSL_ERR_INVALID, "null device", "lif_integrate: null device");
+  if (n == 0) return SPARSL_OK;
+  CK("lif_integrate", cudaSetDevice(d->ordinal));
+  TRY(sparsl::check_device_array(d_v, n * 4, d->ordinal, "v"));
+  TRY(sparsl::check_device_array(d_theta, n * 4, d->ordinal, "theta"));
+  TRY(sparsl::check_device_array(d_cur, n * 4, d->ordinal, "currents"));
+  TRY(sparsl::check_device_array(d_spk, n, d->ordinal, "spikes"));
+  CK("lif_integrate", launch_lif_integrate(d_v, d_theta, d_cur, d_spk, n, decay, v_reset, dtheta,
+                                           stream ? static_cast<cudaStream_t>(stream) : d->stream));
+  return SPARSL_OK;
 }
 
 void* sparsl_dev_stream(sparsl_dev* d) { return d ? d->stream : nullptr; }

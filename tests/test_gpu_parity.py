@@ -160,6 +160,21 @@ def test_lif_integrate_and_fma_counterexample(O, cuda_device):
     assert_bits_equal(v, vw)
     assert_bits_equal(t, tw)
     assert np.array_equal(s.astype(np.uint8), sw)
+    # the device-array entry point, on a torch stream
+    L = _lib.load()
+    dv, dt, dc = (torch.from_numpy(a.copy()).cuda() for a in (v0, t0, cur))
+    ds = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    st = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    assert L.sparsl_dev_lif_integrate_device(cuda_device.handle, dv.data_ptr(), dt.data_ptr(), dc.data_ptr(),
+                                             ds.data_ptr(), n, 0.95, -0.25, 0.05, st.cuda_stream) == 0
+    st.synchronize()
+    assert_bits_equal(dv.cpu().numpy(), vw)
+    assert_bits_equal(dt.cpu().numpy(), tw)
+    assert np.array_equal(ds.cpu().numpy(), sw)
+    host = np.zeros(n, np.float32)
+    assert L.sparsl_dev_lif_integrate_device(cuda_device.handle, host.ctypes.data, dt.data_ptr(), dc.data_ptr(),
+                                             ds.data_ptr(), n, 0.95, -0.25, 0.05, None) == _lib.SPARSL_ERR_INVALID
 
 
 def test_resident_api_equals_slice_api(O, cuda_device):
