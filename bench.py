@@ -66,10 +66,11 @@ BLOCK_NNZ_MAX = 1 << 31
 # Tick-kernel DRAM traffic per algorithmic byte, from an ncu capture of
 # ell_stream_kernel (f32 weights, spike bitmask through the shared-memory
 # summary, LIF epilogue) at 1,048,576 x 1,024: dram__bytes_read.sum +
-# dram__bytes_write.sum over the launch's algorithmic bytes.
-NET_TRAFFIC_RATIO = 4_315_442_000 / 4_312_006_660
+# dram__bytes_write.sum of one launch (8,599,327,488 + 8,067,072 B) over the
+# launch's algorithmic bytes (8,606,973,956 B).
+NET_TRAFFIC_RATIO = 8_607_394_560 / 8_606_973_956
 NET_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the same kernel and spike mode at "
-                      "1,048,576 x 512, per algorithmic byte, scaled to this launch")
+                      "1,048,576 x 1,024 (8.6 GB streamed), per algorithmic byte, scaled to this launch")
 
 
 def peaks():
@@ -84,7 +85,15 @@ def peaks():
 # DRAM traffic per algorithmic byte of each workload's dominant kernel, from
 # ncu captures (dram__bytes_read.sum + dram__bytes_write.sum of one launch
 # over the launch's algorithmic bytes), keyed by workload.
-TRAFFIC_RATIO = {}
+TRAFFIC_RATIO = {
+    "ragged_spmv": ((459_123_968 + 8_070_400) / 408_395_452,
+                    "ncu capture of the same launch (bench.py --workload ragged), 1,000,000 rows"),
+    "spmv": (51_990_000 / 52_800_004, "ncu capture of the same launch (bench.py --workload spmv)"),
+    "spmm_f32": (6.2e9 / 1_164_395_452, "ncu capture of the same launch (bench.py --workload spmm): DRAM "
+                                        "throughput x duration, about 6.2 GB, mostly X-row gathers"),
+    "lif_integrate": ((805_336_832 + 553_707_008) / 1_409_286_144,
+                      "ncu capture of the cell-by-cell form of the kernel at the same size"),
+}
 
 
 def roofline(algo_bytes, ms, kernel, key=None):
@@ -1212,7 +1221,9 @@ def bench_lif_integrate(args, dev, n=1 << 26):
                                                           ds.data_ptr(), n, 0.95, 0.0, 0.0, s.cuda_stream), "lif")
     for _ in range(args.warmup):
         run()
-    # parity: one more step from a fresh state against the oracle
+    # parity: one more step from a fresh state against the oracle (the
+    # warm-up launches must be done before the state is rewritten)
+    s.synchronize()
     dv.copy_(torch.from_numpy(v0))
     dt.copy_(torch.from_numpy(t0))
     torch.cuda.synchronize()

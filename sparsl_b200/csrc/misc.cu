@@ -161,6 +161,51 @@ __global__ void lif_integrate_kernel(float* __restrict__ v, float* __restrict__ 
   }
 }
 
+// The same four cells per thread with 16-byte loads and stores (v, theta and
+// the currents 16-byte aligned, the spike bytes 4-byte aligned); a partial
+// last quad is done cell by cell.
+__device__ __forceinline__ uint8_t lif_cell(float& vv, float& th, float c, float decay, float v_reset,
+                                            float dtheta) {
+  const float vol = fadd(fmul(vv, decay), c);
+  if (vol >= th) {
+    vv = v_reset;
+    th = fadd(th, dtheta);
+    return 1;
+  }
+  vv = vol;
+  return 0;
+}
+
+__global__ void lif_integrate4_kernel(float* __restrict__ v, float* __restrict__ theta,
+                                      const float* __restrict__ cur, uint8_t* __restrict__ spk, uint64_t n,
+                                      float decay, float v_reset, float dtheta) {
+  const uint64_t quads = (n + 3) / 4;
+  for (uint64_t q = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; q < quads;
+       q += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t i = 4 * q;
+    if (i + 4 <= n) {
+      float4 vv = __ldcs(reinterpret_cast<const float4*>(v) + q);
+      float4 th = __ldcs(reinterpret_cast<const float4*>(theta) + q);
+      const float4 c = __ldcs(reinterpret_cast<const float4*>(cur) + q);
+      uchar4 sp;
+      sp.x = lif_cell(vv.x, th.x, c.x, decay, v_reset, dtheta);
+      sp.y = lif_cell(vv.y, th.y, c.y, decay, v_reset, dtheta);
+      sp.z = lif_cell(vv.z, th.z, c.z, decay, v_reset, dtheta);
+      sp.w = lif_cell(vv.w, th.w, c.w, decay, v_reset, dtheta);
+      __stcs(reinterpret_cast<float4*>(v) + q, vv);
+      __stcs(reinterpret_cast<float4*>(theta) + q, th);
+      reinterpret_cast<uchar4*>(spk)[q] = sp;
+    } else {
+      for (uint64_t k = i; k < n; ++k) {
+        float vv = v[k], th = theta[k];
+        spk[k] = lif_cell(vv, th, cur[k], decay, v_reset, dtheta);
+        v[k] = vv;
+        theta[k] = th;
+      }
+    }
+  }
+}
+
 // pack_spikes_into (src/spikes.rs:237-262): LSB first, partial tail word
 // zero-filled, words beyond packed_len(n) cleared.
 __global__ void pack_kernel(const uint8_t* __restrict__ spk, uint64_t n, uint32_t* __restrict__ out,
@@ -329,7 +374,15 @@ cudaError_t launch_gather_weights(const void* w, const uint32_t* idx, uint64_t n
 cudaError_t launch_lif_integrate(float* v, float* theta, const float* cur, uint8_t* spk, uint64_t n,
                                  float decay, float v_reset, float dtheta, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
-  lif_integrate_kernel<<<grid_for(n, 256), 256, 0, s>>>(v, theta, cur, spk, n, decay, v_reset, dtheta);
+  const bool vec = ((uintptr_t)v % 16 == 0) && ((uintptr_t)theta % 16 == 0) && ((uintptr_t)cur % 16 == 0) &&
+                   ((uintptr_t)spk % 4 == 0);
+  if (vec) {
+    const uint64_t quads = (n + 3) / 4;
+    lif_integrate4_kernel<<<grid_for(quads, 256, 148 * 32), 256, 0, s>>>(v, theta, cur, spk, n, decay, v_reset,
+                                                                          dtheta);
+  } else {
+    lif_integrate_kernel<<<grid_for(n, 256), 256, 0, s>>>(v, theta, cur, spk, n, decay, v_reset, dtheta);
+  }
   return cudaGetLastError();
 }
 

@@ -175,6 +175,16 @@ def test_lif_integrate_and_fma_counterexample(O, cuda_device):
     host = np.zeros(n, np.float32)
     assert L.sparsl_dev_lif_integrate_device(cuda_device.handle, host.ctypes.data, dt.data_ptr(), dc.data_ptr(),
                                              ds.data_ptr(), n, 0.95, -0.25, 0.05, None) == _lib.SPARSL_ERR_INVALID
+    # arrays off the 16-byte grid take the cell-by-cell kernel: same bits
+    m = n - 1
+    dv2, dt2, dc2 = (torch.from_numpy(np.concatenate([[0], a])).float().cuda()[1:] for a in (v0[:m], t0[:m], cur[:m]))
+    ds2 = torch.zeros(m + 1, dtype=torch.uint8, device="cuda")[1:]
+    torch.cuda.synchronize()
+    assert L.sparsl_dev_lif_integrate_device(cuda_device.handle, dv2.data_ptr(), dt2.data_ptr(), dc2.data_ptr(),
+                                             ds2.data_ptr(), m, 0.95, -0.25, 0.05, None) == 0
+    assert L.sparsl_dev_wait(cuda_device.handle) == 0
+    assert_bits_equal(dv2.cpu().numpy(), vw[:m])
+    assert np.array_equal(ds2.cpu().numpy(), sw[:m])
 
 
 def test_resident_api_equals_slice_api(O, cuda_device):
