@@ -3,7 +3,7 @@
 // matrices.  Their column and weight arrays are dense [nrows x L] matrices, so
 // a warp's 32 rows x kChunk entries are one 2-D TMA box.
 //
-// Persistent and streaming: one CTA per SM, kEllWarps warps, and every warp
+// Persistent and streaming: one CTA per SM, 12 to 16 warps, and every warp
 // walks its own sequence of 32-row tiles.  Per warp a ring of
 // (column box, weight box) pairs is filled by cp.async.bulk.tensor into
 // swizzled shared memory and signalled by one mbarrier per stage; lane 0
@@ -224,13 +224,13 @@ __device__ __forceinline__ float spike_value(const uint32_t* s_x, const uint32_t
   return __uint_as_float(bit * 0x3f800000u);  // exactly 0.0f or 1.0f
 }
 
-template <int WK, int XM, int EPI, bool COMPACT>
-__global__ void __launch_bounds__(kEllWarps * 32, 1)
+template <int WK, int XM, int EPI, bool COMPACT, int NW>
+__global__ void __launch_bounds__(NW * 32, 1)
     ell_stream_kernel(const __grid_constant__ CUtensorMap tm_idx, const __grid_constant__ CUtensorMap tm_w,
                       const RowLaunch p, uint32_t L, uint32_t gs, uint32_t sum_words, uint32_t nst) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  __shared__ __align__(8) uint64_t bars[kEllWarps][kMaxStages];
-  __shared__ uint32_t s_fifo[kEllWarps][kFifo];
+  __shared__ __align__(8) uint64_t bars[NW][kMaxStages];
+  __shared__ uint32_t s_fifo[NW][kFifo];
   const int lane = threadIdx.x & 31;
   const int wid = threadIdx.x >> 5;
   // 1024-byte alignment keeps every swizzled box on its swizzle period.
@@ -238,11 +238,11 @@ __global__ void __launch_bounds__(kEllWarps * 32, 1)
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int kStageBytes = WBox<WK>::kStage;
   unsigned char* ring = smem + (size_t)wid * nst * kStageBytes;
-  uint32_t* s_x = reinterpret_cast<uint32_t*>(smem + (size_t)kEllWarps * nst * kStageBytes);
+  uint32_t* s_x = reinterpret_cast<uint32_t*>(smem + (size_t)NW * nst * kStageBytes);
 
   const uint32_t ntiles = (p.nlines + 31) / 32;
   const uint32_t nch = (L + kChunk - 1) / kChunk;
-  const uint32_t nwarps = gridDim.x * kEllWarps;
+  const uint32_t nwarps = gridDim.x * NW;
   const uint64_t pol = evict_first_policy();
 
   if (lane == 0) {
@@ -483,25 +483,19 @@ XPlan plan_x(const RowLaunch& p) {
 
 int g_num_sms = 0;
 
-template <int WK, int XM, int EPI, bool COMPACT>
-cudaError_t launch_t(const EllMaps& m, const RowLaunch& p, cudaStream_t stream) {
-  if (!p.tile_ticket) return cudaErrorInvalidValue;
-  auto kern = ell_stream_kernel<WK, XM, EPI, COMPACT>;
+template <int WK, int XM, int EPI, bool COMPACT, int NW>
+cudaError_t launch_nw(const EllMaps& m, const RowLaunch& p, cudaStream_t stream) {
+  auto kern = ell_stream_kernel<WK, XM, EPI, COMPACT, NW>;
   const XPlan xp = plan_x(p);
   constexpr size_t kStage = WBox<WK>::kStage;
   // As many stages per warp as the shared memory left by the spike operand holds.
-  size_t nst = (kSmemBudget - xp.bytes) / ((size_t)kEllWarps * kStage);
+  size_t nst = (kSmemBudget - xp.bytes) / ((size_t)NW * kStage);
   nst = std::min<size_t>(std::max<size_t>(nst, kMinStages), XM == X_DENSE ? kDenseStages : kMaxStages);
-  const size_t smem = 1024 + (size_t)kEllWarps * nst * kStage + xp.bytes;
+  const size_t smem = 1024 + (size_t)NW * nst * kStage + xp.bytes;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  if (!g_num_sms) {
-    int dev = 0;
-    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-    if ((e = cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-  }
   int per_sm = 0;
-  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kEllWarps * 32, smem)) != cudaSuccess)
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NW * 32, smem)) != cudaSuccess)
     return e;
   if (per_sm < 1) return cudaErrorInvalidConfiguration;
   if constexpr (XM == X_DENSE) {
@@ -514,12 +508,49 @@ cudaError_t launch_t(const EllMaps& m, const RowLaunch& p, cudaStream_t stream) 
       return e;
   }
   const uint32_t tiles = (p.nlines + 31) / 32;
-  const uint32_t want = (tiles + kEllWarps - 1) / kEllWarps;
+  const uint32_t want = (tiles + NW - 1) / NW;
   const uint32_t grid = std::max(1u, std::min(want, (uint32_t)(per_sm * g_num_sms)));
-  kern<<<grid, kEllWarps * 32, smem, stream>>>(*reinterpret_cast<const CUtensorMap*>(m.idx),
-                                               *reinterpret_cast<const CUtensorMap*>(m.w), p, m.L, xp.gs,
-                                               xp.sum_words, (uint32_t)nst);
+  kern<<<grid, NW * 32, smem, stream>>>(*reinterpret_cast<const CUtensorMap*>(m.idx),
+                                        *reinterpret_cast<const CUtensorMap*>(m.w), p, m.L, xp.gs, xp.sum_words,
+                                        (uint32_t)nst);
   return cudaGetLastError();
+}
+
+// Warps per CTA.  Every warp streams whole 32-row tiles, so a launch lasts
+// about (the most tiles any warp takes) x (one tile's time), and one tile's
+// time grows with the warps sharing an SM's bandwidth.  When the spike vector
+// is read through the summary (the large networks), the launch takes
+// whichever of 12, 14 and 16 warps gives the smallest ceil(tiles / warps) x
+// warps: a multi-GPU shard of 16,384 tiles runs 10 tiles on some of 1,776
+// warps (an 8 % tail) but at most 8 on 2,072.  Measured at 32,768 tiles:
+// 1.260 ms with 14 warps against 1.296 ms with 12.  Shorter launches keep 12:
+// config 3's 8,192 tiles measured 1.6 % slower with 14 warps, and dense x's
+// gathers want the L1 that more warps' stages would take.
+#ifndef SPARSL_ELL_NW_CHOICE
+#define SPARSL_ELL_NW_CHOICE 1
+#endif
+
+template <int WK, int XM, int EPI, bool COMPACT>
+cudaError_t launch_t(const EllMaps& m, const RowLaunch& p, cudaStream_t stream) {
+  if (!p.tile_ticket) return cudaErrorInvalidValue;
+  cudaError_t e;
+  if (!g_num_sms) {
+    int dev = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+  }
+  if constexpr (XM == X_BITS_GLOBAL && SPARSL_ELL_NW_CHOICE) {
+    const uint64_t tiles = (p.nlines + 31) / 32;
+    auto cost = [&](uint64_t nw) {
+      const uint64_t w = nw * (uint64_t)g_num_sms;
+      return (tiles + w - 1) / w * nw;
+    };
+    const uint64_t c12 = cost(12), c14 = cost(14), c16 = cost(16);
+    if (c14 < c12 && c14 <= c16) return launch_nw<WK, XM, EPI, COMPACT, 14>(m, p, stream);
+    if (c16 < c12 && c16 < c14) return launch_nw<WK, XM, EPI, COMPACT, 16>(m, p, stream);
+    return launch_nw<WK, XM, EPI, COMPACT, 12>(m, p, stream);
+  }
+  return launch_nw<WK, XM, EPI, COMPACT, kEllWarps>(m, p, stream);
 }
 
 template <int WK>

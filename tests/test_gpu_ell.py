@@ -59,9 +59,12 @@ def test_uniform_rows_spmv_and_fused_bit_exact(O, cuda_device, nrows, ncols, L, 
     assert np.array_equal(sp.astype(np.uint8), sw)
 
 
-@pytest.mark.parametrize("n,L", [(4096, 64), (32768, 512), (262144, 512)])
+@pytest.mark.parametrize("n,L", [(4096, 64), (32768, 512), (262144, 512), (60_000, 64), (600_000, 64)])
 def test_uniform_recurrent_network_bit_exact(O, cuda_device, n, L):
-    """The fixed fan-in network tick (trace, state, device-compacted indices)."""
+    """The fixed fan-in network tick (trace, state, device-compacted indices).
+    600,000 rows read the spike vector through the shared-memory summary and
+    launch 16 warps per CTA (18,750 tiles: whichever of 12, 14, 16 leaves the
+    fewest tiles on the busiest warp); the others launch 12."""
     r = np.random.default_rng(n)
     col = np.sort(r.integers(0, n, size=(n, L), dtype=np.uint32), axis=1).reshape(-1)
     rp = (np.arange(n + 1, dtype=np.uint64) * L).astype(np.uint32)
