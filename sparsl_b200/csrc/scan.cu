@@ -234,12 +234,12 @@ __global__ void __launch_bounds__(kScanBlock, SPARSL_SCAN_MIN_BLOCKS) scan_main(
       }
       const Aff htot{__shfl_sync(0xffffffffu, h.a, 31), __shfl_sync(0xffffffffu, h.b, 31)};
       // Lane t's warm-up starts at row t + 32 - W (W = kScanWarmSub); lane 0
-      // starts at halo row 16.  Lanes 1 .. W-1 start in the halo: the prefix
+      // starts at halo row 32 - kScanT0Sub.  Lanes 1 .. W-1 start in the halo: the prefix
       // through halo row t + 31 - W.  The others start in the tile: the halo
       // total, then lane t - W's in-tile exclusive prefix.
       constexpr int W = kScanWarmSub;
       static_assert(W >= 1 && W < 32, "warp 0 warm-up guesses");
-      const float hb = __shfl_sync(0xffffffffu, h.b, lane == 0 ? 15 : (lane + 31 - W) & 31);
+      const float hb = __shfl_sync(0xffffffffu, h.b, lane == 0 ? kScanHaloSub - kScanT0Sub - 1 : (lane + 31 - W) & 31);
       const Aff exw{__shfl_sync(0xffffffffu, ex.a, (lane + 32 - W) & 31),
                     __shfl_sync(0xffffffffu, ex.b, (lane + 32 - W) & 31)};
       w0_guess = lane < W ? hb : comb(htot, exw).b;
@@ -407,7 +407,7 @@ __global__ void __launch_bounds__(kScanBlock, SPARSL_SCAN_MIN_BLOCKS) scan_main(
       r0 = kScanHaloSub + 1;
     } else if (wid == 0) {
       b = w0_guess;
-      r0 = t == 0 ? kScanHaloSub / 2 : t + kScanHaloSub - kScanWarmSub;
+      r0 = t == 0 ? kScanHaloSub - kScanT0Sub : t + kScanHaloSub - kScanWarmSub;
     } else {
       b = s_Eb[t - kScanWarmSub];
       r0 = t - kScanWarmSub + kScanHaloSub;

@@ -21,6 +21,13 @@ constexpr int kScanK = SPARSL_SCAN_K;  // elements per thread (one sub-chunk)
 constexpr int kScanTile = kScanThreads * kScanK;
 constexpr int kScanWarmSub = SPARSL_SCAN_WARM_SUB;  // warm-up of an in-tile guess, in sub-chunks
 constexpr int kScanHaloSub = 32;   // warm-up of a tile's first warp, reaching into the previous tile
+#ifndef SPARSL_SCAN_T0_SUB
+#define SPARSL_SCAN_T0_SUB 16
+#endif
+// Warm-up of a tile's thread 0, in sub-chunks (less than the halo): a miss
+// there is only caught by the cross-tile check and repaired serially.
+constexpr int kScanT0Sub = SPARSL_SCAN_T0_SUB;
+static_assert(kScanT0Sub >= kScanWarmSub && kScanT0Sub < kScanHaloSub, "thread 0 warm-up");
 constexpr int kScanHalo = kScanHaloSub * kScanK;
 // Maps per chunk of the pipelined host-buffer scan (32 MiB each way).
 constexpr uint64_t kScanPipeChunk = 1ull << 22;
