@@ -7,10 +7,11 @@
 // writes.  It parallelises the *search* for each sub-chunk's incoming state
 // instead, and then proves every guess:
 //
-//  * Multiplier chain A (a' = x.a * a) -- made exact by construction.  A
-//    ninth warp per tile runs a decoupled look-back over one 64-bit word per
-//    tile: first the tile's transfer table (aggregate), later the exact
-//    multiplier leaving it (inclusive).  Tables of aggregate tiles compose
+//  * Multiplier chain A (a' = x.a * a) -- made exact by construction.  Each
+//    sub-chunk warp composes its 32 transfer tables; a ninth warp per tile
+//    composes the 8 warp tables and runs a decoupled look-back over one
+//    64-bit word per tile: first the tile's transfer table (aggregate),
+//    later the exact multiplier leaving it (inclusive).  Tables of aggregate tiles compose
 //    exactly onto the nearest inclusive value, which gives the exact A
 //    entering the tile; each sub-chunk's A then comes from its in-tile table
 //    prefix.  A table maps m to the multiplier leaving a run of maps when
@@ -20,12 +21,13 @@
 //  * Offset chain B (b' = x.a * b + x.b) -- speculated, with no look-back.
 //    The recurrence contracts: B's dependence on its value n elements earlier
 //    is a product of n multipliers.  So each thread replays the elements
-//    before its sub-chunk (kScanWarmSub sub-chunks, 192 elements; half the
-//    halo for a tile's thread 0) from a tree-composed guess that assumes
-//    B = 0 at the start of the tile, or of a 32-sub-chunk halo reaching into
-//    the previous tile; that assumption is contracted over at least the
-//    replay plus a warp's sub-chunks, and the replay removes the tree's
-//    rounding.  For contracting data this lands on the sequential trajectory
+//    before its sub-chunk (kScanWarmSub sub-chunks, 160 elements;
+//    kScanT0Sub for a tile's thread 0) from a tree-composed guess that
+//    assumes B = 0 at the start of the tile, or 32 sub-chunks before it for
+//    the first warp (a halo of kScanHaloSub sub-chunks staged with the tile,
+//    and before it the rest, which the look-back warp composes from global
+//    memory); that assumption is contracted over at least 1,024 elements,
+//    and the replay removes the tree's rounding.  For contracting data this lands on the sequential trajectory
 //    bit for bit; the look-back warp works meanwhile.
 //  * Verify: each thread's assumed incoming state is compared bitwise with the
 //    final state its predecessor actually produced.  If every adjacent pair
@@ -67,11 +69,14 @@ __device__ __forceinline__ uint32_t tab_at(uint32_t tab, uint32_t m) { return (t
 // m * 2^-149 entered it, or 8 when that output left the domain {0..7} * 2^-149.
 // Composition (t1 first, then t2) propagates the invalid marker.
 __device__ __forceinline__ uint32_t tab_comb(uint32_t t1, uint32_t t2) {
+  // Nibbles 8..15 of the widened t2 are the invalid marker, so an invalid
+  // entry of t1 (8) selects it.
+  const unsigned long long t2x = (unsigned long long)t2 | 0x8888888800000000ull;
   uint32_t r = 0;
 #pragma unroll
   for (uint32_t m = 0; m < 8; ++m) {
     const uint32_t e = tab_at(t1, m);
-    r |= ((e & 8u) ? 8u : tab_at(t2, e)) << (4 * m);
+    r |= (uint32_t)((t2x >> (4 * e)) & 0xfull) << (4 * m);
   }
   return r;
 }
@@ -82,8 +87,14 @@ __device__ __forceinline__ bool same_bits(Aff x, Aff y) {
   return __float_as_uint(x.a) == __float_as_uint(y.a) && __float_as_uint(x.b) == __float_as_uint(y.b);
 }
 
+// Thread numbering of scan_main: the look-back warp is hardware warp 0
+// (threads 256..287 here), sub-chunk thread t is hardware thread t + 32.  So
+// the look-back warp and sub-chunk warp 0, which carries the halo, run on
+// different SM sub-partitions (warp id mod 4).
+__device__ __forceinline__ int scan_tid() { return (threadIdx.x + kScanBlock - 32) % kScanBlock; }
+
 __device__ __forceinline__ void stamp(const ScanScratch& s, uint32_t tile, int k) {
-  if (s.timeline && threadIdx.x == 0) {
+  if (s.timeline && scan_tid() == 0) {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     s.timeline[(uint64_t)tile * 16 + k] = t;
@@ -95,12 +106,24 @@ constexpr unsigned long long kStIncl = 2ull << 32;  // payload: bits of the exac
 
 __device__ __forceinline__ uint32_t fbits(float x) { return __float_as_uint(x); }
 
-// Acquire-release atomic add at GPU scope: the tile-done count orders each
-// tile's look-back before the last tile clears the look-back words.
-__device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t* p, uint32_t v) {
-  uint32_t old;
-  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
+// 8-byte asynchronous global -> shared copy (cached in L1 on the way).
+__device__ __forceinline__ void cp_async8(float2* dst, const float2* src) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(d), "l"(src) : "memory");
+}
+
+// Two f32 lanes in one 64-bit register (lo = first), and their lane-wise
+// product: mul.rn.f32x2 rounds each product to nearest and keeps subnormals,
+// exactly as two separate fmul.rn.
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ unsigned long long fmul2(unsigned long long x, unsigned long long y) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(x), "l"(y));
+  return r;
 }
 
 // One thread walks the exact multiplier across a tile's 256 sub-chunks from
@@ -127,24 +150,36 @@ __device__ void walk_multiplier(float A, int first, const float2* sm, const uint
   }
 }
 
-// Two tiles per SM: a tile (32 sub-chunk rows of halo + 256 of tile, 32
-// maps each, padded) takes 76 KB of shared memory.
+// Three tiles per SM: a tile (16 sub-chunk rows of halo + 256 of tile, 32
+// maps each, padded) takes 70 KB of dynamic shared memory, and 72 registers
+// per thread.
 #ifndef SPARSL_SCAN_MIN_BLOCKS
-#define SPARSL_SCAN_MIN_BLOCKS 2
+#define SPARSL_SCAN_MIN_BLOCKS 3
 #endif
 __global__ void __launch_bounds__(kScanBlock, SPARSL_SCAN_MIN_BLOCKS) scan_main(const float2* __restrict__ in, float2* __restrict__ out,
                                                        uint64_t n, ScanScratch s, uint32_t* err, int has_entry,
                                                        float2 entry, const float2* entry_dev) {
   extern __shared__ __align__(16) float2 sm[];  // kRows x kRowStride
-  __shared__ float s_Eb[kScanThreads];  // in-tile exclusive guess of B (from identity)
-  __shared__ uint32_t s_tab[kScanThreads];
+  // s_Eb (phases 2-3) shares words with s_fa (phases 4-6); s_tab (phases
+  // 2-3) with s_fb (phases 4-6): each pair is separated by the barrier that
+  // ends phase 3.
+  __shared__ float s_u1[kScanThreads];
+  __shared__ uint32_t s_u2[kScanThreads];
+  float* const s_Eb = s_u1;    // in-tile exclusive guess of B (from identity)
+  uint32_t* const s_tab = s_u2;
+  __shared__ uint32_t s_tabx[kScanThreads];  // in-warp exclusive prefix of the tables
+  __shared__ uint32_t s_wtab[8];             // each warp's composed table
+  __shared__ uint32_t s_Awarp[8];            // fast path: multiplier entering each warp (m of m * 2^-149)
+  __shared__ int s_fast;
+  __shared__ float s_outb;  // B after the outer sub-chunks (before the halo), from B = 0
   __shared__ float s_Ain[kScanThreads + 1];
-  __shared__ float s_fa[kScanThreads], s_fb[kScanThreads];
+  float* const s_fa = s_u1;
+  float* const s_fb = reinterpret_cast<float*>(s_u2);
   __shared__ float s_wa[8], s_wb[8];
   __shared__ float s_wb0;  // thread 0's warmed-up entry B
   __shared__ uint32_t s_tile;
 
-  const int t = threadIdx.x;
+  const int t = scan_tid();
   const int lane = t & 31;
   const int wid = t >> 5;
   const bool lb_warp = wid == kScanThreads / 32;  // the look-back warp
@@ -157,22 +192,51 @@ __global__ void __launch_bounds__(kScanBlock, SPARSL_SCAN_MIN_BLOCKS) scan_main(
   stamp(s, tile, 0);
 
   // ---- 1. stage halo + tile into padded shared memory (identity outside [0, n)) ----
+  // Sub-chunks before the halo that the look-back warp composes from global
+  // memory, so that warp 0's guesses assume B = 0 32 sub-chunks before the
+  // tile, as far back as a full-length halo would.
+  constexpr int kOuterSub = 32 - kScanHaloSub;
+  float2 ov[kOuterSub > 0 ? kOuterSub : 1];
   {
-    constexpr int kPer = (kScanHalo + kScanTile) / kScanBlock;
-    static_assert((kScanHalo + kScanTile) % kScanBlock == 0, "tile staging");
-    float2 v[kPer];
+    // The look-back warp issues its reads of the outer sub-chunks first
+    // (lane k: kOuterSub consecutive maps).
+    if (kOuterSub > 0 && lb_warp) {
+#pragma unroll
+      for (int i = 0; i < kOuterSub; ++i) {
+        const int64_t g = (int64_t)tile_start - kScanHalo - kOuterSub * 32 + lane * kOuterSub + i;
+        ov[i] = (g >= 0 && (uint64_t)g < n) ? __ldg(in + g) : make_float2(1.0f, 0.0f);
+      }
+    }
+    // Asynchronous 8-byte copies straight into the padded rows: every load
+    // of the tile is in flight at once and none holds a register.
+    constexpr int kStage = kScanHalo + kScanTile;
+    constexpr int kPer = (kStage + kScanBlock - 1) / kScanBlock;
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
       const int li = t + i * kScanBlock;
-      const int64_t g = (int64_t)tile_start - kScanHalo + li;
-      v[i] = make_float2(1.0f, 0.0f);
-      if (g >= 0 && (uint64_t)g < n) v[i] = __ldg(in + g);
+      if (kStage % kScanBlock == 0 || li < kStage) {
+        const int64_t g = (int64_t)tile_start - kScanHalo + li;
+        float2* dst = sm + (li / kScanK) * kRowStride + (li % kScanK);
+        if (g >= 0 && (uint64_t)g < n)
+          cp_async8(dst, in + g);
+        else
+          *dst = make_float2(1.0f, 0.0f);
+      }
     }
+    if (kOuterSub > 0 && lb_warp) {
+      // The outer sub-chunks composed in order (lane k's maps, then a warp
+      // scan); warp 0's guesses continue from their B.
+      Aff o{ov[0].x, ov[0].y};
 #pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      const int li = t + i * kScanBlock;
-      sm[(li / kScanK) * kRowStride + (li % kScanK)] = v[i];
+      for (int i = 1; i < kOuterSub; ++i) o = comb(o, Aff{ov[i].x, ov[i].y});
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const Aff u = Aff{__shfl_up_sync(0xffffffffu, o.a, d), __shfl_up_sync(0xffffffffu, o.b, d)};
+        if (lane >= d) o = comb(u, o);
+      }
+      if (lane == 31) s_outb = o.b;
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
     // A run that continues a longer sequence: its first map is the entry
     // state combined with x[0], exactly as the fold combines it; the
     // copy-first rule then emits it unchanged.  The thread that staged x[0]
@@ -193,19 +257,43 @@ __global__ void __launch_bounds__(kScanBlock, SPARSL_SCAN_MIN_BLOCKS) scan_main(
   float w0_guess = 0.f;  // warp 0: guessed B at the start of its warm-up
   if (!lb_warp) {
     const float2* row = sm + (t + kScanHaloSub) * kRowStride;
+    // The sub-chunk's transfer table first: the look-back warp waits for it.
+    // Entries m and m + 1 ride in one packed multiply (two separate f32
+    // products, rounded to nearest, subnormals kept).
+    uint32_t tab = 0;
+    {
+      unsigned long long v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] = pack2(__uint_as_float(2 * i), __uint_as_float(2 * i + 1));
+#pragma unroll
+      for (int j = 0; j < kScanK; ++j) {
+        const unsigned long long xx = pack2(row[j].x, row[j].x);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = fmul2(xx, v[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t b0 = (uint32_t)v[i], b1 = (uint32_t)(v[i] >> 32);
+        tab |= (b0 <= 7u ? b0 : 8u) << (8 * i);
+        tab |= (b1 <= 7u ? b1 : 8u) << (8 * i + 4);
+      }
+    }
+    s_tab[t] = tab;
+    // Compose the warp's 32 tables now, so that the look-back warp only
+    // composes 8 and publishes the tile's table early.
+    uint32_t itab = tab;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const uint32_t o = __shfl_up_sync(0xffffffffu, itab, d);
+      if (lane >= d) itab = tab_comb(o, itab);
+    }
+    const uint32_t xtab = __shfl_up_sync(0xffffffffu, itab, 1);
+    s_tabx[t] = lane == 0 ? kTabId : xtab;
+    if (lane == 31) s_wtab[wid] = itab;
+    asm volatile("bar.arrive 3, %0;" ::"n"(kScanBlock) : "memory");
     Aff agg{row[0].x, row[0].y};
 #pragma unroll
     for (int j = 1; j < kScanK; ++j) agg = comb(agg, Aff{row[j].x, row[j].y});
-    uint32_t tab = 0;
-#pragma unroll
-    for (uint32_t m = 0; m < 8; ++m) {
-      float v = __uint_as_float(m);
-#pragma unroll
-      for (int j = 0; j < kScanK; ++j) v = fmul(row[j].x, v);
-      const uint32_t b = fbits(v);
-      tab |= (b <= 7u ? b : 8u) << (4 * m);
-    }
-    s_tab[t] = tab;
     inc = agg;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
@@ -220,46 +308,54 @@ __global__ void __launch_bounds__(kScanBlock, SPARSL_SCAN_MIN_BLOCKS) scan_main(
       Aff ex{__shfl_up_sync(0xffffffffu, inc.a, 1), __shfl_up_sync(0xffffffffu, inc.b, 1)};
       if (lane == 0) ex = Aff{1.f, 0.f};
       s_Eb[t] = ex.b;
-      // Warp 0's warm-up guesses reach into the 32-sub-chunk halo: lane t
-      // composes halo sub-chunk t, a warp scan chains them (from B = 0 at the
-      // halo start), and the halo total continues into the in-tile prefix.
-      const float2* hrow = sm + t * kRowStride;
-      Aff h{hrow[0].x, hrow[0].y};
+      // Warp 0's warm-up guesses reach into the halo: lane t < H composes
+      // halo sub-chunk t, a warp scan chains them (from the look-back warp's
+      // B before the halo), and the halo total continues into the in-tile
+      // prefix.
+      Aff h{1.f, 0.f};
+      if (lane < kScanHaloSub) {
+        const float2* hrow = sm + lane * kRowStride;
+        h = Aff{hrow[0].x, hrow[0].y};
 #pragma unroll
-      for (int j = 1; j < kScanK; ++j) h = comb(h, Aff{hrow[j].x, hrow[j].y});
+        for (int j = 1; j < kScanK; ++j) h = comb(h, Aff{hrow[j].x, hrow[j].y});
+      }
 #pragma unroll
       for (int d = 1; d < 32; d <<= 1) {
         const Aff o = Aff{__shfl_up_sync(0xffffffffu, h.a, d), __shfl_up_sync(0xffffffffu, h.b, d)};
         if (lane >= d) h = comb(o, h);
       }
+      const float ob = kOuterSub > 0 ? s_outb : 0.f;  // B entering the halo, from B = 0 at the outer start
+      h.b = fadd(fmul(h.a, ob), h.b);
       const Aff htot{__shfl_sync(0xffffffffu, h.a, 31), __shfl_sync(0xffffffffu, h.b, 31)};
-      // Lane t's warm-up starts at row t + 32 - W (W = kScanWarmSub); lane 0
-      // starts at halo row 32 - kScanT0Sub.  Lanes 1 .. W-1 start in the halo: the prefix
-      // through halo row t + 31 - W.  The others start in the tile: the halo
-      // total, then lane t - W's in-tile exclusive prefix.
+      // Lane t's warm-up starts at row t + H - W (H = kScanHaloSub, W =
+      // kScanWarmSub); lane 0 starts at halo row H - kScanT0Sub.  Lanes
+      // 1 .. W-1 start in the halo: the prefix through halo row t + H - 1 - W.
+      // The others start in the tile: the halo total, then lane t - W's
+      // in-tile exclusive prefix.
       constexpr int W = kScanWarmSub;
-      static_assert(W >= 1 && W < 32, "warp 0 warm-up guesses");
-      const float hb = __shfl_sync(0xffffffffu, h.b, lane == 0 ? kScanHaloSub - kScanT0Sub - 1 : (lane + 31 - W) & 31);
+      constexpr int H = kScanHaloSub;
+      static_assert(W >= 1 && W <= H, "warp 0 warm-up guesses");
+      const float hb = __shfl_sync(0xffffffffu, h.b, lane == 0 ? H - kScanT0Sub - 1 : (lane + H - 1 - W) & 31);
       const Aff exw{__shfl_sync(0xffffffffu, ex.a, (lane + 32 - W) & 31),
                     __shfl_sync(0xffffffffu, ex.b, (lane + 32 - W) & 31)};
       w0_guess = lane < W ? hb : comb(htot, exw).b;
     }
   }
   // Warp 0's warm-up needs nothing from the block scan: it only signals the
-  // barrier and starts at once.  The other warps finish the block scan first.
-  if (wid == 0) {
+  // barrier and starts at once, and so does the look-back warp, which waits
+  // for the warps' tables instead.  The other warps finish the block scan.
+  if (wid == 0 || lb_warp) {
     asm volatile("bar.arrive 1, %0;" ::"n"(kScanBlock) : "memory");
+    if (lb_warp) asm volatile("bar.sync 3, %0;" ::"n"(kScanBlock) : "memory");
   } else {
     asm volatile("bar.sync 1, %0;" ::"n"(kScanBlock) : "memory");
-    if (!lb_warp) {
-      Aff wpre{s_wa[0], s_wb[0]};
-      for (int w2 = 1; w2 < wid; ++w2) wpre = comb(wpre, Aff{s_wa[w2], s_wb[w2]});
-      inc = comb(wpre, inc);
-      float exb = __shfl_up_sync(0xffffffffu, inc.b, 1);
-      if (lane == 0) exb = wpre.b;
-      s_Eb[t] = exb;
-      asm volatile("bar.sync 2, %0;" ::"n"(kScanThreads - 32) : "memory");
-    }
+    Aff wpre{s_wa[0], s_wb[0]};
+    for (int w2 = 1; w2 < wid; ++w2) wpre = comb(wpre, Aff{s_wa[w2], s_wb[w2]});
+    inc = comb(wpre, inc);
+    float exb = __shfl_up_sync(0xffffffffu, inc.b, 1);
+    if (lane == 0) exb = wpre.b;
+    s_Eb[t] = exb;
+    asm volatile("bar.sync 2, %0;" ::"n"(kScanThreads - 32) : "memory");
   }
   stamp(s, tile, 2);
 
@@ -278,20 +374,18 @@ __global__ void __launch_bounds__(kScanBlock, SPARSL_SCAN_MIN_BLOCKS) scan_main(
         s_Ain[1] = A;
         walk_multiplier(A, 1, sm, s_tab, s_Ain);
         st_relaxed_u64(s.flags, kStIncl | fbits(s_Ain[kScanThreads]));
+        s_fast = 0;
       }
     } else {
-      // Lane k composes the tables of sub-chunks 8k .. 8k+7; a warp scan
-      // then gives every lane its entry table and the tile's table.
-      uint32_t lt = s_tab[8 * lane];
+      // Lane w < 8 holds warp w's composed table; a scan over the 8 lanes
+      // gives each its entry table (ext) and lane 7 the tile's table.
+      uint32_t it = lane < 8 ? s_wtab[lane] : kTabId;
 #pragma unroll
-      for (int i = 1; i < 8; ++i) lt = tab_comb(lt, s_tab[8 * lane + i]);
-      uint32_t it = lt;
-#pragma unroll
-      for (int d = 1; d < 32; d <<= 1) {
+      for (int d = 1; d < 8; d <<= 1) {
         const uint32_t o = __shfl_up_sync(0xffffffffu, it, d);
         if (lane >= d) it = tab_comb(o, it);
       }
-      const uint32_t TG = __shfl_sync(0xffffffffu, it, 31);
+      const uint32_t TG = __shfl_sync(0xffffffffu, it, 7);
       uint32_t ext = __shfl_up_sync(0xffffffffu, it, 1);
       if (lane == 0) ext = kTabId;
       if (lane == 0) st_relaxed_u64(s.flags + tile, kStAgg | TG);
@@ -370,18 +464,19 @@ __global__ void __launch_bounds__(kScanBlock, SPARSL_SCAN_MIN_BLOCKS) scan_main(
       const bool fast = ok && in_domain(Aent) && !(tab_at(TG, fbits(Aent)) & 8u);
       if (fast) {
         const uint32_t m = fbits(Aent);
-        if (lane == 0) st_relaxed_u64(s.flags + tile, kStIncl | tab_at(TG, m));  // successors stop here
-        uint32_t v = tab_at(ext, m);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          s_Ain[8 * lane + i] = __uint_as_float(v);
-          v = tab_at(s_tab[8 * lane + i], v);
+        if (lane == 0) {
+          st_relaxed_u64(s.flags + tile, kStIncl | tab_at(TG, m));  // successors stop here
+          s_Ain[0] = Aent;
+          s_Ain[kScanThreads] = __uint_as_float(tab_at(TG, m));
+          s_fast = 1;
         }
-        if (lane == 31) s_Ain[kScanThreads] = __uint_as_float(v);
+        // Sub-chunk c of warp w enters with s_tabx[c] applied to s_Awarp[w].
+        if (lane < 8) s_Awarp[lane] = tab_at(ext, m);
       } else if (lane == 0) {
         s_Ain[0] = Aent;
         walk_multiplier(Aent, 0, sm, s_tab, s_Ain);
         st_relaxed_u64(s.flags + tile, kStIncl | fbits(s_Ain[kScanThreads]));
+        s_fast = 0;
       }
       if (s.timeline && lane == 0) {
         s.timeline[(uint64_t)tile * 16 + 11] = windows;
@@ -391,12 +486,12 @@ __global__ void __launch_bounds__(kScanBlock, SPARSL_SCAN_MIN_BLOCKS) scan_main(
     }
   } else if (!copy_first) {
     // Each thread replays the elements before its sub-chunk from a tree
-    // guess that assumes B = 0 at the start of the tile (warps 1-7) or of the
-    // halo (warp 0); by contraction over the replay and the sub-chunks
-    // before it that no longer shows, and the replay removes the tree's
-    // rounding.  Replays are kScanWarmSub sub-chunks, except thread 0's,
-    // which only the cross-tile check (and a serial repair) would catch: it
-    // replays half the halo.  In tile 0 the first element is copied, so warp
+    // guess that assumes B = 0 at the start of the tile (warps 1-7) or 32
+    // sub-chunks before it (warp 0); by contraction over the replay and the
+    // sub-chunks before it that no longer shows, and the replay removes the
+    // tree's rounding.  Replays are kScanWarmSub sub-chunks, except thread
+    // 0's, which only the cross-tile check (and a serial repair) would catch:
+    // it replays kScanT0Sub.  In tile 0 the first element is copied, so warp
     // 0 starts there exactly.
     int r0;
     float b;
@@ -423,20 +518,6 @@ __global__ void __launch_bounds__(kScanBlock, SPARSL_SCAN_MIN_BLOCKS) scan_main(
     wb = b;
     if (t == 0) s_wb0 = b;
   }
-  // The look-back warp is done with the look-back words: count the tile out.
-  // The last tile to do so clears them for the next call (no tile reads them
-  // after its own look-back).
-  if (lb_warp) {
-    uint32_t last = 0;
-    if (lane == 0) last = atom_add_acq_rel(s.ticket + 1, 1u) == ntiles - 1 ? 1u : 0u;
-    if (__shfl_sync(0xffffffffu, last, 0)) {
-      for (uint64_t i = lane; i < ntiles; i += 32) s.flags[i] = 0ull;
-      if (lane == 0) {
-        s.ticket[0] = 0;
-        s.ticket[1] = 0;
-      }
-    }
-  }
   __syncthreads();  // every warm-up read is done before rows are overwritten
   stamp(s, tile, 3);
 
@@ -452,7 +533,7 @@ __global__ void __launch_bounds__(kScanBlock, SPARSL_SCAN_MIN_BLOCKS) scan_main(
       b = wrow[0].y;
       j0 = 1;
     } else {
-      a = s_Ain[t];  // exact by construction
+      a = s_fast ? __uint_as_float(tab_at(s_tabx[t], s_Awarp[wid])) : s_Ain[t];  // exact by construction
       b = wb;
     }
     assumed = Aff{a, b};
@@ -538,8 +619,13 @@ __global__ void __launch_bounds__(kScanBlock, SPARSL_SCAN_MIN_BLOCKS) scan_main(
 }
 
 // Cross-tile check: every tile's assumed entry state against the exit state
-// its predecessor produced, bit for bit.
+// its predecessor produced, bit for bit.  It runs after every tile is done,
+// so it also returns the look-back words and the ticket to zero for the next
+// call.
 __global__ void __launch_bounds__(256) scan_check(ScanScratch s, uint32_t ntiles) {
+  for (uint32_t T = blockIdx.x * blockDim.x + threadIdx.x; T < ntiles; T += gridDim.x * blockDim.x)
+    s.flags[T] = 0ull;
+  if (blockIdx.x == 0 && threadIdx.x == 0) s.ticket[0] = 0;
   for (uint32_t T = blockIdx.x * blockDim.x + threadIdx.x + 1; T < ntiles; T += gridDim.x * blockDim.x) {
     const Aff l{s.last[2 * (uint64_t)(T - 1)], s.last[2 * (uint64_t)(T - 1) + 1]};
     const Aff a{s.assumed[2 * (uint64_t)T], s.assumed[2 * (uint64_t)T + 1]};
@@ -707,6 +793,9 @@ cudaError_t launch_scan(const float* in, float* out, uint64_t n, const ScanScrat
   const size_t smem = sizeof(float2) * kRows * kRowStride;
   cudaError_t e = cudaFuncSetAttribute(scan_main, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
+  // All of the unified L1/shared storage as shared memory: three tiles per SM.
+  e = cudaFuncSetAttribute(scan_main, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (e != cudaSuccess) return e;
   const float2 ent = entry ? make_float2(entry[0], entry[1]) : make_float2(1.0f, 0.0f);
   scan_main<<<(unsigned)ntiles, kScanBlock, smem, stream>>>(reinterpret_cast<const float2*>(in),
                                                               reinterpret_cast<float2*>(out), n, s, err,
@@ -714,7 +803,7 @@ cudaError_t launch_scan(const float* in, float* out, uint64_t n, const ScanScrat
                                                               reinterpret_cast<const float2*>(entry_dev));
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  if (ntiles > 1) {
+  {
     const uint32_t blocks = (uint32_t)std::min<uint64_t>((ntiles + 255) / 256, 592);
     scan_check<<<blocks, 256, 0, stream>>>(s, (uint32_t)ntiles);
     e = cudaGetLastError();

@@ -6,23 +6,29 @@
 
 namespace sparsl {
 
-// Sub-chunks of 32 maps with a 192-map warm-up replay: at 2^26 maps 0.455 ms
-// against 0.497 ms for 16-map sub-chunks with a 128-map replay (the replay is
-// amortised over twice the output), and no repairs instead of one.
+// Sub-chunks of 32 maps with a 160-map warm-up replay (the replay is
+// amortised over 32 maps of output).
 #ifndef SPARSL_SCAN_K
 #define SPARSL_SCAN_K 32
 #endif
 #ifndef SPARSL_SCAN_WARM_SUB
-#define SPARSL_SCAN_WARM_SUB 6
+#define SPARSL_SCAN_WARM_SUB 5
 #endif
 constexpr int kScanThreads = 256;  // sub-chunk threads per tile (8 warps)
 constexpr int kScanBlock = kScanThreads + 32;  // plus one look-back warp
 constexpr int kScanK = SPARSL_SCAN_K;  // elements per thread (one sub-chunk)
 constexpr int kScanTile = kScanThreads * kScanK;
 constexpr int kScanWarmSub = SPARSL_SCAN_WARM_SUB;  // warm-up of an in-tile guess, in sub-chunks
-constexpr int kScanHaloSub = 32;   // warm-up of a tile's first warp, reaching into the previous tile
+#ifndef SPARSL_SCAN_HALO_SUB
+#define SPARSL_SCAN_HALO_SUB 16
+#endif
+// Rows of the previous tile staged with a tile for its first warp's warm-up,
+// in sub-chunks (the look-back warp composes the 32 - kScanHaloSub before
+// them from global memory).
+constexpr int kScanHaloSub = SPARSL_SCAN_HALO_SUB;
+static_assert(kScanHaloSub >= 1 && kScanHaloSub <= 32, "halo rows (one per lane of warp 0)");
 #ifndef SPARSL_SCAN_T0_SUB
-#define SPARSL_SCAN_T0_SUB 16
+#define SPARSL_SCAN_T0_SUB 10
 #endif
 // Warm-up of a tile's thread 0, in sub-chunks (less than the halo): a miss
 // there is only caught by the cross-tile check and repaired serially.
@@ -36,7 +42,7 @@ constexpr uint64_t kScanPipeChunk = 1ull << 22;
 // left in its zero state (or self-resetting) after each call.
 struct ScanScratch {
   unsigned long long* flags;  // ntiles look-back words: [33:32] status, [31:0] payload
-  uint32_t* ticket;         // [0] tile ticket, [1] done counter
+  uint32_t* ticket;         // [0] tile ticket
   float* assumed;           // 2 * ntiles: thread 0's assumed incoming state
   float* last;              // 2 * ntiles: each tile's last output state
   uint32_t* mis_bits;       // ntiles * 8 words: in-tile sub-chunk mismatches
