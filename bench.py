@@ -88,7 +88,9 @@ def peaks():
 TRAFFIC_RATIO = {
     "ragged_spmv": ((459_123_968 + 8_070_400) / 408_395_452,
                     "ncu capture of the same launch (bench.py --workload ragged), 1,000,000 rows"),
-    "spmv": (51_990_000 / 52_800_004, "ncu capture of the same launch (bench.py --workload spmv)"),
+    "spmv": (39_812_352 / 52_800_004, "ncu capture of the same launch (bench.py --workload spmv): the panel "
+                                      "layout's 16-bit panel-relative columns read less than the CSR bytes"),
+    "spmv_f16": (27_011_584 / 40_000_004, "ncu capture of the same launch (bench.py --workload spmv), f16 weights"),
     "spmm_f32": (6.2e9 / 1_164_395_452, "ncu capture of the same launch (bench.py --workload spmm): DRAM "
                                         "throughput x duration, about 6.2 GB, mostly X-row gathers"),
     "lif_integrate": ((805_336_832 + 553_707_008) / 1_409_286_144,
@@ -719,7 +721,7 @@ def bench_spmv(args, dev, want_cpu):
     algo16 = col.size * 6 + (SPMV_N + 1) * 4 + SPMV_N * 4 + 2 * SPMV_N * 4
     f16, ms16 = measure(op16, L.sparsl_op_spmv_device, dx, SPMV_N, algo16,
                         lambda ref: O.spmv(csr, w16, x, ref, par=True))
-    f16["roofline"] = roofline(algo16, ms16, "ell_stream_kernel<f16 weights, dense x>", "spmv_f16")
+    f16["roofline"] = roofline(algo16, ms16, "panel_spmv_kernel<f16 weights, x in shared-memory panels>", "spmv_f16")
     del op16
     opt = dev.prepare_with_transpose(S.Csr(rp, col, SPMV_N), SPMV_N, w)
     xt = r.uniform(0.0, 1.0, SPMV_N).astype(np.float32)
@@ -762,7 +764,7 @@ def bench_spmv(args, dev, want_cpu):
             "e2e": {"value": algo / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 2 * SPMV_N * 4,
                     "d2h_bytes_per_step": SPMV_N * 4, "path": "sparsl_op_spmv, pinned host x/y"},
             "bit_exact_vs_oracle": exact, "cpu_baseline": cpu,
-            "roofline": roofline(algo, ms, "ell_stream_kernel<f32, dense x>", "spmv"),
+            "roofline": roofline(algo, ms, "panel_spmv_kernel<f32, x in shared-memory panels>", "spmv"),
             "f16_weights": f16, "transpose": tr, "reverse_index": rev}
 
 

@@ -27,6 +27,7 @@
 #include "common.cuh"
 #include "csc.cuh"
 #include "ell.cuh"
+#include "panel.cuh"
 #include "host.hpp"
 #include "misc.cuh"
 #include "net.cuh"
@@ -354,6 +355,10 @@ struct sparsl_op {
   DBuf sell_ptr, sell_row, sell_eidx, w_sell, sell_ctr;
   // Uniform row length: TMA tensor maps over col / w as [nrows x L] matrices.
   EllMaps ell;
+  // Uniform row length and x within kPanelMaxPanels shared-memory panels:
+  // the tile-interleaved copy of col / w for the dense-x SpMV (panel.cu).
+  PanelOp panel;
+  DBuf pcol, pw, psplit;
   uint32_t ell_epoch = 0;  // tag of the last compacting TMA launch's flags
   // resident scratch (the write / step / sync API)
   DBuf rx, rxs[2], ry, rv, rth, rspk;
@@ -445,6 +450,8 @@ RowLaunch fwd_launch(sparsl_op* op) {
 // Forward launches take the TMA-pipelined kernel when the operator's rows all
 // have the same length, the generic row-fold kernel otherwise.
 cudaError_t launch_fwd(sparsl_op* op, const RowLaunch& p, cudaStream_t s) {
+  if (op->panel.ok && p.xmode == X_DENSE && p.epilogue == EPI_ACCUM && !p.eidx && !p.out_bits && !p.idx_list)
+    return launch_panel_spmv(op->panel, p.x, p.y, s);
   if (!op->ell.ok && op->row_ordered && !p.eidx) {
     // Skewed rows: warps fold rows in descending-length order; the packed
     // spike words (and from them the index list) come from the spike bytes.
@@ -1327,6 +1334,30 @@ int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int 
     bool uniform = L <= 0xffffffffull;
     for (uint64_t r = 0; uniform && r <= nrows; ++r) uniform = (uint64_t)row_ptr[r] == r * L;
     if (uniform) ell_encode(op->ell, op->col.as<uint32_t>(), op->w.p, wkind_of(precision), nrows, (uint32_t)L);
+    // Dense-x SpMV with x in shared memory: the operator's own (not a
+    // borrowed) arrays, interleaved by tiles of 32 rows, up to 2^30 entries.
+    uint32_t width = 0, npanels = 0;
+    if (uniform && !borrow && nnz <= (1ull << 30) && L <= kPanelMaxRowLen &&
+        panel_geometry(op->ncols, width, npanels)) {
+      PALLOC(op->pcol, panel_col_elems(nrows, (uint32_t)L) * 2, false, "interleaved col");
+      PALLOC(op->pw, panel_w_elems(nrows, (uint32_t)L) * wbytes, false, "interleaved values");
+      PALLOC(op->psplit, panel_split_elems(nrows, npanels) * 2, false, "panel split points");
+      if (launch_panel_build(op->col.as<uint32_t>(), nrows, (uint32_t)L, width, npanels, op->pcol.as<uint16_t>(),
+                             op->psplit.as<uint16_t>(), op->stream) != cudaSuccess ||
+          launch_panel_weights(op->w.p, nrows, (uint32_t)L, (int)wbytes, op->pw.p, op->stream) != cudaSuccess)
+        return bail(fail_cuda("prepare", cudaGetLastError()));
+      PanelOp& pn = op->panel;
+      pn.col16 = op->pcol.as<uint16_t>();
+      pn.w = op->pw.p;
+      pn.split = op->psplit.as<uint16_t>();
+      pn.wkind = wkind_of(precision);
+      pn.nrows = (uint32_t)nrows;
+      pn.L = (uint32_t)L;
+      pn.ncols = op->ncols;
+      pn.width = width;
+      pn.npanels = npanels;
+      pn.ok = true;
+    }
   }
   // SpMM work units.  Equal rows: fixed runs of rows.  Otherwise rows by
   // descending length (ties by index), cut into units of >= kSpmmUnitNnz
@@ -1442,7 +1473,7 @@ void sparsl_op_destroy(sparsl_op* op) {
                   &op->rspk,    &op->idx_list, &op->tile_flags, &op->ticket, &op->trace, &op->sx,
                   &op->sbits,   &op->sy,      &op->sv,      &op->sth,     &op->sspk,
                   &op->spmm_order, &op->spmm_units, &op->spmm_ctr, &op->spmm_rorder, &op->spmm_runits,
-                  &op->row_order};
+                  &op->row_order, &op->pcol, &op->pw, &op->psplit};
   for (DBuf* b : bufs) dfree(*b);
   op->err.release();
   if (op->side) cudaStreamSynchronize(op->side);
@@ -1475,6 +1506,7 @@ int sparsl_op_weight_precision(sparsl_op* op) { return op ? op->precision : -1; 
 int sparsl_op_layouts(sparsl_op* op) {
   if (!op) return 0;
   return (op->ell.ok ? SPARSL_LAYOUT_ELL : 0) | (op->row_ordered ? SPARSL_LAYOUT_ROW_ORDER : 0) |
+         (op->panel.ok ? SPARSL_LAYOUT_X_PANELS : 0) |
          (op->sell_ok ? SPARSL_LAYOUT_SLICED_REVERSE : 0) |
          (op->has_t && !op->sell_ok ? SPARSL_LAYOUT_CSC : 0);
 }
@@ -1501,6 +1533,7 @@ int sparsl_op_force_plain_row_fold(sparsl_op* op) {
   // forward launch through the generic row fold in natural row order.
   op->ell.ok = false;
   op->row_ordered = false;
+  op->panel.ok = false;
   return SPARSL_OK;
 }
 
@@ -1518,6 +1551,9 @@ int sparsl_op_set_weights(sparsl_op* op, const float* weights, uint64_t n) {
     encode_narrow(op->precision, weights, narrow.data(), n);
     CK("set_weights", cudaMemcpyAsync(op->w.p, narrow.data(), n * 2, cudaMemcpyHostToDevice, op->stream));
   }
+  if (op->panel.ok)
+    CK("set_weights", launch_panel_weights(op->w.p, op->nrows, op->panel.L, op->precision == 0 ? 4 : 2, op->pw.p,
+                                           op->stream));
   if (op->sell_ok)
     CK("set_weights", launch_gather_weights(op->w.p, op->sell_eidx.as<uint32_t>(), op->sell_total,
                                             op->precision == 0 ? 4 : 2, op->w_sell.p, op->stream));

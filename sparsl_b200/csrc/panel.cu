@@ -1,0 +1,307 @@
+// Dense-x SpMV over a uniform-length operator with x in shared memory.
+//
+// The streaming row fold (ell.cu) gathers x through L1, one scattered sector
+// per gathered entry, and that gather rate bounds it.  Here one CTA per SM
+// stages a panel of x (up to 216 KiB) in shared memory, where a warp's 32
+// random gathers cost a few bank cycles instead of 32 L1 sectors.  When x is
+// wider than one panel the CTA walks the panels in order: every lane owns one
+// row and keeps the row's running fold in a register, and in panel k folds
+// the row's entries whose columns fall in that panel.  The columns of a row
+// are non-decreasing (the CSR gate's rule, src/sparse.rs:31), so those
+// entries are the positions [split_k, split_k+1) that follow the ones panel
+// k - 1 folded: each entry is folded once, in stored order, and the result is
+// the reference's row_dot bit for bit (src/backend/mod.rs:2259-2267).
+//
+// The operator is read from the tile-interleaved copy described in
+// panel.cuh: 16-bit panel-relative columns and the weights in 16-byte groups
+// per lane, so one load brings a lane 8 columns, and a warp's load is 512
+// contiguous bytes.  Two batches of 8 positions are in flight while a third
+// folds, and a pass's first two batches load while the panel is copied in.
+#include <algorithm>
+#include <atomic>
+
+#include "common.cuh"
+#include "panel.cuh"
+
+namespace sparsl {
+namespace {
+
+constexpr uint32_t kPanelMaxWarps = 24;
+
+struct PanelLaunch {
+  const uint4* col16;  // 16-byte groups of 8 columns
+  const uint4* w;      // 16-byte groups of 4 (f32) or 8 (16-bit) weights
+  const uint16_t* split;
+  const float* x;
+  float* y;
+  uint32_t nrows, L, ncols, width, npanels;
+  uint32_t Lg;  // 8-position groups per row: ceil(L / 8)
+};
+
+__device__ __forceinline__ void cp_async16(float4* dst, const float4* src) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+
+// Entry positions jb .. jb + 7 (jb a multiple of 8) of one lane's row.
+template <int WK>
+struct Batch {
+  uint4 c;
+  uint4 w[WK == W_F32 ? 2 : 1];
+  __device__ __forceinline__ void load(const PanelLaunch& p, uint64_t tile, uint32_t lane, uint32_t jb) {
+    const uint64_t g = (tile * p.Lg + jb / 8) * 32 + lane;
+    c = __ldg(p.col16 + g);
+    if constexpr (WK == W_F32) {
+      const uint64_t gw = (tile * p.Lg * 2 + jb / 4) * 32 + lane;
+      w[0] = __ldg(p.w + gw);
+      w[1] = __ldg(p.w + gw + 32);
+    } else {
+      w[0] = __ldg(p.w + g);
+    }
+  }
+  __device__ __forceinline__ uint32_t col(int u) const {
+    const uint32_t h = u < 2 ? c.x : u < 4 ? c.y : u < 6 ? c.z : c.w;
+    return (u & 1) ? h >> 16 : h & 0xffffu;
+  }
+  __device__ __forceinline__ float weight(int u) const {
+    if constexpr (WK == W_F32) {
+      const uint4& q = w[u / 4];
+      const uint32_t b = (u & 3) == 0 ? q.x : (u & 3) == 1 ? q.y : (u & 3) == 2 ? q.z : q.w;
+      return __uint_as_float(b);
+    } else {
+      const uint32_t h = u < 2 ? w[0].x : u < 4 ? w[0].y : u < 6 ? w[0].z : w[0].w;
+      const uint32_t bits = (u & 1) ? h >> 16 : h & 0xffffu;
+      return WK == W_F16 ? widen_f16(bits) : widen_bf16(bits);
+    }
+  }
+};
+
+template <int WK>
+__global__ void __launch_bounds__(kPanelMaxWarps * 32, 1) panel_spmv_kernel(const PanelLaunch p) {
+  extern __shared__ __align__(16) float xs[];
+  const uint32_t lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const uint32_t ntiles = (p.nrows + 31) / 32;
+  const uint32_t wave = gridDim.x * nw;  // tiles in flight: one per warp
+  const bool x16 = ((uintptr_t)p.x & 15u) == 0;
+  for (uint32_t t0 = 0; t0 < ntiles; t0 += wave) {
+    const uint32_t tile = t0 + blockIdx.x * nw + wid;
+    const bool has = tile < ntiles;  // warp-uniform
+    const uint32_t row = tile * 32 + lane;
+    const bool valid = has && row < p.nrows;
+    float acc = 0.f;
+    for (uint32_t pn = 0; pn < p.npanels; ++pn) {
+      const uint32_t pbase = pn * p.width;
+      const uint32_t pw = min(p.width, p.ncols - pbase);  // floats in this panel
+      // This lane folds positions [lo, hi) in this panel; the warp walks
+      // 8-position batches over the union of its lanes' ranges.
+      uint32_t lo = 0, hi = 0, jb = 0, jend = 0;
+      Batch<WK> cur, b1, b2;
+      __syncthreads();  // the previous panel's gathers are done
+      if (has) {
+        const uint16_t* sp = p.split + ((uint64_t)tile * (p.npanels + 1) + pn) * 32 + lane;
+        lo = sp[0];
+        hi = sp[32];
+        jb = __reduce_min_sync(0xffffffffu, lo < hi ? lo : 0xffffffffu) & ~7u;
+        jend = __reduce_max_sync(0xffffffffu, lo < hi ? hi : 0u);
+        // The pass's first positions do not depend on x: their loads are in
+        // flight while the panel arrives.
+        if (jb < jend) cur.load(p, tile, lane, jb);
+        if (jb + 8 < jend) b1.load(p, tile, lane, jb + 8);
+      }
+      // Each CTA starts the panel copy at its own offset, so the SMs do not
+      // all ask the same L2 slices for the same lines at once.
+      if (x16) {
+        const uint32_t n4 = pw / 4;
+        const uint32_t off = n4 ? ((uint32_t)(((uint64_t)blockIdx.x * n4) / gridDim.x) & ~31u) % n4 : 0;
+        const float4* src = reinterpret_cast<const float4*>(p.x + pbase);
+        float4* dst = reinterpret_cast<float4*>(xs);
+        for (uint32_t i = threadIdx.x; i < n4; i += blockDim.x) {
+          uint32_t m = i + off;
+          if (m >= n4) m -= n4;
+          cp_async16(dst + m, src + m);  // every copy of the thread in flight at once
+        }
+        for (uint32_t i = (pw & ~3u) + threadIdx.x; i < pw; i += blockDim.x) xs[i] = __ldg(p.x + pbase + i);
+        asm volatile("cp.async.wait_all;" ::: "memory");
+      } else {
+        for (uint32_t i = threadIdx.x; i < pw; i += blockDim.x) xs[i] = __ldg(p.x + pbase + i);
+      }
+      __syncthreads();
+      if (!has || jb >= jend) continue;
+      // Columns are panel-relative and below the panel width, so every
+      // gather stays inside the staged panel; only positions in [lo, hi)
+      // are folded.
+      auto step = [&](Batch<WK>& f, Batch<WK>& l) {
+        if (jb + 16 < jend) l.load(p, tile, lane, jb + 16);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float xv = xs[f.col(u)];
+          const uint32_t e = jb + u;
+          if (e >= lo && e < hi) acc = fadd(acc, fmul(f.weight(u), xv));
+        }
+        jb += 8;
+        return jb < jend;
+      };
+      while (step(cur, b2) && step(b1, cur) && step(b2, b1)) {
+      }
+    }
+    if (valid) p.y[row] = fadd(p.y[row], acc);
+  }
+}
+
+// One thread per row: the row's first entry in each panel, by binary search
+// over its non-decreasing columns.
+__global__ void panel_split_kernel(const uint32_t* __restrict__ col, uint64_t nrows, uint32_t L, uint32_t width,
+                                   uint32_t npanels, uint16_t* __restrict__ split, uint64_t rows_pad) {
+  for (uint64_t r = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; r < rows_pad;
+       r += (uint64_t)gridDim.x * blockDim.x) {
+    uint16_t* out = split + ((r / 32) * (npanels + 1)) * 32 + (r & 31);
+    if (r >= nrows) {
+      for (uint32_t k = 0; k <= npanels; ++k) out[(uint64_t)k * 32] = 0;
+      continue;
+    }
+    const uint32_t* c = col + r * L;
+    out[0] = 0;
+    for (uint32_t k = 1; k < npanels; ++k) {
+      const uint32_t bound = k * width;
+      uint32_t a = 0, b = L;  // first position with c >= bound
+      while (a < b) {
+        const uint32_t m = (a + b) / 2;
+        if (c[m] < bound) a = m + 1;
+        else b = m;
+      }
+      out[(uint64_t)k * 32] = (uint16_t)a;
+    }
+    out[(uint64_t)npanels * 32] = (uint16_t)L;
+  }
+}
+
+// Output element o of an interleaved array with g positions per 16-byte
+// group: which row and entry position it holds.
+__device__ __forceinline__ void panel_slot(uint64_t o, uint32_t g, uint32_t groups, uint64_t& row, uint32_t& j) {
+  const uint32_t jj = (uint32_t)(o % g);
+  const uint64_t q = o / g;  // (tile * groups + group) * 32 + lane
+  const uint32_t lane = (uint32_t)(q & 31);
+  const uint64_t tg = q >> 5;
+  row = (tg / groups) * 32 + lane;
+  j = (uint32_t)(tg % groups) * g + jj;
+}
+
+__global__ void panel_col_kernel(const uint32_t* __restrict__ col, uint64_t nrows, uint32_t L, uint32_t width,
+                                 uint16_t* __restrict__ col16, uint64_t total) {
+  const uint32_t groups = (L + 7) / 8;
+  for (uint64_t o = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; o < total;
+       o += (uint64_t)gridDim.x * blockDim.x) {
+    uint64_t row;
+    uint32_t j;
+    panel_slot(o, 8, groups, row, j);
+    uint16_t v = 0;
+    if (row < nrows && j < L) v = (uint16_t)(col[row * L + j] % width);
+    col16[o] = v;
+  }
+}
+
+template <typename T>
+__global__ void panel_w_kernel(const T* __restrict__ w, uint64_t nrows, uint32_t L, T* __restrict__ out,
+                               uint64_t total) {
+  constexpr uint32_t g = 16 / sizeof(T);
+  const uint32_t groups = (L + 7) / 8 * (8 / g);
+  for (uint64_t o = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; o < total;
+       o += (uint64_t)gridDim.x * blockDim.x) {
+    uint64_t row;
+    uint32_t j;
+    panel_slot(o, g, groups, row, j);
+    out[o] = (row < nrows && j < L) ? w[row * L + j] : T(0);
+  }
+}
+
+constexpr int kPanelDevSlots = 64;
+
+// Per device: the SM count, and the kernels' shared-memory limit raised once
+// (host calls inside the launch path would sit between a caller's events).
+int panel_sms(int dev) {
+  static std::atomic<int> sms[kPanelDevSlots];
+  if (dev < 0 || dev >= kPanelDevSlots) {
+    int v = 0;
+    return cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess ? v : 0;
+  }
+  int v = sms[dev].load(std::memory_order_relaxed);
+  if (v == 0 && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+    sms[dev].store(v, std::memory_order_relaxed);
+  return v;
+}
+
+template <int WK>
+cudaError_t go(int dev, const PanelLaunch& p, uint32_t grid, uint32_t threads, size_t smem, cudaStream_t s) {
+  static std::atomic<bool> ready[kPanelDevSlots];
+  const bool cached = dev >= 0 && dev < kPanelDevSlots;
+  if (!cached || !ready[dev].load(std::memory_order_acquire)) {
+    cudaError_t e = cudaFuncSetAttribute(panel_spmv_kernel<WK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)(kPanelMaxFloats * 4));
+    if (e != cudaSuccess) return e;
+    if (cached) ready[dev].store(true, std::memory_order_release);
+  }
+  panel_spmv_kernel<WK><<<grid, threads, smem, s>>>(p);
+  return cudaGetLastError();
+}
+
+uint32_t grid_for(uint64_t total) { return (uint32_t)std::min<uint64_t>((total + 255) / 256, 148ull * 16); }
+
+}  // namespace
+
+bool panel_geometry(uint64_t ncols, uint32_t& width, uint32_t& npanels) {
+  if (ncols == 0) return false;
+  const uint64_t np = (ncols + kPanelMaxFloats - 1) / kPanelMaxFloats;
+  if (np > kPanelMaxPanels) return false;
+  const uint64_t w = ((ncols + np - 1) / np + 3) & ~3ull;
+  width = (uint32_t)std::min<uint64_t>(w, kPanelMaxFloats);
+  npanels = (uint32_t)((ncols + width - 1) / width);
+  return npanels <= kPanelMaxPanels;
+}
+
+cudaError_t launch_panel_build(const uint32_t* col, uint64_t nrows, uint32_t L, uint32_t width, uint32_t npanels,
+                               uint16_t* col16, uint16_t* split, cudaStream_t stream) {
+  if (nrows == 0 || L == 0 || L > kPanelMaxRowLen || width == 0) return cudaErrorInvalidValue;
+  const uint64_t rows_pad = panel_tiles(nrows) * 32;
+  panel_split_kernel<<<grid_for(rows_pad), 256, 0, stream>>>(col, nrows, L, width, npanels, split, rows_pad);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const uint64_t total = panel_col_elems(nrows, L);
+  panel_col_kernel<<<grid_for(total), 256, 0, stream>>>(col, nrows, L, width, col16, total);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_panel_weights(const void* w, uint64_t nrows, uint32_t L, int esize, void* out,
+                                 cudaStream_t stream) {
+  if (nrows == 0 || L == 0) return cudaSuccess;
+  const uint64_t total = panel_w_elems(nrows, L);
+  if (esize == 4)
+    panel_w_kernel<uint32_t><<<grid_for(total), 256, 0, stream>>>(static_cast<const uint32_t*>(w), nrows, L,
+                                                                   static_cast<uint32_t*>(out), total);
+  else
+    panel_w_kernel<uint16_t><<<grid_for(total), 256, 0, stream>>>(static_cast<const uint16_t*>(w), nrows, L,
+                                                                   static_cast<uint16_t*>(out), total);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_panel_spmv(const PanelOp& op, const float* x, float* y, cudaStream_t stream) {
+  if (!op.ok || op.width == 0 || op.width > kPanelMaxFloats) return cudaErrorInvalidValue;
+  if (op.nrows == 0) return cudaSuccess;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const int sms = panel_sms(dev);
+  const uint32_t ntiles = (op.nrows + 31) / 32;
+  const uint32_t grid = std::min<uint32_t>(ntiles, (uint32_t)std::max(sms, 1));
+  const uint32_t nw = std::min<uint32_t>(kPanelMaxWarps, (ntiles + grid - 1) / grid);
+  const PanelLaunch p{reinterpret_cast<const uint4*>(op.col16),
+                      reinterpret_cast<const uint4*>(op.w),
+                      op.split, x, y, op.nrows, op.L, op.ncols, op.width, op.npanels, (op.L + 7) / 8};
+  const size_t smem = (size_t)op.width * 4;
+  switch (op.wkind) {
+    case W_F32: return go<W_F32>(dev, p, grid, nw * 32, smem, stream);
+    case W_F16: return go<W_F16>(dev, p, grid, nw * 32, smem, stream);
+    default: return go<W_BF16>(dev, p, grid, nw * 32, smem, stream);
+  }
+}
+
+}  // namespace sparsl

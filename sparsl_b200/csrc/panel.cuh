@@ -1,0 +1,65 @@
+// Dense-x SpMV for operators with a uniform row length, with x staged in
+// shared memory one column panel at a time (panel.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sparsl {
+
+// A panel is at most 216 KiB of x (one CTA per SM holds it); an operator
+// takes this path when x fits in kPanelMaxPanels of them and its rows have
+// at most kPanelMaxRowLen entries.
+constexpr uint32_t kPanelMaxFloats = 55296;
+constexpr uint32_t kPanelMaxPanels = 4;
+constexpr uint32_t kPanelMaxRowLen = 65535;
+
+// Tile-interleaved copy of a uniform-length CSR operator, built at prepare.
+// Rows go in tiles of 32 (one per lane of a warp); within a tile, entry
+// positions go in groups of 16 bytes per lane, so a lane reads 8 columns or
+// 16 bytes of weights with one load and a warp reads 512 contiguous bytes.
+//   col16[((T * Lc + j / 8) * 32 + lane) * 8 + j % 8]      Lc = ceil(L / 8)
+//     the column minus the start of its panel (below kPanelMaxFloats < 2^16)
+//   w[((T * Lw + j / G) * 32 + lane) * G + j % G]            G = 16 / weight bytes,
+//                                                            Lw = 8 * Lc / G
+//   split[(T * (npanels + 1) + k) * 32 + lane]
+//     the row's first entry in panel k (0 for k = 0, L for k = npanels)
+// Rows past nrows in the last tile and positions past L are padding: their
+// split points are all 0, so no pass folds them.
+struct PanelOp {
+  const uint16_t* col16 = nullptr;
+  const void* w = nullptr;    // f32, or binary16 / bfloat16 bits
+  const uint16_t* split = nullptr;
+  int wkind = 0;              // WeightKind
+  uint32_t nrows = 0, L = 0, ncols = 0;
+  uint32_t width = 0;         // panel width in floats (a multiple of 4)
+  uint32_t npanels = 0;
+  bool ok = false;
+};
+
+// Panel geometry for ncols columns: false when x needs more than
+// kPanelMaxPanels panels.
+bool panel_geometry(uint64_t ncols, uint32_t& width, uint32_t& npanels);
+
+// Elements of each interleaved array.
+inline uint64_t panel_tiles(uint64_t nrows) { return (nrows + 31) / 32; }
+inline uint64_t panel_col_elems(uint64_t nrows, uint32_t L) { return panel_tiles(nrows) * 32 * 8 * ((L + 7) / 8); }
+// Positions are padded to a multiple of 8 in both arrays (one batch).
+inline uint64_t panel_w_elems(uint64_t nrows, uint32_t L) { return panel_tiles(nrows) * 32 * 8 * ((L + 7) / 8); }
+inline uint64_t panel_split_elems(uint64_t nrows, uint32_t npanels) { return panel_tiles(nrows) * 32 * (npanels + 1); }
+
+// Builds col16 and split from the row-major [nrows x L] column array.
+cudaError_t launch_panel_build(const uint32_t* col, uint64_t nrows, uint32_t L, uint32_t width, uint32_t npanels,
+                               uint16_t* col16, uint16_t* split, cudaStream_t stream);
+// Interleaves the row-major [nrows x L] weights (esize bytes each: 4 or 2).
+cudaError_t launch_panel_weights(const void* w, uint64_t nrows, uint32_t L, int esize, void* out,
+                                 cudaStream_t stream);
+
+// y[r] = y[r] + fold_r, fold_r the strict left fold from 0.0 of w * x over
+// row r's entries in stored order (src/backend/mod.rs:2259-2267), for a
+// dense x of op.ncols floats.  The columns of a row are non-decreasing, so
+// its entries in panel k follow those in panel k - 1: panel by panel, a
+// lane folds each entry of its row once, in order.
+cudaError_t launch_panel_spmv(const PanelOp& op, const float* x, float* y, cudaStream_t stream);
+
+}  // namespace sparsl
