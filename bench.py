@@ -91,6 +91,8 @@ TRAFFIC_RATIO = {
     "spmv": (39_812_352 / 52_800_004, "ncu capture of the same launch (bench.py --workload spmv): the panel "
                                       "layout's 16-bit panel-relative columns read less than the CSR bytes"),
     "spmv_f16": (27_011_584 / 40_000_004, "ncu capture of the same launch (bench.py --workload spmv), f16 weights"),
+    "spmv_t": ((51_352_832 + 18_432) / 52_800_004, "ncu capture of the same launch (bench.py --workload spmv): "
+                                                   "the transpose's slices pad each column to its slice's longest"),
     "spmm_f32": (6.2e9 / 1_164_395_452, "ncu capture of the same launch (bench.py --workload spmm): DRAM "
                                         "throughput x duration, about 6.2 GB, mostly X-row gathers"),
     "lif_integrate": ((805_336_832 + 553_707_008) / 1_409_286_144,
@@ -732,8 +734,8 @@ def bench_spmv(args, dev, want_cpu):
     algot = col.size * 8 + (SPMV_N + 1) * 4 + SPMV_N * 4 + 2 * SPMV_N * 4
     tr, mst = measure(opt, L.sparsl_op_spmv_t_device, dxt, SPMV_N, algot,
                       lambda ref: O.spmv_t(csc, w, xt, ref, par=True))
-    tr["roofline"] = roofline(algot, mst, "sell_fold_kernel (transpose over the sliced-ELL reverse index)",
-                              "spmv_t")
+    tr["roofline"] = roofline(algot, mst, "panel_spmv_kernel<f32> (transpose: x panels over the sliced-ELL "
+                                          "reverse index)", "spmv_t")
     del opt
     # The reverse index itself, built on the GPU from device arrays (gate
     # included; wall clock of the blocking C-ABI call) against the oracle's

@@ -197,14 +197,17 @@ enum {
   SPARSL_LAYOUT_ROW_ORDER = 2,      /* skewed rows: row folds in descending-length order */
   SPARSL_LAYOUT_SLICED_REVERSE = 4, /* transpose: sliced-ELL reverse index */
   SPARSL_LAYOUT_CSC = 8,            /* transpose: plain reverse index (hub columns) */
-  SPARSL_LAYOUT_X_PANELS = 16       /* uniform rows, x in <= 4 shared-memory panels: dense-x SpMV
+  SPARSL_LAYOUT_X_PANELS = 16,      /* uniform rows, x in <= 4 shared-memory panels: dense-x SpMV
                                        reads a tile-interleaved copy of col / values */
+  SPARSL_LAYOUT_T_X_PANELS = 32     /* the same for the transpose product, from the sliced-ELL
+                                       reverse index (x of nrows values in <= 4 panels) */
 };
 int sparsl_op_layouts(sparsl_op *op);
 /* Test and diagnostic hook, no reference counterpart: forget the operator's
- * uniform-row layouts (TMA stream and x panels) and its descending-length
- * row order, so every later forward product runs on the generic row-fold
- * engine in natural row order.  The engine choice at prepare stays a function of the operator's
+ * uniform-row layouts (TMA stream and x panels), its descending-length row
+ * order and its transpose x panels, so every later forward product runs on
+ * the generic row-fold engine in natural row order and the transpose on the
+ * reverse index itself.  The engine choice at prepare stays a function of the operator's
  * shape alone; this only lets a caller compare the engines on one operator.
  * Results are identical either way. */
 int sparsl_op_force_plain_row_fold(sparsl_op *op);

@@ -359,6 +359,10 @@ struct sparsl_op {
   // the tile-interleaved copy of col / w for the dense-x SpMV (panel.cu).
   PanelOp panel;
   DBuf pcol, pw, psplit;
+  // The same for the transpose product, built from the sliced-ELL reverse
+  // index when x (one value per row) fits the panels.
+  PanelOp tpanel;
+  DBuf tcol, tw, tsplit, ttoff;
   uint32_t ell_epoch = 0;  // tag of the last compacting TMA launch's flags
   // resident scratch (the write / step / sync API)
   DBuf rx, rxs[2], ry, rv, rth, rspk;
@@ -1305,6 +1309,45 @@ int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int 
                                 op->stream) != cudaSuccess)
         return bail(fail_cuda("prepare", cudaGetLastError()));
       op->sell_ok = true;
+      // The transpose product with x in shared-memory panels: the reverse
+      // index's slices are already tiles of 32 lines; each is padded to a
+      // multiple of 8 positions.
+      uint32_t twidth = 0, tnp = 0;
+      uint32_t max_depth = 0;
+      for (uint64_t sl = 0; sl < nslices; ++sl) max_depth = std::max(max_depth, depth[sl]);
+      if (!borrow && nnz <= (1ull << 30) && max_depth <= kPanelMaxRowLen && panel_geometry(nrows, twidth, tnp)) {
+        std::vector<uint64_t> to(nslices + 1, 0);
+        for (uint64_t sl = 0; sl < nslices; ++sl) to[sl + 1] = to[sl] + (depth[sl] + 7) / 8;
+        PALLOC(op->ttoff, (nslices + 1) * 8, false, "transpose panel offsets");
+        PALLOC(op->tcol, to[nslices] * 256 * 2, false, "transpose panel rows");
+        PALLOC(op->tw, to[nslices] * 256 * wbytes, false, "transpose panel values");
+        PALLOC(op->tsplit, nslices * 32 * (tnp + 1) * 2, false, "transpose panel split points");
+        if (cudaMemcpyAsync(op->ttoff.p, to.data(), (nslices + 1) * 8, cudaMemcpyHostToDevice, op->stream) !=
+                cudaSuccess ||
+            launch_panel_build_sell(op->sell_ptr.as<unsigned long long>(), op->col_ptr.as<uint32_t>(),
+                                    op->sell_row.as<uint32_t>(), nc, (uint32_t)nslices, op->ttoff.as<uint64_t>(),
+                                    twidth, tnp, op->tcol.as<uint16_t>(), op->tsplit.as<uint16_t>(),
+                                    op->stream) != cudaSuccess ||
+            launch_panel_weights_sell(op->sell_ptr.as<unsigned long long>(), op->col_ptr.as<uint32_t>(),
+                                      op->w_sell.p, nc, (uint32_t)nslices, op->ttoff.as<uint64_t>(), (int)wbytes,
+                                      op->tw.p, op->stream) != cudaSuccess)
+          return bail(fail_cuda("prepare", cudaGetLastError()));
+        // The host offsets must outlive the asynchronous copy.
+        rc = wait_op(op, "prepare");
+        if (rc != SPARSL_OK) return bail(rc);
+        PanelOp& tp = op->tpanel;
+        tp.col16 = op->tcol.as<uint16_t>();
+        tp.w = op->tw.p;
+        tp.split = op->tsplit.as<uint16_t>();
+        tp.toff = op->ttoff.as<uint64_t>();
+        tp.wkind = wkind_of(precision);
+        tp.nrows = (uint32_t)nc;
+        tp.L = 0;
+        tp.ncols = (uint32_t)nrows;
+        tp.width = twidth;
+        tp.npanels = tnp;
+        tp.ok = true;
+      }
     } else {
       std::swap(op->csc_row, tmp.row);
       std::swap(op->csc_eidx, tmp.eidx);
@@ -1473,7 +1516,7 @@ void sparsl_op_destroy(sparsl_op* op) {
                   &op->rspk,    &op->idx_list, &op->tile_flags, &op->ticket, &op->trace, &op->sx,
                   &op->sbits,   &op->sy,      &op->sv,      &op->sth,     &op->sspk,
                   &op->spmm_order, &op->spmm_units, &op->spmm_ctr, &op->spmm_rorder, &op->spmm_runits,
-                  &op->row_order, &op->pcol, &op->pw, &op->psplit};
+                  &op->row_order, &op->pcol, &op->pw, &op->psplit, &op->tcol, &op->tw, &op->tsplit, &op->ttoff};
   for (DBuf* b : bufs) dfree(*b);
   op->err.release();
   if (op->side) cudaStreamSynchronize(op->side);
@@ -1506,7 +1549,7 @@ int sparsl_op_weight_precision(sparsl_op* op) { return op ? op->precision : -1; 
 int sparsl_op_layouts(sparsl_op* op) {
   if (!op) return 0;
   return (op->ell.ok ? SPARSL_LAYOUT_ELL : 0) | (op->row_ordered ? SPARSL_LAYOUT_ROW_ORDER : 0) |
-         (op->panel.ok ? SPARSL_LAYOUT_X_PANELS : 0) |
+         (op->panel.ok ? SPARSL_LAYOUT_X_PANELS : 0) | (op->tpanel.ok ? SPARSL_LAYOUT_T_X_PANELS : 0) |
          (op->sell_ok ? SPARSL_LAYOUT_SLICED_REVERSE : 0) |
          (op->has_t && !op->sell_ok ? SPARSL_LAYOUT_CSC : 0);
 }
@@ -1534,6 +1577,7 @@ int sparsl_op_force_plain_row_fold(sparsl_op* op) {
   op->ell.ok = false;
   op->row_ordered = false;
   op->panel.ok = false;
+  op->tpanel.ok = false;
   return SPARSL_OK;
 }
 
@@ -1557,6 +1601,10 @@ int sparsl_op_set_weights(sparsl_op* op, const float* weights, uint64_t n) {
   if (op->sell_ok)
     CK("set_weights", launch_gather_weights(op->w.p, op->sell_eidx.as<uint32_t>(), op->sell_total,
                                             op->precision == 0 ? 4 : 2, op->w_sell.p, op->stream));
+  if (op->tpanel.ok)
+    CK("set_weights", launch_panel_weights_sell(op->sell_ptr.as<unsigned long long>(), op->col_ptr.as<uint32_t>(),
+                                                op->w_sell.p, op->ncols, op->sell_slices, op->tpanel.toff,
+                                                op->precision == 0 ? 4 : 2, op->tw.p, op->stream));
   else if (op->has_t)
     CK("set_weights", launch_gather_weights(op->w.p, op->csc_eidx.as<uint32_t>(), n, op->precision == 0 ? 4 : 2,
                                             op->w_csc.p, op->stream));
@@ -1616,6 +1664,7 @@ int sparsl_op_spmv_spikes(sparsl_op* op, const uint32_t* spikes, uint64_t words,
 // The transpose product: the sliced-ELL fold when the operator has it, the
 // row-fold engine over the CSC lines otherwise.
 static cudaError_t launch_transpose(sparsl_op* op, const float* x, float* y, cudaStream_t s) {
+  if (op->tpanel.ok) return launch_panel_spmv(op->tpanel, x, y, s);
   if (op->sell_ok) {
     SellLaunch p;
     p.slice_ptr = op->sell_ptr.as<uint64_t>();

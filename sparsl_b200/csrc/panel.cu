@@ -32,6 +32,7 @@ struct PanelLaunch {
   const uint4* col16;  // 16-byte groups of 8 columns
   const uint4* w;      // 16-byte groups of 4 (f32) or 8 (16-bit) weights
   const uint16_t* split;
+  const uint64_t* toff;  // ragged lines: group offset of each tile (null: tile * Lg)
   const float* x;
   float* y;
   uint32_t nrows, L, ncols, width, npanels;
@@ -48,11 +49,12 @@ template <int WK>
 struct Batch {
   uint4 c;
   uint4 w[WK == W_F32 ? 2 : 1];
-  __device__ __forceinline__ void load(const PanelLaunch& p, uint64_t tile, uint32_t lane, uint32_t jb) {
-    const uint64_t g = (tile * p.Lg + jb / 8) * 32 + lane;
+  // gbase: the tile's first 8-position group.
+  __device__ __forceinline__ void load(const PanelLaunch& p, uint64_t gbase, uint32_t lane, uint32_t jb) {
+    const uint64_t g = (gbase + jb / 8) * 32 + lane;
     c = __ldg(p.col16 + g);
     if constexpr (WK == W_F32) {
-      const uint64_t gw = (tile * p.Lg * 2 + jb / 4) * 32 + lane;
+      const uint64_t gw = (gbase * 2 + jb / 4) * 32 + lane;
       w[0] = __ldg(p.w + gw);
       w[1] = __ldg(p.w + gw + 32);
     } else {
@@ -88,6 +90,7 @@ __global__ void __launch_bounds__(kPanelMaxWarps * 32, 1) panel_spmv_kernel(cons
     const bool has = tile < ntiles;  // warp-uniform
     const uint32_t row = tile * 32 + lane;
     const bool valid = has && row < p.nrows;
+    const uint64_t gbase = !has ? 0 : p.toff ? __ldg(p.toff + tile) : (uint64_t)tile * p.Lg;
     float acc = 0.f;
     for (uint32_t pn = 0; pn < p.npanels; ++pn) {
       const uint32_t pbase = pn * p.width;
@@ -105,8 +108,8 @@ __global__ void __launch_bounds__(kPanelMaxWarps * 32, 1) panel_spmv_kernel(cons
         jend = __reduce_max_sync(0xffffffffu, lo < hi ? hi : 0u);
         // The pass's first positions do not depend on x: their loads are in
         // flight while the panel arrives.
-        if (jb < jend) cur.load(p, tile, lane, jb);
-        if (jb + 8 < jend) b1.load(p, tile, lane, jb + 8);
+        if (jb < jend) cur.load(p, gbase, lane, jb);
+        if (jb + 8 < jend) b1.load(p, gbase, lane, jb + 8);
       }
       // Each CTA starts the panel copy at its own offset, so the SMs do not
       // all ask the same L2 slices for the same lines at once.
@@ -131,7 +134,7 @@ __global__ void __launch_bounds__(kPanelMaxWarps * 32, 1) panel_spmv_kernel(cons
       // gather stays inside the staged panel; only positions in [lo, hi)
       // are folded.
       auto step = [&](Batch<WK>& f, Batch<WK>& l) {
-        if (jb + 16 < jend) l.load(p, tile, lane, jb + 16);
+        if (jb + 16 < jend) l.load(p, gbase, lane, jb + 16);
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const float xv = xs[f.col(u)];
@@ -214,6 +217,68 @@ __global__ void panel_w_kernel(const T* __restrict__ w, uint64_t nrows, uint32_t
   }
 }
 
+// One CTA per slice (tile of 32 lines): its lines' entries into the
+// 16-byte-group layout.  Positions past a line's length are padding (0).
+__global__ void panel_sell_col_kernel(const unsigned long long* __restrict__ slice_ptr,
+                                      const uint32_t* __restrict__ line_ptr, const uint32_t* __restrict__ sell_idx,
+                                      uint64_t nlines, uint32_t nslices, const uint64_t* __restrict__ toff,
+                                      uint32_t width, uint16_t* __restrict__ col16) {
+  for (uint32_t T = blockIdx.x; T < nslices; T += gridDim.x) {
+    const uint64_t base = slice_ptr[T], g0 = toff[T], n = (toff[T + 1] - g0) * 256;
+    for (uint64_t e = threadIdx.x; e < n; e += blockDim.x) {
+      const uint32_t lane = (uint32_t)(e >> 3) & 31u;
+      const uint32_t j = (uint32_t)(e >> 8) * 8 + (uint32_t)(e & 7);
+      const uint64_t line = (uint64_t)T * 32 + lane;
+      const uint32_t len = line < nlines ? line_ptr[line + 1] - line_ptr[line] : 0u;
+      col16[g0 * 256 + e] = j < len ? (uint16_t)(sell_idx[base + (uint64_t)j * 32 + lane] % width) : (uint16_t)0;
+    }
+  }
+}
+
+template <typename T>
+__global__ void panel_sell_w_kernel(const unsigned long long* __restrict__ slice_ptr,
+                                    const uint32_t* __restrict__ line_ptr, const T* __restrict__ w_sell,
+                                    uint64_t nlines, uint32_t nslices, const uint64_t* __restrict__ toff,
+                                    T* __restrict__ out) {
+  constexpr uint32_t g = 16 / sizeof(T);  // positions per 16-byte group
+  for (uint32_t S = blockIdx.x; S < nslices; S += gridDim.x) {
+    const uint64_t base = slice_ptr[S], g0 = toff[S], n = (toff[S + 1] - g0) * 256;
+    for (uint64_t e = threadIdx.x; e < n; e += blockDim.x) {
+      const uint32_t lane = (uint32_t)(e / g) & 31u;
+      const uint32_t j = (uint32_t)(e / (g * 32)) * g + (uint32_t)(e % g);
+      const uint64_t line = (uint64_t)S * 32 + lane;
+      const uint32_t len = line < nlines ? line_ptr[line + 1] - line_ptr[line] : 0u;
+      out[g0 * 256 + e] = j < len ? w_sell[base + (uint64_t)j * 32 + lane] : T(0);
+    }
+  }
+}
+
+// One thread per line (all 32 of every slice): the line's first entry in
+// each panel, by binary search over its ascending indices.
+__global__ void panel_sell_split_kernel(const unsigned long long* __restrict__ slice_ptr,
+                                        const uint32_t* __restrict__ line_ptr, const uint32_t* __restrict__ sell_idx,
+                                        uint64_t nlines, uint64_t lines_pad, uint32_t width, uint32_t npanels,
+                                        uint16_t* __restrict__ split) {
+  for (uint64_t r = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; r < lines_pad;
+       r += (uint64_t)gridDim.x * blockDim.x) {
+    uint16_t* out = split + ((r / 32) * (npanels + 1)) * 32 + (r & 31);
+    const uint32_t len = r < nlines ? line_ptr[r + 1] - line_ptr[r] : 0u;
+    const uint32_t* c = sell_idx + slice_ptr[r / 32] + (r & 31);  // entry j at c[32 * j]
+    out[0] = 0;
+    for (uint32_t k = 1; k < npanels; ++k) {
+      const uint32_t bound = k * width;
+      uint32_t a = 0, b = len;
+      while (a < b) {
+        const uint32_t m = (a + b) / 2;
+        if (c[(uint64_t)m * 32] < bound) a = m + 1;
+        else b = m;
+      }
+      out[(uint64_t)k * 32] = (uint16_t)a;
+    }
+    out[(uint64_t)npanels * 32] = (uint16_t)len;
+  }
+}
+
 constexpr int kPanelDevSlots = 64;
 
 // Per device: the SM count, and the kernels' shared-memory limit raised once
@@ -283,6 +348,38 @@ cudaError_t launch_panel_weights(const void* w, uint64_t nrows, uint32_t L, int 
   return cudaGetLastError();
 }
 
+cudaError_t launch_panel_build_sell(const unsigned long long* slice_ptr, const uint32_t* line_ptr,
+                                    const uint32_t* sell_idx, uint64_t nlines, uint32_t nslices, const uint64_t* toff,
+                                    uint32_t width, uint32_t npanels, uint16_t* col16, uint16_t* split,
+                                    cudaStream_t stream) {
+  if (nslices == 0) return cudaSuccess;
+  if (width == 0) return cudaErrorInvalidValue;
+  const uint32_t blocks = std::min<uint32_t>(nslices, 148u * 8);
+  panel_sell_col_kernel<<<blocks, 256, 0, stream>>>(slice_ptr, line_ptr, sell_idx, nlines, nslices, toff, width, col16);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const uint64_t lines_pad = (uint64_t)nslices * 32;
+  panel_sell_split_kernel<<<grid_for(lines_pad), 256, 0, stream>>>(slice_ptr, line_ptr, sell_idx, nlines, lines_pad,
+                                                                    width, npanels, split);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_panel_weights_sell(const unsigned long long* slice_ptr, const uint32_t* line_ptr,
+                                      const void* w_sell, uint64_t nlines, uint32_t nslices, const uint64_t* toff,
+                                      int esize, void* out, cudaStream_t stream) {
+  if (nslices == 0) return cudaSuccess;
+  const uint32_t blocks = std::min<uint32_t>(nslices, 148u * 8);
+  if (esize == 4)
+    panel_sell_w_kernel<uint32_t><<<blocks, 256, 0, stream>>>(slice_ptr, line_ptr,
+                                                               static_cast<const uint32_t*>(w_sell), nlines, nslices,
+                                                               toff, static_cast<uint32_t*>(out));
+  else
+    panel_sell_w_kernel<uint16_t><<<blocks, 256, 0, stream>>>(slice_ptr, line_ptr,
+                                                               static_cast<const uint16_t*>(w_sell), nlines, nslices,
+                                                               toff, static_cast<uint16_t*>(out));
+  return cudaGetLastError();
+}
+
 cudaError_t launch_panel_spmv(const PanelOp& op, const float* x, float* y, cudaStream_t stream) {
   if (!op.ok || op.width == 0 || op.width > kPanelMaxFloats) return cudaErrorInvalidValue;
   if (op.nrows == 0) return cudaSuccess;
@@ -295,7 +392,7 @@ cudaError_t launch_panel_spmv(const PanelOp& op, const float* x, float* y, cudaS
   const uint32_t nw = std::min<uint32_t>(kPanelMaxWarps, (ntiles + grid - 1) / grid);
   const PanelLaunch p{reinterpret_cast<const uint4*>(op.col16),
                       reinterpret_cast<const uint4*>(op.w),
-                      op.split, x, y, op.nrows, op.L, op.ncols, op.width, op.npanels, (op.L + 7) / 8};
+                      op.split, op.toff, x, y, op.nrows, op.L, op.ncols, op.width, op.npanels, (op.L + 7) / 8};
   const size_t smem = (size_t)op.width * 4;
   switch (op.wkind) {
     case W_F32: return go<W_F32>(dev, p, grid, nw * 32, smem, stream);

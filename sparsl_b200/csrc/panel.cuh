@@ -26,12 +26,19 @@ constexpr uint32_t kPanelMaxRowLen = 65535;
 //     the row's first entry in panel k (0 for k = 0, L for k = npanels)
 // Rows past nrows in the last tile and positions past L are padding: their
 // split points are all 0, so no pass folds them.
+//
+// The same layout serves lines of different lengths (the transpose product
+// over the sliced-ELL reverse index: a line is a column, its entries are its
+// rows in ascending order, x is indexed by row): tile T then holds
+// toff[T + 1] - toff[T] groups of 8 positions (its longest line, padded), at
+// group offset toff[T] instead of T * Lc.
 struct PanelOp {
   const uint16_t* col16 = nullptr;
   const void* w = nullptr;    // f32, or binary16 / bfloat16 bits
   const uint16_t* split = nullptr;
+  const uint64_t* toff = nullptr;  // ragged lines: 8-position groups before tile T
   int wkind = 0;              // WeightKind
-  uint32_t nrows = 0, L = 0, ncols = 0;
+  uint32_t nrows = 0, L = 0, ncols = 0;  // lines, uniform line length (0 when ragged), x length
   uint32_t width = 0;         // panel width in floats (a multiple of 4)
   uint32_t npanels = 0;
   bool ok = false;
@@ -54,6 +61,19 @@ cudaError_t launch_panel_build(const uint32_t* col, uint64_t nrows, uint32_t L, 
 // Interleaves the row-major [nrows x L] weights (esize bytes each: 4 or 2).
 cudaError_t launch_panel_weights(const void* w, uint64_t nrows, uint32_t L, int esize, void* out,
                                  cudaStream_t stream);
+
+// The same copy of a sliced-ELL operator (slices of 32 lines; entry j of
+// line 32 * T + l at slice_ptr[T] + 32 * j + l; line lengths from line_ptr;
+// the entries' gathered index, here a row, ascending within a line): col16
+// and split from the rows, and (separately, for new weights) the weights
+// from the sliced-ELL weight array.  toff holds nslices + 1 group offsets.
+cudaError_t launch_panel_build_sell(const unsigned long long* slice_ptr, const uint32_t* line_ptr,
+                                    const uint32_t* sell_idx, uint64_t nlines, uint32_t nslices, const uint64_t* toff,
+                                    uint32_t width, uint32_t npanels, uint16_t* col16, uint16_t* split,
+                                    cudaStream_t stream);
+cudaError_t launch_panel_weights_sell(const unsigned long long* slice_ptr, const uint32_t* line_ptr,
+                                      const void* w_sell, uint64_t nlines, uint32_t nslices, const uint64_t* toff,
+                                      int esize, void* out, cudaStream_t stream);
 
 // y[r] = y[r] + fold_r, fold_r the strict left fold from 0.0 of w * x over
 // row r's entries in stored order (src/backend/mod.rs:2259-2267), for a

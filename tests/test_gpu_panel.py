@@ -5,7 +5,9 @@ Covers one to four panels, several row waves, ragged last tiles, columns at
 and around the panel edges (rows that stop in one panel and resume in the
 next, rows that skip whole panels, duplicate columns), the three weight
 precisions, new weights after prepare, an x that is not 16-byte aligned, and
-the widest x that still takes the TMA stream instead."""
+the widest x that still takes the TMA stream instead.  The transpose product
+over the same panels (built from the sliced-ELL reverse index, x indexed by
+row) is checked the same way against the oracle and the reverse-index fold."""
 import numpy as np
 import pytest
 
@@ -138,3 +140,82 @@ def test_widest_x_past_the_panels_takes_the_stream(O, cuda_device):
     csr, w = _uniform(O, 1500, 4 * MAX_PANEL + 1, 16, 31)
     op, _, _ = _check(O, cuda_device, csr, w, S.WeightPrecision.F32, 32, panels=False)
     assert op.layouts() & ELL
+
+
+T_PANELS = 32  # SPARSL_LAYOUT_T_X_PANELS
+SLICED = 4     # SPARSL_LAYOUT_SLICED_REVERSE
+
+
+def _check_t(O, dev, csr, w, precision, seed, panels=True):
+    """spmv_t through the transpose x panels against the oracle and against
+    the sliced-ELL fold of the same operator."""
+    wq = O.quantise(int(precision), w)
+    nrows = len(csr.row_ptr) - 1
+    op = dev.prepare_with_transpose_precision(S.Csr(csr.row_ptr, csr.col, csr.ncols), csr.ncols, w, precision)
+    # The panel copy is built from the sliced-ELL reverse index; an operator
+    # whose slices would pad too much keeps the plain reverse index instead.
+    lay = op.layouts()
+    assert bool(lay & T_PANELS) == (panels and bool(lay & SLICED))
+    ref = dev.prepare_with_transpose_precision(S.Csr(csr.row_ptr, csr.col, csr.ncols), csr.ncols, w, precision)
+    ref.force_plain_row_fold()
+    assert not ref.layouts() & T_PANELS
+    r = np.random.default_rng(seed)
+    xt = r.uniform(-1, 1, nrows).astype(np.float32)
+    yt0 = r.uniform(-1, 1, csr.ncols).astype(np.float32)
+    got, alt = yt0.copy(), yt0.copy()
+    op.spmv_t(xt, got)
+    ref.spmv_t(xt, alt)
+    want = O.spmv_t(O.csc_from_csr(csr, csr.ncols), wq, xt, yt0.copy())
+    assert_bits_equal(got, want, "transpose panels vs oracle")
+    assert_bits_equal(alt, want, "reverse-index fold vs oracle")
+    return op, xt, yt0
+
+
+@pytest.mark.parametrize("nrows,ncols,L", [
+    (40, 33, 5),              # one slice, ragged last slice
+    (100_000, 100_000, 64),   # config 1's shape: two panels over the rows
+    (150_000, 2000, 16),      # three panels, long columns (~1,200 entries)
+    (4 * MAX_PANEL, 5000, 4), # four full panels
+])
+@pytest.mark.parametrize("precision", [S.WeightPrecision.F32, S.WeightPrecision.F16])
+def test_transpose_panels_bit_exact(O, cuda_device, nrows, ncols, L, precision):
+    csr, w = _uniform(O, nrows, ncols, L, nrows + 3 * L)
+    op, _, _ = _check_t(O, cuda_device, csr, w, precision, L)
+    if nrows >= 100_000:
+        assert op.layouts() & T_PANELS
+
+
+def test_transpose_panels_ragged_slices(O, cuda_device):
+    """Rows of 1 to 40 entries and columns whose popularity grows sixfold
+    across the matrix: every slice is padded to its own longest column, so
+    the tiles have different depths, and short columns finish early."""
+    r = np.random.default_rng(17)
+    nrows, ncols = 120_000, 3000
+    pop = 1.0 + 5.0 * np.arange(ncols) / ncols
+    pop /= pop.sum()
+    lens = r.integers(1, 41, nrows)
+    rows = [np.sort(r.choice(ncols, k, replace=False, p=pop)) for k in lens]
+    rp = np.zeros(nrows + 1, np.uint64)
+    np.cumsum(lens, out=rp[1:])
+    col = np.concatenate(rows).astype(np.uint32)
+    w = r.standard_normal(col.size).astype(np.float32)
+    csr = O.Csr(rp.astype(np.uint32), col, ncols)
+    op, _, _ = _check_t(O, cuda_device, csr, w, S.WeightPrecision.F32, 18)
+    assert op.layouts() & T_PANELS
+
+
+def test_transpose_panel_copy_follows_new_weights(O, cuda_device):
+    csr, w = _uniform(O, 70_000, 5000, 12, 41)
+    op, xt, yt0 = _check_t(O, cuda_device, csr, w, S.WeightPrecision.Bf16, 42)
+    w2 = np.random.default_rng(43).uniform(-2, 2, w.size).astype(np.float32)
+    op.set_weights(w2)
+    got = yt0.copy()
+    op.spmv_t(xt, got)
+    want = O.spmv_t(O.csc_from_csr(csr, csr.ncols), O.quantise(int(S.WeightPrecision.Bf16), w2), xt, yt0.copy())
+    assert_bits_equal(got, want, "spmv_t after set_weights")
+
+
+def test_transpose_rows_past_the_panels_keep_the_reverse_index(O, cuda_device):
+    csr, w = _uniform(O, 4 * MAX_PANEL + 1, 3000, 2, 51)
+    op, _, _ = _check_t(O, cuda_device, csr, w, S.WeightPrecision.F32, 52, panels=False)
+    assert op.layouts() & SLICED
