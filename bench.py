@@ -86,8 +86,9 @@ def peaks():
 # ncu captures (dram__bytes_read.sum + dram__bytes_write.sum of one launch
 # over the launch's algorithmic bytes), keyed by workload.
 TRAFFIC_RATIO = {
-    "ragged_spmv": ((459_123_968 + 8_070_400) / 408_395_452,
-                    "ncu capture of the same launch (bench.py --workload ragged), 1,000,000 rows"),
+    "ragged_spmv": ((452_783_104 + 11_910_144) / 408_395_452,
+                    "ncu capture of the same launch (bench.py --workload ragged), 1,000,000 rows: the ordered "
+                    "copy's tiles are padded to their longest row, and x is gathered from DRAM once"),
     "spmv": (39_812_352 / 52_800_004, "ncu capture of the same launch (bench.py --workload spmv): the panel "
                                       "layout's 16-bit panel-relative columns read less than the CSR bytes"),
     "spmv_f16": (27_011_584 / 40_000_004, "ncu capture of the same launch (bench.py --workload spmv), f16 weights"),
@@ -1138,7 +1139,8 @@ def bench_ragged(args, op, csr, w, s, flush):
             "ms_per_step": ms, "algorithmic_bytes": algo, "bit_exact_vs_oracle": exact,
             "config": f"the SpMM matrix ({n:,} rows, {nnz:,} nnz, Zipf(1.5) lengths) times a dense x U[0,1]; "
                       "L2 flushed before every launch",
-            "roofline": roofline(algo, ms, "row_fold_kernel<f32, dense x, descending-length order>", "ragged_spmv")}
+            "roofline": roofline(algo, ms, "ordered_fold_kernel<f32> (rows in descending-length order, "
+                                           "tile-interleaved copy)", "ragged_spmv")}
     # Recurrent ticks (fused spike SpMV + LIF + packing + index list), timed
     # from the initial state; the timed ticks are checked against the CPU.
     ticks = 20

@@ -199,13 +199,15 @@ enum {
   SPARSL_LAYOUT_CSC = 8,            /* transpose: plain reverse index (hub columns) */
   SPARSL_LAYOUT_X_PANELS = 16,      /* uniform rows, x in <= 4 shared-memory panels: dense-x SpMV
                                        reads a tile-interleaved copy of col / values */
-  SPARSL_LAYOUT_T_X_PANELS = 32     /* the same for the transpose product, from the sliced-ELL
+  SPARSL_LAYOUT_T_X_PANELS = 32,    /* the same for the transpose product, from the sliced-ELL
                                        reverse index (x of nrows values in <= 4 panels) */
+  SPARSL_LAYOUT_ORDERED_COPY = 64   /* skewed rows: a tile-interleaved copy in descending-length
+                                       order for dense-x SpMV */
 };
 int sparsl_op_layouts(sparsl_op *op);
 /* Test and diagnostic hook, no reference counterpart: forget the operator's
  * uniform-row layouts (TMA stream and x panels), its descending-length row
- * order and its transpose x panels, so every later forward product runs on
+ * order and ordered copy, and its transpose x panels, so every later forward product runs on
  * the generic row-fold engine in natural row order and the transpose on the
  * reverse index itself.  The engine choice at prepare stays a function of the operator's
  * shape alone; this only lets a caller compare the engines on one operator.

@@ -363,6 +363,10 @@ struct sparsl_op {
   // index when x (one value per row) fits the panels.
   PanelOp tpanel;
   DBuf tcol, tw, tsplit, ttoff;
+  // Skewed rows: the rows in descending-length order, tile-interleaved, for
+  // dense-x SpMV at high occupancy (panel.cu); its order is spmm_order.
+  OrderedOp ordered;
+  DBuf ocol, ow, olen, otoff;
   uint32_t ell_epoch = 0;  // tag of the last compacting TMA launch's flags
   // resident scratch (the write / step / sync API)
   DBuf rx, rxs[2], ry, rv, rth, rspk;
@@ -454,6 +458,8 @@ RowLaunch fwd_launch(sparsl_op* op) {
 // Forward launches take the TMA-pipelined kernel when the operator's rows all
 // have the same length, the generic row-fold kernel otherwise.
 cudaError_t launch_fwd(sparsl_op* op, const RowLaunch& p, cudaStream_t s) {
+  if (op->ordered.ok && p.xmode == X_DENSE && p.epilogue == EPI_ACCUM && !p.eidx && !p.out_bits && !p.idx_list)
+    return launch_ordered_spmv(op->ordered, p.x, p.y, s);
   if (op->panel.ok && p.xmode == X_DENSE && p.epilogue == EPI_ACCUM && !p.eidx && !p.out_bits && !p.idx_list)
     return launch_panel_spmv(op->panel, p.x, p.y, s);
   if (!op->ell.ok && op->row_ordered && !p.eidx) {
@@ -1480,6 +1486,35 @@ int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int 
       PALLOC(op->spmm_units, sp_units.size() * 4, false, "spmm units");
       cudaMemcpyAsync(op->spmm_order.p, sp_order.data(), nrows * 4, cudaMemcpyHostToDevice, op->stream);
       cudaMemcpyAsync(op->spmm_units.p, sp_units.data(), sp_units.size() * 4, cudaMemcpyHostToDevice, op->stream);
+      // Skewed rows, the operator's own arrays, up to 2^30 entries: the
+      // ordered copy for dense-x SpMV.  Tile T holds rows sp_order[32T ..
+      // 32T + 31], padded to its first (longest) row, rounded up to 8.
+      if (op->row_ordered && !borrow && nnz <= (1ull << 30)) {
+        const uint64_t nt = (nrows + 31) / 32;
+        std::vector<uint64_t> to(nt + 1, 0);
+        for (uint64_t T = 0; T < nt; ++T) to[T + 1] = to[T] + (len(sp_order[T * 32]) + 7) / 8;
+        PALLOC(op->otoff, (nt + 1) * 8, false, "ordered offsets");
+        PALLOC(op->ocol, to[nt] * 256 * 4, false, "ordered col");
+        PALLOC(op->ow, to[nt] * 256 * wbytes, false, "ordered values");
+        PALLOC(op->olen, nt * 32 * 4, false, "ordered lengths");
+        if (cudaMemcpyAsync(op->otoff.p, to.data(), (nt + 1) * 8, cudaMemcpyHostToDevice, op->stream) !=
+                cudaSuccess ||
+            launch_ordered_build(op->row_ptr.as<uint32_t>(), op->col.as<uint32_t>(), op->w.p, (int)wbytes,
+                                 op->spmm_order.as<uint32_t>(), nrows, op->otoff.as<uint64_t>(),
+                                 op->ocol.as<uint32_t>(), op->ow.p, op->olen.as<uint32_t>(), op->stream) !=
+                cudaSuccess)
+          return bail(fail_cuda("prepare", cudaGetLastError()));
+        cudaStreamSynchronize(op->stream);  // the host offsets outlive the copy
+        OrderedOp& od = op->ordered;
+        od.col = op->ocol.as<uint32_t>();
+        od.w = op->ow.p;
+        od.len = op->olen.as<uint32_t>();
+        od.toff = op->otoff.as<uint64_t>();
+        od.order = op->spmm_order.as<uint32_t>();
+        od.wkind = wkind_of(precision);
+        od.nrows = (uint32_t)nrows;
+        od.ok = true;
+      }
       if (ranged) {
         const uint64_t per = (nrows + kSpmmRanges - 1) / kSpmmRanges;
         op->spmm_range_unit.push_back(0);
@@ -1516,7 +1551,8 @@ void sparsl_op_destroy(sparsl_op* op) {
                   &op->rspk,    &op->idx_list, &op->tile_flags, &op->ticket, &op->trace, &op->sx,
                   &op->sbits,   &op->sy,      &op->sv,      &op->sth,     &op->sspk,
                   &op->spmm_order, &op->spmm_units, &op->spmm_ctr, &op->spmm_rorder, &op->spmm_runits,
-                  &op->row_order, &op->pcol, &op->pw, &op->psplit, &op->tcol, &op->tw, &op->tsplit, &op->ttoff};
+                  &op->row_order, &op->pcol, &op->pw, &op->psplit, &op->tcol, &op->tw, &op->tsplit, &op->ttoff,
+                  &op->ocol, &op->ow, &op->olen, &op->otoff};
   for (DBuf* b : bufs) dfree(*b);
   op->err.release();
   if (op->side) cudaStreamSynchronize(op->side);
@@ -1550,6 +1586,7 @@ int sparsl_op_layouts(sparsl_op* op) {
   if (!op) return 0;
   return (op->ell.ok ? SPARSL_LAYOUT_ELL : 0) | (op->row_ordered ? SPARSL_LAYOUT_ROW_ORDER : 0) |
          (op->panel.ok ? SPARSL_LAYOUT_X_PANELS : 0) | (op->tpanel.ok ? SPARSL_LAYOUT_T_X_PANELS : 0) |
+         (op->ordered.ok ? SPARSL_LAYOUT_ORDERED_COPY : 0) |
          (op->sell_ok ? SPARSL_LAYOUT_SLICED_REVERSE : 0) |
          (op->has_t && !op->sell_ok ? SPARSL_LAYOUT_CSC : 0);
 }
@@ -1578,6 +1615,7 @@ int sparsl_op_force_plain_row_fold(sparsl_op* op) {
   op->row_ordered = false;
   op->panel.ok = false;
   op->tpanel.ok = false;
+  op->ordered.ok = false;
   return SPARSL_OK;
 }
 
@@ -1595,6 +1633,9 @@ int sparsl_op_set_weights(sparsl_op* op, const float* weights, uint64_t n) {
     encode_narrow(op->precision, weights, narrow.data(), n);
     CK("set_weights", cudaMemcpyAsync(op->w.p, narrow.data(), n * 2, cudaMemcpyHostToDevice, op->stream));
   }
+  if (op->ordered.ok)
+    CK("set_weights", launch_ordered_weights(op->row_ptr.as<uint32_t>(), op->w.p, op->precision == 0 ? 4 : 2,
+                                             op->ordered.order, op->nrows, op->ordered.toff, op->ow.p, op->stream));
   if (op->panel.ok)
     CK("set_weights", launch_panel_weights(op->w.p, op->nrows, op->panel.L, op->precision == 0 ? 4 : 2, op->pw.p,
                                            op->stream));

@@ -217,6 +217,144 @@ __global__ void panel_w_kernel(const T* __restrict__ w, uint64_t nrows, uint32_t
   }
 }
 
+// ---- Ordered copy (skewed operators): no panels, x gathered from global ----
+
+struct OrdLaunch {
+  const uint4* col;  // 16-byte groups of 4 columns
+  const uint4* w;    // 16-byte groups of 4 (f32) or 8 (16-bit) weights
+  const uint32_t* len;
+  const uint64_t* toff;
+  const uint32_t* order;
+  const float* x;
+  float* y;
+  uint32_t nrows;
+};
+
+template <int WK>
+struct OBatch {
+  uint4 c[2];
+  uint4 w[WK == W_F32 ? 2 : 1];
+  __device__ __forceinline__ void load(const OrdLaunch& p, uint64_t gbase, uint32_t lane, uint32_t jb) {
+    const uint64_t g4 = (gbase * 2 + jb / 4) * 32 + lane;
+    c[0] = __ldg(p.col + g4);
+    c[1] = __ldg(p.col + g4 + 32);
+    if constexpr (WK == W_F32) {
+      w[0] = __ldg(p.w + g4);
+      w[1] = __ldg(p.w + g4 + 32);
+    } else {
+      w[0] = __ldg(p.w + (gbase + jb / 8) * 32 + lane);
+    }
+  }
+  __device__ __forceinline__ uint32_t col(int u) const {
+    const uint4& q = c[u / 4];
+    return (u & 3) == 0 ? q.x : (u & 3) == 1 ? q.y : (u & 3) == 2 ? q.z : q.w;
+  }
+  __device__ __forceinline__ float weight(int u) const {
+    if constexpr (WK == W_F32) {
+      const uint4& q = w[u / 4];
+      return __uint_as_float((u & 3) == 0 ? q.x : (u & 3) == 1 ? q.y : (u & 3) == 2 ? q.z : q.w);
+    } else {
+      const uint32_t h = u < 2 ? w[0].x : u < 4 ? w[0].y : u < 6 ? w[0].z : w[0].w;
+      const uint32_t bits = (u & 1) ? h >> 16 : h & 0xffffu;
+      return WK == W_F16 ? widen_f16(bits) : widen_bf16(bits);
+    }
+  }
+};
+
+constexpr int kOrdWarps = 8;
+
+// One warp per tile of 32 length-ordered rows, one row per lane; no shared
+// memory, so many warps share an SM and keep many x gathers in flight.  Two
+// batches of 8 positions load while a third folds; a row folds its first
+// len positions in order, so the result is row_dot bit for bit.
+template <int WK>
+__global__ void __launch_bounds__(kOrdWarps * 32, 2) ordered_fold_kernel(const OrdLaunch p) {
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t tile = blockIdx.x * kOrdWarps + (threadIdx.x >> 5);
+  const uint32_t ntiles = (p.nrows + 31) / 32;
+  if (tile >= ntiles) return;  // warp-uniform
+  const uint32_t line = tile * 32 + lane;
+  const bool valid = line < p.nrows;
+  const uint32_t hi = valid ? __ldg(p.len + line) : 0u;
+  const uint32_t jend = __reduce_max_sync(0xffffffffu, hi);
+  const uint64_t gbase = __ldg(p.toff + tile);
+  float acc = 0.f;
+  uint32_t jb = 0;
+  OBatch<WK> cur, b1, b2;
+  if (jend > 0) cur.load(p, gbase, lane, 0);
+  if (jend > 8) b1.load(p, gbase, lane, 8);
+  auto step = [&](OBatch<WK>& f, OBatch<WK>& l) {
+    if (jb + 16 < jend) l.load(p, gbase, lane, jb + 16);
+    float xv[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) xv[u] = __ldg(p.x + f.col(u));  // padding positions hold column 0
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (jb + u < hi) acc = fadd(acc, fmul(f.weight(u), xv[u]));
+    jb += 8;
+    return jb < jend;
+  };
+  if (jend > 0) {
+    while (step(cur, b2) && step(b1, cur) && step(b2, b1)) {
+    }
+  }
+  if (valid) {
+    const uint32_t r = __ldg(p.order + line);
+    p.y[r] = fadd(p.y[r], acc);
+  }
+}
+
+// One CTA per tile: the tile's columns (groups of 4 positions) and lengths.
+__global__ void ordered_col_kernel(const uint32_t* __restrict__ rp, const uint32_t* __restrict__ col,
+                                   const uint32_t* __restrict__ order, uint64_t nrows, uint64_t ntiles,
+                                   const uint64_t* __restrict__ toff, uint32_t* __restrict__ ocol,
+                                   uint32_t* __restrict__ olen) {
+  for (uint64_t T = blockIdx.x; T < ntiles; T += gridDim.x) {
+    const uint64_t g0 = toff[T], n = (toff[T + 1] - g0) * 256;
+    for (uint64_t e = threadIdx.x; e < n; e += blockDim.x) {
+      const uint32_t lane = (uint32_t)(e >> 2) & 31u;
+      const uint32_t j = (uint32_t)(e >> 7) * 4 + (uint32_t)(e & 3);
+      const uint64_t line = T * 32 + lane;
+      uint32_t v = 0;
+      if (line < nrows) {
+        const uint32_t r = order[line], a = rp[r];
+        if (j < rp[r + 1] - a) v = col[(uint64_t)a + j];
+      }
+      ocol[g0 * 256 + e] = v;
+    }
+    if (threadIdx.x < 32) {
+      const uint64_t line = T * 32 + threadIdx.x;
+      uint32_t l = 0;
+      if (line < nrows) {
+        const uint32_t r = order[line];
+        l = rp[r + 1] - rp[r];
+      }
+      olen[line] = l;
+    }
+  }
+}
+
+template <typename T>
+__global__ void ordered_w_kernel(const uint32_t* __restrict__ rp, const T* __restrict__ w,
+                                 const uint32_t* __restrict__ order, uint64_t nrows, uint64_t ntiles,
+                                 const uint64_t* __restrict__ toff, T* __restrict__ ow) {
+  constexpr uint32_t g = 16 / sizeof(T);
+  for (uint64_t S = blockIdx.x; S < ntiles; S += gridDim.x) {
+    const uint64_t g0 = toff[S], n = (toff[S + 1] - g0) * 256;
+    for (uint64_t e = threadIdx.x; e < n; e += blockDim.x) {
+      const uint32_t lane = (uint32_t)(e / g) & 31u;
+      const uint32_t j = (uint32_t)(e / (g * 32)) * g + (uint32_t)(e % g);
+      const uint64_t line = S * 32 + lane;
+      T v = T(0);
+      if (line < nrows) {
+        const uint32_t r = order[line], a = rp[r];
+        if (j < rp[r + 1] - a) v = w[(uint64_t)a + j];
+      }
+      ow[g0 * 256 + e] = v;
+    }
+  }
+}
+
 // One CTA per slice (tile of 32 lines): its lines' entries into the
 // 16-byte-group layout.  Positions past a line's length are padding (0).
 __global__ void panel_sell_col_kernel(const unsigned long long* __restrict__ slice_ptr,
@@ -377,6 +515,47 @@ cudaError_t launch_panel_weights_sell(const unsigned long long* slice_ptr, const
     panel_sell_w_kernel<uint16_t><<<blocks, 256, 0, stream>>>(slice_ptr, line_ptr,
                                                                static_cast<const uint16_t*>(w_sell), nlines, nslices,
                                                                toff, static_cast<uint16_t*>(out));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ordered_weights(const uint32_t* row_ptr, const void* w, int esize, const uint32_t* order,
+                                   uint64_t nrows, const uint64_t* toff, void* ow, cudaStream_t stream) {
+  const uint64_t ntiles = (nrows + 31) / 32;
+  if (ntiles == 0) return cudaSuccess;
+  const uint32_t blocks = (uint32_t)std::min<uint64_t>(ntiles, 148ull * 8);
+  if (esize == 4)
+    ordered_w_kernel<uint32_t><<<blocks, 256, 0, stream>>>(row_ptr, static_cast<const uint32_t*>(w), order, nrows,
+                                                            ntiles, toff, static_cast<uint32_t*>(ow));
+  else
+    ordered_w_kernel<uint16_t><<<blocks, 256, 0, stream>>>(row_ptr, static_cast<const uint16_t*>(w), order, nrows,
+                                                            ntiles, toff, static_cast<uint16_t*>(ow));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ordered_build(const uint32_t* row_ptr, const uint32_t* col, const void* w, int esize,
+                                 const uint32_t* order, uint64_t nrows, const uint64_t* toff, uint32_t* ocol,
+                                 void* ow, uint32_t* olen, cudaStream_t stream) {
+  const uint64_t ntiles = (nrows + 31) / 32;
+  if (ntiles == 0) return cudaSuccess;
+  const uint32_t blocks = (uint32_t)std::min<uint64_t>(ntiles, 148ull * 8);
+  ordered_col_kernel<<<blocks, 256, 0, stream>>>(row_ptr, col, order, nrows, ntiles, toff, ocol, olen);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  return launch_ordered_weights(row_ptr, w, esize, order, nrows, toff, ow, stream);
+}
+
+cudaError_t launch_ordered_spmv(const OrderedOp& op, const float* x, float* y, cudaStream_t stream) {
+  if (!op.ok) return cudaErrorInvalidValue;
+  if (op.nrows == 0) return cudaSuccess;
+  const uint32_t ntiles = (op.nrows + 31) / 32;
+  const uint32_t blocks = (ntiles + kOrdWarps - 1) / kOrdWarps;
+  const OrdLaunch p{reinterpret_cast<const uint4*>(op.col), reinterpret_cast<const uint4*>(op.w), op.len, op.toff,
+                    op.order, x, y, op.nrows};
+  switch (op.wkind) {
+    case W_F32: ordered_fold_kernel<W_F32><<<blocks, kOrdWarps * 32, 0, stream>>>(p); break;
+    case W_F16: ordered_fold_kernel<W_F16><<<blocks, kOrdWarps * 32, 0, stream>>>(p); break;
+    default: ordered_fold_kernel<W_BF16><<<blocks, kOrdWarps * 32, 0, stream>>>(p); break;
+  }
   return cudaGetLastError();
 }
 

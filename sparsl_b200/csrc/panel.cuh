@@ -75,6 +75,36 @@ cudaError_t launch_panel_weights_sell(const unsigned long long* slice_ptr, const
                                       const void* w_sell, uint64_t nlines, uint32_t nslices, const uint64_t* toff,
                                       int esize, void* out, cudaStream_t stream);
 
+// Skewed operators (rows of very different lengths): a copy of the rows in
+// descending-length order, 32 per tile, each tile padded to its longest row
+// (a multiple of 8 positions), with 32-bit columns, so that dense-x SpMV runs
+// without shared memory at high occupancy: one warp per tile, x gathered
+// from global memory (L2-resident for the sizes that take this path).
+//   col[((toff[T] * 2 + j / 4) * 32 + lane) * 4 + j % 4]
+//   w  as in the panel copy, with gbase = toff[T]
+//   len[32 * T + lane]: the row's length; order[32 * T + lane]: the row
+struct OrderedOp {
+  const uint32_t* col = nullptr;
+  const void* w = nullptr;
+  const uint32_t* len = nullptr;
+  const uint64_t* toff = nullptr;  // 8-position groups before tile T
+  const uint32_t* order = nullptr; // rows by descending length
+  int wkind = 0;
+  uint32_t nrows = 0;
+  bool ok = false;
+};
+
+// Builds col, w and len from the CSR arrays (row_ptr, col, w of esize bytes)
+// and the order; toff holds ntiles + 1 group offsets.
+cudaError_t launch_ordered_build(const uint32_t* row_ptr, const uint32_t* col, const void* w, int esize,
+                                 const uint32_t* order, uint64_t nrows, const uint64_t* toff, uint32_t* ocol,
+                                 void* ow, uint32_t* olen, cudaStream_t stream);
+// Rebuilds only the weights (new weights after prepare).
+cudaError_t launch_ordered_weights(const uint32_t* row_ptr, const void* w, int esize, const uint32_t* order,
+                                   uint64_t nrows, const uint64_t* toff, void* ow, cudaStream_t stream);
+// y[r] = y[r] + fold_r over the ordered copy (same fold as below).
+cudaError_t launch_ordered_spmv(const OrderedOp& op, const float* x, float* y, cudaStream_t stream);
+
 // y[r] = y[r] + fold_r, fold_r the strict left fold from 0.0 of w * x over
 // row r's entries in stored order (src/backend/mod.rs:2259-2267), for a
 // dense x of op.ncols floats.  The columns of a row are non-decreasing, so

@@ -7,7 +7,8 @@ next, rows that skip whole panels, duplicate columns), the three weight
 precisions, new weights after prepare, an x that is not 16-byte aligned, and
 the widest x that still takes the TMA stream instead.  The transpose product
 over the same panels (built from the sliced-ELL reverse index, x indexed by
-row) is checked the same way against the oracle and the reverse-index fold."""
+row) is checked the same way against the oracle and the reverse-index fold,
+and so is the ordered copy that skewed operators use for dense-x SpMV."""
 import numpy as np
 import pytest
 
@@ -219,3 +220,62 @@ def test_transpose_rows_past_the_panels_keep_the_reverse_index(O, cuda_device):
     csr, w = _uniform(O, 4 * MAX_PANEL + 1, 3000, 2, 51)
     op, _, _ = _check_t(O, cuda_device, csr, w, S.WeightPrecision.F32, 52, panels=False)
     assert op.layouts() & SLICED
+
+
+ORDERED = 64  # SPARSL_LAYOUT_ORDERED_COPY
+ROW_ORDER = 2  # SPARSL_LAYOUT_ROW_ORDER
+
+
+def _skewed(O, nrows, ncols, seed, cap=3000, empty_every=0):
+    r = np.random.default_rng(seed)
+    lens = np.minimum(r.zipf(1.5, nrows), min(cap, ncols))
+    if empty_every:
+        lens[::empty_every] = 0
+    rp = np.zeros(nrows + 1, np.uint64)
+    np.cumsum(lens, out=rp[1:])
+    col = np.concatenate([np.sort(r.choice(ncols, k, replace=False)) if k else np.zeros(0, np.int64)
+                          for k in lens]).astype(np.uint32)
+    w = (r.standard_normal(col.size) * 0.5).astype(np.float32)
+    return O.Csr(rp.astype(np.uint32), col, ncols), w
+
+
+@pytest.mark.parametrize("nrows,ncols,empty_every", [(40, 50, 7), (20_000, 300_000, 0), (200_000, 50_000, 13)])
+@pytest.mark.parametrize("precision", [S.WeightPrecision.F32, S.WeightPrecision.F16, S.WeightPrecision.Bf16])
+def test_ordered_copy_spmv_bit_exact(O, cuda_device, nrows, ncols, empty_every, precision):
+    """Skewed rows (Zipf lengths, some empty): dense-x SpMV over the ordered
+    copy against the oracle and the generic row fold; y holds -0.0 values so
+    an empty row's y + 0.0 is checked too."""
+    csr, w = _skewed(O, nrows, ncols, nrows + ncols, empty_every=empty_every)
+    wq = O.quantise(int(precision), w)
+    op = cuda_device.prepare_with(S.Csr(csr.row_ptr, csr.col, ncols), ncols, w, precision)
+    lay = op.layouts()
+    assert bool(lay & ORDERED) == bool(lay & ROW_ORDER)
+    if nrows >= 20_000:
+        assert lay & ORDERED
+    ref = cuda_device.prepare_with(S.Csr(csr.row_ptr, csr.col, ncols), ncols, w, precision)
+    ref.force_plain_row_fold()
+    assert not ref.layouts() & (ORDERED | ROW_ORDER)
+    r = np.random.default_rng(3)
+    x = r.uniform(-1, 1, ncols).astype(np.float32)
+    y0 = r.uniform(-1, 1, nrows).astype(np.float32)
+    y0[::5] = -0.0
+    got, gen = y0.copy(), y0.copy()
+    op.spmv(x, got)
+    ref.spmv(x, gen)
+    want = O.spmv(csr, wq, x, y0.copy())
+    assert_bits_equal(got, want, "ordered copy vs oracle")
+    assert_bits_equal(gen, want, "generic row fold vs oracle")
+
+
+def test_ordered_copy_follows_new_weights(O, cuda_device):
+    csr, w = _skewed(O, 50_000, 20_000, 77)
+    op = cuda_device.prepare(S.Csr(csr.row_ptr, csr.col, csr.ncols), csr.ncols, w)
+    assert op.layouts() & ORDERED
+    r = np.random.default_rng(78)
+    x = r.uniform(-1, 1, csr.ncols).astype(np.float32)
+    y0 = r.uniform(-1, 1, 50_000).astype(np.float32)
+    w2 = r.uniform(-2, 2, w.size).astype(np.float32)
+    op.set_weights(w2)
+    got = y0.copy()
+    op.spmv(x, got)
+    assert_bits_equal(got, O.spmv(csr, w2, x, y0.copy()), "ordered spmv after set_weights")
