@@ -86,9 +86,12 @@ def peaks():
 # ncu captures (dram__bytes_read.sum + dram__bytes_write.sum of one launch
 # over the launch's algorithmic bytes), keyed by workload.
 TRAFFIC_RATIO = {
-    "ragged_spmv": ((452_783_104 + 11_910_144) / 408_395_452,
+    "ragged_spmv": ((457_363_456 + 1_466_112) / 408_395_452,
                     "ncu capture of the same launch (bench.py --workload ragged), 1,000,000 rows: the ordered "
                     "copy's tiles are padded to their longest row, and x is gathered from DRAM once"),
+    "ragged_tick": ((457_627_904 + 3_647_616) / 408_645_452,
+                    "ncu capture of the tick kernel's launches (bench.py --workload ragged): the ordered fold with "
+                    "the spike bitmask in shared memory; packing and compaction not counted"),
     "spmv": (39_812_352 / 52_800_004, "ncu capture of the same launch (bench.py --workload spmv): the panel "
                                       "layout's 16-bit panel-relative columns read less than the CSR bytes"),
     "spmv_f16": (27_011_584 / 40_000_004, "ncu capture of the same launch (bench.py --workload spmv), f16 weights"),
@@ -1139,8 +1142,8 @@ def bench_ragged(args, op, csr, w, s, flush):
             "ms_per_step": ms, "algorithmic_bytes": algo, "bit_exact_vs_oracle": exact,
             "config": f"the SpMM matrix ({n:,} rows, {nnz:,} nnz, Zipf(1.5) lengths) times a dense x U[0,1]; "
                       "L2 flushed before every launch",
-            "roofline": roofline(algo, ms, "ordered_fold_kernel<f32> (rows in descending-length order, "
-                                           "tile-interleaved copy)", "ragged_spmv")}
+            "roofline": roofline(algo, ms, "ordered_fold_kernel<f32, dense x> (rows of 1,024+ entries a warp "
+                                           "each, the rest from the tile-interleaved ordered copy)", "ragged_spmv")}
     # Recurrent ticks (fused spike SpMV + LIF + packing + index list), timed
     # from the initial state; the timed ticks are checked against the CPU.
     ticks = 20
@@ -1176,7 +1179,7 @@ def bench_ragged(args, op, csr, w, s, flush):
             "bit_exact_vs_oracle": ok,
             "config": f"the SpMM matrix as a recurrent network (weights x 0.05), decay 0.95, theta 1, reset 0, "
                       "Bernoulli(0.02) initial spikes",
-            "roofline": roofline(talgo, per, "row_fold_kernel<f32, spike bitmask, LIF, descending-length order> + "
+            "roofline": roofline(talgo, per, "ordered_fold_kernel<f32, spike bitmask in shared memory, LIF> + "
                                              "pack_kernel + compact_bits_kernel", "ragged_tick"),
             "cpu_baseline": {"value": ticks / cpu_s, "unit": "ticks/s", "cores": O.num_threads(), "kind": "port",
                              "sample": f"the same {ticks} ticks (the parity check), CpuParallel restatement"}}

@@ -458,19 +458,28 @@ RowLaunch fwd_launch(sparsl_op* op) {
 // Forward launches take the TMA-pipelined kernel when the operator's rows all
 // have the same length, the generic row-fold kernel otherwise.
 cudaError_t launch_fwd(sparsl_op* op, const RowLaunch& p, cudaStream_t s) {
-  if (op->ordered.ok && p.xmode == X_DENSE && p.epilogue == EPI_ACCUM && !p.eidx && !p.out_bits && !p.idx_list)
-    return launch_ordered_spmv(op->ordered, p.x, p.y, s);
   if (op->panel.ok && p.xmode == X_DENSE && p.epilogue == EPI_ACCUM && !p.eidx && !p.out_bits && !p.idx_list)
     return launch_panel_spmv(op->panel, p.x, p.y, s);
   if (!op->ell.ok && op->row_ordered && !p.eidx) {
     // Skewed rows: warps fold rows in descending-length order; the packed
     // spike words (and from them the index list) come from the spike bytes.
-    RowLaunch q = p;
-    q.order = op->row_order.as<uint32_t>();
-    q.out_bits = nullptr;
-    q.idx_list = nullptr;
-    q.idx_count = nullptr;
-    cudaError_t e = launch_rows(q, s);
+    cudaError_t e;
+    const bool bits = p.xmode != X_DENSE;
+    if (op->ordered.ok && (!bits || (uint64_t)p.xbits_words * 4 <= kOrderedBitsMaxBytes)) {
+      // The ordered fold: long rows a warp each, the rest 32 rows of similar
+      // length per warp, no staging; a spike operand sits in shared memory.
+      const bool lif = p.epilogue == EPI_LIF;
+      e = launch_ordered_fold(op->ordered, bits ? nullptr : p.x, bits ? p.xbits : nullptr, bits ? p.xbits_words : 0,
+                              lif ? nullptr : p.y, lif ? p.v : nullptr, lif ? p.theta : nullptr,
+                              lif ? p.spikes : nullptr, p.decay, p.v_reset, p.dtheta, s);
+    } else {
+      RowLaunch q = p;
+      q.order = op->row_order.as<uint32_t>();
+      q.out_bits = nullptr;
+      q.idx_list = nullptr;
+      q.idx_count = nullptr;
+      e = launch_rows(q, s);
+    }
     if (e != cudaSuccess || !p.out_bits) return e;
     const uint64_t words = ((uint64_t)p.nlines + 31) / 32;
     e = launch_pack(p.spikes, p.nlines, p.out_bits, words, s);
@@ -1487,12 +1496,16 @@ int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int 
       cudaMemcpyAsync(op->spmm_order.p, sp_order.data(), nrows * 4, cudaMemcpyHostToDevice, op->stream);
       cudaMemcpyAsync(op->spmm_units.p, sp_units.data(), sp_units.size() * 4, cudaMemcpyHostToDevice, op->stream);
       // Skewed rows, the operator's own arrays, up to 2^30 entries: the
-      // ordered copy for dense-x SpMV.  Tile T holds rows sp_order[32T ..
-      // 32T + 31], padded to its first (longest) row, rounded up to 8.
+      // ordered fold.  The rows of kOrderedLongRow entries or more (a prefix
+      // of the descending order) are folded one warp each from the CSR
+      // arrays; tile T of the copy holds rows sp_order[nlong + 32T ..], padded
+      // to its first (longest) row, rounded up to 8.
       if (op->row_ordered && !borrow && nnz <= (1ull << 30)) {
-        const uint64_t nt = (nrows + 31) / 32;
+        uint64_t nlong = 0;
+        while (nlong < nrows && len(sp_order[nlong]) >= kOrderedLongRow) ++nlong;
+        const uint64_t nshort = nrows - nlong, nt = (nshort + 31) / 32;
         std::vector<uint64_t> to(nt + 1, 0);
-        for (uint64_t T = 0; T < nt; ++T) to[T + 1] = to[T] + (len(sp_order[T * 32]) + 7) / 8;
+        for (uint64_t T = 0; T < nt; ++T) to[T + 1] = to[T] + (len(sp_order[nlong + T * 32]) + 7) / 8;
         PALLOC(op->otoff, (nt + 1) * 8, false, "ordered offsets");
         PALLOC(op->ocol, to[nt] * 256 * 4, false, "ordered col");
         PALLOC(op->ow, to[nt] * 256 * wbytes, false, "ordered values");
@@ -1500,7 +1513,7 @@ int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int 
         if (cudaMemcpyAsync(op->otoff.p, to.data(), (nt + 1) * 8, cudaMemcpyHostToDevice, op->stream) !=
                 cudaSuccess ||
             launch_ordered_build(op->row_ptr.as<uint32_t>(), op->col.as<uint32_t>(), op->w.p, (int)wbytes,
-                                 op->spmm_order.as<uint32_t>(), nrows, op->otoff.as<uint64_t>(),
+                                 op->spmm_order.as<uint32_t>() + nlong, nshort, op->otoff.as<uint64_t>(),
                                  op->ocol.as<uint32_t>(), op->ow.p, op->olen.as<uint32_t>(), op->stream) !=
                 cudaSuccess)
           return bail(fail_cuda("prepare", cudaGetLastError()));
@@ -1511,8 +1524,12 @@ int prepare_body(sparsl_dev* d, const PrepSrc& src, const sparsl_shape& sh, int 
         od.len = op->olen.as<uint32_t>();
         od.toff = op->otoff.as<uint64_t>();
         od.order = op->spmm_order.as<uint32_t>();
+        od.row_ptr = op->row_ptr.as<uint32_t>();
+        od.csr_col = op->col.as<uint32_t>();
+        od.csr_w = op->w.p;
         od.wkind = wkind_of(precision);
         od.nrows = (uint32_t)nrows;
+        od.nlong = (uint32_t)nlong;
         od.ok = true;
       }
       if (ranged) {
@@ -1635,7 +1652,9 @@ int sparsl_op_set_weights(sparsl_op* op, const float* weights, uint64_t n) {
   }
   if (op->ordered.ok)
     CK("set_weights", launch_ordered_weights(op->row_ptr.as<uint32_t>(), op->w.p, op->precision == 0 ? 4 : 2,
-                                             op->ordered.order, op->nrows, op->ordered.toff, op->ow.p, op->stream));
+                                             op->ordered.order + op->ordered.nlong,
+                                             op->nrows - op->ordered.nlong, op->ordered.toff, op->ow.p,
+                                             op->stream));
   if (op->panel.ok)
     CK("set_weights", launch_panel_weights(op->w.p, op->nrows, op->panel.L, op->precision == 0 ? 4 : 2, op->pw.p,
                                            op->stream));

@@ -22,6 +22,7 @@
 
 #include "common.cuh"
 #include "panel.cuh"
+#include "rows.cuh"
 
 namespace sparsl {
 namespace {
@@ -224,9 +225,19 @@ struct OrdLaunch {
   const uint4* w;    // 16-byte groups of 4 (f32) or 8 (16-bit) weights
   const uint32_t* len;
   const uint64_t* toff;
-  const uint32_t* order;
-  const float* x;
-  float* y;
+  const uint32_t* order;   // all rows by descending length
+  const uint32_t* rp;      // CSR arrays, for the long rows
+  const uint32_t* ccol;
+  const void* cw;
+  uint32_t nlong;          // rows folded one warp each (the first nlong of order)
+  const float* x;          // dense operand
+  const uint32_t* xbits;   // or the spike bitmask (staged in shared memory)
+  uint32_t xbits_words;
+  float* y;                // EPI_ACCUM
+  float* v;                // EPI_LIF state and spike bytes
+  float* theta;
+  uint8_t* spikes;
+  float decay, v_reset, dtheta;
   uint32_t nrows;
 };
 
@@ -261,46 +272,129 @@ struct OBatch {
   }
 };
 
-constexpr int kOrdWarps = 8;
+constexpr int kOrdWarps = 8;       // dense x: 8-warp CTAs, one tile per warp
+constexpr int kOrdBitsWarps = 24;  // spike bitmask in shared memory: one 24-warp CTA per SM
 
-// One warp per tile of 32 length-ordered rows, one row per lane; no shared
-// memory, so many warps share an SM and keep many x gathers in flight.  Two
-// batches of 8 positions load while a third folds; a row folds its first
-// len positions in order, so the result is row_dot bit for bit.
-template <int WK>
-__global__ void __launch_bounds__(kOrdWarps * 32, 2) ordered_fold_kernel(const OrdLaunch p) {
+// The ordered fold.  The first nlong rows of the descending order (the long
+// ones) take a warp each: lane k loads entries k, k + 32, ... of a 128-entry
+// chunk straight from the CSR arrays (coalesced), gathers and multiplies
+// them, and the products reach the fold one by one through shuffles, in
+// stored order, while the next chunk's loads are in flight.  The other rows
+// take a lane each over the tile-interleaved copy, 32 rows of similar length
+// per warp, with two batches of 8 positions loading while a third folds.
+// Either way a row folds its entries in order from 0.0, so the sum is
+// row_dot bit for bit; the epilogue (y + sum, or the LIF step of
+// src/backend/mod.rs:2461-2472) goes to the row through the order.  A dense
+// x is gathered from global memory with no shared memory, so many 8-warp
+// CTAs share an SM; a spike bitmask is staged in shared memory by persistent
+// CTAs, one per SM, whose warps stride over the rows and tiles.
+template <int WK, int XM, int EPI>
+__global__ void __launch_bounds__(XM == X_DENSE ? kOrdWarps * 32 : kOrdBitsWarps * 32, XM == X_DENSE ? 2 : 1)
+    ordered_fold_kernel(const OrdLaunch p) {
+  extern __shared__ __align__(16) uint32_t s_bits[];
   const uint32_t lane = threadIdx.x & 31;
-  const uint32_t tile = blockIdx.x * kOrdWarps + (threadIdx.x >> 5);
-  const uint32_t ntiles = (p.nrows + 31) / 32;
-  if (tile >= ntiles) return;  // warp-uniform
-  const uint32_t line = tile * 32 + lane;
-  const bool valid = line < p.nrows;
-  const uint32_t hi = valid ? __ldg(p.len + line) : 0u;
-  const uint32_t jend = __reduce_max_sync(0xffffffffu, hi);
-  const uint64_t gbase = __ldg(p.toff + tile);
-  float acc = 0.f;
-  uint32_t jb = 0;
-  OBatch<WK> cur, b1, b2;
-  if (jend > 0) cur.load(p, gbase, lane, 0);
-  if (jend > 8) b1.load(p, gbase, lane, 8);
-  auto step = [&](OBatch<WK>& f, OBatch<WK>& l) {
-    if (jb + 16 < jend) l.load(p, gbase, lane, jb + 16);
-    float xv[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) xv[u] = __ldg(p.x + f.col(u));  // padding positions hold column 0
-#pragma unroll
-    for (int u = 0; u < 8; ++u)
-      if (jb + u < hi) acc = fadd(acc, fmul(f.weight(u), xv[u]));
-    jb += 8;
-    return jb < jend;
-  };
-  if (jend > 0) {
-    while (step(cur, b2) && step(b1, cur) && step(b2, b1)) {
-    }
+  const uint32_t nw = blockDim.x >> 5;
+  const uint32_t ntiles = (p.nrows - p.nlong + 31) / 32;
+  if constexpr (XM == X_BITS_SMEM) {
+    const uint32_t nvec = p.xbits_words >> 2;
+    for (uint32_t i = threadIdx.x; i < nvec; i += blockDim.x)
+      reinterpret_cast<uint4*>(s_bits)[i] = __ldg(reinterpret_cast<const uint4*>(p.xbits) + i);
+    for (uint32_t i = (nvec << 2) + threadIdx.x; i < p.xbits_words; i += blockDim.x) s_bits[i] = __ldg(p.xbits + i);
+    __syncthreads();
   }
-  if (valid) {
-    const uint32_t r = __ldg(p.order + line);
-    p.y[r] = fadd(p.y[r], acc);
+  auto gather = [&](uint32_t c) -> float {
+    if constexpr (XM == X_DENSE)
+      return __ldg(p.x + c);
+    else
+      return (float)((s_bits[c >> 5] >> (c & 31)) & 1u);
+  };
+  auto epilogue = [&](uint32_t r, float acc) {
+    if constexpr (EPI == EPI_ACCUM) {
+      p.y[r] = fadd(p.y[r], acc);
+    } else {
+      // lif_step: two roundings, then >= theta.
+      float vv = p.v[r], th = p.theta[r];
+      const float vol = fadd(fmul(vv, p.decay), acc);
+      uint8_t spike = 0;
+      if (vol >= th) {
+        spike = 1;
+        vv = p.v_reset;
+        th = fadd(th, p.dtheta);
+      } else {
+        vv = vol;
+      }
+      p.v[r] = vv;
+      p.theta[r] = th;
+      p.spikes[r] = spike;
+    }
+  };
+  const uint32_t gwarp = blockIdx.x * nw + (threadIdx.x >> 5), nwarps = gridDim.x * nw;
+  for (uint32_t lr = gwarp; lr < p.nlong; lr += nwarps) {
+    const uint32_t r = __ldg(p.order + lr);
+    const uint32_t a = __ldg(p.rp + r), n = __ldg(p.rp + r + 1) - a;
+    float acc = 0.f;
+    uint32_t c[4], cn[4];
+    float w[4], wn[4];
+    auto load = [&](uint32_t k0, uint32_t* cc, float* ww) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t e = k0 + 32 * q + lane;
+        cc[q] = 0;
+        ww[q] = 0.f;
+        if (e < n) {
+          cc[q] = __ldg(p.ccol + a + e);
+          ww[q] = load_weight<WK>(p.cw, (uint64_t)a + e);
+        }
+      }
+    };
+    load(0, c, w);
+    for (uint32_t k0 = 0; k0 < n; k0 += 128) {
+      if (k0 + 128 < n) load(k0 + 128, cn, wn);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float prod = fmul(w[q], gather(c[q]));
+        const uint32_t base = k0 + 32 * q;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const float t = __shfl_sync(0xffffffffu, prod, k);
+          if (base + k < n) acc = fadd(acc, t);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        c[q] = cn[q];
+        w[q] = wn[q];
+      }
+    }
+    if (lane == 0) epilogue(r, acc);
+  }
+  for (uint32_t tile = gwarp; tile < ntiles; tile += nwarps) {
+    const uint32_t line = tile * 32 + lane;
+    const bool valid = line < p.nrows - p.nlong;
+    const uint32_t hi = valid ? __ldg(p.len + line) : 0u;
+    const uint32_t jend = __reduce_max_sync(0xffffffffu, hi);
+    const uint64_t gbase = __ldg(p.toff + tile);
+    float acc = 0.f;
+    uint32_t jb = 0;
+    OBatch<WK> cur, b1, b2;
+    if (jend > 0) cur.load(p, gbase, lane, 0);
+    if (jend > 8) b1.load(p, gbase, lane, 8);
+    auto step = [&](OBatch<WK>& f, OBatch<WK>& l) {
+      if (jb + 16 < jend) l.load(p, gbase, lane, jb + 16);
+      float xv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) xv[u] = gather(f.col(u));  // padding positions hold column 0
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (jb + u < hi) acc = fadd(acc, fmul(f.weight(u), xv[u]));
+      jb += 8;
+      return jb < jend;
+    };
+    if (jend > 0) {
+      while (step(cur, b2) && step(b1, cur) && step(b2, b1)) {
+      }
+    }
+    if (valid) epilogue(__ldg(p.order + p.nlong + line), acc);
   }
 }
 
@@ -544,19 +638,80 @@ cudaError_t launch_ordered_build(const uint32_t* row_ptr, const uint32_t* col, c
   return launch_ordered_weights(row_ptr, w, esize, order, nrows, toff, ow, stream);
 }
 
-cudaError_t launch_ordered_spmv(const OrderedOp& op, const float* x, float* y, cudaStream_t stream) {
-  if (!op.ok) return cudaErrorInvalidValue;
-  if (op.nrows == 0) return cudaSuccess;
-  const uint32_t ntiles = (op.nrows + 31) / 32;
-  const uint32_t blocks = (ntiles + kOrdWarps - 1) / kOrdWarps;
-  const OrdLaunch p{reinterpret_cast<const uint4*>(op.col), reinterpret_cast<const uint4*>(op.w), op.len, op.toff,
-                    op.order, x, y, op.nrows};
-  switch (op.wkind) {
-    case W_F32: ordered_fold_kernel<W_F32><<<blocks, kOrdWarps * 32, 0, stream>>>(p); break;
-    case W_F16: ordered_fold_kernel<W_F16><<<blocks, kOrdWarps * 32, 0, stream>>>(p); break;
-    default: ordered_fold_kernel<W_BF16><<<blocks, kOrdWarps * 32, 0, stream>>>(p); break;
+namespace {
+
+template <int WK, int XM, int EPI>
+cudaError_t ordered_go(const OrdLaunch& p, cudaStream_t stream) {
+  const uint32_t work = p.nlong + (p.nrows - p.nlong + 31) / 32;  // long rows and tiles, a warp each
+  if constexpr (XM == X_DENSE) {
+    const uint32_t blocks = std::max<uint32_t>(1, (work + kOrdWarps - 1) / kOrdWarps);
+    ordered_fold_kernel<WK, XM, EPI><<<blocks, kOrdWarps * 32, 0, stream>>>(p);
+  } else {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const size_t smem = ((size_t)p.xbits_words * 4 + 15) & ~(size_t)15;
+    e = cudaFuncSetAttribute(ordered_fold_kernel<WK, XM, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+    if (e != cudaSuccess) return e;
+    const uint32_t blocks = std::max<uint32_t>(
+        1, std::min<uint32_t>((work + kOrdBitsWarps - 1) / kOrdBitsWarps, (uint32_t)std::max(panel_sms(dev), 1)));
+    ordered_fold_kernel<WK, XM, EPI><<<blocks, kOrdBitsWarps * 32, smem, stream>>>(p);
   }
   return cudaGetLastError();
+}
+
+template <int XM, int EPI>
+cudaError_t ordered_wk(int wkind, const OrdLaunch& p, cudaStream_t stream) {
+  switch (wkind) {
+    case W_F32: return ordered_go<W_F32, XM, EPI>(p, stream);
+    case W_F16: return ordered_go<W_F16, XM, EPI>(p, stream);
+    default: return ordered_go<W_BF16, XM, EPI>(p, stream);
+  }
+}
+
+OrdLaunch ordered_launch(const OrderedOp& op) {
+  OrdLaunch p{};
+  p.col = reinterpret_cast<const uint4*>(op.col);
+  p.w = reinterpret_cast<const uint4*>(op.w);
+  p.len = op.len;
+  p.toff = op.toff;
+  p.order = op.order;
+  p.rp = op.row_ptr;
+  p.ccol = op.csr_col;
+  p.cw = op.csr_w;
+  p.nlong = op.nlong;
+  p.nrows = op.nrows;
+  return p;
+}
+
+}  // namespace
+
+cudaError_t launch_ordered_spmv(const OrderedOp& op, const float* x, float* y, cudaStream_t stream) {
+  return launch_ordered_fold(op, x, nullptr, 0, y, nullptr, nullptr, nullptr, 0.f, 0.f, 0.f, stream);
+}
+
+cudaError_t launch_ordered_fold(const OrderedOp& op, const float* x, const uint32_t* xbits, uint32_t xbits_words,
+                                float* y, float* v, float* theta, uint8_t* spikes, float decay, float v_reset,
+                                float dtheta, cudaStream_t stream) {
+  if (!op.ok || (xbits && (uint64_t)xbits_words * 4 > kOrderedBitsMaxBytes)) return cudaErrorInvalidValue;
+  if (op.nrows == 0) return cudaSuccess;
+  OrdLaunch p = ordered_launch(op);
+  p.x = x;
+  p.xbits = xbits;
+  p.xbits_words = xbits_words;
+  p.y = y;
+  p.v = v;
+  p.theta = theta;
+  p.spikes = spikes;
+  p.decay = decay;
+  p.v_reset = v_reset;
+  p.dtheta = dtheta;
+  const bool lif = v != nullptr;
+  if (xbits)
+    return lif ? ordered_wk<X_BITS_SMEM, EPI_LIF>(op.wkind, p, stream)
+               : ordered_wk<X_BITS_SMEM, EPI_ACCUM>(op.wkind, p, stream);
+  return lif ? ordered_wk<X_DENSE, EPI_LIF>(op.wkind, p, stream) : ordered_wk<X_DENSE, EPI_ACCUM>(op.wkind, p, stream);
 }
 
 cudaError_t launch_panel_spmv(const PanelOp& op, const float* x, float* y, cudaStream_t stream) {

@@ -75,22 +75,31 @@ cudaError_t launch_panel_weights_sell(const unsigned long long* slice_ptr, const
                                       const void* w_sell, uint64_t nlines, uint32_t nslices, const uint64_t* toff,
                                       int esize, void* out, cudaStream_t stream);
 
-// Skewed operators (rows of very different lengths): a copy of the rows in
-// descending-length order, 32 per tile, each tile padded to its longest row
-// (a multiple of 8 positions), with 32-bit columns, so that dense-x SpMV runs
-// without shared memory at high occupancy: one warp per tile, x gathered
-// from global memory (L2-resident for the sizes that take this path).
+// Skewed operators (rows of very different lengths): the rows in
+// descending-length order.  The first nlong rows (kOrderedLongRow entries or
+// more) are folded one warp per row straight from the CSR arrays, 32
+// consecutive entries per load.  The rest are copied 32 per tile, each tile
+// padded to its longest row (a multiple of 8 positions), with 32-bit
+// columns, and folded one lane per row.
 //   col[((toff[T] * 2 + j / 4) * 32 + lane) * 4 + j % 4]
 //   w  as in the panel copy, with gbase = toff[T]
-//   len[32 * T + lane]: the row's length; order[32 * T + lane]: the row
+//   len[32 * T + lane]: the row's length; the row is order[nlong + 32 * T + lane]
+#ifndef SPARSL_ORDERED_LONG_ROW
+#define SPARSL_ORDERED_LONG_ROW 1024
+#endif
+constexpr uint32_t kOrderedLongRow = SPARSL_ORDERED_LONG_ROW;
 struct OrderedOp {
   const uint32_t* col = nullptr;
   const void* w = nullptr;
   const uint32_t* len = nullptr;
-  const uint64_t* toff = nullptr;  // 8-position groups before tile T
-  const uint32_t* order = nullptr; // rows by descending length
+  const uint64_t* toff = nullptr;     // 8-position groups before tile T
+  const uint32_t* order = nullptr;    // all rows by descending length
+  const uint32_t* row_ptr = nullptr;  // the CSR arrays, for the long rows
+  const uint32_t* csr_col = nullptr;
+  const void* csr_w = nullptr;
   int wkind = 0;
-  uint32_t nrows = 0;
+  uint32_t nrows = 0;  // all rows
+  uint32_t nlong = 0;  // rows folded one warp each
   bool ok = false;
 };
 
@@ -104,6 +113,15 @@ cudaError_t launch_ordered_weights(const uint32_t* row_ptr, const void* w, int e
                                    uint64_t nrows, const uint64_t* toff, void* ow, cudaStream_t stream);
 // y[r] = y[r] + fold_r over the ordered copy (same fold as below).
 cudaError_t launch_ordered_spmv(const OrderedOp& op, const float* x, float* y, cudaStream_t stream);
+
+// The same fold with a dense x or a spike bitmask (staged in shared memory,
+// at most kOrderedBitsMaxBytes), then either y[r] = y[r] + fold_r (v null) or
+// the LIF step on row r's v, theta and spike byte (src/backend/mod.rs:
+// 2461-2472).  The spike bytes are the whole output: the caller packs them.
+constexpr uint64_t kOrderedBitsMaxBytes = 200 * 1024;
+cudaError_t launch_ordered_fold(const OrderedOp& op, const float* x, const uint32_t* xbits, uint32_t xbits_words,
+                                float* y, float* v, float* theta, uint8_t* spikes, float decay, float v_reset,
+                                float dtheta, cudaStream_t stream);
 
 // y[r] = y[r] + fold_r, fold_r the strict left fold from 0.0 of w * x over
 // row r's entries in stored order (src/backend/mod.rs:2259-2267), for a
