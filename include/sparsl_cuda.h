@@ -202,7 +202,8 @@ enum {
   SPARSL_LAYOUT_T_X_PANELS = 32,    /* the same for the transpose product, from the sliced-ELL
                                        reverse index (x of nrows values in <= 4 panels) */
   SPARSL_LAYOUT_ORDERED_COPY = 64   /* skewed rows: a tile-interleaved copy in descending-length
-                                       order for dense-x SpMV */
+                                       order, used by every forward product whose operand is dense
+                                       or a spike vector of at most 200 KB */
 };
 int sparsl_op_layouts(sparsl_op *op);
 /* Test and diagnostic hook, no reference counterpart: forget the operator's

@@ -17,6 +17,10 @@
 // per lane, so one load brings a lane 8 columns, and a warp's load is 512
 // contiguous bytes.  Two batches of 8 positions are in flight while a third
 // folds, and a pass's first two batches load while the panel is copied in.
+//
+// The file also holds the ordered fold for skewed operators (rows of very
+// different lengths), which reads a copy in the same 16-byte-group layout
+// but has no panels: see ordered_fold_kernel.
 #include <algorithm>
 #include <atomic>
 
