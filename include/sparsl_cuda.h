@@ -438,6 +438,18 @@ void *sparsl_net_stream(sparsl_net *net);
 int sparsl_net_read_state(sparsl_net *net, uint32_t *x_spikes_global, uint64_t words, float *v_local,
                           float *theta_local, uint64_t local_rows);
 int sparsl_net_trace(sparsl_net *net, uint32_t *out, uint64_t cap, uint64_t *n_out);
+/* sparsl_net_write_state + sparsl_net_steps + sparsl_net_read_state in one
+ * call, over the same host buffers (read, then overwritten with the state
+ * after the last tick; the network counterpart of the resident
+ * write_lif_state / recurrent_steps / sync_lif_state sequence,
+ * mod.rs:1737, :1889-1932, :1960).  Each block's v and theta are copied in on
+ * their own stream and its first tick waits for them alone; each block's
+ * copy back starts when its last tick kernel ends, so with pinned host
+ * memory (sparsl_host_alloc) the copies of one block run under the kernels
+ * of the others.  Blocking, like sparsl_net_steps; the trace as after it. */
+int sparsl_net_steps_host(sparsl_net *net, uint32_t *x_spikes_global, uint64_t words, float *v_local,
+                          float *theta_local, uint64_t local_rows, float decay, float v_reset,
+                          float delta_theta, uint64_t steps);
 /* Bracket the fused tick kernels of each of the next (up to max_ticks) ticks
  * with CUDA events on the net's stream; 0 turns timing off. */
 int sparsl_net_set_timing(sparsl_net *net, uint64_t max_ticks);

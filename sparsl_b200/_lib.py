@@ -136,6 +136,7 @@ SIGNATURES = {
     "sparsl_net_wait": (i32, [vp]),
     "sparsl_net_stream": (vp, [vp]),
     "sparsl_net_read_state": (i32, [vp, vp, u64, vp, vp, u64]),
+    "sparsl_net_steps_host": (i32, [vp, vp, u64, vp, vp, u64, f32, f32, f32, u64]),
     "sparsl_net_trace": (i32, [vp, vp, u64, ctypes.POINTER(u64)]),
     "sparsl_net_set_timing": (i32, [vp, u64]),
     "sparsl_net_kernel_ms": (i32, [vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(u64)]),

@@ -2388,6 +2388,13 @@ struct sparsl_net {
   // offset, [parity][rank] peer words at this rank's slice, [rank] mailboxes.
   DBuf peer_out, peer_slice, peer_box;
   uint32_t tick = 0;  // ticks run so far (the same on every rank)
+  // sparsl_net_steps_host: copy streams and per-block events, made at its
+  // first call.  Block b's state arrives on copy_in (ev_in[b]); its first
+  // tick waits for that alone, and its copy back starts on copy_out when its
+  // last tick kernel ends (ev_out[b]), under the other blocks' kernels.
+  cudaStream_t copy_in = nullptr, copy_out = nullptr;
+  std::vector<cudaEvent_t> ev_in, ev_out;
+  cudaEvent_t ev_copied = nullptr;
 };
 
 namespace {
@@ -2589,6 +2596,14 @@ void sparsl_net_destroy(sparsl_net* net) {
   dfree(net->trace);
   net->err.release();
   if (net->side) cudaStreamSynchronize(net->side);
+  for (cudaStream_t c : {net->copy_in, net->copy_out})
+    if (c) {
+      cudaStreamSynchronize(c);
+      cudaStreamDestroy(c);
+    }
+  for (cudaEvent_t e : net->ev_in) cudaEventDestroy(e);
+  for (cudaEvent_t e : net->ev_out) cudaEventDestroy(e);
+  if (net->ev_copied) cudaEventDestroy(net->ev_copied);
   if (net->ev) cudaEventDestroy(net->ev);
   if (net->ev_fork) cudaEventDestroy(net->ev_fork);
   if (net->ev_join) cudaEventDestroy(net->ev_join);
@@ -2616,7 +2631,10 @@ int sparsl_net_write_state(sparsl_net* net, const uint32_t* xs, uint64_t words, 
   return wait_bounded(net->stream, net->ev, net->err.d, net->err.h, "net_write_state");
 }
 
-static int net_enqueue(sparsl_net* net, float decay, float v_reset, float dtheta, uint64_t steps) {
+// in_ev / out_ev (one per block, or null): block b's first tick kernel
+// waits for in_ev[b], and out_ev[b] is recorded when its last one ends.
+static int net_enqueue(sparsl_net* net, float decay, float v_reset, float dtheta, uint64_t steps,
+                       const cudaEvent_t* in_ev = nullptr, const cudaEvent_t* out_ev = nullptr) {
   if (!net->trace.p || net->trace_cap < steps) {
     const uint64_t cap = std::max<uint64_t>(steps, 1024);
     if (ensure(net->trace, cap * 4, true, net->stream) != cudaSuccess)
@@ -2654,7 +2672,10 @@ static int net_enqueue(sparsl_net* net, float decay, float v_reset, float dtheta
       } else {
         all_pushed = false;
       }
-      CK("net_steps", launch_fwd(op, p, (b & 1) ? net->side : net->stream));
+      cudaStream_t bs = (b & 1) ? net->side : net->stream;
+      if (in_ev && t == 0) CK("net_steps", cudaStreamWaitEvent(bs, in_ev[b], 0));
+      CK("net_steps", launch_fwd(op, p, bs));
+      if (out_ev && t + 1 == steps) CK("net_steps", cudaEventRecord(out_ev[b], bs));
     }
     if (fork) {
       CK("net_steps", cudaEventRecord(net->ev_join, net->side));
@@ -2741,6 +2762,76 @@ int sparsl_net_read_state(sparsl_net* net, uint32_t* xs, uint64_t words, float* 
   }
   CK("net_read_state", launch_canary_check(set, net->err.d, net->stream));
   return wait_bounded(net->stream, net->ev, net->err.d, net->err.h, "net_read_state");
+}
+
+int sparsl_net_steps_host(sparsl_net* net, uint32_t* xs, uint64_t words, float* v, float* theta, uint64_t local_rows,
+                          float decay, float v_reset, float dtheta, uint64_t steps) {
+  ADMIT();
+  TRY(check_min("x_spikes", words, net->words));
+  TRY(check_len("v", local_rows, net->local_rows));
+  if (steps == 0) return SPARSL_OK;
+  CK("net_steps_host", cudaSetDevice(net->dev->ordinal));
+  const size_t nb = net->blocks.size();
+  if (!net->copy_in) {
+    cudaStream_t ci = nullptr, co = nullptr;
+    CK("net_steps_host", cudaStreamCreateWithFlags(&ci, cudaStreamNonBlocking));
+    net->copy_in = ci;
+    CK("net_steps_host", cudaStreamCreateWithFlags(&co, cudaStreamNonBlocking));
+    net->copy_out = co;
+    CK("net_steps_host", cudaEventCreateWithFlags(&net->ev_copied, cudaEventDisableTiming));
+    for (size_t b = 0; b < nb; ++b) {
+      cudaEvent_t a = nullptr, c = nullptr;
+      CK("net_steps_host", cudaEventCreateWithFlags(&a, cudaEventDisableTiming));
+      net->ev_in.push_back(a);
+      CK("net_steps_host", cudaEventCreateWithFlags(&c, cudaEventDisableTiming));
+      net->ev_out.push_back(c);
+    }
+  }
+  // Work already on the net's stream (an earlier sparsl_net_steps_async)
+  // ends before copy_in overwrites any state.
+  CK("net_steps_host", cudaEventRecord(net->ev_copied, net->stream));
+  CK("net_steps_host", cudaStreamWaitEvent(net->copy_in, net->ev_copied, 0));
+  // The spike vector first, on the net's stream (every block's first tick
+  // reads all of it), then each block's v and theta on copy_in.
+  CK("net_steps_host", cudaMemcpyAsync(net->xs[net->cur].p, xs, net->words * 4, cudaMemcpyHostToDevice, net->stream));
+  for (size_t b = 0; b < nb; ++b) {
+    sparsl_op* op = net->blocks[b];
+    const uint64_t o = net->block_off[b];
+    if (op->nrows) {
+      CK("net_steps_host", cudaMemcpyAsync(op->rv.p, v + o, (uint64_t)op->nrows * 4, cudaMemcpyHostToDevice, net->copy_in));
+      CK("net_steps_host",
+         cudaMemcpyAsync(op->rth.p, theta + o, (uint64_t)op->nrows * 4, cudaMemcpyHostToDevice, net->copy_in));
+    }
+    CK("net_steps_host", cudaEventRecord(net->ev_in[b], net->copy_in));
+  }
+  TRY(net_enqueue(net, decay, v_reset, dtheta, steps, net->ev_in.data(), net->ev_out.data()));
+  CanarySet set;
+  set.ptr[set.count++] = net->xs[0].canary();
+  set.ptr[set.count++] = net->xs[1].canary();
+  for (size_t b = 0; b < nb; ++b) {
+    sparsl_op* op = net->blocks[b];
+    const uint64_t o = net->block_off[b];
+    if (!op->nrows) continue;
+    CK("net_steps_host", cudaStreamWaitEvent(net->copy_out, net->ev_out[b], 0));
+    CK("net_steps_host", cudaMemcpyAsync(v + o, op->rv.p, (uint64_t)op->nrows * 4, cudaMemcpyDeviceToHost, net->copy_out));
+    CK("net_steps_host",
+       cudaMemcpyAsync(theta + o, op->rth.p, (uint64_t)op->nrows * 4, cudaMemcpyDeviceToHost, net->copy_out));
+    if (set.count + 2 <= CanarySet::kMax) {
+      set.ptr[set.count++] = op->rv.canary();
+      set.ptr[set.count++] = op->rth.canary();
+    }
+  }
+  // The spike vector after the last tick (and its exchange), then join.
+  CK("net_steps_host", cudaMemcpyAsync(xs, net->xs[net->cur].p, net->words * 4, cudaMemcpyDeviceToHost, net->stream));
+  CK("net_steps_host", cudaEventRecord(net->ev_copied, net->copy_out));
+  CK("net_steps_host", cudaStreamWaitEvent(net->stream, net->ev_copied, 0));
+  CK("net_steps_host", launch_canary_check(set, net->err.d, net->stream));
+  int rc = wait_bounded(net->stream, net->ev, net->err.d, net->err.h, "net_steps_host");
+  if (rc != SPARSL_OK && net->comm && g_quarantine.load()) {
+    g_nccl.CommAbort(net->comm);
+    net->comm = nullptr;
+  }
+  return rc;
 }
 
 int sparsl_net_set_timing(sparsl_net* net, uint64_t max_ticks) {

@@ -36,11 +36,13 @@ def _skewed_csr(O, n, seed):
     return O.Csr(rp.astype(np.uint32), col, n)
 
 
-@pytest.mark.parametrize("n,deg,splits", [(4096, 64, [2048, 2048]), (6016, 200, [1024, 32, 4960]),
-                                          (8192, 0, [4096, 4096])])
-def test_net_ticks_match_oracle_recurrent_steps(O, cuda_device, n, deg, splits):
+NETS = [(4096, 64, [2048, 2048]), (6016, 200, [1024, 32, 4960]), (8192, 0, [4096, 4096])]
+
+
+def _net_case(O, dev, n, deg, splits):
+    """A network of row blocks and its initial state (deg 0: power-law rows,
+    whose blocks fold in descending-length order)."""
     rng = O.Rng(0xE7 + n)
-    # deg 0: power-law rows, whose blocks fold in descending-length order
     csr = O.random_csr(n, n, deg, rng) if deg else _skewed_csr(O, n, n)
     w = O.random_vec(csr.nnz, 0.5, rng)
     v0 = O.random_vec(n, 1.0, rng)
@@ -51,8 +53,14 @@ def test_net_ticks_match_oracle_recurrent_steps(O, cuda_device, n, deg, splits):
         rp = (csr.row_ptr[r:r + k + 1] - csr.row_ptr[r]).astype(np.uint32)
         col = csr.col[csr.row_ptr[r]:csr.row_ptr[r + k]]
         ww = w[csr.row_ptr[r]:csr.row_ptr[r + k]]
-        ops.append(cuda_device.prepare(S.Csr(rp, col, n), n, ww))
+        ops.append(dev.prepare(S.Csr(rp, col, n), n, ww))
         r += k
+    return csr, w, v0, t0, xs0, ops
+
+
+@pytest.mark.parametrize("n,deg,splits", NETS)
+def test_net_ticks_match_oracle_recurrent_steps(O, cuda_device, n, deg, splits):
+    csr, w, v0, t0, xs0, ops = _net_case(O, cuda_device, n, deg, splits)
     L = _lib.load()
     net = _make_net(cuda_device, ops, 0, n)
     try:
@@ -72,6 +80,64 @@ def test_net_ticks_match_oracle_recurrent_steps(O, cuda_device, n, deg, splits):
         assert_bits_equal(t, tw)
     finally:
         L.sparsl_net_destroy(net)
+
+
+class _Host:
+    """Host arrays for the state: pinned (sparsl_host_alloc) or pageable."""
+
+    def __init__(self, L, pinned, like):
+        self.L, self.ptr = L, None
+        if pinned:
+            self.ptr = L.sparsl_host_alloc(max(like.nbytes, 16))
+            buf = (ctypes.c_char * like.nbytes).from_address(self.ptr)
+            self.a = np.frombuffer(buf, dtype=like.dtype, count=like.size)
+        else:
+            self.a = np.empty_like(like)
+        self.a[:] = like
+
+    def free(self):
+        if self.ptr:
+            self.L.sparsl_host_free(self.ptr)
+
+
+@pytest.mark.parametrize("n,deg,splits", NETS)
+@pytest.mark.parametrize("pinned", [True, False])
+def test_net_steps_host_matches_oracle_recurrent_steps(O, cuda_device, n, deg, splits, pinned):
+    """State in from host buffers, ticks, state back into the same buffers,
+    each block's copies on their own streams: one-tick and four-tick calls
+    against the oracle's ticks, the trace of each call, and a call made while
+    ticks of sparsl_net_steps_async are still in flight (its copies must wait
+    for them)."""
+    csr, w, v0, t0, xs0, ops = _net_case(O, cuda_device, n, deg, splits)
+    L = _lib.load()
+    net = _make_net(cuda_device, ops, 0, n)
+    hx, hv, ht = _Host(L, pinned, xs0), _Host(L, pinned, v0), _Host(L, pinned, t0)
+    xw, vw, tw, sw = xs0.copy(), v0.copy(), t0.copy(), np.zeros(n, np.uint8)
+    try:
+        for k in (1, 1, 1, 4):
+            _check(L.sparsl_net_steps_host(net, hx.a.ctypes.data, hx.a.size, hv.a.ctypes.data, ht.a.ctypes.data, n,
+                                           0.95, 0.0, 0.0, k))
+            want = O.recurrent_steps(csr, w, xw, vw, tw, sw, 0.95, 0.0, 0.0, k)
+            trace = np.zeros(k, np.uint32)
+            cnt = ctypes.c_uint64()
+            _check(L.sparsl_net_trace(net, trace.ctypes.data, k, ctypes.byref(cnt)))
+            assert cnt.value == k and np.array_equal(trace, want)
+            assert np.array_equal(hx.a, xw)
+            assert_bits_equal(hv.a, vw)
+            assert_bits_equal(ht.a, tw)
+        # Two ticks from the device state, not waited for; then one tick from
+        # the host state, which must replace the device state only after them.
+        _check(L.sparsl_net_steps_async(net, 0.95, 0.0, 0.0, 2))
+        _check(L.sparsl_net_steps_host(net, hx.a.ctypes.data, hx.a.size, hv.a.ctypes.data, ht.a.ctypes.data, n,
+                                       0.95, 0.0, 0.0, 1))
+        O.recurrent_steps(csr, w, xw, vw, tw, sw, 0.95, 0.0, 0.0, 1)
+        assert np.array_equal(hx.a, xw)
+        assert_bits_equal(hv.a, vw)
+        assert_bits_equal(ht.a, tw)
+    finally:
+        L.sparsl_net_destroy(net)
+        for h in (hx, hv, ht):
+            h.free()
 
 
 def test_workload_generator_matches_its_definition(O, cuda_device):
