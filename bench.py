@@ -1317,7 +1317,7 @@ def bench_lif(args, dev, want_cpu):
                   "e2e tick")
             hs.a[:] = S.pack_spikes(ho.a)  # the host-side pack_spikes_into of the reference API
 
-    e2e_ms = events_ms(st, torch.cuda.current_device(), e2e)
+    e2e_ms = statistics.median(events_ms(st, torch.cuda.current_device(), e2e) for _ in range(3))
     for h in (hs, hv, ht, ho):
         h.free()
     cpu = None

@@ -240,7 +240,11 @@ int sparsl_op_spmv_t(sparsl_op *op, const float *x, uint64_t x_len, float *y, ui
  * copy streams, each range folded as soon as its rows are in. */
 int sparsl_op_spmm(sparsl_op *op, const float *x, uint64_t x_len, uint64_t n_vec, float *y,
                    uint64_t y_len);
-/* SparseOp::fused_spmv_lif (mod.rs:1609-1636). */
+/* SparseOp::fused_spmv_lif (mod.rs:1609-1636).  This and the spike variant
+ * below: when v, theta and the spike bytes are all pinned host memory the
+ * device can address (sparsl_host_alloc), the tick reads and writes them in
+ * place over PCIe and only the operand is copied; otherwise they are staged
+ * through device copies. */
 int sparsl_op_fused_lif(sparsl_op *op, const float *x, uint64_t x_len, float *v, float *theta,
                         uint8_t *spikes, uint64_t n, float decay, float v_reset, float delta_theta);
 /* SparseOp::fused_spmv_spikes_lif (mod.rs:1644-1678). */
@@ -442,11 +446,14 @@ int sparsl_net_trace(sparsl_net *net, uint32_t *out, uint64_t cap, uint64_t *n_o
  * call, over the same host buffers (read, then overwritten with the state
  * after the last tick; the network counterpart of the resident
  * write_lif_state / recurrent_steps / sync_lif_state sequence,
- * mod.rs:1737, :1889-1932, :1960).  Each block's v and theta are copied in on
- * their own stream and its first tick waits for them alone; each block's
- * copy back starts when its last tick kernel ends, so with pinned host
- * memory (sparsl_host_alloc) the copies of one block run under the kernels
- * of the others.  Blocking, like sparsl_net_steps; the trace as after it. */
+ * mod.rs:1737, :1889-1932, :1960).  When v_local and theta_local are pinned
+ * host memory the device can address (sparsl_host_alloc), the first tick's
+ * kernels read them over PCIe and the last tick's kernels write the new
+ * state back into them (as well as into the device copy), so only the spike
+ * vector is copied.  Otherwise each block's v and theta are copied in on
+ * their own stream, its first tick waits for them alone, and its copy back
+ * starts when its last tick kernel ends.  Blocking, like sparsl_net_steps;
+ * the trace as after it. */
 int sparsl_net_steps_host(sparsl_net *net, uint32_t *x_spikes_global, uint64_t words, float *v_local,
                           float *theta_local, uint64_t local_rows, float decay, float v_reset,
                           float delta_theta, uint64_t steps);

@@ -471,7 +471,8 @@ cudaError_t launch_fwd(sparsl_op* op, const RowLaunch& p, cudaStream_t s) {
       const bool lif = p.epilogue == EPI_LIF;
       e = launch_ordered_fold(op->ordered, bits ? nullptr : p.x, bits ? p.xbits : nullptr, bits ? p.xbits_words : 0,
                               lif ? nullptr : p.y, lif ? p.v : nullptr, lif ? p.theta : nullptr,
-                              lif ? p.spikes : nullptr, p.decay, p.v_reset, p.dtheta, s);
+                              lif ? p.spikes : nullptr, p.decay, p.v_reset, p.dtheta, s,
+                              LifHostState{p.v_src, p.theta_src, p.v_mirror, p.theta_mirror});
     } else {
       RowLaunch q = p;
       q.order = op->row_order.as<uint32_t>();
@@ -1849,14 +1850,34 @@ int sparsl_op_spmm(sparsl_op* op, const float* x, uint64_t x_len, uint64_t n_vec
   return finish(op, "spmm");
 }
 
+// True when ptr is pinned host memory that the current device can address;
+// *dptr is then that address.  Such memory can be read and written by
+// kernels directly, over PCIe.
+static bool host_mapped(const void* ptr, void** dptr) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+    cudaGetLastError();  // an unknown pointer is not an error here
+    return false;
+  }
+  *dptr = a.devicePointer;
+  return a.type == cudaMemoryTypeHost && a.devicePointer != nullptr;
+}
+
 static int fused_common(sparsl_op* op, const float* x, const uint32_t* bits, float* v, float* theta, uint8_t* spk,
                         float decay, float v_reset, float dtheta, const char* name) {
   std::lock_guard<std::mutex> lk(op->mu);
   CK(name, cudaSetDevice(op->dev->ordinal));
   const uint64_t nr = op->nrows;
-  ALLOC(op->sv, nr * 4 + 16, true, "v staging");
-  ALLOC(op->sth, nr * 4 + 16, true, "theta staging");
-  ALLOC(op->sspk, nr + 16, true, "spike staging");
+  // v, theta and the spike bytes in pinned host memory: the tick's epilogue
+  // reads and writes them in place (a tile's state is loaded when its
+  // stream starts), so only the operand is copied.
+  void *dv = nullptr, *dth = nullptr, *dspk = nullptr;
+  const bool mapped = host_mapped(v, &dv) && host_mapped(theta, &dth) && host_mapped(spk, &dspk);
+  if (!mapped) {
+    ALLOC(op->sv, nr * 4 + 16, true, "v staging");
+    ALLOC(op->sth, nr * 4 + 16, true, "theta staging");
+    ALLOC(op->sspk, nr + 16, true, "spike staging");
+  }
   RowLaunch p = fwd_launch(op);
   if (x && op->ext_x) {
     p.x = op->ext_x;  // a bound x replaces the slice (metal.rs:2686-2688)
@@ -1869,15 +1890,22 @@ static int fused_common(sparsl_op* op, const float* x, const uint32_t* bits, flo
     if (op->words()) CK(name, cudaMemcpyAsync(op->sbits.p, bits, op->words() * 4, cudaMemcpyHostToDevice, op->stream));
     set_bits_mode(p, op->sbits.as<uint32_t>(), op->words());
   }
-  CK(name, cudaMemcpyAsync(op->sv.p, v, nr * 4, cudaMemcpyHostToDevice, op->stream));
-  CK(name, cudaMemcpyAsync(op->sth.p, theta, nr * 4, cudaMemcpyHostToDevice, op->stream));
   p.epilogue = EPI_LIF;
-  p.v = op->sv.as<float>();
-  p.theta = op->sth.as<float>();
-  p.spikes = op->sspk.as<uint8_t>();
   p.decay = decay;
   p.v_reset = v_reset;
   p.dtheta = dtheta;
+  if (mapped) {
+    p.v = static_cast<float*>(dv);
+    p.theta = static_cast<float*>(dth);
+    p.spikes = static_cast<uint8_t*>(dspk);
+    CK(name, launch_fwd(op, p, op->stream));
+    return finish(op, name);
+  }
+  CK(name, cudaMemcpyAsync(op->sv.p, v, nr * 4, cudaMemcpyHostToDevice, op->stream));
+  CK(name, cudaMemcpyAsync(op->sth.p, theta, nr * 4, cudaMemcpyHostToDevice, op->stream));
+  p.v = op->sv.as<float>();
+  p.theta = op->sth.as<float>();
+  p.spikes = op->sspk.as<uint8_t>();
   CK(name, launch_fwd(op, p, op->stream));
   CK(name, cudaMemcpyAsync(v, op->sv.p, nr * 4, cudaMemcpyDeviceToHost, op->stream));
   CK(name, cudaMemcpyAsync(theta, op->sth.p, nr * 4, cudaMemcpyDeviceToHost, op->stream));
@@ -2633,8 +2661,12 @@ int sparsl_net_write_state(sparsl_net* net, const uint32_t* xs, uint64_t words, 
 
 // in_ev / out_ev (one per block, or null): block b's first tick kernel
 // waits for in_ev[b], and out_ev[b] is recorded when its last one ends.
+// hv / hth (device-usable pointers to pinned host arrays of local_rows
+// floats, or null): the first tick reads v / theta from them and the last
+// tick writes the new state to them as well as to the device.
 static int net_enqueue(sparsl_net* net, float decay, float v_reset, float dtheta, uint64_t steps,
-                       const cudaEvent_t* in_ev = nullptr, const cudaEvent_t* out_ev = nullptr) {
+                       const cudaEvent_t* in_ev = nullptr, const cudaEvent_t* out_ev = nullptr, float* hv = nullptr,
+                       float* hth = nullptr) {
   if (!net->trace.p || net->trace_cap < steps) {
     const uint64_t cap = std::max<uint64_t>(steps, 1024);
     if (ensure(net->trace, cap * 4, true, net->stream) != cudaSuccess)
@@ -2664,6 +2696,14 @@ static int net_enqueue(sparsl_net* net, float decay, float v_reset, float dtheta
       lif_resident_launch(op, p, decay, v_reset, dtheta);
       p.out_bits = dst + (net->row_offset + net->block_off[b]) / 32;
       p.err = net->err.d;
+      if (hv && t == 0) {
+        p.v_src = hv + net->block_off[b];
+        p.theta_src = hth + net->block_off[b];
+      }
+      if (hv && t + 1 == steps) {
+        p.v_mirror = hv + net->block_off[b];
+        p.theta_mirror = hth + net->block_off[b];
+      }
       // The TMA tick stores its words into the peers' copies itself.
       if (peer && op->ell.ok) {
         p.peer_out = net->peer_out.as<uint32_t*>() + (q * nb + b) * net->nranks;
@@ -2772,6 +2812,32 @@ int sparsl_net_steps_host(sparsl_net* net, uint32_t* xs, uint64_t words, float* 
   if (steps == 0) return SPARSL_OK;
   CK("net_steps_host", cudaSetDevice(net->dev->ordinal));
   const size_t nb = net->blocks.size();
+  // Pinned host arrays that this device can address: the first tick reads
+  // the state from them and the last one writes it back, over PCIe, from
+  // inside the tick kernels (a tile's state is loaded when its stream
+  // starts).  Only the spike vector is copied.
+  void *dv = nullptr, *dth = nullptr;
+  if (host_mapped(v, &dv) && host_mapped(theta, &dth)) {
+    CK("net_steps_host", cudaMemcpyAsync(net->xs[net->cur].p, xs, net->words * 4, cudaMemcpyHostToDevice, net->stream));
+    TRY(net_enqueue(net, decay, v_reset, dtheta, steps, nullptr, nullptr, static_cast<float*>(dv),
+                    static_cast<float*>(dth)));
+    CK("net_steps_host", cudaMemcpyAsync(xs, net->xs[net->cur].p, net->words * 4, cudaMemcpyDeviceToHost, net->stream));
+    CanarySet set;
+    set.ptr[set.count++] = net->xs[0].canary();
+    set.ptr[set.count++] = net->xs[1].canary();
+    for (size_t b = 0; b < nb && set.count + 2 <= CanarySet::kMax; ++b) {
+      if (!net->blocks[b]->nrows) continue;
+      set.ptr[set.count++] = net->blocks[b]->rv.canary();
+      set.ptr[set.count++] = net->blocks[b]->rth.canary();
+    }
+    CK("net_steps_host", launch_canary_check(set, net->err.d, net->stream));
+    int rc = wait_bounded(net->stream, net->ev, net->err.d, net->err.h, "net_steps_host");
+    if (rc != SPARSL_OK && net->comm && g_quarantine.load()) {
+      g_nccl.CommAbort(net->comm);
+      net->comm = nullptr;
+    }
+    return rc;
+  }
   if (!net->copy_in) {
     cudaStream_t ci = nullptr, co = nullptr;
     CK("net_steps_host", cudaStreamCreateWithFlags(&ci, cudaStreamNonBlocking));

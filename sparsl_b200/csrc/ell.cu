@@ -305,6 +305,17 @@ __global__ void __launch_bounds__(NW * 32, 1)
   while (ok && fifo_r != fifo_w) {
     const uint32_t tile = s_fifo[wid][fifo_r++ % kFifo];
     float sum = 0.0f;
+    // The tile's LIF state is loaded now and used after its last chunk, so
+    // the load's latency (a PCIe round trip when the state is in host
+    // memory) hides under the tile's stream.
+    float v_in = 0.f, th_in = 0.f;
+    if constexpr (EPI != EPI_ACCUM) {
+      const uint32_t l = tile * 32 + lane;
+      if (l < p.nlines) {
+        v_in = (p.v_src ? p.v_src : p.v)[l];
+        th_in = (p.theta_src ? p.theta_src : p.theta)[l];
+      }
+    }
     for (uint32_t c = 0; c < nch; ++c) {
       if (!mbar_wait(&bars[wid][c_slot], c_phase)) {
         ok = false;
@@ -401,8 +412,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
     } else {
       bool spike = false;
       if (valid) {
-        float vv = p.v[line];
-        float th = p.theta[line];
+        float vv = v_in;
+        float th = th_in;
         const float vol = fadd(fmul(vv, p.decay), sum);
         if (vol >= th) {
           spike = true;
@@ -414,6 +425,10 @@ __global__ void __launch_bounds__(NW * 32, 1)
         p.v[line] = vv;
         p.theta[line] = th;
         p.spikes[line] = spike ? 1 : 0;
+        if (p.v_mirror) {
+          p.v_mirror[line] = vv;
+          p.theta_mirror[line] = th;
+        }
       }
       const uint32_t ballot = __ballot_sync(0xffffffffu, spike);
       if (p.out_bits && lane == 0) {

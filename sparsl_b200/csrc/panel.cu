@@ -241,6 +241,7 @@ struct OrdLaunch {
   float* v;                // EPI_LIF state and spike bytes
   float* theta;
   uint8_t* spikes;
+  LifHostState hs;         // optional state in host memory
   float decay, v_reset, dtheta;
   uint32_t nrows;
 };
@@ -317,7 +318,7 @@ __global__ void __launch_bounds__(XM == X_DENSE ? kOrdWarps * 32 : kOrdBitsWarps
       p.y[r] = fadd(p.y[r], acc);
     } else {
       // lif_step: two roundings, then >= theta.
-      float vv = p.v[r], th = p.theta[r];
+      float vv = (p.hs.v_src ? p.hs.v_src : p.v)[r], th = (p.hs.theta_src ? p.hs.theta_src : p.theta)[r];
       const float vol = fadd(fmul(vv, p.decay), acc);
       uint8_t spike = 0;
       if (vol >= th) {
@@ -330,6 +331,10 @@ __global__ void __launch_bounds__(XM == X_DENSE ? kOrdWarps * 32 : kOrdBitsWarps
       p.v[r] = vv;
       p.theta[r] = th;
       p.spikes[r] = spike;
+      if (p.hs.v_mirror) {
+        p.hs.v_mirror[r] = vv;
+        p.hs.theta_mirror[r] = th;
+      }
     }
   };
   const uint32_t gwarp = blockIdx.x * nw + (threadIdx.x >> 5), nwarps = gridDim.x * nw;
@@ -697,7 +702,7 @@ cudaError_t launch_ordered_spmv(const OrderedOp& op, const float* x, float* y, c
 
 cudaError_t launch_ordered_fold(const OrderedOp& op, const float* x, const uint32_t* xbits, uint32_t xbits_words,
                                 float* y, float* v, float* theta, uint8_t* spikes, float decay, float v_reset,
-                                float dtheta, cudaStream_t stream) {
+                                float dtheta, cudaStream_t stream, const LifHostState& hs) {
   if (!op.ok || (xbits && (uint64_t)xbits_words * 4 > kOrderedBitsMaxBytes)) return cudaErrorInvalidValue;
   if (op.nrows == 0) return cudaSuccess;
   OrdLaunch p = ordered_launch(op);
@@ -708,6 +713,7 @@ cudaError_t launch_ordered_fold(const OrderedOp& op, const float* x, const uint3
   p.v = v;
   p.theta = theta;
   p.spikes = spikes;
+  p.hs = hs;
   p.decay = decay;
   p.v_reset = v_reset;
   p.dtheta = dtheta;

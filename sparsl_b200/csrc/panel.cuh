@@ -119,9 +119,18 @@ cudaError_t launch_ordered_spmv(const OrderedOp& op, const float* x, float* y, c
 // the LIF step on row r's v, theta and spike byte (src/backend/mod.rs:
 // 2461-2472).  The spike bytes are the whole output: the caller packs them.
 constexpr uint64_t kOrderedBitsMaxBytes = 200 * 1024;
+// Optional LIF state in pinned, mapped host memory: read from v_src /
+// theta_src instead of v / theta when set, and the new values written to
+// v_mirror / theta_mirror too when set.
+struct LifHostState {
+  const float* v_src = nullptr;
+  const float* theta_src = nullptr;
+  float* v_mirror = nullptr;
+  float* theta_mirror = nullptr;
+};
 cudaError_t launch_ordered_fold(const OrderedOp& op, const float* x, const uint32_t* xbits, uint32_t xbits_words,
                                 float* y, float* v, float* theta, uint8_t* spikes, float decay, float v_reset,
-                                float dtheta, cudaStream_t stream);
+                                float dtheta, cudaStream_t stream, const LifHostState& hs = LifHostState{});
 
 // y[r] = y[r] + fold_r, fold_r the strict left fold from 0.0 of w * x over
 // row r's entries in stored order (src/backend/mod.rs:2259-2267), for a

@@ -209,8 +209,8 @@ __global__ void __launch_bounds__(kRowWarps * 32) row_fold_kernel(const RowLaunc
     // lif_step (src/backend/mod.rs:2461-2472): two roundings, then >= theta.
     bool spike = false;
     if (valid) {
-      float vv = p.v[line];
-      float th = p.theta[line];
+      float vv = (p.v_src ? p.v_src : p.v)[line];
+      float th = (p.theta_src ? p.theta_src : p.theta)[line];
       const float vol = fadd(fmul(vv, p.decay), sum);
       if (vol >= th) {
         spike = true;
@@ -222,6 +222,10 @@ __global__ void __launch_bounds__(kRowWarps * 32) row_fold_kernel(const RowLaunc
       p.v[line] = vv;
       p.theta[line] = th;
       p.spikes[line] = spike ? 1 : 0;
+      if (p.v_mirror) {
+        p.v_mirror[line] = vv;
+        p.theta_mirror[line] = th;
+      }
     }
     // Lane i of the ballot is line 32w+i: exactly the LSB-first packing of
     // src/spikes.rs:237-262, with tail bits of a partial word left zero.

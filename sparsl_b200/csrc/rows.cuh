@@ -45,6 +45,14 @@ struct RowLaunch {
   float* v = nullptr;
   float* theta = nullptr;
   uint8_t* spikes = nullptr;
+  // Optional state in pinned, mapped host memory (a tick that takes its
+  // state from the host or returns it there): when set, v / theta are read
+  // from v_src / theta_src instead, and the new values are written to
+  // v_mirror / theta_mirror as well as to v / theta.
+  const float* v_src = nullptr;
+  const float* theta_src = nullptr;
+  float* v_mirror = nullptr;
+  float* theta_mirror = nullptr;
   uint32_t* out_bits = nullptr;    // optional packed spike words (word = line / 32)
   // Network ticks across GPUs (TMA path): each packed word is also stored
   // into every peer's copy of the spike vector (peer_out[r] is peer r's

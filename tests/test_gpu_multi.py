@@ -61,7 +61,7 @@ def _network(kind):
     return O, n, rp, col, w, v0, t0, O.pack_spikes(s0)
 
 
-def _rank(rank, kind, mode, steps, skip_rank, q_id, q_out, q_done):
+def _rank(rank, kind, mode, steps, skip_rank, q_id, q_out, q_done, via_host=False):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     sys.path.insert(0, ROOT)
     import torch
@@ -99,6 +99,33 @@ def _rank(rank, kind, mode, steps, skip_rank, q_id, q_out, q_done):
             assert L.sparsl_net_write_state(h, xs0.ctypes.data, xs0.size, vl.ctypes.data, tl.ctypes.data, local) == 0
             if rank == skip_rank:
                 res["skipped"] = True
+            elif via_host:
+                # The same ticks as calls of sparsl_net_steps_host, the state
+                # going through host buffers between calls: pinned buffers
+                # (read and written by the tick kernels over PCIe) or
+                # pageable ones (copied on the copy streams).
+                xs, trace, rc = xs0.copy(), [], 0
+                if via_host == "pinned":
+                    pins = [L.sparsl_host_alloc(local * 4) for _ in range(2)]
+                    hv, ht = (np.frombuffer((ctypes.c_char * (local * 4)).from_address(q), np.float32, local)
+                              for q in pins)
+                    hv[:], ht[:] = vl, tl
+                    vl, tl = hv, ht
+                for k in (1, 2, steps - 3):
+                    rc = L.sparsl_net_steps_host(h, xs.ctypes.data, xs.size, vl.ctypes.data, tl.ctypes.data, local,
+                                                 0.95, 0.0, 0.0, k)
+                    if rc:
+                        break
+                    tr = np.zeros(k, np.uint32)
+                    cnt = ctypes.c_uint64()
+                    assert L.sparsl_net_trace(h, tr.ctypes.data, k, ctypes.byref(cnt)) == 0
+                    trace += tr.tolist()
+                res["rc"] = rc
+                res["err"] = _lib.last_error() if rc else ""
+                res.update(trace=trace, v=vl.tobytes(), t=tl.tobytes(), xs=xs.tobytes())
+                if via_host == "pinned":
+                    for q in pins:
+                        L.sparsl_host_free(q)
             else:
                 if skip_rank is not None:
                     L.sparsl_set_timeout_ms(3000)
@@ -129,12 +156,12 @@ def _rank(rank, kind, mode, steps, skip_rank, q_id, q_out, q_done):
     q_out.put(res)
 
 
-def _run(kind, mode, steps=30, skip_rank=None):
+def _run(kind, mode, steps=30, skip_rank=None, via_host=False):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q_id, q_out, q_done = ctx.Queue(), ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, kind, mode, steps, skip_rank, q_id, q_out, q_done))
+    procs = [ctx.Process(target=_rank, args=(r, kind, mode, steps, skip_rank, q_id, q_out, q_done, via_host))
              for r in range(N_GPUS)]
     for p in procs:
         p.start()
@@ -150,8 +177,9 @@ def _run(kind, mode, steps=30, skip_rank=None):
 @needs_two
 @pytest.mark.parametrize("kind", ["uniform", "power_law"])
 @pytest.mark.parametrize("mode", [0, 1], ids=["peer", "nccl"])
-def test_two_gpu_ticks_match_the_oracle(O, kind, mode):
-    res = _run(kind, mode)
+@pytest.mark.parametrize("via_host", [None, "pinned", "pageable"], ids=["resident", "host_pinned", "host_pageable"])
+def test_two_gpu_ticks_match_the_oracle(O, kind, mode, via_host):
+    res = _run(kind, mode, via_host=via_host)
     O_, n, rp, col, w, v0, t0, xs0 = _network(kind)
     v, t, sp, xs = v0.copy(), t0.copy(), np.zeros(n, np.uint8), xs0.copy()
     want = O.recurrent_steps(O.Csr(rp, col, n), w, xs, v, t, sp, 0.95, 0.0, 0.0, 30, par=True)
