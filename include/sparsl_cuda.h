@@ -228,7 +228,10 @@ int sparsl_op_test_mark_canary(sparsl_op *op);
 int sparsl_op_has_transpose(sparsl_op *op);       /* mod.rs:1594 */
 /* SparseOp::set_weights (mod.rs:1392-1409). */
 int sparsl_op_set_weights(sparsl_op *op, const float *weights, uint64_t n);
-/* SparseOp::spmv (mod.rs:1411-1429): y += A x. */
+/* SparseOp::spmv (mod.rs:1411-1429): y += A x.  This and spmv_spikes: a y in
+ * pinned host memory the device can address (sparsl_host_alloc) is
+ * accumulated into in place over PCIe; otherwise it is staged through a
+ * device copy. */
 int sparsl_op_spmv(sparsl_op *op, const float *x, uint64_t x_len, float *y, uint64_t y_len);
 /* SparseOp::spmv_spikes (mod.rs:1449-1468). */
 int sparsl_op_spmv_spikes(sparsl_op *op, const uint32_t *spikes, uint64_t words, float *y,

@@ -1672,6 +1672,19 @@ int sparsl_op_set_weights(sparsl_op* op, const float* weights, uint64_t n) {
   return wait_op(op, "set_weights");
 }
 
+// True when ptr is pinned host memory that the current device can address;
+// *dptr is then that address.  Such memory can be read and written by
+// kernels directly, over PCIe.
+static bool host_mapped(const void* ptr, void** dptr) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+    cudaGetLastError();  // an unknown pointer is not an error here
+    return false;
+  }
+  *dptr = a.devicePointer;
+  return a.type == cudaMemoryTypeHost && a.devicePointer != nullptr;
+}
+
 int sparsl_op_spmv(sparsl_op* op, const float* x, uint64_t x_len, float* y, uint64_t y_len) {
   ADMIT();
   TRY(check_min("x", x_len, op->ncols));
@@ -1690,15 +1703,20 @@ int sparsl_op_spmv(sparsl_op* op, const float* x, uint64_t x_len, float* y, uint
       CK("spmv", cudaMemcpyAsync(op->sx.p, x, (uint64_t)op->ncols * 4, cudaMemcpyHostToDevice, op->stream));
     p.x = op->sx.as<float>();
   }
+  // A pinned y (and no bound y) is accumulated into in place, over PCIe.
+  void* dy = nullptr;
+  const bool mapped = !op->ext_y && host_mapped(y, &dy);
   if (op->ext_y) {
     p.y = op->ext_y;
+  } else if (mapped) {
+    p.y = static_cast<float*>(dy);
   } else {
     ALLOC(op->sy, (uint64_t)op->nrows * 4 + 16, true, "y staging");
     CK("spmv", cudaMemcpyAsync(op->sy.p, y, (uint64_t)op->nrows * 4, cudaMemcpyHostToDevice, op->stream));
     p.y = op->sy.as<float>();
   }
   CK("spmv", launch_fwd(op, p, op->stream));
-  CK("spmv", cudaMemcpyAsync(y, p.y, (uint64_t)op->nrows * 4, cudaMemcpyDeviceToHost, op->stream));
+  if (!mapped) CK("spmv", cudaMemcpyAsync(y, p.y, (uint64_t)op->nrows * 4, cudaMemcpyDeviceToHost, op->stream));
   return finish(op, "spmv");
 }
 
@@ -1710,15 +1728,23 @@ int sparsl_op_spmv_spikes(sparsl_op* op, const uint32_t* spikes, uint64_t words,
   std::lock_guard<std::mutex> lk(op->mu);
   CK("spmv_spikes", cudaSetDevice(op->dev->ordinal));
   ALLOC(op->sbits, op->words() * 4 + 16, false, "spike staging");
-  ALLOC(op->sy, (uint64_t)op->nrows * 4 + 16, true, "y staging");
   if (op->words())
     CK("spmv_spikes", cudaMemcpyAsync(op->sbits.p, spikes, op->words() * 4, cudaMemcpyHostToDevice, op->stream));
-  CK("spmv_spikes", cudaMemcpyAsync(op->sy.p, y, (uint64_t)op->nrows * 4, cudaMemcpyHostToDevice, op->stream));
   RowLaunch p = fwd_launch(op);
   set_bits_mode(p, op->sbits.as<uint32_t>(), op->words());
-  p.y = op->sy.as<float>();
+  // A pinned y is accumulated into in place, over PCIe.
+  void* dy = nullptr;
+  const bool mapped = host_mapped(y, &dy);
+  if (mapped) {
+    p.y = static_cast<float*>(dy);
+  } else {
+    ALLOC(op->sy, (uint64_t)op->nrows * 4 + 16, true, "y staging");
+    CK("spmv_spikes", cudaMemcpyAsync(op->sy.p, y, (uint64_t)op->nrows * 4, cudaMemcpyHostToDevice, op->stream));
+    p.y = op->sy.as<float>();
+  }
   CK("spmv_spikes", launch_fwd(op, p, op->stream));
-  CK("spmv_spikes", cudaMemcpyAsync(y, op->sy.p, (uint64_t)op->nrows * 4, cudaMemcpyDeviceToHost, op->stream));
+  if (!mapped)
+    CK("spmv_spikes", cudaMemcpyAsync(y, op->sy.p, (uint64_t)op->nrows * 4, cudaMemcpyDeviceToHost, op->stream));
   return finish(op, "spmv_spikes");
 }
 
@@ -1848,19 +1874,6 @@ int sparsl_op_spmm(sparsl_op* op, const float* x, uint64_t x_len, uint64_t n_vec
   CK("spmm", cudaEventRecord(op->down_ev, op->down));
   CK("spmm", cudaStreamWaitEvent(op->stream, op->down_ev, 0));
   return finish(op, "spmm");
-}
-
-// True when ptr is pinned host memory that the current device can address;
-// *dptr is then that address.  Such memory can be read and written by
-// kernels directly, over PCIe.
-static bool host_mapped(const void* ptr, void** dptr) {
-  cudaPointerAttributes a{};
-  if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
-    cudaGetLastError();  // an unknown pointer is not an error here
-    return false;
-  }
-  *dptr = a.devicePointer;
-  return a.type == cudaMemoryTypeHost && a.devicePointer != nullptr;
 }
 
 static int fused_common(sparsl_op* op, const float* x, const uint32_t* bits, float* v, float* theta, uint8_t* spk,

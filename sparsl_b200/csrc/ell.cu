@@ -305,15 +305,19 @@ __global__ void __launch_bounds__(NW * 32, 1)
   while (ok && fifo_r != fifo_w) {
     const uint32_t tile = s_fifo[wid][fifo_r++ % kFifo];
     float sum = 0.0f;
-    // The tile's LIF state is loaded now and used after its last chunk, so
-    // the load's latency (a PCIe round trip when the state is in host
+    // The tile's y (or LIF state) is loaded now and used after its last
+    // chunk, so the load's latency (a PCIe round trip when it is in host
     // memory) hides under the tile's stream.
     float v_in = 0.f, th_in = 0.f;
-    if constexpr (EPI != EPI_ACCUM) {
+    {
       const uint32_t l = tile * 32 + lane;
       if (l < p.nlines) {
-        v_in = (p.v_src ? p.v_src : p.v)[l];
-        th_in = (p.theta_src ? p.theta_src : p.theta)[l];
+        if constexpr (EPI == EPI_ACCUM) {
+          v_in = p.y[l];
+        } else {
+          v_in = (p.v_src ? p.v_src : p.v)[l];
+          th_in = (p.theta_src ? p.theta_src : p.theta)[l];
+        }
       }
     }
     for (uint32_t c = 0; c < nch; ++c) {
@@ -408,7 +412,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
     const uint32_t line = row0 + lane;
     const bool valid = line < p.nlines;
     if constexpr (EPI == EPI_ACCUM) {
-      if (valid) p.y[line] = fadd(p.y[line], sum);
+      if (valid) p.y[line] = fadd(v_in, sum);
     } else {
       bool spike = false;
       if (valid) {

@@ -97,6 +97,9 @@ __global__ void __launch_bounds__(kPanelMaxWarps * 32, 1) panel_spmv_kernel(cons
     const bool valid = has && row < p.nrows;
     const uint64_t gbase = !has ? 0 : p.toff ? __ldg(p.toff + tile) : (uint64_t)tile * p.Lg;
     float acc = 0.f;
+    // y is loaded now and used after the last panel, so the load's latency
+    // (a PCIe round trip when y is in host memory) hides under the folds.
+    const float y_in = valid ? p.y[row] : 0.f;
     for (uint32_t pn = 0; pn < p.npanels; ++pn) {
       const uint32_t pbase = pn * p.width;
       const uint32_t pw = min(p.width, p.ncols - pbase);  // floats in this panel
@@ -152,7 +155,7 @@ __global__ void __launch_bounds__(kPanelMaxWarps * 32, 1) panel_spmv_kernel(cons
       while (step(cur, b2) && step(b1, cur) && step(b2, b1)) {
       }
     }
-    if (valid) p.y[row] = fadd(p.y[row], acc);
+    if (valid) p.y[row] = fadd(y_in, acc);
   }
 }
 

@@ -1,4 +1,4 @@
-"""The fused SpMV + LIF calls with their state in pinned host memory.
+"""The slice calls with their outputs and state in pinned host memory.
 
 When v, theta and the spike bytes are pinned host memory that the GPU can
 address (sparsl_host_alloc), the tick's epilogue reads and writes them in
@@ -6,7 +6,8 @@ place over PCIe instead of staging them through device copies.  Checked bit
 for bit against the oracle on the three engines a tick can take (the TMA
 stream for uniform rows, the ordered fold for skewed rows, the plain row
 fold), with a dense and a spike operand, a ragged last tile, and a mix of
-pinned and pageable buffers (which takes the copying route)."""
+pinned and pageable buffers (which takes the copying route).  Likewise y of
+the forward SpMV and spike SpMV, accumulated in place by every engine."""
 import ctypes
 
 import numpy as np
@@ -45,13 +46,30 @@ def _skewed(O, nrows, ncols, seed):
     return O.Csr(rp.astype(np.uint32), col, ncols)
 
 
-def _operator(O, dev, kind, nrows, ncols, seed):
+PANELS, ELL, ORDERED = 16, 1, 64  # SPARSL_LAYOUT_X_PANELS, _ELL, _ORDERED_COPY
+
+
+def _uniform(O, nrows, ncols, L, seed):
+    """Rows of exactly L sorted random columns (the TMA stream's and the
+    panels' operators)."""
+    r = np.random.default_rng(seed)
+    col = np.sort(r.integers(0, ncols, size=(nrows, L), dtype=np.uint32), axis=1).reshape(-1)
+    rp = (np.arange(nrows + 1, dtype=np.uint64) * L).astype(np.uint32)
+    return O.Csr(rp, col, ncols)
+
+
+def _operator(O, dev, kind, nrows, ncols, seed, L=48):
+    """kind: "uniform" (equal rows), "skewed" (Zipf lengths: the ordered
+    fold) or "plain" (equal rows forced onto the plain row fold)."""
     rng = O.Rng(seed)
-    csr = _skewed(O, nrows, ncols, seed) if kind == "skewed" else O.random_csr(nrows, ncols, 48, rng)
+    csr = _skewed(O, nrows, ncols, seed) if kind == "skewed" else _uniform(O, nrows, ncols, L, seed)
     w = O.random_vec(csr.nnz, 0.5, rng)
     op = dev.prepare(S.Csr(csr.row_ptr, csr.col, ncols), ncols, w)
     if kind == "plain":
         op.force_plain_row_fold()
+    lay = op.layouts()
+    assert bool(lay & ELL) == (kind == "uniform")
+    assert bool(lay & ORDERED) == (kind == "skewed")
     return csr, w, op
 
 
@@ -107,3 +125,33 @@ def test_pinned_and_pageable_mixed(O, cuda_device):
     finally:
         hv.free()
         ht.free()
+
+
+@pytest.mark.parametrize("kind,nrows,ncols,L", [
+    ("uniform", 3000, 3000, 48),    # x in shared-memory panels; spikes on the TMA stream
+    ("uniform", 1031, 230_000, 16), # x past the panels: the TMA stream for both
+    ("skewed", 4096, 3000, 0),      # the ordered fold
+    ("plain", 1031, 3000, 48),      # the plain row fold
+])
+def test_pinned_y_spmv_matches_oracle(O, cuda_device, kind, nrows, ncols, L):
+    """y += A x and y += A s into a pinned y, accumulated in place over PCIe
+    by every engine a forward product can take."""
+    csr, w, op = _operator(O, cuda_device, kind, nrows, ncols, 0x99 + nrows, L)
+    assert bool(op.layouts() & PANELS) == (kind == "uniform" and ncols == 3000)
+    r = np.random.default_rng(nrows)
+    y0 = r.uniform(-1, 1, nrows).astype(np.float32)
+    y0[::7] = -0.0
+    x = r.uniform(-1, 1, ncols).astype(np.float32)
+    packed = O.pack_spikes((r.random(ncols) < 0.3).astype(np.uint8))
+    hy = _Pinned(y0)
+    try:
+        want = y0.copy()
+        for _ in range(2):
+            op.spmv(x, hy.a)
+            O.spmv(csr, w, x, want)
+            assert_bits_equal(hy.a, want, f"{kind} spmv")
+        op.spmv_spikes(packed, hy.a)
+        O.spmv_spikes(csr, w, packed, want)
+        assert_bits_equal(hy.a, want, f"{kind} spmv_spikes")
+    finally:
+        hy.free()
