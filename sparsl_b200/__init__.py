@@ -14,6 +14,7 @@ from .backend import (  # noqa: F401
     CsrError,
     DeviceBuffer,
     Device,
+    HostBuffer,
     LifParams,
     LifParamsError,
     OpError,

@@ -640,6 +640,50 @@ class DeviceBuffer:
             pass
 
 
+class _PinnedBlock:
+    """Owns one sparsl_host_alloc block; freed when the last reference goes."""
+
+    def __init__(self, ptr: int):
+        self.ptr = ptr
+
+    def release(self) -> None:
+        if self.ptr:
+            _lib.load().sparsl_host_free(self.ptr)
+            self.ptr = 0
+
+    def __del__(self):
+        try:
+            self.release()
+        except Exception:
+            pass
+
+
+class HostBuffer:
+    """Page-locked host memory that the GPU can address (``sparsl_host_alloc``),
+    as a numpy array (``.array``).  Passed as ``y`` of ``spmv`` /
+    ``spmv_spikes``, or as ``v``, ``theta`` and the spike bytes of the fused
+    LIF calls (all three), it is read and written in place by the kernels over
+    PCIe instead of being staged through device copies; the results are the
+    same bit for bit.  The memory lives while the buffer or any view of it
+    does."""
+
+    def __init__(self, n: int, dtype=np.float32):
+        dt = np.dtype(dtype)
+        n = int(n)
+        nbytes = max(n * dt.itemsize, 16)
+        ptr = _lib.load().sparsl_host_alloc(nbytes)
+        if not ptr:
+            raise OpError("Backend", "page-locked host allocation failed (is a CUDA device present?)",
+                          reason="host allocation failed")
+        buf = (ctypes.c_char * nbytes).from_address(ptr)
+        buf._block = _PinnedBlock(ptr)  # every view of buf keeps the block alive
+        self._buf = buf
+        self.array = np.frombuffer(buf, dtype=dt, count=n)
+
+    def data_ptr(self) -> int:
+        return ctypes.addressof(self._buf)
+
+
 # --------------------------------------------------------------------------
 # SparseOp (mod.rs:1281-2108)
 # --------------------------------------------------------------------------

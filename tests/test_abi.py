@@ -160,3 +160,26 @@ def test_csr_from_adjacency_and_parts():
     with pytest.raises(S.CsrError):
         S.Csr.from_parts([0, 2], [1, 0], 2)
     assert S.Csr.from_parts([0, 2], [0, 1], 2).nnz() == 2
+
+
+def test_host_buffer_is_pinned_or_refused():
+    """HostBuffer: page-locked host memory as a numpy array where a CUDA device
+    exists, the Backend error where none does.  A view of the array keeps the
+    memory alive after the buffer object is gone."""
+    import gc
+
+    import torch
+
+    if not torch.cuda.is_available():
+        with pytest.raises(S.OpError) as e:
+            S.HostBuffer(100)
+        assert e.value.kind == "Backend"
+        return
+    h = S.HostBuffer(100, np.float32)
+    assert h.array.dtype == np.float32 and h.array.size == 100 and h.array.flags.writeable
+    assert h.data_ptr() == h.array.ctypes.data
+    view = h.array[10:20]
+    del h
+    gc.collect()
+    view[:] = 3.0
+    assert float(view.sum()) == 30.0

@@ -8,15 +8,12 @@ stream for uniform rows, the ordered fold for skewed rows, the plain row
 fold), with a dense and a spike operand, a ragged last tile, and a mix of
 pinned and pageable buffers (which takes the copying route).  Likewise y of
 the forward SpMV and spike SpMV, accumulated in place by every engine."""
-import ctypes
-
 import numpy as np
 import pytest
 
 from conftest import assert_bits_equal
 
 import sparsl_b200 as S
-from sparsl_b200 import _lib
 
 pytestmark = pytest.mark.gpu
 
@@ -24,17 +21,15 @@ PARAMS = S.LifParams.new(0.9, 0.0, 0.1)
 
 
 class _Pinned:
-    """A numpy array over sparsl_host_alloc memory."""
+    """A pinned copy of `like` (sparsl_b200.HostBuffer)."""
 
     def __init__(self, like):
-        self.L = _lib.load()
-        self.ptr = self.L.sparsl_host_alloc(max(like.nbytes, 16))
-        buf = (ctypes.c_char * max(like.nbytes, 1)).from_address(self.ptr)
-        self.a = np.frombuffer(buf, dtype=like.dtype, count=like.size)
+        self.h = S.HostBuffer(like.size, like.dtype)
+        self.a = self.h.array
         self.a[:] = like
 
     def free(self):
-        self.L.sparsl_host_free(self.ptr)
+        del self.a, self.h
 
 
 def _skewed(O, nrows, ncols, seed):
