@@ -23,6 +23,11 @@ with the oracle's CpuParallel tick over the same arrays: the global spike
 trace, each rank's final membrane state and the final spike words.  At N=1
 that CPU run over the whole network is also the reported CPU baseline.
 
+``e2e`` is the same tick through the C ABI from host state: every step,
+``sparsl_net_steps_host`` takes the spike vector and this rank's membrane
+state from pinned host buffers, runs one tick and returns them (the tick
+kernels read and write the state over PCIe; the spike vector is copied).
+
 Other workloads (``--workload``): ``spmv`` (100k x 100k, 64 distinct sorted
 columns per row), ``scan`` (2^26 affine maps, a ~ U[0.9, 1], b ~ N(0, 1)),
 ``lif`` (262,144 neurons x fan-in 512, 1000-tick network on one GPU),
