@@ -2852,19 +2852,33 @@ int sparsl_net_steps_host(sparsl_net* net, uint32_t* xs, uint64_t words, float* 
     return rc;
   }
   if (!net->copy_in) {
+    // All or nothing: the net keeps the streams and events only when every
+    // one of them was made.
     cudaStream_t ci = nullptr, co = nullptr;
-    CK("net_steps_host", cudaStreamCreateWithFlags(&ci, cudaStreamNonBlocking));
-    net->copy_in = ci;
-    CK("net_steps_host", cudaStreamCreateWithFlags(&co, cudaStreamNonBlocking));
-    net->copy_out = co;
-    CK("net_steps_host", cudaEventCreateWithFlags(&net->ev_copied, cudaEventDisableTiming));
-    for (size_t b = 0; b < nb; ++b) {
-      cudaEvent_t a = nullptr, c = nullptr;
-      CK("net_steps_host", cudaEventCreateWithFlags(&a, cudaEventDisableTiming));
-      net->ev_in.push_back(a);
-      CK("net_steps_host", cudaEventCreateWithFlags(&c, cudaEventDisableTiming));
-      net->ev_out.push_back(c);
+    cudaEvent_t cp = nullptr;
+    std::vector<cudaEvent_t> ei(nb, nullptr), eo(nb, nullptr);
+    bool ok = cudaStreamCreateWithFlags(&ci, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaStreamCreateWithFlags(&co, cudaStreamNonBlocking) == cudaSuccess &&
+              cudaEventCreateWithFlags(&cp, cudaEventDisableTiming) == cudaSuccess;
+    for (size_t b = 0; ok && b < nb; ++b)
+      ok = cudaEventCreateWithFlags(&ei[b], cudaEventDisableTiming) == cudaSuccess &&
+           cudaEventCreateWithFlags(&eo[b], cudaEventDisableTiming) == cudaSuccess;
+    if (!ok) {
+      const cudaError_t e = cudaGetLastError();
+      for (cudaEvent_t x : ei)
+        if (x) cudaEventDestroy(x);
+      for (cudaEvent_t x : eo)
+        if (x) cudaEventDestroy(x);
+      if (cp) cudaEventDestroy(cp);
+      if (co) cudaStreamDestroy(co);
+      if (ci) cudaStreamDestroy(ci);
+      return fail(SPARSL_ERR_BACKEND, "copy stream creation failed", cudaGetErrorString(e));
     }
+    net->copy_in = ci;
+    net->copy_out = co;
+    net->ev_copied = cp;
+    net->ev_in = std::move(ei);
+    net->ev_out = std::move(eo);
   }
   // Work already on the net's stream (an earlier sparsl_net_steps_async)
   // ends before copy_in overwrites any state.
